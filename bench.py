@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gated DeltaNet hot path.  Prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: all 48 GDN layers of Qwen3.5/3.8-27B
+decode one token for a batch of B = 256 sequences; per layer and sequence the
+fp32 state (48 value heads x 128 x 128) is read and written once, in place.
+A step is the 48 per-layer launches of ``gdn_recurrent_fwd`` (sequential, as
+the layers of a real model are), replayed from a CUDA graph.  The metric is
+state bytes moved (read + write) per second of device time.
+
+N > 1 GPUs (torchrun, one process per GPU): the K-head groups are sharded
+(rank r owns 16/N key heads and their 48/N value heads) over a global batch
+of B*N sequences, so per-GPU work is fixed ("weak" scaling), and after every
+layer the bf16 head outputs are all-gathered over NCCL (the layer-boundary
+collective), overlapped with the next layer on a side stream.
+
+``--impl reference`` times the reference's CPU path (the C oracle's
+restatement of delta::run_reference, all host threads) on a bounded sample of
+the same workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "qwen3.8-27b-mlx_b200")
+for _p in (os.path.join(PKG, "python"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "GDN decode state HBM GB/s vs ~8 TB/s; chunked prefill tokens/s at 1/2/4/8 GPU"
+D = 128
+HK, HV = 16, 48
+STATE_BYTES = D * D * 4                   # one (Dv, Dk) fp32 head state
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            pass
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            if self.uuid and self.uuid.replace("GPU-", "") not in f[1]:
+                continue
+            rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# the decode workload
+# ---------------------------------------------------------------------------
+
+class DecodeLayers:
+    """Device buffers of L stacked GDN layers for one rank's head shard."""
+
+    def __init__(self, L, B, hk, hv, device, seed):
+        self.L, self.B, self.hk, self.hv = L, B, hk, hv
+        g = torch.Generator(device=device)
+        self.q, self.k, self.v, self.a, self.b = [], [], [], [], []
+        self.A_log, self.dt_bias, self.S, self.o = [], [], [], []
+        for layer in range(L):
+            g.manual_seed(seed * 1000 + layer)
+            qf = torch.randn((B, 1, hk, D), generator=g, device=device).bfloat16().float()
+            kf = torch.randn((B, 1, hk, D), generator=g, device=device).bfloat16().float()
+            qf = qf * torch.rsqrt((qf * qf).sum(-1, keepdim=True) + 1e-6) * D ** -0.5
+            kf = kf * torch.rsqrt((kf * kf).sum(-1, keepdim=True) + 1e-6)
+            self.q.append(qf.bfloat16().contiguous())
+            self.k.append(kf.bfloat16().contiguous())
+            self.v.append(torch.randn((B, 1, hv, D), generator=g, device=device).bfloat16())
+            self.a.append(torch.randn((B, 1, hv), generator=g, device=device))
+            self.b.append(torch.randn((B, 1, hv), generator=g, device=device))
+            self.A_log.append(torch.rand((hv,), generator=g, device=device) * float(np.log(16.0)))
+            self.dt_bias.append(torch.rand((hv,), generator=g, device=device))
+            self.S.append(torch.randn((B, hv, D, D), generator=g, device=device) * 0.05)
+            self.o.append(torch.empty((B, 1, hv, D), dtype=torch.bfloat16, device=device))
+
+    def state_bytes(self, B=None):
+        return 2 * (B or self.B) * self.hv * STATE_BYTES * self.L
+
+
+def launch_layer(lib, X, layer, B, stream_handle, q=None, k=None, v=None, a=None, b=None, o=None):
+    """One gdn_recurrent_fwd launch over the first B sequences of one layer
+    (in-place state update, bf16 output)."""
+    import gdn_b200 as G
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    S = X.S[layer]
+    rc = lib.gdn_recurrent_fwd(P(q if q is not None else X.q[layer]), P(k if k is not None else X.k[layer]),
+                               P(v if v is not None else X.v[layer]), P(a if a is not None else X.a[layer]),
+                               P(b if b is not None else X.b[layer]), P(X.A_log[layer]), P(X.dt_bias[layer]),
+                               P(S), P(S), P(o if o is not None else X.o[layer]), None,
+                               B, 1, X.hk, X.hv, D, D, G.F_O_BF16, stream_handle)
+    if rc != 0:
+        raise RuntimeError(f"gdn_recurrent_fwd failed: {rc} {lib.gdn_last_error().decode()}")
+
+
+def time_graph(fn, steps, warmup, device, world):
+    """Capture fn() (one step) in a CUDA graph, warm up, then time `steps`
+    replays with CUDA events; returns max-over-ranks milliseconds."""
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        fn()                                 # load modules outside the capture
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    del g
+    return max_over_ranks(ms, world, device)
+
+
+def run_ours(args, world, rank, local):
+    import gdn_b200 as G
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lib = G.lib()
+    hk, hv = HK // world, HV // world
+    B = args.batch
+    Bg = B * world                                  # global batch; every rank holds all of it for its heads
+    L = args.layers
+    X = DecodeLayers(L, Bg, hk, hv, device, seed=17 + rank)
+    torch.cuda.synchronize(device)
+    hbm_peak, _, peak_kind = peaks()
+
+    gathered = None
+    comm = None
+    if world > 1:
+        gathered = [torch.empty((world,) + tuple(X.o[i].shape), dtype=torch.bfloat16, device=device)
+                    for i in range(L)]
+        comm = torch.cuda.Stream(device)
+
+    def step(Bsub=Bg):
+        st = torch.cuda.current_stream(device)
+        h = ctypes.c_void_p(st.cuda_stream)
+        for layer in range(L):
+            launch_layer(lib, X, layer, Bsub, h)
+            if world > 1:
+                comm.wait_stream(st)
+                with torch.cuda.stream(comm):
+                    torch.distributed.all_gather_into_tensor(gathered[layer], X.o[layer])
+        if world > 1:
+            st.wait_stream(comm)
+
+    # --- headline: graph-replayed steps (N == 1) or eager steps with the gathers (N > 1)
+    with ClockSampler(device) as clk:
+        if world == 1:
+            ms = time_graph(step, args.steps, args.warmup, device, world)
+        else:
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize(device)
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize(device)
+            barrier(world)
+            ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    clocks = clk.summary()
+    ms_step = ms / args.steps
+    bytes_step_rank = X.state_bytes()
+    value = world * bytes_step_rank / (ms_step * 1e-3) / 1e9
+
+    # --- roofline: the dominant kernel's average launch duration (CUDA events per launch)
+    st = torch.cuda.current_stream(device)
+    h = ctypes.c_void_p(st.cuda_stream)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    durs = []
+    for _ in range(max(1, min(args.steps, 20))):
+        for layer in range(L):
+            evs[layer][0].record(st)
+            launch_layer(lib, X, layer, Bg, h)
+            evs[layer][1].record(st)
+        torch.cuda.synchronize(device)
+        durs += [a.elapsed_time(b) for a, b in evs]
+    launch_ms = statistics.mean(durs)
+    per_launch = 2 * Bg * hv * STATE_BYTES
+    achieved = per_launch / (launch_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                "frac_of_8TBps": round(achieved / 8000.0, 4),
+                "kernel": "recurrent_kernel", "bytes_per_launch": per_launch,
+                "launch_ms": round(launch_ms, 5), "traffic": args.traffic}
+
+    # --- batch sweep (B in {1, 16, 64, 256})
+    sweep = {}
+    if world == 1 and args.sweep:
+        for Bs in [int(x) for x in args.sweep.split(",") if x]:
+            if Bs > Bg:
+                continue
+            msb = time_graph(lambda: step(Bs), max(args.steps, 20), args.warmup, device, world)
+            sweep[str(Bs)] = round(X.state_bytes(Bs) / (msb / max(args.steps, 20) * 1e-3) / 1e9, 1)
+
+    # --- end to end through the C ABI with host buffers (pipelined per layer)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, lib, X, Bg, device, world)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(seconds=args.cpu_seconds)
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE config-0 distributions, independent seed per layer)",
+        "config": {"workload": f"config1: {L} GDN layers, decode T=1, B={Bg} per GPU shard, "
+                               f"Hk={HK} Hv={HV} Dk=Dv=128, fp32 state in place, bf16 q/k/v/o",
+                   "global_batch": Bg, "seq_len": 1, "layers": L,
+                   "parallelism": "single" if world == 1 else f"kheads{world}+allgather",
+                   "heads_per_gpu": {"k": hk, "v": hv},
+                   "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
+                   "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
+        "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
+        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu,
+    }
+    return line
+
+
+def run_e2e(args, lib, X, Bg, device, world):
+    """Same metric through the C ABI with the per-step inputs copied from
+    pinned host memory and the outputs read back, all inside the timed region.
+    Copies of layer l+1 overlap the kernel of layer l (two slots per buffer)."""
+    L = X.L
+    names = ("q", "k", "v", "a", "b")
+    host = [{n: getattr(X, n)[i].cpu().pin_memory() for n in names} for i in range(L)]
+    o_host = [torch.empty(X.o[i].shape, dtype=X.o[i].dtype).pin_memory() for i in range(L)]
+    slots = [{n: torch.empty_like(getattr(X, n)[0]) for n in names} for _ in range(2)]
+    o_slots = [torch.empty_like(X.o[0]) for _ in range(2)]
+    h2d_b = sum(t.numel() * t.element_size() for t in host[0].values()) * L
+    d2h_b = sum(t.numel() * t.element_size() for t in o_host)
+    comp = torch.cuda.current_stream(device)
+    cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready = [ev(), ev()]
+    slot_free = [ev(), ev()]
+    out_done = [ev(), ev()]
+    kdone = [ev(), ev()]
+    hcomp = ctypes.c_void_p(comp.cuda_stream)
+
+    def step():
+        for layer in range(L):
+            s = layer % 2
+            cin.wait_event(slot_free[s])
+            with torch.cuda.stream(cin):
+                for n in names:
+                    slots[s][n].copy_(host[layer][n], non_blocking=True)
+            in_ready[s].record(cin)
+            comp.wait_event(in_ready[s])
+            comp.wait_event(out_done[s])
+            launch_layer(lib, X, layer, Bg, hcomp, o=o_slots[s], **slots[s])
+            kdone[s].record(comp)
+            slot_free[s].record(comp)
+            cout.wait_event(kdone[s])
+            with torch.cuda.stream(cout):
+                o_host[layer].copy_(o_slots[s], non_blocking=True)
+            out_done[s].record(cout)
+        comp.wait_stream(cout)
+
+    for e in slot_free + out_done:
+        e.record(comp)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps // 2)
+    e0.record(comp)
+    cin.wait_stream(comp)
+    for _ in range(steps):
+        step()
+    e1.record(comp)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world, device) / steps
+    value = world * X.state_bytes() / (ms * 1e-3) / 1e9
+    return {"value": round(value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d_b,
+            "d2h_bytes_per_step": d2h_b, "ms_per_step": round(ms, 4), "steps": steps,
+            "api": "gdn_recurrent_fwd (C ABI via ctypes), pinned host inputs/outputs"}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's per-token recurrence (C oracle, all host threads)
+# ---------------------------------------------------------------------------
+
+def cpu_sample(B=1, L=48, seed=5):
+    import gdn_oracle as O
+    rng = np.random.default_rng(seed)
+    layers = []
+    for _ in range(L):
+        inp = O.synth_decode_inputs(rng, B, 1)
+        inp["S"] = inp.pop("S0")
+        layers.append(inp)
+    return layers
+
+
+def cpu_step(layers, threads):
+    import gdn_oracle as O
+    for x in layers:
+        O.recurrent_c(x["q"], x["k"], x["v"], x["a"], x["b"], x["A_log"], x["dt_bias"], x["S"],
+                      S_out=x["S"], nthreads=threads)
+
+
+def cpu_baseline(seconds=10.0, B=1):
+    threads = os.cpu_count() or 1
+    layers = cpu_sample(B)
+    cpu_step(layers, threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_step(layers, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = n * 2 * B * HV * STATE_BYTES * len(layers) / el / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} steps of 48 layers x B={B} decode, C restatement of delta::run_reference "
+                      f"(oracle/gdn_oracle.c, OpenMP over heads), {el:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    B = 1
+    layers = cpu_sample(B)
+    for _ in range(args.warmup):
+        cpu_step(layers, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(layers, threads)
+    el = time.perf_counter() - t0
+    ms = el * 1e3 / args.steps
+    gbs = 2 * B * HV * STATE_BYTES * len(layers) / (ms * 1e-3) / 1e9
+    sample = (f"each step: 48 layers x B={B} of the config-1 decode (a bounded sample of B=256), "
+              f"C restatement of delta::run_reference (oracle/gdn_oracle.c), {threads} threads")
+    return {"metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config-0 distributions)",
+            "config": {"workload": "config1: 48 GDN layers, decode T=1 (CPU sample B=1)", "global_batch": B,
+                       "seq_len": 1, "layers": 48, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU shard")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--sweep", default="1,16,64")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per launch from an ncu capture, reported as roofline.traffic")
+    ap.add_argument("--small", action="store_true", help="ncu-sized case: B=16, 2 layers, no extras")
+    args = ap.parse_args()
+    if args.small:
+        args.batch, args.layers, args.sweep = 16, 2, ""
+        args.no_e2e = args.no_cpu_baseline = True
+    args.warmup = max(args.warmup, 0)
+
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                             device_id=torch.device("cuda", local))
+    try:
+        line = run_ours(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

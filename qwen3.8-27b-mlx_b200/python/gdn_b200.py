@@ -1,0 +1,161 @@
+"""ctypes binding of the GDN C ABI (include/gdn_b200.h) for torch tensors.
+
+This is the host layer a Python caller uses: it checks dtypes, shapes,
+devices and contiguity of torch tensors, then passes raw device pointers and
+the current CUDA stream to ``libgdn_b200.so``.  Errors come back as
+``GdnError`` carrying the library's status code and message.  There is no
+fallback: if the library is missing or the tensors are not on a CUDA device,
+the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.environ.get("GDN_B200_LIB", os.path.join(PKG, "libgdn_b200.so"))
+
+GDN_OK = 0
+GDN_ERR_NULL = -1
+GDN_ERR_SHAPE = -2
+GDN_ERR_ALIGN = -3
+GDN_ERR_FLAGS = -4
+GDN_ERR_ALIAS = -5
+GDN_ERR_CUDA = -6
+GDN_ERR_RANGE = -7
+
+F_QKV_F32 = 0x1
+F_O_BF16 = 0x2
+F_GATES_DIRECT = 0x4
+F_QK_L2NORM = 0x8
+
+D = 128
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_u = ctypes.c_uint
+
+# name -> argtypes; every symbol include/gdn_b200.h declares
+SIGNATURES = {
+    "gdn_last_error": [],
+    "gdn_version": [],
+    "gdn_recurrent_fwd": [_vp] * 11 + [_i] * 6 + [_u, _vp],
+    "gdn_recurrent_fwd_from_ckpt": [_vp] * 9 + [_i] + [_vp] * 4 + [_i] * 6 + [_u, _vp],
+    "gdn_delta_run": [_vp] * 9 + [_i] * 5 + [_vp],
+}
+
+_lib = None
+
+
+class GdnError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"gdn error {code}: {msg}")
+        self.code = code
+
+
+def lib():
+    """Load libgdn_b200.so (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built; run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_char_p if name == "gdn_last_error" else ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != GDN_OK:
+        raise GdnError(rc, lib().gdn_last_error().decode())
+
+
+def ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dev(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("GDN tensors must live on a CUDA device")
+        if not t.is_contiguous():
+            raise ValueError("GDN tensors must be contiguous")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("GDN tensors must share one device")
+    return dev
+
+
+def recurrent_fwd(q, k, v, a, b, A_log=None, dt_bias=None, state_in=None, state_out=None,
+                  o=None, ckpt=None, *, gates_direct=False, l2norm=False,
+                  o_dtype=torch.float32):
+    """One decode / verify step through ``gdn_recurrent_fwd``.
+
+    q, k (B,T,Hk,128) and v (B,T,Hv,128), all bf16 or all fp32; a, b (B,T,Hv)
+    fp32; A_log, dt_bias (Hv,) fp32; state_in (B,Hv,128,128) fp32 or None.
+    Missing outputs are allocated.  Returns (o, state_out, ckpt).
+    """
+    B, T, Hk, Dk = q.shape
+    Hv = v.shape[2]
+    flags = 0
+    if q.dtype == torch.float32:
+        flags |= F_QKV_F32
+    elif q.dtype != torch.bfloat16:
+        raise ValueError("q, k, v must be bf16 or fp32")
+    if not (k.dtype == v.dtype == q.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    if gates_direct:
+        flags |= F_GATES_DIRECT
+    if l2norm:
+        flags |= F_QK_L2NORM
+    if o_dtype == torch.bfloat16:
+        flags |= F_O_BF16
+    dev = _dev(q, k, v, a, b, A_log, dt_bias, state_in, state_out, o, ckpt)
+    if o is None:
+        o = torch.empty((B, T, Hv, v.shape[-1]), dtype=o_dtype, device=dev)
+    if state_out is None and ckpt is None:
+        state_out = torch.empty((B, Hv, v.shape[-1], Dk), dtype=torch.float32, device=dev)
+    check(lib().gdn_recurrent_fwd(ptr(q), ptr(k), ptr(v), ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                  ptr(state_in), ptr(state_out), ptr(o), ptr(ckpt),
+                                  B, T, Hk, Hv, Dk, v.shape[-1], flags, stream_ptr(dev)))
+    return o, state_out, ckpt
+
+
+def recurrent_fwd_from_ckpt(q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src, commit_n,
+                            state_out=None, o=None, ckpt=None, err_flag=None, *,
+                            l2norm=False, o_dtype=torch.float32):
+    """Decode / verify step whose start state is the committed checkpoint
+    ``commit_n[b]`` of the previous verify block (``gdn_recurrent_fwd_from_ckpt``)."""
+    B, T, Hk, Dk = q.shape
+    Hv = v.shape[2]
+    flags = (F_QKV_F32 if q.dtype == torch.float32 else 0) | (F_QK_L2NORM if l2norm else 0)
+    if o_dtype == torch.bfloat16:
+        flags |= F_O_BF16
+    if commit_n.dtype != torch.int32:
+        raise ValueError("commit_n must be int32")
+    dev = _dev(q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src, commit_n, state_out, o, ckpt, err_flag)
+    if o is None:
+        o = torch.empty((B, T, Hv, D), dtype=o_dtype, device=dev)
+    if state_out is None and ckpt is None:
+        state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
+    Tsrc = ckpt_src.shape[2]
+    check(lib().gdn_recurrent_fwd_from_ckpt(ptr(q), ptr(k), ptr(v), ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                            ptr(state_prev), ptr(ckpt_src), ptr(commit_n), Tsrc,
+                                            ptr(state_out), ptr(o), ptr(ckpt), ptr(err_flag),
+                                            B, T, Hk, Hv, Dk, D, flags, stream_ptr(dev)))
+    return o, state_out, ckpt
