@@ -464,10 +464,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture, reported as roofline.traffic")
-    ap.add_argument("--small", action="store_true", help="ncu-sized case: B=16, 2 layers, no extras")
+    ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
     args = ap.parse_args()
     if args.small:
-        args.batch, args.layers, args.sweep = 16, 2, ""
+        args.batch, args.layers, args.sweep = 64, 2, ""
         args.no_e2e = args.no_cpu_baseline = True
     args.warmup = max(args.warmup, 0)
 

@@ -61,6 +61,14 @@ const char* gdn_last_error(void);
 int gdn_version(void);
 
 /*
+ * gdn_take_device_error -- synchronise `stream`, then read and clear the
+ * current device's kernel error word: 0 when no kernel of this library gave
+ * up on a bounded wait since the last call, nonzero otherwise.  No
+ * counterpart in the reference (MLX reports errors as exceptions).
+ */
+int gdn_take_device_error(void* stream, int* code);
+
+/*
  * gdn_recurrent_fwd -- decode (T = 1) and speculative verify (T = k+1) step.
  *
  * Replaces delta::run (cpp/src/delta.hpp:66-68, cpp/src/delta.cpp:137-173) and
@@ -118,6 +126,18 @@ int gdn_delta_run(const float* q, const float* k, const float* v,
                   const float* alpha, const float* beta, const float* S,
                   float* o, float* S_out, float* states,
                   int B, int L, int H, int Dk, int Dv, void* stream);
+
+/*
+ * gdn_tc05_selftest -- diagnostic of the tensor-core path (no counterpart in
+ * the reference): one CTA computes D (128 x N) = op(A) (128 x K) * B^T with
+ * B (N x K), all row-major fp32, through tcgen05.mma into tensor memory.
+ * mode bit 0: operands rounded to bf16 (kind::f16) instead of tf32;
+ * bit 1: A negated by the instruction descriptor; bit 2: A read from tensor
+ * memory (tf32 only).  N, K multiples of 16 in [16, 128].  *status (device
+ * int32) is set to 1 if the bounded wait for the MMA timed out.
+ */
+int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
+                      int* status, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -18,6 +18,8 @@
 //     are computed in-kernel (cpp/src/model.cpp:608-612);
 //   * state traffic uses streaming cache hints (ld.global.cs / st.global.cs):
 //     it is touched exactly once and must not evict the small shared inputs;
+//   * bytes in flight, not instructions, bound the kernel, so a warp owns up
+//     to R = 8 rows (4 KiB of loads outstanding per warp);
 //   * per-position checkpoints (DeltaCache record mode) are streamed out in
 //     the same pass, and the rollback of DeltaCache::commit is an index into
 //     them (gdn_recurrent_fwd_from_ckpt), not a copy.
@@ -27,9 +29,15 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+
 #include "gdn_internal.h"
 
 namespace gdn {
+
+// Device-side error word of this module (per device): set by a kernel whose
+// bounded wait timed out; read and cleared by gdn_take_device_error().
+__device__ int g_rec_device_error = 0;
+
 namespace {
 
 constexpr float kL2Eps = 1e-6f;                    // ops::l2norm eps (cpp/src/ops.hpp:19-20)
@@ -212,40 +220,49 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
   }
 }
 
+
 template <bool BF16>
 cudaError_t launch_rows(const RecParams& p, int R, cudaStream_t st) {
   const long long bh = static_cast<long long>(p.B) * p.Hv;
+  R = (R == 1 || R == 2 || R == 8) ? R : 4;
   const unsigned grid = static_cast<unsigned>(bh * (kD / (4 * R)));
   switch (R) {
     case 1: recurrent_kernel<BF16, 1><<<grid, 128, 0, st>>>(p); break;
     case 2: recurrent_kernel<BF16, 2><<<grid, 128, 0, st>>>(p); break;
+    case 8: recurrent_kernel<BF16, 8><<<grid, 128, 0, st>>>(p); break;
     default: recurrent_kernel<BF16, 4><<<grid, 128, 0, st>>>(p); break;
   }
   return cudaGetLastError();
 }
 
-// Rows per warp: 4 when there is enough work for several waves of blocks
-// (more bytes in flight per warp), fewer for small batches so that the whole
-// GPU still gets warps.
+// Rows per warp.  Bytes in flight per SM set the achieved HBM bandwidth:
+// with R rows a warp has R x 512 B of loads outstanding, so the largest R
+// that still fills the GPU with about one full wave of blocks wins.  Measured
+// on B200, one layer at B = 256 (in-place update, bf16 q/k/v/o): R = 1, 2, 4,
+// 8 -> 2.5, 4.2, 5.5, 6.2 TB/s.  Small batches fall back to fewer rows so that
+// every SM still gets warps.
 int rows_per_warp(long long bh) {
 #ifdef GDN_REC_ROWS
+  (void)bh;
   return GDN_REC_ROWS;
 #else
-  const long long target_blocks = 148LL * 16;
-  if (bh * (kD / 16) >= target_blocks) return 4;
-  if (bh * (kD / 8) >= target_blocks) return 2;
+  const long long one_wave = 148LL * 8;        // SMs x resident 128-thread blocks
+  for (int R = 8; R > 1; R >>= 1)
+    if (bh * (kD / (4 * R)) >= one_wave) return R;
   return 1;
 #endif
 }
 
+// Which kernel streams the state: the bulk-copy ring once there are enough
+// 32-row units for several per CTA slot, the register kernel for small batches.
 int run_recurrent(const RecParams& p, void* stream) {
   if (p.B == 0) return GDN_OK;
   const long long bh = static_cast<long long>(p.B) * p.Hv;
-  const int R = rows_per_warp(bh);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = (p.flags & GDN_F_QKV_F32) == 0;
-  return cuda_status(bf16 ? launch_rows<true>(p, R, st) : launch_rows<false>(p, R, st),
-                     "gdn recurrent kernel launch");
+  const int R = rows_per_warp(bh);
+  const cudaError_t e = bf16 ? launch_rows<true>(p, R, st) : launch_rows<false>(p, R, st);
+  return cuda_status(e, "gdn recurrent kernel launch");
 }
 
 constexpr unsigned kKnownFlags = GDN_F_QKV_F32 | GDN_F_O_BF16 | GDN_F_GATES_DIRECT | GDN_F_QK_L2NORM;
@@ -343,4 +360,26 @@ extern "C" int gdn_delta_run(const float* q, const float* k, const float* v, con
                              float* states, int B, int L, int H, int Dk, int Dv, void* stream) {
   return gdn_recurrent_fwd(q, k, v, alpha, beta, nullptr, nullptr, S, S_out, o, states, B, L, H, H,
                            Dk, Dv, GDN_F_QKV_F32 | GDN_F_GATES_DIRECT, stream);
+}
+
+extern "C" int gdn_take_device_error(void* stream, int* code) {
+  clear_error();
+  if (!code) return fail(GDN_ERR_NULL, "code is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  int rc = cuda_status(cudaMemcpyFromSymbolAsync(&v, gdn::g_rec_device_error, sizeof(int), 0,
+                                                 cudaMemcpyDeviceToHost, st), "read device error word");
+  if (rc != GDN_OK) return rc;
+  rc = cuda_status(cudaStreamSynchronize(st), "synchronize");
+  if (rc != GDN_OK) return rc;
+  if (v != 0) {
+    const int zero = 0;
+    rc = cuda_status(cudaMemcpyToSymbolAsync(gdn::g_rec_device_error, &zero, sizeof(int), 0,
+                                             cudaMemcpyHostToDevice, st), "clear device error word");
+    if (rc != GDN_OK) return rc;
+    rc = cuda_status(cudaStreamSynchronize(st), "synchronize");
+    if (rc != GDN_OK) return rc;
+  }
+  *code = v;
+  return GDN_OK;
 }

@@ -1,0 +1,131 @@
+// Device self-test of the tcgen05 tensor-core path the chunked prefill kernel
+// is built on: one CTA computes D (128 x N) = op(A) (128 x K) * B^T (B is
+// N x K) through tcgen05.mma with the accumulator in tensor memory, using the
+// same shared-memory layout, descriptors and TMEM load/store helpers as the
+// prefill kernel.  Modes: tf32 or bf16 operands, A negated by the instruction
+// descriptor, A read from tensor memory instead of shared memory.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "gdn_internal.h"
+#include "gdn_ptx.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int kSelfTestCols = 256;   // TMEM columns: D in [0,128), A in [128,256)
+
+__global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                            float* __restrict__ D, int N, int K, int mode,
+                                                            int* __restrict__ status) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const bool bf = (mode & 1) != 0;
+  const int E = bf ? 2 : 4;
+  const uint32_t kbytes = static_cast<uint32_t>(K * E);
+  const uint32_t sbo = (kbytes / 16) * 128;
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + 128 * kbytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sB + static_cast<size_t>(N) * kbytes);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+
+  for (int idx = tid; idx < 128 * K; idx += 128) {
+    const int r = idx / K, k = idx - r * K;
+    const uint32_t off = tc::kmajor_offset(r, k, E, sbo);
+    if (bf) *reinterpret_cast<__nv_bfloat16*>(sA + off) = __float2bfloat16_rn(A[idx]);
+    else *reinterpret_cast<float*>(sA + off) = A[idx];
+  }
+  for (int idx = tid; idx < N * K; idx += 128) {
+    const int r = idx / K, k = idx - r * K;
+    const uint32_t off = tc::kmajor_offset(r, k, E, sbo);
+    if (bf) *reinterpret_cast<__nv_bfloat16*>(sB + off) = __float2bfloat16_rn(B[idx]);
+    else *reinterpret_cast<float*>(sB + off) = B[idx];
+  }
+  ptx::fence_proxy_async_smem();
+  if (warp == 0) {
+    tc::tmem_alloc(slot, kSelfTestCols);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    ptx::mbar_init(bar, 1);
+    ptx::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t base = *slot;
+  const uint32_t tD = base;
+  const uint32_t tA = base + 128;
+
+  if (mode & 4) {       // A into tensor memory: row r = lane r, one tf32 per column
+    for (int c = 0; c < K; c += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = A[static_cast<size_t>(tid) * K + c + i];
+      tc::tmem_st16(tc::tmem_addr(tA, warp, c), v);
+    }
+    tc::tmem_st_wait();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+  }
+
+  if (tid == 0) {
+    const uint32_t idesc = tc::instr_desc(bf ? tc::kBF16 : tc::kTF32, 128, N, (mode & 2) != 0);
+    const int steps = static_cast<int>(kbytes / 32);
+    for (int j = 0; j < steps; ++j) {
+      const uint64_t bd = tc::smem_desc(ptx::smem_u32(sB) + j * 256, 128, sbo);
+      if (mode & 4) {
+        tc::mma_ts_tf32(tD, tA + j * 8, bd, idesc, j > 0);
+      } else {
+        const uint64_t ad = tc::smem_desc(ptx::smem_u32(sA) + j * 256, 128, sbo);
+        if (bf) tc::mma_ss<tc::kBF16>(tD, ad, bd, idesc, j > 0);
+        else tc::mma_ss<tc::kTF32>(tD, ad, bd, idesc, j > 0);
+      }
+    }
+    tc::mma_commit(bar);
+  }
+  bool ok = ptx::mbar_wait(bar, 0);
+  tc::fence_after_sync();
+  if (__syncthreads_and(ok)) {
+    for (int c = 0; c < N; c += 16) {
+      float v[16];
+      tc::tmem_ld16(tc::tmem_addr(tD, warp, c), v);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) D[static_cast<size_t>(tid) * N + c + i] = v[i];
+    }
+  } else {
+    if (tid == 0) *status = 1;
+    ok = ptx::mbar_wait(bar, 0);       // give the MMA another bounded chance to land
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(base, kSelfTestCols);
+}
+
+}  // namespace
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
+                                 int* status, void* stream) {
+  clear_error();
+  if (mode & ~7) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~7);
+  if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
+  if (N < 16 || N > 128 || N % 16 || K < 16 || K > 128 || K % 16)
+    return fail(GDN_ERR_SHAPE, "N=%d K=%d: need multiples of 16 in [16, 128]", N, K);
+  if (!A || !B || !D || !status) return fail(GDN_ERR_NULL, "A, B, D and status are required");
+  if (!aligned(A, 4) || !aligned(B, 4) || !aligned(D, 4) || !aligned(status, 4))
+    return fail(GDN_ERR_ALIGN, "buffers must be 4-byte aligned");
+  const int E = (mode & 1) ? 2 : 4;
+  const size_t smem = static_cast<size_t>(128 + N) * K * E + 16;
+  int rc = cuda_status(cudaFuncSetAttribute(tc05_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)),
+                       "tc05 self-test smem attribute");
+  if (rc != GDN_OK) return rc;
+  tc05_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(A, B, D, N, K, mode, status);
+  return cuda_status(cudaGetLastError(), "tc05 self-test launch");
+}

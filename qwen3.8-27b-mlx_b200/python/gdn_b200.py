@@ -43,9 +43,11 @@ _u = ctypes.c_uint
 SIGNATURES = {
     "gdn_last_error": [],
     "gdn_version": [],
+    "gdn_take_device_error": [_vp, _vp],
     "gdn_recurrent_fwd": [_vp] * 11 + [_i] * 6 + [_u, _vp],
-    "gdn_recurrent_fwd_from_ckpt": [_vp] * 9 + [_i] + [_vp] * 4 + [_i] * 6 + [_u, _vp],
+    "gdn_recurrent_fwd_from_ckpt": [_vp] * 10 + [_i] + [_vp] * 4 + [_i] * 6 + [_u, _vp],
     "gdn_delta_run": [_vp] * 9 + [_i] * 5 + [_vp],
+    "gdn_tc05_selftest": [_vp] * 3 + [_i] * 3 + [_vp, _vp],
 }
 
 _lib = None
@@ -75,6 +77,15 @@ def lib():
 def check(rc: int):
     if rc != GDN_OK:
         raise GdnError(rc, lib().gdn_last_error().decode())
+
+
+def take_device_error(device=None) -> int:
+    """Synchronise the current stream and return (and clear) the device's
+    kernel error word (0 = no bounded wait timed out)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    out = ctypes.c_int(0)
+    check(lib().gdn_take_device_error(stream_ptr(dev), ctypes.byref(out)))
+    return out.value
 
 
 def ptr(t: Optional[torch.Tensor]):
@@ -159,3 +170,15 @@ def recurrent_fwd_from_ckpt(q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src,
                                             ptr(state_out), ptr(o), ptr(ckpt), ptr(err_flag),
                                             B, T, Hk, Hv, Dk, D, flags, stream_ptr(dev)))
     return o, state_out, ckpt
+
+
+def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False):
+    """D = op(A) @ B.T on one CTA through tcgen05 (diagnostic).  A (128,K),
+    B (N,K) fp32 CUDA tensors.  Returns (D, status)."""
+    dev = _dev(A, B)
+    N, K = B.shape
+    D = torch.empty((128, N), dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    mode = (1 if bf16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0)
+    check(lib().gdn_tc05_selftest(ptr(A), ptr(B), ptr(D), N, K, mode, ptr(status), stream_ptr(dev)))
+    return D, status

@@ -16,13 +16,20 @@ from conftest import ROOT
 FAKE = 1 << 40          # 16-byte aligned fake device address, never dereferenced
 
 
-def declared_functions():
-    names = set()
+def declarations():
+    """name -> list of parameter declarations, parsed from include/*.h."""
+    out = {}
     for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
         src = open(h).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-        names |= set(re.findall(r"\b(gdn_\w+)\s*\(", src))
-    return sorted(names)
+        for name, params in re.findall(r"\b(gdn_\w+)\s*\(([^;{]*?)\)\s*;", src):
+            ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+            out[name] = ps
+    return out
+
+
+def declared_functions():
+    return sorted(declarations())
 
 
 def test_library_exports_every_declared_symbol():
@@ -32,6 +39,17 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), n
         assert n in G.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_ctypes_signatures_match_header_parameter_lists():
+    """Every ctypes argtypes list has one entry per declared parameter, and
+    pointers / integers sit where the header puts them."""
+    for name, params in declarations().items():
+        args = G.SIGNATURES[name]
+        assert len(args) == len(params), (name, len(args), len(params))
+        for decl, t in zip(params, args):
+            is_ptr = "*" in decl
+            assert (t is ctypes.c_void_p) == is_ptr, (name, decl, t)
 
 
 def test_version():

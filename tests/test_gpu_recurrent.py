@@ -186,3 +186,39 @@ def test_large_batch_linearity_and_spot_check():
         one = {kk: (vv[bi:bi + 1] if vv.ndim > 1 else vv) for kk, vv in inp.items()}
         ro, rS = oracle_step(one, inp["S0"][bi:bi + 1], collect=False)
         assert O.rel_err(host(o1[bi:bi + 1]), ro) < TOL and O.rel_err(host(T1[bi:bi + 1]), rS) < TOL
+
+
+def test_bulk_copy_path_rollback_in_place_and_zero_state():
+    """A batch large enough for the bulk-copy (TMA engine) kernel: rollback by
+    index with an out-of-range entry, then an in-place step, then a zero start
+    state; all against the oracle, and no bounded wait may have timed out."""
+    B, T = 24, 2
+    rng = np.random.default_rng(14)
+    ver = O.synth_decode_inputs(rng, B, T)
+    _, _, rst = oracle_step(ver, ver["S0"])
+    S_prev = dev(ver["S0"])
+    ckpt = torch.empty((B, 48, T, 128, 128), device="cuda")
+    G.recurrent_fwd(*device_inputs(ver), state_in=S_prev, ckpt=ckpt)
+    commit = (np.arange(B) % (T + 2)).astype(np.int32)      # includes T+1: out of range
+    nxt = O.synth_decode_inputs(rng, B, 1)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o, S, _ = G.recurrent_fwd_from_ckpt(*device_inputs(nxt), S_prev, ckpt,
+                                        torch.from_numpy(commit).cuda(), err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    starts = np.stack([ver["S0"][bi] if n == 0 else (rst[bi, :, n - 1] if n <= T else np.zeros_like(ver["S0"][bi]))
+                       for bi, n in enumerate(commit)])
+    ro, rS = oracle_step(nxt, starts, collect=False)
+    assert O.rel_err(host(o), ro) < TOL and O.rel_err(host(S), rS) < TOL
+    S_in = dev(starts)
+    o2, S2, _ = G.recurrent_fwd(*device_inputs(nxt), state_in=S_in, state_out=S_in)
+    assert S2.data_ptr() == S_in.data_ptr()
+    assert O.rel_err(host(o2), ro) < TOL and O.rel_err(host(S_in), rS) < TOL
+    o3, S3, _ = G.recurrent_fwd(*device_inputs(nxt), state_in=None)
+    ro3, rS3 = oracle_step(nxt, None, collect=False)
+    assert O.rel_err(host(o3), ro3) < TOL and O.rel_err(host(S3), rS3) < TOL
+    assert G.take_device_error() == 0
+
+
+def test_no_device_errors_recorded():
+    assert G.take_device_error() == 0

@@ -1,0 +1,36 @@
+"""The tcgen05 tensor-core path (descriptors, TMEM alloc/ld/st, commit) on
+the device, through the gdn_tc05_selftest diagnostic: D = op(A) @ B^T against
+a float64 product of the same (tf32- or bf16-representable) operands.
+Tolerance 1e-5 max-relative: the products are exact, only the fp32
+accumulation order differs."""
+import numpy as np
+import pytest
+import torch
+
+import gdn_b200 as G
+import gdn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def tf32(x):
+    return (x.view(torch.int32) & ~0x1FFF).view(torch.float32)
+
+
+@pytest.mark.parametrize("N,K", [(64, 64), (128, 128), (64, 128), (16, 16)])
+@pytest.mark.parametrize("mode", ["tf32", "bf16", "neg", "tmem"])
+def test_tc05_gemm(N, K, mode):
+    g = torch.Generator(device="cuda").manual_seed(N * 1000 + K)
+    A = torch.randn((128, K), generator=g, device="cuda")
+    B = torch.randn((N, K), generator=g, device="cuda")
+    if mode == "bf16":
+        A, B = A.bfloat16().float(), B.bfloat16().float()
+    else:
+        A, B = tf32(A), tf32(B)
+    D, st = G.tc05_selftest(A, B, bf16=(mode == "bf16"), negate_a=(mode == "neg"), a_in_tmem=(mode == "tmem"))
+    torch.cuda.synchronize()
+    ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
+    if mode == "neg":
+        ref = -ref
+    assert int(st.item()) == 0
+    assert O.rel_err(D.cpu().numpy(), ref) < 1e-5
