@@ -54,6 +54,13 @@ extern "C" {
 #define GDN_F_QK_L2NORM     0x8u  /* l2-normalise q, k per head (eps 1e-6 inside the
                                      rsqrt) and scale q by Dk^-1/2 inside the kernel */
 
+/* ---- flags of the front-end / back-end kernels --------------------------- */
+#define GDN_F_CONV_BF16_OPS 0x100u  /* conv: MLX's per-op bf16 arithmetic (each product and
+                                       partial sum rounded) instead of fp32 accumulation */
+#define GDN_F_CONV_NO_SILU  0x200u  /* conv: skip the SiLU after the convolution */
+#define GDN_F_NORM_IN_BF16  0x400u  /* gated norm: o is bf16 (default fp32) */
+#define GDN_F_NORM_OUT_F32  0x800u  /* gated norm: out is fp32 (default bf16) */
+
 /* Human-readable text of the last error on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
@@ -126,6 +133,74 @@ int gdn_delta_run(const float* q, const float* k, const float* v,
                   const float* alpha, const float* beta, const float* S,
                   float* o, float* S_out, float* states,
                   int B, int L, int H, int Dk, int Dv, void* stream);
+
+/*
+ * gdn_chunked_fwd -- prefill: the chunked (WY / UT) form of the recurrence
+ * over whole sequences, on the tensor cores.  Replaces chunked_delta
+ * (python/qwen35.py:365-431) together with its gate, l2norm, q-scale and
+ * head-repeat prologue (python/qwen35.py:586-600): q, k are the raw conv
+ * outputs, normalised inside the kernel when GDN_F_QK_L2NORM is set.
+ * Matches the reference's chunk size (64) and its clip of alpha at 1e-6.
+ *   q, k   bf16, element (token t, key head i, d) at q[t*q_stride + i*128 + d]
+ *   v      bf16, element (t, value head h, d) at v[t*v_stride + h*128 + d]
+ *          (for the conv output (T, 10240): q = y, k = y + 2048,
+ *          v = y + 4096, all strides 10240)
+ *   a, b   (T, Hv) fp32 gate pre-activations; A_log, dt_bias (Hv) fp32
+ *   state_in, state_out (B, Hv, Dv, Dk) fp32; NULL in = zeros; may be equal
+ *   o      (T, Hv, Dv) fp32 (GDN_F_O_BF16: bf16), token-major like the input
+ *   cu_seqlens  NULL (B sequences of T tokens; token t of sequence b is row
+ *          b*T + t) or device int32 (B+1) offsets of packed sequences.
+ * Flags: GDN_F_QK_L2NORM, GDN_F_O_BF16.  Strides multiples of 8 elements;
+ * q, k, v, states 16-byte aligned.  One CTA per (sequence, value head).
+ */
+int gdn_chunked_fwd(const void* q, const void* k, const void* v,
+                    long long q_stride, long long k_stride, long long v_stride,
+                    const float* a, const float* b, const float* A_log, const float* dt_bias,
+                    const float* state_in, float* state_out, void* o,
+                    const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                    unsigned flags, void* stream);
+
+/*
+ * gdn_conv1d_fwd -- causal depthwise conv1d (kernel K = 4, no bias) over the
+ * concatenated q|k|v channels, then SiLU: the front end of
+ * GatedDeltaNet::operator() (DepthwiseConv::operator(), cpp/src/model.cpp:
+ * 385-395, and the silu at :588; python/qwen35.py:642-660, :581).
+ *   x      (B, T, C) bf16, or packed (T, C) when cu_seqlens is given
+ *   w      (C, K) bf16 -- the stored (C, 1, K) conv1d weight
+ *   state_in  (B, K-1, C) bf16 carried window, NULL for zeros
+ *   state_out (B, K-1, C) bf16 or NULL: the last K-1 rows of [state_in; x_b]
+ *   y      like x, bf16: silu(conv) (GDN_F_CONV_NO_SILU: conv only)
+ *   cu_seqlens  NULL (B sequences of T tokens) or device int32 (B+1) offsets
+ *          of B packed sequences: cu[0] = 0, nondecreasing, cu[B] = T.
+ * fp32 products and sums by default; GDN_F_CONV_BF16_OPS rounds every
+ * product and partial sum to bf16 as MLX does for bf16 activations.
+ * C a multiple of 8; x, w, y, states 16-byte aligned; y must not overlap x.
+ */
+int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in, void* state_out, void* y,
+                   const int32_t* cu_seqlens, int B, int T, int C, int K, unsigned flags,
+                   void* stream);
+
+/*
+ * gdn_conv_commit -- conv half of DeltaCache::commit (cpp/src/model.cpp:
+ * 446-447, python/qwen35.py:320-323) after a recorded block of T tokens:
+ * state_out[b] = rows n .. n+K-2 of [state_prev[b]; x[b]] with n = commit_n[b]
+ * (device int32, 0 <= n <= T).  Out-of-range n uses n = 0 and sets *err_flag.
+ *   state_prev (B, K-1, C) bf16 or NULL (zeros); x (B, T, C) bf16.
+ */
+int gdn_conv_commit(const void* state_prev, const void* x, const int32_t* commit_n, void* state_out,
+                    int32_t* err_flag, int B, int T, int C, int K, void* stream);
+
+/*
+ * gdn_gated_rmsnorm_fwd -- normalise, then gate (GatedRMSNorm,
+ * cpp/src/model.cpp:350-354, python/qwen35.py:159-180):
+ *   out = o * rsqrt(mean(o^2) + eps) * gamma * silu(z)
+ * over rows of D = 128.  o (rows, D) fp32 (GDN_F_NORM_IN_BF16: bf16), z (rows,
+ * D) bf16, gamma (D) fp32 used as stored (not zero-centred), out (rows, D)
+ * bf16 (GDN_F_NORM_OUT_F32: fp32).  out may equal o when both are the same
+ * dtype and width.
+ */
+int gdn_gated_rmsnorm_fwd(const void* o, const void* z, const float* gamma, void* out, long long rows,
+                          int D, float eps, unsigned flags, void* stream);
 
 /*
  * gdn_tc05_selftest -- diagnostic of the tensor-core path (no counterpart in

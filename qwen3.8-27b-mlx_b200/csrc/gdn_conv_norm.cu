@@ -1,0 +1,353 @@
+// Front end and back end of the Gated DeltaNet block, sm_100a:
+//
+//   * gdn_conv1d_fwd: causal depthwise conv1d (kernel 4, no bias) over the
+//     concatenated q|k|v channels with its carried window, then SiLU
+//     (cpp/src/model.cpp:385-395 and :588; python/qwen35.py:642-660).
+//   * gdn_conv_commit: the conv half of DeltaCache::commit
+//     (cpp/src/model.cpp:446-447): window = rows n .. n+K-2 of [state; x].
+//   * gdn_gated_rmsnorm_fwd: normalise, then gate
+//     (cpp/src/model.cpp:350-354): rms_norm(o, gamma, eps) * silu(z).
+//
+// All three are HBM-bound streams of bf16 activations: 16-byte vector loads
+// and stores, one pass over the data, fp32 arithmetic in registers.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "gdn_internal.h"
+
+namespace gdn {
+namespace {
+
+constexpr int kConvK = 4;            // linear_conv_kernel_dim (python/qwen35.py:92)
+constexpr int kConvVec = 8;          // channels per thread (one 16-byte bf16 vector)
+constexpr int kConvThreads = 128;
+constexpr int kConvRun = 32;         // tokens per thread
+
+struct alignas(16) Bf16x8 {
+  __nv_bfloat162 h[4];
+};
+
+__device__ __forceinline__ void unpack8(const Bf16x8& v, float (&f)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(v.h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ Bf16x8 pack8(const float (&f)[8]) {
+  Bf16x8 v;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v.h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
+// Sequence of packed token `tok` (binary search over cu_seqlens[0..B]).
+__device__ __forceinline__ int seq_of(const int32_t* cu, int B, long long tok) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= tok) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+struct ConvParams {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w;          // (C, K)
+  const __nv_bfloat16* state_in;   // (B, K-1, C) or null
+  __nv_bfloat16* state_out;        // (B, K-1, C) or null
+  __nv_bfloat16* y;
+  const int32_t* cu;               // (B+1) or null: uniform B x T
+  long long total;                 // tokens
+  int B, T, C;
+  unsigned flags;
+};
+
+// One thread: 8 channels x a run of up to 32 consecutive packed tokens, with
+// the 3-row causal window in registers, so every x element is read once
+// (plus a 3-row halo at the start of the run).
+__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvParams p) {
+  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * kConvVec;
+  if (c0 >= p.C) return;
+  const long long t_begin = static_cast<long long>(blockIdx.y) * kConvRun;
+  if (t_begin >= p.total) return;
+  const long long t_end = t_begin + kConvRun < p.total ? t_begin + kConvRun : p.total;
+  const bool silu = !(p.flags & GDN_F_CONV_NO_SILU);
+  const bool bf16_ops = (p.flags & GDN_F_CONV_BF16_OPS) != 0;
+
+  float w[kConvK][kConvVec];
+  {
+    // w is (C, K): the 8 channels x 4 taps are 32 contiguous bf16
+    const Bf16x8* wp = reinterpret_cast<const Bf16x8*>(p.w + static_cast<size_t>(c0) * kConvK);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float f[8];
+      unpack8(wp[q], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int flat = q * 8 + e;                 // = channel_offset * K + tap
+        w[flat % kConvK][flat / kConvK] = f[e];
+      }
+    }
+  }
+
+  // token range of sequence `seq`: packed offsets, or seq*T .. seq*T+T
+  auto seq_begin = [&](int sq) -> long long { return p.cu ? p.cu[sq] : static_cast<long long>(sq) * p.T; };
+  auto seq_end = [&](int sq) -> long long { return p.cu ? p.cu[sq + 1] : static_cast<long long>(sq + 1) * p.T; };
+  int seq = p.cu ? seq_of(p.cu, p.B, t_begin) : static_cast<int>(t_begin / p.T);
+  long long s_begin = seq_begin(seq);
+  long long s_end = seq_end(seq);
+
+  float win[kConvK - 1][kConvVec];
+  auto load_window = [&](long long t) {
+    // rows t-3 .. t-1 of [state; x] for the sequence that holds t
+#pragma unroll
+    for (int j = 0; j < kConvK - 1; ++j) {
+      const long long pos = t - s_begin - (kConvK - 1) + j;     // position in the sequence
+      const long long row = s_begin + pos;                       // packed row (guards a bad cu_seqlens)
+      if (pos >= 0 && row >= 0 && row < p.total) {
+        unpack8(*reinterpret_cast<const Bf16x8*>(p.x + row * p.C + c0), win[j]);
+      } else if (p.state_in && pos < 0 && pos >= -(kConvK - 1)) {
+        const long long srow = (kConvK - 1) + pos;               // 0 .. K-2
+        unpack8(*reinterpret_cast<const Bf16x8*>(p.state_in + (static_cast<long long>(seq) * (kConvK - 1) + srow) * p.C + c0),
+                win[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
+      }
+    }
+  };
+  load_window(t_begin);
+
+  for (long long t = t_begin; t < t_end; ++t) {
+    if (t >= s_end && seq < p.B - 1) {   // crossed into the next sequence
+      ++seq;
+      s_begin = seq_begin(seq);
+      s_end = seq_end(seq);
+      while (t >= s_end && seq < p.B - 1) {   // skip empty packed sequences
+        ++seq;
+        s_begin = seq_begin(seq);
+        s_end = seq_end(seq);
+      }
+      load_window(t);
+    }
+    float xv[kConvVec];
+    unpack8(*reinterpret_cast<const Bf16x8*>(p.x + t * p.C + c0), xv);
+    float out[kConvVec];
+#pragma unroll
+    for (int e = 0; e < kConvVec; ++e) {
+      float acc;
+      if (bf16_ops) {   // MLX per-op bf16: each product and each partial sum rounded
+        acc = bf16r(win[0][e] * w[0][e]);
+        acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
+        acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
+        acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
+        if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
+      } else {
+        acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
+        if (silu) acc = acc * sigmoid_f(acc);
+      }
+      out[e] = acc;
+    }
+    *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = pack8(out);
+#pragma unroll
+    for (int e = 0; e < kConvVec; ++e) {
+      win[0][e] = win[1][e];
+      win[1][e] = win[2][e];
+      win[2][e] = xv[e];
+    }
+    if (p.state_out && t == s_end - 1) {
+      // the carried window: the last K-1 rows of [state; x]
+#pragma unroll
+      for (int j = 0; j < kConvK - 1; ++j)
+        *reinterpret_cast<Bf16x8*>(p.state_out + (static_cast<long long>(seq) * (kConvK - 1) + j) * p.C + c0) =
+            pack8(win[j]);
+    }
+  }
+}
+
+// Sequences of length 0 still get their window carried: state_out = state_in.
+__global__ void conv_empty_kernel(const ConvParams p) {
+  const int seq = blockIdx.y;
+  const long long len = p.cu ? static_cast<long long>(p.cu[seq + 1] - p.cu[seq]) : p.T;
+  if (len != 0) return;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * kConvVec;
+  if (c0 >= p.C) return;
+  for (int j = 0; j < kConvK - 1; ++j) {
+    const size_t off = (static_cast<size_t>(seq) * (kConvK - 1) + j) * p.C + c0;
+    Bf16x8 v;
+    if (p.state_in) {
+      v = *reinterpret_cast<const Bf16x8*>(p.state_in + off);
+    } else {
+      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      v = pack8(z);
+    }
+    *reinterpret_cast<Bf16x8*>(p.state_out + off) = v;
+  }
+}
+
+// commit: window of sequence b = rows n_b .. n_b+K-2 of [state_prev; x_b].
+__global__ void conv_commit_kernel(const __nv_bfloat16* state_prev, const __nv_bfloat16* x, const int32_t* n,
+                                   __nv_bfloat16* state_out, int T, int C, int32_t* err) {
+  const int b = blockIdx.y;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * kConvVec;
+  if (c0 >= C) return;
+  const int nb = n[b];
+  const bool ok = nb >= 0 && nb <= T;
+  if (!ok && err && c0 == 0) atomicExch(err, 1);
+  for (int j = 0; j < kConvK - 1; ++j) {
+    const int row = (ok ? nb : 0) + j;                    // row of [state (K-1 rows); x (T rows)]
+    Bf16x8 v;
+    if (row < kConvK - 1) {
+      if (state_prev) {
+        v = *reinterpret_cast<const Bf16x8*>(state_prev + (static_cast<size_t>(b) * (kConvK - 1) + row) * C + c0);
+      } else {
+        float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        v = pack8(z);
+      }
+    } else {
+      v = *reinterpret_cast<const Bf16x8*>(x + (static_cast<size_t>(b) * T + (row - (kConvK - 1))) * C + c0);
+    }
+    *reinterpret_cast<Bf16x8*>(state_out + (static_cast<size_t>(b) * (kConvK - 1) + j) * C + c0) = v;
+  }
+}
+
+// Gated RMSNorm: one warp per (token, head) row of 128; lane j holds 4
+// consecutive elements.  out = o * rsqrt(mean(o^2) + eps) * gamma * silu(z).
+__global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const void* o, const __nv_bfloat16* z, const float* gamma,
+                                                           void* out, long long rows, float eps, unsigned flags) {
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const size_t base = static_cast<size_t>(row) * kD + lane * 4;
+  float x[4];
+  if (flags & GDN_F_NORM_IN_BF16) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(o) + base);
+    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    x[0] = lo.x; x[1] = lo.y; x[2] = hi.x; x[3] = hi.y;
+  } else {
+    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(o) + base);
+    x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
+  }
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(ss / static_cast<float>(kD) + eps);
+  const uint2 zr = *reinterpret_cast<const uint2*>(z + base);
+  const float2 zlo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zr.x));
+  const float2 zhi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zr.y));
+  const float zz[4] = {zlo.x, zlo.y, zhi.x, zhi.y};
+  const float4 g = *reinterpret_cast<const float4*>(gamma + lane * 4);
+  const float gg[4] = {g.x, g.y, g.z, g.w};
+  float y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) y[i] = (x[i] * r * gg[i]) * (zz[i] * sigmoid_f(zz[i]));
+  if (flags & GDN_F_NORM_OUT_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(out) + base) = make_float4(y[0], y[1], y[2], y[3]);
+  } else {
+    __nv_bfloat162 a = __floats2bfloat162_rn(y[0], y[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(y[2], y[3]);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&a);
+    w.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + base) = w;
+  }
+}
+
+}  // namespace
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in, void* state_out, void* y,
+                              const int32_t* cu_seqlens, int B, int T, int C, int K, unsigned flags,
+                              void* stream) {
+  clear_error();
+  if (flags & ~(GDN_F_CONV_BF16_OPS | GDN_F_CONV_NO_SILU))
+    return fail(GDN_ERR_FLAGS, "unknown conv flag bits 0x%x", flags);
+  if (K != kConvK) return fail(GDN_ERR_SHAPE, "K=%d: only the model's kernel size 4 is built", K);
+  if (B < 0 || T < 0 || C <= 0 || C % kConvVec)
+    return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d C=%d (C must be a positive multiple of 8)", B, T, C);
+  if (B == 0) return GDN_OK;
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  if (!w || (total > 0 && (!x || !y))) return fail(GDN_ERR_NULL, "w, and x and y when there are tokens, are required");
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(state_in, 16) || !aligned(state_out, 16))
+    return fail(GDN_ERR_ALIGN, "conv buffers must be 16-byte aligned");
+  const size_t xbytes = static_cast<size_t>(total) * C * 2;
+  const size_t sbytes = static_cast<size_t>(B) * (kConvK - 1) * C * 2;
+  if (total > 0 && (y == x || overlap(y, xbytes, x, xbytes)))
+    return fail(GDN_ERR_ALIAS, "y must not overlap x (the halo rows are re-read)");
+  if (overlap(state_out, sbytes, state_in, sbytes) || overlap(state_out, sbytes, x, xbytes) ||
+      overlap(state_out, sbytes, y, xbytes))
+    return fail(GDN_ERR_ALIAS, "state_out overlaps an input or y");
+  ConvParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+               static_cast<const __nv_bfloat16*>(state_in), static_cast<__nv_bfloat16*>(state_out),
+               static_cast<__nv_bfloat16*>(y), cu_seqlens, total, B, cu_seqlens ? 0 : T, C, flags};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned gx = static_cast<unsigned>((C / kConvVec + kConvThreads - 1) / kConvThreads);
+  if (total > 0) {
+    const long long gy = (total + kConvRun - 1) / kConvRun;
+    if (gy > 65535LL * 1024) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
+    // grid.y is limited to 65535: fold extra runs into grid.z is not needed below 2M tokens
+    if (gy > 65535) return fail(GDN_ERR_SHAPE, "at most %d tokens per call", 65535 * kConvRun);
+    conv1d_kernel<<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
+    int rc = cuda_status(cudaGetLastError(), "conv1d launch");
+    if (rc != GDN_OK) return rc;
+  }
+  if (state_out) {
+    if (B > 65535) return fail(GDN_ERR_SHAPE, "B=%d too large", B);
+    conv_empty_kernel<<<dim3(gx, static_cast<unsigned>(B)), kConvThreads, 0, st>>>(p);
+    int rc = cuda_status(cudaGetLastError(), "conv1d empty-sequence launch");
+    if (rc != GDN_OK) return rc;
+  }
+  return GDN_OK;
+}
+
+extern "C" int gdn_conv_commit(const void* state_prev, const void* x, const int32_t* commit_n, void* state_out,
+                               int32_t* err_flag, int B, int T, int C, int K, void* stream) {
+  clear_error();
+  if (K != kConvK) return fail(GDN_ERR_SHAPE, "K=%d: only 4 is built", K);
+  if (B < 0 || T < 0 || C <= 0 || C % kConvVec) return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d C=%d", B, T, C);
+  if (B == 0) return GDN_OK;
+  if (!commit_n || !state_out || (!x && T > 0)) return fail(GDN_ERR_NULL, "commit_n, state_out and x are required");
+  if (!aligned(state_prev, 16) || !aligned(x, 16) || !aligned(state_out, 16) || !aligned(commit_n, 4) ||
+      !aligned(err_flag, 4))
+    return fail(GDN_ERR_ALIGN, "buffers must be 16-byte aligned (commit_n, err_flag 4-byte)");
+  const size_t sbytes = static_cast<size_t>(B) * (kConvK - 1) * C * 2;
+  const size_t xbytes = static_cast<size_t>(B) * T * C * 2;
+  if (overlap(state_out, sbytes, state_prev, sbytes) || overlap(state_out, sbytes, x, xbytes))
+    return fail(GDN_ERR_ALIAS, "state_out overlaps state_prev or x");
+  if (B > 65535) return fail(GDN_ERR_SHAPE, "B=%d too large", B);
+  const unsigned gx = static_cast<unsigned>((C / kConvVec + kConvThreads - 1) / kConvThreads);
+  conv_commit_kernel<<<dim3(gx, static_cast<unsigned>(B)), kConvThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(state_prev), static_cast<const __nv_bfloat16*>(x), commit_n,
+      static_cast<__nv_bfloat16*>(state_out), T, C, err_flag);
+  return cuda_status(cudaGetLastError(), "conv commit launch");
+}
+
+extern "C" int gdn_gated_rmsnorm_fwd(const void* o, const void* z, const float* gamma, void* out, long long rows,
+                                     int D, float eps, unsigned flags, void* stream) {
+  clear_error();
+  if (flags & ~(GDN_F_NORM_IN_BF16 | GDN_F_NORM_OUT_F32)) return fail(GDN_ERR_FLAGS, "unknown norm flags 0x%x", flags);
+  if (D != kD || rows < 0) return fail(GDN_ERR_SHAPE, "D=%d rows=%lld: only D = 128 is built", D, rows);
+  if (rows == 0) return GDN_OK;
+  if (!o || !z || !gamma || !out) return fail(GDN_ERR_NULL, "o, z, gamma and out are required");
+  if (!aligned(o, 16) || !aligned(z, 8) || !aligned(gamma, 16) || !aligned(out, 16))
+    return fail(GDN_ERR_ALIGN, "o, gamma, out 16-byte and z 8-byte aligned");
+  const size_t ib = static_cast<size_t>(rows) * kD * ((flags & GDN_F_NORM_IN_BF16) ? 2 : 4);
+  const size_t ob = static_cast<size_t>(rows) * kD * ((flags & GDN_F_NORM_OUT_F32) ? 4 : 2);
+  if (out != o && overlap(out, ob, o, ib)) return fail(GDN_ERR_ALIAS, "out partially overlaps o");
+  if (overlap(out, ob, z, static_cast<size_t>(rows) * kD * 2)) return fail(GDN_ERR_ALIAS, "out overlaps z");
+  if ((rows + 7) / 8 > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many rows");
+  gated_rmsnorm_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      o, static_cast<const __nv_bfloat16*>(z), gamma, out, rows, eps, flags);
+  return cuda_status(cudaGetLastError(), "gated rmsnorm launch");
+}

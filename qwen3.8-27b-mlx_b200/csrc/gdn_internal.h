@@ -29,6 +29,10 @@ inline bool overlap(const void* p, size_t n, const void* q, size_t m) {
   return a < b + m && b < a + n;
 }
 
+// Address of this device's error word (set by kernels whose bounded waits
+// give up), cached per device; GDN_OK or GDN_ERR_CUDA.
+int device_error_ptr(int** out);
+
 constexpr int kD = 128;  // Dk = Dv, fixed by the model (TextConfig, python/qwen35.py:88-91)
 
 }  // namespace gdn

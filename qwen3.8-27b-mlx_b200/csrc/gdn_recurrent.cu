@@ -33,11 +33,6 @@
 #include "gdn_internal.h"
 
 namespace gdn {
-
-// Device-side error word of this module (per device): set by a kernel whose
-// bounded wait timed out; read and cleared by gdn_take_device_error().
-__device__ int g_rec_device_error = 0;
-
 namespace {
 
 constexpr float kL2Eps = 1e-6f;                    // ops::l2norm eps (cpp/src/ops.hpp:19-20)
@@ -360,26 +355,4 @@ extern "C" int gdn_delta_run(const float* q, const float* k, const float* v, con
                              float* states, int B, int L, int H, int Dk, int Dv, void* stream) {
   return gdn_recurrent_fwd(q, k, v, alpha, beta, nullptr, nullptr, S, S_out, o, states, B, L, H, H,
                            Dk, Dv, GDN_F_QKV_F32 | GDN_F_GATES_DIRECT, stream);
-}
-
-extern "C" int gdn_take_device_error(void* stream, int* code) {
-  clear_error();
-  if (!code) return fail(GDN_ERR_NULL, "code is NULL");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int v = 0;
-  int rc = cuda_status(cudaMemcpyFromSymbolAsync(&v, gdn::g_rec_device_error, sizeof(int), 0,
-                                                 cudaMemcpyDeviceToHost, st), "read device error word");
-  if (rc != GDN_OK) return rc;
-  rc = cuda_status(cudaStreamSynchronize(st), "synchronize");
-  if (rc != GDN_OK) return rc;
-  if (v != 0) {
-    const int zero = 0;
-    rc = cuda_status(cudaMemcpyToSymbolAsync(gdn::g_rec_device_error, &zero, sizeof(int), 0,
-                                             cudaMemcpyHostToDevice, st), "clear device error word");
-    if (rc != GDN_OK) return rc;
-    rc = cuda_status(cudaStreamSynchronize(st), "synchronize");
-    if (rc != GDN_OK) return rc;
-  }
-  *code = v;
-  return GDN_OK;
 }

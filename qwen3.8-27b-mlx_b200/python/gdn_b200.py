@@ -32,6 +32,10 @@ F_QKV_F32 = 0x1
 F_O_BF16 = 0x2
 F_GATES_DIRECT = 0x4
 F_QK_L2NORM = 0x8
+F_CONV_BF16_OPS = 0x100
+F_CONV_NO_SILU = 0x200
+F_NORM_IN_BF16 = 0x400
+F_NORM_OUT_F32 = 0x800
 
 D = 128
 
@@ -48,6 +52,10 @@ SIGNATURES = {
     "gdn_recurrent_fwd_from_ckpt": [_vp] * 10 + [_i] + [_vp] * 4 + [_i] * 6 + [_u, _vp],
     "gdn_delta_run": [_vp] * 9 + [_i] * 5 + [_vp],
     "gdn_tc05_selftest": [_vp] * 3 + [_i] * 3 + [_vp, _vp],
+    "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
+    "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
+    "gdn_conv_commit": [_vp] * 5 + [_i] * 4 + [_vp],
+    "gdn_gated_rmsnorm_fwd": [_vp] * 4 + [ctypes.c_longlong, _i, ctypes.c_float, _u, _vp],
 }
 
 _lib = None
@@ -182,3 +190,78 @@ def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False):
     mode = (1 if bf16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0)
     check(lib().gdn_tc05_selftest(ptr(A), ptr(B), ptr(D), N, K, mode, ptr(status), stream_ptr(dev)))
     return D, status
+
+
+def conv1d_fwd(x, w, state_in=None, state_out=None, y=None, cu_seqlens=None, *, bf16_ops=False, silu=True):
+    """Causal depthwise conv1d + SiLU (gdn_conv1d_fwd).  x (B,T,C) bf16, or
+    packed (T,C) with cu_seqlens (B+1) int32; w (C,4) bf16; state_in
+    (B,3,C) bf16 or None.  Returns (y, state_out)."""
+    if cu_seqlens is not None:
+        T, C = x.shape
+        B = cu_seqlens.numel() - 1
+        if cu_seqlens.dtype != torch.int32:
+            raise ValueError("cu_seqlens must be int32")
+    else:
+        B, T, C = x.shape
+    dev = _dev(x, w, state_in, state_out, y, cu_seqlens)
+    if y is None:
+        y = torch.empty_like(x)
+    flags = (F_CONV_BF16_OPS if bf16_ops else 0) | (0 if silu else F_CONV_NO_SILU)
+    check(lib().gdn_conv1d_fwd(ptr(x), ptr(w), ptr(state_in), ptr(state_out), ptr(y), ptr(cu_seqlens),
+                               B, T, C, w.shape[1], flags, stream_ptr(dev)))
+    return y, state_out
+
+
+def conv_commit(state_prev, x, commit_n, state_out=None, err_flag=None):
+    """Conv window after accepting commit_n[b] tokens of a recorded block."""
+    B, T, C = x.shape
+    dev = _dev(state_prev, x, commit_n, state_out, err_flag)
+    if state_out is None:
+        state_out = torch.empty((B, 3, C), dtype=torch.bfloat16, device=dev)
+    check(lib().gdn_conv_commit(ptr(state_prev), ptr(x), ptr(commit_n), ptr(state_out), ptr(err_flag),
+                                B, T, C, 4, stream_ptr(dev)))
+    return state_out
+
+
+def gated_rmsnorm_fwd(o, z, gamma, out=None, eps=1e-6, out_dtype=torch.bfloat16):
+    """out = rms_norm(o, gamma, eps) * silu(z) over the last dim (128)."""
+    dev = _dev(o, z, gamma, out)
+    rows = o.numel() // D
+    flags = (F_NORM_IN_BF16 if o.dtype == torch.bfloat16 else 0) | \
+        (F_NORM_OUT_F32 if out_dtype == torch.float32 else 0)
+    if out is None:
+        out = torch.empty(o.shape, dtype=out_dtype, device=dev)
+    check(lib().gdn_gated_rmsnorm_fwd(ptr(o), ptr(z), ptr(gamma), ptr(out), rows, D, eps, flags,
+                                      stream_ptr(dev)))
+    return out
+
+
+def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=None, cu_seqlens=None, *,
+                l2norm=True, o_dtype=torch.float32, B=None, T=None):
+    """Chunked prefill (gdn_chunked_fwd).  q, k: (..., Hk, 128) bf16 views of
+    token-major rows (any token stride); v: (..., Hv, 128).  Leading dims are
+    (B, T) or, with cu_seqlens, (total,).  Returns (o, state_out)."""
+    Hk, Hv = q.shape[-2], v.shape[-2]
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
+            raise ValueError("q, k, v must be bf16 with contiguous 128-wide heads")
+    qs, ks, vs = q.stride(-3), k.stride(-3), v.stride(-3)
+    if cu_seqlens is not None:
+        B = cu_seqlens.numel() - 1
+        T = q.shape[0]
+        lead = (T,)
+    else:
+        B, T = q.shape[0], q.shape[1]
+        lead = (B, T)
+        if B > 1 and (q.stride(0) != T * qs or k.stride(0) != T * ks or v.stride(0) != T * vs):
+            raise ValueError("batch rows must follow each other (token-major storage)")
+    dev = _dev(a, b, A_log, dt_bias, state_in, state_out, o, cu_seqlens)
+    if o is None:
+        o = torch.empty(lead + (Hv, D), dtype=o_dtype, device=dev)
+    if state_out is None:
+        state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
+    flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0)
+    check(lib().gdn_chunked_fwd(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,
+                                flags, stream_ptr(dev)))
+    return o, state_out
