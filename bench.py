@@ -213,10 +213,12 @@ def time_graph(fn, steps, warmup, device, world):
 
 def run_ours(args, world, rank, local):
     import gdn_b200 as G
+    import gdn_shard
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     lib = G.lib()
-    hk, hv = HK // world, HV // world
+    shard = gdn_shard.head_shard(rank, world, HK, HV)
+    hk, hv = shard.hk, shard.hv
     B = args.batch
     Bg = B * world                                  # global batch; every rank holds all of it for its heads
     L = args.layers
@@ -304,6 +306,14 @@ def run_ours(args, world, rank, local):
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(seconds=args.cpu_seconds)
 
+    prefill = None
+    if not args.no_prefill:
+        del X
+        torch.cuda.empty_cache()
+        prefill = run_prefill(args, lib, device, world)
+        if world == 1 and rank == 0 and not args.no_cpu_baseline:
+            prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
+
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -317,7 +327,7 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
                    "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
-        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu,
+        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu, "prefill": prefill,
     }
     return line
 
@@ -382,6 +392,190 @@ def run_e2e(args, lib, X, Bg, device, world):
     return {"value": round(value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d_b,
             "d2h_bytes_per_step": d2h_b, "ms_per_step": round(ms, 4), "steps": steps,
             "api": "gdn_recurrent_fwd (C ABI via ctypes), pinned host inputs/outputs"}
+
+
+# ---------------------------------------------------------------------------
+# prefill: BASELINE config 3 (conv -> chunked recurrence -> gated norm)
+# ---------------------------------------------------------------------------
+
+FLOP_PER_TOKEN_HEAD = 12 * 64 * 128 + 6 * 128 * 128      # chunked WY form, C = 64, D = 128
+
+
+class PrefillLayer:
+    """One GDN layer's prefill inputs on the device (BASELINE config 3/4
+    distributions) for a shard of hk key / hv value heads: x (tokens, C)
+    bf16 projection output (C = 2*hk*128 + hv*128), conv weights, z, gamma,
+    gate inputs.  `lens` packs sequences of those lengths (cu_seqlens)."""
+
+    def __init__(self, lens, device, seed, hk=HK, hv=HV):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        C = 2 * hk * D + hv * D
+        self.lens = list(lens)
+        self.B, self.N = len(self.lens), int(sum(self.lens))
+        self.hk, self.hv, self.C = hk, hv, C
+        cu = np.concatenate([[0], np.cumsum(self.lens)]).astype(np.int32)
+        self.cu = torch.from_numpy(cu).to(device)
+        self.uniform = len(set(self.lens)) == 1
+        self.T = self.lens[0] if self.uniform else self.N
+        self.x = torch.randn((self.N, C), generator=g, device=device).bfloat16()
+        self.w = (torch.randn((C, 4), generator=g, device=device) * 0.5).bfloat16()
+        self.z = torch.randn((self.N, hv, D), generator=g, device=device).bfloat16()
+        self.gamma = 1 + 0.1 * torch.randn((D,), generator=g, device=device)
+        self.a = torch.randn((self.N, hv), generator=g, device=device)
+        self.b = torch.randn((self.N, hv), generator=g, device=device)
+        self.A_log = torch.rand((hv,), generator=g, device=device) * float(np.log(16.0))
+        self.dt_bias = torch.rand((hv,), generator=g, device=device)
+        self.y = torch.empty_like(self.x)
+        self.o = torch.empty((self.N, hv, D), dtype=torch.float32, device=device)
+        self.S = torch.empty((self.B, hv, D, D), dtype=torch.float32, device=device)
+        self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
+
+    def _cu(self):
+        return None if self.uniform else ctypes.c_void_p(self.cu.data_ptr())
+
+    def conv(self, lib, h):
+        import gdn_b200 as G
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        rc = lib.gdn_conv1d_fwd(P(self.x), P(self.w), None, None, P(self.y), self._cu(), self.B, self.T, self.C, 4, 0, h)
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+        del G
+
+    def chunked(self, lib, h):
+        import gdn_b200 as G
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        hk, C = self.hk, self.C
+        base = self.y.data_ptr()
+        q = ctypes.c_void_p(base)
+        k = ctypes.c_void_p(base + hk * D * 2)
+        v = ctypes.c_void_p(base + 2 * hk * D * 2)
+        rc = lib.gdn_chunked_fwd(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
+                                 None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
+                                 G.F_QK_L2NORM, h)
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+
+    def norm(self, lib, h):
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        rc = lib.gdn_gated_rmsnorm_fwd(P(self.o), P(self.z), P(self.gamma), P(self.out),
+                                       self.N * self.hv, D, ctypes.c_float(1e-6), 0, h)
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+
+    def step(self, lib, h):
+        self.conv(lib, h)
+        self.chunked(lib, h)
+        self.norm(lib, h)
+
+    def flops(self):
+        return FLOP_PER_TOKEN_HEAD * self.N * self.hv
+
+
+def config4_lengths(seed=4, B=8, lo=16384, hi=65536):
+    """B=8 sequences of seeded lengths uniform in [16384, 65536]."""
+    rng = np.random.default_rng(seed)
+    return [int(x) for x in rng.integers(lo, hi + 1, size=B)]
+
+
+def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
+    """Max-over-ranks ms of one layer (conv -> chunked -> norm, and for N > 1
+    the all-gather of the bf16 head outputs) and per-kernel ms (CUDA events)."""
+    st = torch.cuda.current_stream(device)
+    h = ctypes.c_void_p(st.cuda_stream)
+
+    def layer():
+        X.step(lib, h)
+        if gathered is not None:
+            torch.distributed.all_gather_into_tensor(gathered, X.out)
+
+    for _ in range(warmup):
+        layer()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        layer()
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    durs = {"conv": [], "chunked": [], "norm": []}
+    for _ in range(max(1, min(steps, 3))):
+        ev[0].record(st); X.conv(lib, h); ev[1].record(st)
+        X.chunked(lib, h); ev[2].record(st)
+        X.norm(lib, h); ev[3].record(st)
+        torch.cuda.synchronize(device)
+        durs["conv"].append(ev[0].elapsed_time(ev[1]))
+        durs["chunked"].append(ev[1].elapsed_time(ev[2]))
+        durs["norm"].append(ev[2].elapsed_time(ev[3]))
+    return ms, {k: statistics.mean(v) for k, v in durs.items()}
+
+
+def run_prefill(args, lib, device, world):
+    """Configs 3 and 4 on this rank's K-head shard (16/N key, 48/N value heads);
+    for N > 1 each layer ends with the NCCL all-gather of the bf16 outputs.
+    tokens/s counts the layer's tokens once (all heads) per max-over-ranks second."""
+    import gdn_shard
+    _, tf_peak, peak_kind = peaks()
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    shard = gdn_shard.head_shard(rank, world, HK, HV)
+    hk, hv = shard.hk, shard.hv
+    res = {}
+    cases = [("config3", [args.prefill_T])]
+    if args.config4:
+        cases.append(("config4", config4_lengths()))
+    for name, lens in cases:
+        X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
+        gathered = None
+        if world > 1:
+            gathered = torch.empty((world,) + tuple(X.out.shape), dtype=torch.bfloat16, device=device)
+        steps = max(2, args.steps // 10) if name == "config4" else max(3, args.steps // 5)
+        ms, kms = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1) if name == "config4"
+                                     else max(args.warmup, 3), gathered)
+        achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
+        res[name] = {
+            "workload": (f"{name}: {X.B} seq, {X.N} tokens, conv(C={X.C}, K=4)+SiLU -> chunked C=64 "
+                         f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
+                         + (" -> NCCL all-gather" if world > 1 else "")),
+            "tokens_per_s": round(X.N / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+            "kernel_ms": {k: round(v, 4) for k, v in kms.items()},
+            "roofline": {"bound": "tensor", "kernel": "chunked_kernel", "achieved": round(achieved, 2),
+                         "peak": tf_peak, "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
+                         "peak_kind": peak_kind + " bf16 dense (the kernel runs tf32)",
+                         "flop_per_launch": X.flops(), "flop_per_token_head": FLOP_PER_TOKEN_HEAD}}
+        del X, gathered
+        torch.cuda.empty_cache()
+    return res
+
+
+def cpu_prefill_baseline(T=512, seconds=10.0):
+    """The reference's prefill CPU path (chunked_delta, numpy oracle with BLAS
+    threads) plus conv and gated norm on a bounded sample; tokens/s."""
+    import gdn_oracle as O
+    rng = np.random.default_rng(7)
+    C = 2 * HK * D + HV * D
+    x = O.bf16_round(rng.standard_normal((1, T, C), dtype=np.float32))
+    w = O.bf16_round(rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5))
+    z = O.bf16_round(rng.standard_normal((1, T, HV, D), dtype=np.float32))
+    gamma = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    a = rng.standard_normal((1, T, HV), dtype=np.float32)
+    b = rng.standard_normal((1, T, HV), dtype=np.float32)
+    A_log = rng.uniform(0.0, np.log(16.0), (HV,)).astype(np.float32)
+    dt = rng.uniform(0.0, 1.0, (HV,)).astype(np.float32)
+    wts = O.BlockWeights(conv_w=w, A_log=A_log, dt_bias=dt, gamma=gamma)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.gdn_block(x, z.reshape(1, T, HV * D), a, b, wts)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": round(n * T / el, 1), "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} x config-3 layer at T={T} (numpy restatement of the reference's CPU prefill: "
+                      f"conv, chunked_delta, gated norm; BLAS threads = all cores), {el:.1f} s"}
 
 
 # ---------------------------------------------------------------------------
@@ -465,10 +659,14 @@ def main():
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture, reported as roofline.traffic")
     ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-T", type=int, default=4096)
+    ap.add_argument("--config4", action="store_true", help="also time one layer of config 4 (B=8 varlen 16K-64K)")
+    ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     args = ap.parse_args()
     if args.small:
         args.batch, args.layers, args.sweep = 64, 2, ""
-        args.no_e2e = args.no_cpu_baseline = True
+        args.no_e2e = args.no_cpu_baseline = args.no_prefill = True
     args.warmup = max(args.warmup, 0)
 
     world, rank, local = dist_env()
@@ -482,6 +680,14 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=torch.device("cuda", local))
     try:
+        if args.prefill_only:
+            import gdn_b200 as G
+            device = torch.device("cuda", local)
+            torch.cuda.set_device(device)
+            line = {"prefill": run_prefill(args, G.lib(), device, world)}
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return 0
         line = run_ours(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)

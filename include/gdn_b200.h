@@ -208,7 +208,8 @@ int gdn_gated_rmsnorm_fwd(const void* o, const void* z, const float* gamma, void
  * B (N x K), all row-major fp32, through tcgen05.mma into tensor memory.
  * mode bit 0: operands rounded to bf16 (kind::f16) instead of tf32;
  * bit 1: A negated by the instruction descriptor; bit 2: A read from tensor
- * memory (tf32 only).  N, K multiples of 16 in [16, 128].  *status (device
+ * memory (tf32 only); bit 3: A laid out MN-major in shared memory; bit 4: B
+ * laid out MN-major.  N, K multiples of 16 in [16, 128].  *status (device
  * int32) is set to 1 if the bounded wait for the MMA timed out.
  */
 int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,

@@ -37,28 +37,50 @@
 #include "gdn_ptx.cuh"
 
 namespace gdn {
+
+#ifdef GDN_CHUNK_TIMING
+__device__ long long g_chunk_timing[16];
+#define GDN_TICK(slot)                                                          \
+  do {                                                                          \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {                                  \
+      const long long now_ = clock64();                                         \
+      g_chunk_timing[slot] += now_ - tick_;                                     \
+      tick_ = now_;                                                             \
+    }                                                                           \
+  } while (0)
+#else
+#define GDN_TICK(slot) \
+  do {                 \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kC = 64;          // tokens per chunk (python/qwen35.py:365)
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;   // 8 warps: warp w owns TMEM lane quarter w % 4, column half w / 4
 
-// shared memory map, bytes; operands in the K-major no-swizzle layout
+// shared memory map, bytes; tensor-core operands in the K-major no-swizzle
+// layout (LBO 128 B), written row-wise so that a warp's stores hit distinct banks
 constexpr uint32_t kSbo128 = (kD * 4 / 16) * 128;   // 8-row group stride of 128-wide fp32 rows
 constexpr uint32_t kSbo64 = (kC * 4 / 16) * 128;    // ... of 64-wide fp32 rows
-constexpr uint32_t kOffKQ = 0;                      // [K; Q]   128 x 128  (64 KiB)
-constexpr uint32_t kOffKt = kOffKQ + 128 * kD * 4;  // K^T      128 x 64   (32 KiB)
-constexpr uint32_t kOffVt = kOffKt + kD * kC * 4;   // V^T, U^T 128 x 64   (32 KiB)
-constexpr uint32_t kOffTi = kOffVt + kD * kC * 4;   // T^-1      64 x 64   (16 KiB)
-constexpr uint32_t kOffM = kOffTi + kC * kC * 4;    // M         64 x 64   (16 KiB)
-constexpr uint32_t kOffW = kOffM + kC * kC * 4;     // W         64 x 128  (32 KiB)
-constexpr uint32_t kOffA = kOffW + kC * kD * 4;     // A, plain row-major 64 x 64 (16 KiB)
-constexpr uint32_t kOffY = kOffA + kC * kC * 4;     // solve temporaries 3 x 16 x 16
+constexpr int kPad = kC + 1;                        // row stride of the plain solve arrays
+constexpr uint32_t kOffKQ = 0;                      // [K; Q] rows            128 x 128 (64 KiB)
+constexpr uint32_t kOffKt = kOffKQ + 128 * kD * 4;  // K^T, scaled            128 x 64  (32 KiB)
+constexpr uint32_t kOffVt = kOffKt + kD * kC * 4;   // V^T diag(beta), U^T    128 x 64  (32 KiB)
+constexpr uint32_t kOffTi = kOffVt + kD * kC * 4;   // T^-1                    64 x 64  (16 KiB)
+constexpr uint32_t kOffM = kOffTi + kC * kC * 4;    // M (must follow T^-1)    64 x 64  (16 KiB)
+constexpr uint32_t kOffW = kOffM + kC * kC * 4;     // W rows 64 x 128 (32 KiB); X during the solve
+constexpr uint32_t kOffA = kOffW + kC * kD * 4;     // A, plain, row stride 65
+constexpr uint32_t kOffY = kOffA + kC * kPad * 4;   // solve temporaries 3 x 16 x 16
 constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 8 x 64
 constexpr uint32_t kOffBar = kOffSc + 8 * kC * 4;   // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 320, kColU = 384, kColY = 448;
+// [0,128) R (tf32), [128,256) R (fp32 master, state-update accumulator),
+// [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
+// [384,448) U^T; [448,512) y^T
+constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 384, kColY = 448;
 
 struct ChunkParams {
   const __nv_bfloat16* q;
@@ -84,10 +106,10 @@ __device__ __forceinline__ float* at(unsigned char* base, int r, int c, uint32_t
   return reinterpret_cast<float*>(base + tc::kmajor_offset(r, c, 4, sbo));
 }
 
-// 64 bf16 starting at p (16-byte aligned) -> fp32
-__device__ __forceinline__ void load64(const __nv_bfloat16* p, bool valid, float (&f)[64]) {
+// 32 bf16 starting at p (16-byte aligned) -> fp32
+__device__ __forceinline__ void load32(const __nv_bfloat16* p, bool valid, float (&f)[32]) {
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
+  for (int q = 0; q < 4; ++q) {
     uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(p) + q) : make_uint4(0, 0, 0, 0);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -99,10 +121,11 @@ __device__ __forceinline__ void load64(const __nv_bfloat16* p, bool valid, float
   }
 }
 
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
   float t[16];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < N / 16; ++c) {
     tc::tmem_ld16(taddr + c * 16, t);
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[c * 16 + i] = t[i];
@@ -118,6 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   unsigned char* sTi = sm + kOffTi;
   unsigned char* sM = sm + kOffM;
   unsigned char* sW = sm + kOffW;
+  float* sX = reinterpret_cast<float*>(sm + kOffW);   // T^-1 in plain form while solving
   float* sA = reinterpret_cast<float*>(sm + kOffA);
   float* sY = reinterpret_cast<float*>(sm + kOffY);
   float* sc = reinterpret_cast<float*>(sm + kOffSc);
@@ -135,6 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const int quarter = warp & 3;       // TMEM lanes 32*quarter ..
+  const int half = warp >> 2;         // column half of the epilogues
+  const int row = quarter * 32 + lane;  // TMEM lane of this thread
   const int bh = blockIdx.x;
   const int b = bh / p.Hv;
   const int h = bh - b * p.Hv;
@@ -167,32 +194,38 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tb = *tslot;
-  const uint32_t tR = tb + kColR, tDR = tb + kColDR, tGP = tb + kColGP;
-  const uint32_t tW = tb + kColW, tU = tb + kColU, tY = tb + kColY;
-  const uint32_t my = static_cast<uint32_t>(warp * 32) << 16;     // this warp's lane quarter
+  const uint32_t my = static_cast<uint32_t>(quarter * 32) << 16;      // this warp's lane quarter
+  const uint32_t tR = tb + kColR + my, tDR = tb + kColDR + my, tGP = tb + kColGP + my;
+  const uint32_t tW = tb + kColW + my, tU = tb + kColU + my, tY = tb + kColY + my;
 
-  // initial state row dv = tid into the fp32 master
+  // initial state: row dv = row, columns [64*half, 64*half+64), into the fp32 master
   {
-    const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + tid) * kD : nullptr;
-    for (int c = 0; c < kD; c += 16) {
+    const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + row) * kD + half * 64 : nullptr;
+    for (int c = 0; c < 64; c += 16) {
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
         const float4 f = src ? *reinterpret_cast<const float4*>(src + c + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
       }
-      tc::tmem_st16(tDR + my + c, v);
+      tc::tmem_st16(tDR + half * 64 + c, v);
     }
     tc::tmem_st_wait();
   }
 
   uint32_t phase = 0;
   bool failed = false;
+#ifdef GDN_CHUNK_TIMING
+  long long tick_ = clock64();
+#endif
+  // one warp polls the MMA barrier, the others wait at the CTA barrier
   auto mma_wait = [&]() -> bool {
-    const bool ok = ptx::mbar_wait(bar, phase);
+    bool ok = true;
+    if (warp == 0) ok = ptx::mbar_wait(bar, phase);
     phase ^= 1u;
+    const bool all_ok = !__syncthreads_or(!ok);
     tc::fence_after_sync();
-    return !__syncthreads_or(!ok);
+    return all_ok;
   };
   auto desc = [](const unsigned char* base, uint32_t byte_off, uint32_t sbo) {
     return tc::smem_desc(ptx::smem_u32(base) + byte_off, 128, sbo);
@@ -228,109 +261,131 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
       s_ratio[tid] = expf(gl - s_gam[tid]);
       if (tid == 0) s_misc[0] = expf(gl);
     }
-    __syncthreads();
+    GDN_TICK(0);
 
-    // ---- stage K, Q, V of the chunk: thread -> (token i, half hf of 64 dims) --
+    // ---- rows of K and Q (thread -> token i, 32-dim quarter qd) and their norms
     {
-      const int i = tid >> 1;
-      const int hf = tid & 1;
+      const int i = tid >> 2;
+      const int qd = tid & 3;
       const bool valid = i < nvalid;
-      const long long tok = t0 + i;
-      float f[64];
-      // K: raw rows of [K; Q], and K^T diag(beta g r_k)
-      load64(p.k + (valid ? tok : s0) * p.k_stride + kh * kD + hf * 64, valid, f);
+      const long long tok = valid ? t0 + i : s0;
+      float f[32];
+      load32(p.k + tok * p.k_stride + kh * kD + qd * 32, valid, f);
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) ss += f[e] * f[e];
+      for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      const float rk = l2 ? rsqrtf(ss + 1e-6f) : 1.f;
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
 #pragma unroll
-      for (int e = 0; e < 64; e += 4)
-        *reinterpret_cast<float4*>(at(sKQ, i, hf * 64 + e, kSbo128)) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-      const float sk = s_beta[i] * s_g[i] * rk;
-#pragma unroll
-      for (int e = 0; e < 64; ++e) *at(sKt, hf * 64 + e, i, kSbo64) = tc::to_tf32(f[e] * sk);
-      // Q: raw rows (rescaled by g r_q after the G/P product)
-      load64(p.q + (valid ? tok : s0) * p.q_stride + kh * kD + hf * 64, valid, f);
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(at(sKQ, i, qd * 32 + e, kSbo128)) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+      if (qd == 0) s_rk[i] = l2 ? rsqrtf(ss + 1e-6f) : 1.f;
+      load32(p.q + tok * p.q_stride + kh * kD + qd * 32, valid, f);
       ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) ss += f[e] * f[e];
+      for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      const float rq = l2 ? rsqrtf(ss + 1e-6f) * qscale : 1.f;
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
 #pragma unroll
-      for (int e = 0; e < 64; e += 4)
-        *reinterpret_cast<float4*>(at(sKQ, kC + i, hf * 64 + e, kSbo128)) =
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(at(sKQ, kC + i, qd * 32 + e, kSbo128)) =
             make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-      // V^T diag(beta)
-      load64(p.v + (valid ? tok : s0) * p.v_stride + h * kD + hf * 64, valid, f);
-      const float bv = s_beta[i];
+      if (qd == 0) s_rq[i] = l2 ? rsqrtf(ss + 1e-6f) * qscale : 1.f;
+    }
+    __syncthreads();
+    GDN_TICK(1);
+
+    // ---- columns: K^T diag(beta g r_k) (threads 0-127 -> dk), V^T diag(beta)
+    //      (threads 128-255 -> dv), read column-wise from global, row-wise stores
+    {
+      const int c = tid & 127;
+      const bool is_k = tid < 128;
+      const __nv_bfloat16* src = (is_k ? p.k + kh * kD + c : p.v + h * kD + c) + t0 * (is_k ? p.k_stride : p.v_stride);
+      const long long stride = is_k ? p.k_stride : p.v_stride;
+      unsigned char* dst = is_k ? sKt : sVt;
+      __nv_bfloat16 raw[kC];                    // all 64 loads in flight before any use
 #pragma unroll
-      for (int e = 0; e < 64; ++e) *at(sVt, hf * 64 + e, i, kSbo64) = tc::to_tf32(f[e] * bv);
-      if (hf == 0) {
-        s_rk[i] = rk;
-        s_rq[i] = rq;
+      for (int j = 0; j < kC; ++j) raw[j] = j < nvalid ? src[j * stride] : __float2bfloat16_rn(0.f);
+#pragma unroll
+      for (int j = 0; j < kC; j += 4) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int jj = j + e;
+          const float sc_ = is_k ? s_beta[jj] * s_g[jj] * s_rk[jj] : s_beta[jj];
+          x[e] = tc::to_tf32(__bfloat162float(raw[jj]) * sc_);
+        }
+        *reinterpret_cast<float4*>(at(dst, c, j, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
       }
     }
     ptx::fence_proxy_async_smem();
+    GDN_TICK(2);
 
     // ---- state operand for this chunk: tR = tf32(R), tDR = g_last * R ---------
     {
       const float gl = s_misc[0];
-      for (int c = 0; c < kD; c += 16) {
+      for (int c = 0; c < 64; c += 16) {
         float v[16], r[16];
-        tc::tmem_ld16(tDR + my + c, v);
+        tc::tmem_ld16(tDR + half * 64 + c, v);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           r[i] = tc::to_tf32(v[i]);
           v[i] *= gl;
         }
-        tc::tmem_st16(tR + my + c, r);
-        tc::tmem_st16(tDR + my + c, v);
+        tc::tmem_st16(tR + half * 64 + c, r);
+        tc::tmem_st16(tDR + half * 64 + c, v);
       }
       tc::tmem_st_wait();
     }
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(3);
 
-    // ---- (a)  [K; Q] K^T -> G, P ----------------------------------------------
+    // ---- (a)  [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127) --------------------
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
       for (int j = 0; j < kD / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tGP, desc(sKQ, j * 256, kSbo128), desc(sKQ, j * 256, kSbo128), id, j > 0);
+        tc::mma_ss<tc::kTF32>(tb + kColGP, desc(sKQ, j * 256, kSbo128), desc(sKQ, j * 256, kSbo128), id, j > 0);
       tc::mma_commit(bar);
     }
     if (!mma_wait()) {
       failed = true;
       break;
     }
+    GDN_TICK(4);
 
-    // ---- A (strictly lower) and M (lower), Q rows rescaled -----------------
+    // ---- A (strictly lower, plain), M (lower), Q rows rescaled by g r_q --------
     {
-      float row[64];
-      tmem_ld64(tGP + my, row);
-      if (warp < 2) {
-        const int i = tid;
+      float gp[32];
+      tmem_ld<32>(tGP + half * 32, gp);
+      if (quarter < 2) {
+        const int i = row;
         const float fi = s_beta[i] * s_rk[i];
         const float gi = s_gam[i];
-        float* Ar = sA + i * kC;
+        float* Ar = sA + i * kPad + half * 32;
 #pragma unroll
-        for (int j = 0; j < kC; ++j) Ar[j] = (j < i) ? fi * s_rk[j] * expf(gi - s_gam[j]) * row[j] : 0.f;
+        for (int e = 0; e < 32; ++e) {
+          const int j = half * 32 + e;
+          Ar[e] = (j < i) ? fi * s_rk[j] * expf(gi - s_gam[j]) * gp[e] : 0.f;
+        }
       } else {
-        const int i = tid - kC;
+        const int i = row - kC;
         const float fi = s_rq[i];
         const float gi = s_gam[i];
 #pragma unroll
-        for (int j = 0; j < kC; j += 4) {
+        for (int e = 0; e < 32; e += 4) {
           float m[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            m[e] = (j + e <= i) ? tc::to_tf32(fi * s_rk[j + e] * expf(gi - s_gam[j + e]) * row[j + e]) : 0.f;
-          *reinterpret_cast<float4*>(at(sM, i, j, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
+          for (int u = 0; u < 4; ++u) {
+            const int j = half * 32 + e + u;
+            m[u] = (j <= i) ? tc::to_tf32(fi * s_rk[j] * expf(gi - s_gam[j]) * gp[e + u]) : 0.f;
+          }
+          *reinterpret_cast<float4*>(at(sM, i, half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
         }
         const float sq = s_g[i] * s_rq[i];
-        for (int c = 0; c < kD; c += 4) {
+        for (int c = half * 64; c < half * 64 + 64; c += 4) {
           float4* qp = reinterpret_cast<float4*>(at(sKQ, kC + i, c, kSbo128));
           float4 v = *qp;
           v.x = tc::to_tf32(v.x * sq);
@@ -341,14 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
         }
       }
     }
-    // zero T^-1 (its upper blocks stay zero)
-    for (int e = tid; e < kC * kC; e += kThreads) *at(sTi, e >> 6, e & 63, kSbo64) = 0.f;
     __syncthreads();
+    GDN_TICK(5);
 
-    // ---- T^-1 = (I + A)^-1: 16x16 diagonal blocks, then block diagonals ------
+    // ---- T^-1 = (I + A)^-1: 16x16 diagonal blocks by substitution, then block
+    //      diagonals X_ij = -X_ii sum_{k=j}^{i-1} A_ik X_kj; plain arrays, row stride 65
     if (tid < kC) {
       const int blk = tid >> 4, c = tid & 15;
-      const float* Ab = sA + (blk * 16) * kC + blk * 16;
+      const float* Ab = sA + (blk * 16) * kPad + blk * 16;
       float col[16];
 #pragma unroll
       for (int r = 0; r < 16; ++r) col[r] = (r == c) ? 1.f : 0.f;
@@ -358,12 +413,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
           float s = 0.f;
 #pragma unroll
           for (int m = 0; m < r; ++m)
-            if (m >= c) s += Ab[r * kC + m] * col[m];
+            if (m >= c) s += Ab[r * kPad + m] * col[m];
           col[r] = -s;
         }
       }
 #pragma unroll
-      for (int r = 0; r < 16; ++r) *at(sTi, blk * 16 + r, blk * 16 + c, kSbo64) = col[r];
+      for (int r = 0; r < 16; ++r) sX[(blk * 16 + r) * kPad + blk * 16 + c] = col[r];
     }
     __syncthreads();
     for (int d = 1; d < 4; ++d) {
@@ -371,10 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
       for (int e = tid; e < nt * 256; e += kThreads) {
         const int t = e >> 8, r = (e >> 4) & 15, c = e & 15;
         const int bj = t, bi = t + d;
+        const float* Ar = sA + (bi * 16 + r) * kPad;
         float y = 0.f;
         for (int kb = bj; kb < bi; ++kb) {
 #pragma unroll
-          for (int m = 0; m < 16; ++m) y += sA[(bi * 16 + r) * kC + kb * 16 + m] * *at(sTi, kb * 16 + m, bj * 16 + c, kSbo64);
+          for (int m = 0; m < 16; ++m) y += Ar[kb * 16 + m] * sX[(kb * 16 + m) * kPad + bj * 16 + c];
         }
         sY[e] = y;
       }
@@ -382,80 +438,104 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
       for (int e = tid; e < nt * 256; e += kThreads) {
         const int t = e >> 8, r = (e >> 4) & 15, c = e & 15;
         const int bj = t, bi = t + d;
+        const float* Xr = sX + (bi * 16 + r) * kPad + bi * 16;
         float x = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; ++m) x += *at(sTi, bi * 16 + r, bi * 16 + m, kSbo64) * sY[(t << 8) + (m << 4) + c];
-        *at(sTi, bi * 16 + r, bj * 16 + c, kSbo64) = -x;
+        for (int m = 0; m < 16; ++m) x += Xr[m] * sY[(t << 8) + (m << 4) + c];
+        sX[(bi * 16 + r) * kPad + bj * 16 + c] = -x;
       }
       __syncthreads();
     }
-    for (int e = tid; e < kC * kC; e += kThreads) {
-      float* x = at(sTi, e >> 6, e & 63, kSbo64);
-      *x = tc::to_tf32(*x);
+    // T^-1 into the operand layout, rounded to tf32, zeros above the diagonal blocks
+    {
+      const int i = tid >> 2;
+      const int c0 = (tid & 3) * 16;
+#pragma unroll
+      for (int c = c0; c < c0 + 16; c += 4) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = ((c + u) >> 4) <= (i >> 4) ? tc::to_tf32(sX[i * kPad + c + u]) : 0.f;
+        *reinterpret_cast<float4*>(at(sTi, i, c, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
+      }
     }
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(6);
 
-    // ---- (b) U0^T = V^T diag(beta) T^-T,  (c) W^T = K^T diag(beta g r_k) T^-T --
+    // ---- (b) U0^T = V^T diag(beta) T^-T;  (c) W = [T^-1; *] (K^T diag(beta g r_k))^T
+    //      (M = 128: rows 64-127 of A read the M buffer and are discarded)
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
+      const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
+      const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
       for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tU, desc(sVt, j * 256, kSbo64), desc(sTi, j * 256, kSbo64), id, j > 0);
+        tc::mma_ss<tc::kTF32>(tb + kColU, desc(sVt, j * 256, kSbo64), desc(sTi, j * 256, kSbo64), id64, j > 0);
       for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tW, desc(sKt, j * 256, kSbo64), desc(sTi, j * 256, kSbo64), id, j > 0);
+        tc::mma_ss<tc::kTF32>(tb + kColW, desc(sTi, j * 256, kSbo64), desc(sKt, j * 256, kSbo64), id128, j > 0);
       tc::mma_commit(bar);
     }
     if (!mma_wait()) {
       failed = true;
       break;
     }
+    GDN_TICK(7);
 
-    // ---- W (row-major operand), K^T rescaled for the state update -----------
-    {
+    // ---- W rows into the operand buffer (warps on lanes 0-63); K^T rescaled
+    //      by ratio r_k for the state update (warps on lanes 64-127)
+    if (quarter < 2) {
       float w[64];
-      tmem_ld64(tW + my, w);
-      const int dk = tid;
+      tmem_ld<64>(tW + half * 64, w);
+      const int i = row;
 #pragma unroll
-      for (int i = 0; i < kC; ++i) *at(sW, i, dk, kSbo128) = tc::to_tf32(w[i]);
+      for (int e = 0; e < 64; e += 4)
+        *reinterpret_cast<float4*>(at(sW, i, half * 64 + e, kSbo128)) =
+            make_float4(tc::to_tf32(w[e]), tc::to_tf32(w[e + 1]), tc::to_tf32(w[e + 2]), tc::to_tf32(w[e + 3]));
+    } else {
+      const int dk = (tid & 63) + 64 * half;
+      const __nv_bfloat16* src = p.k + kh * kD + dk + t0 * p.k_stride;
+      __nv_bfloat16 raw[kC];
+#pragma unroll
+      for (int j = 0; j < kC; ++j) raw[j] = j < nvalid ? src[j * p.k_stride] : __float2bfloat16_rn(0.f);
 #pragma unroll
       for (int j = 0; j < kC; j += 4) {
-        float kk[4];
+        float x[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) kk[e] = tc::to_tf32(*at(sKQ, j + e, dk, kSbo128) * s_ratio[j + e] * s_rk[j + e]);
-        *reinterpret_cast<float4*>(at(sKt, dk, j, kSbo64)) = make_float4(kk[0], kk[1], kk[2], kk[3]);
+        for (int e = 0; e < 4; ++e) x[e] = tc::to_tf32(__bfloat162float(raw[j + e]) * s_ratio[j + e] * s_rk[j + e]);
+        *reinterpret_cast<float4*>(at(sKt, dk, j, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
       }
     }
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(8);
 
     // ---- (d) U^T = U0^T - R W^T ----------------------------------------------
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
-      for (int j = 0; j < kD / 8; ++j) tc::mma_ts_tf32(tU, tR + j * 8, desc(sW, j * 256, kSbo128), id, 1);
+      for (int j = 0; j < kD / 8; ++j) tc::mma_ts_tf32(tb + kColU, tb + kColR + j * 8, desc(sW, j * 256, kSbo128), id, 1);
       tc::mma_commit(bar);
     }
     if (!mma_wait()) {
       failed = true;
       break;
     }
+    GDN_TICK(9);
 
-    // ---- U^T into shared memory (the V^T buffer) ------------------------------
+    // ---- U^T rows into shared memory (the V^T buffer) -------------------------
     {
-      float u[64];
-      tmem_ld64(tU + my, u);
-      const int dv = tid;
+      float u[32];
+      tmem_ld<32>(tU + half * 32, u);
 #pragma unroll
-      for (int i = 0; i < kC; i += 4)
-        *reinterpret_cast<float4*>(at(sVt, dv, i, kSbo64)) =
-            make_float4(tc::to_tf32(u[i]), tc::to_tf32(u[i + 1]), tc::to_tf32(u[i + 2]), tc::to_tf32(u[i + 3]));
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(at(sVt, row, half * 32 + e, kSbo64)) =
+            make_float4(tc::to_tf32(u[e]), tc::to_tf32(u[e + 1]), tc::to_tf32(u[e + 2]), tc::to_tf32(u[e + 3]));
     }
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(10);
 
     // ---- (e) y^T = R Qs^T + U^T M^T,  (f) R += U^T diag(ratio r_k) K ---------
     if (tid == 0) {
@@ -463,47 +543,51 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
       const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
       const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
       for (int j = 0; j < kD / 8; ++j)
-        tc::mma_ts_tf32(tY, tR + j * 8, desc(sKQ, 8 * kSbo128 + j * 256, kSbo128), id64, j > 0);
+        tc::mma_ts_tf32(tb + kColY, tb + kColR + j * 8, desc(sKQ, 8 * kSbo128 + j * 256, kSbo128), id64, j > 0);
       for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tY, desc(sVt, j * 256, kSbo64), desc(sM, j * 256, kSbo64), id64, 1);
+        tc::mma_ss<tc::kTF32>(tb + kColY, desc(sVt, j * 256, kSbo64), desc(sM, j * 256, kSbo64), id64, 1);
       for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tDR, desc(sVt, j * 256, kSbo64), desc(sKt, j * 256, kSbo64), id128, 1);
+        tc::mma_ss<tc::kTF32>(tb + kColDR, desc(sVt, j * 256, kSbo64), desc(sKt, j * 256, kSbo64), id128, 1);
       tc::mma_commit(bar);
     }
     if (!mma_wait()) {
       failed = true;
       break;
     }
+    GDN_TICK(11);
 
-    // ---- o rows of the chunk -------------------------------------------------
+    // ---- o rows of the chunk: thread -> (dv = row, tokens of its half) --------
     {
-      float y[64];
-      tmem_ld64(tY + my, y);
-      const int dv = tid;
+      float y[32];
+      tmem_ld<32>(tY + half * 32, y);
+      const size_t orow = static_cast<size_t>(p.Hv) * kD;
+      const size_t base = (static_cast<size_t>(t0 + half * 32) * p.Hv + h) * kD + row;
+      const int nv = nvalid - half * 32;
       if (p.flags & GDN_F_O_BF16) {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o);
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
 #pragma unroll
-        for (int i = 0; i < kC; ++i)
-          if (i < nvalid) o[(static_cast<size_t>(t0 + i) * p.Hv + h) * kD + dv] = __float2bfloat16_rn(y[i]);
+        for (int i = 0; i < 32; ++i)
+          if (i < nv) o[i * orow] = __float2bfloat16_rn(y[i]);
       } else {
-        float* o = static_cast<float*>(p.o);
+        float* o = static_cast<float*>(p.o) + base;
 #pragma unroll
-        for (int i = 0; i < kC; ++i)
-          if (i < nvalid) o[(static_cast<size_t>(t0 + i) * p.Hv + h) * kD + dv] = y[i];
+        for (int i = 0; i < 32; ++i)
+          if (i < nv) o[i * orow] = y[i];
       }
     }
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(12);
   }
 
   if (failed) {
     if (tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(bar, phase);      // one more bounded chance for an MMA in flight
   } else if (p.state_out) {
-    float* dst = p.state_out + (static_cast<size_t>(bh) * kD + tid) * kD;
-    for (int c = 0; c < kD; c += 16) {
+    float* dst = p.state_out + (static_cast<size_t>(bh) * kD + row) * kD + half * 64;
+    for (int c = 0; c < 64; c += 16) {
       float v[16];
-      tc::tmem_ld16(tDR + my + c, v);
+      tc::tmem_ld16(tDR + half * 64 + c, v);
       tc::tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
@@ -572,3 +656,14 @@ extern "C" int gdn_chunked_fwd(const void* q, const void* k, const void* v, long
   chunked_kernel<<<static_cast<unsigned>(B * Hv), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_status(cudaGetLastError(), "chunked kernel launch");
 }
+
+#ifdef GDN_CHUNK_TIMING
+extern "C" int gdn_debug_chunk_timing(long long* out, int reset) {
+  int rc = cuda_status(cudaMemcpyFromSymbol(out, gdn::g_chunk_timing, sizeof(long long) * 16), "timing read");
+  if (rc == GDN_OK && reset) {
+    long long z[16] = {0};
+    rc = cuda_status(cudaMemcpyToSymbol(gdn::g_chunk_timing, z, sizeof(z)), "timing reset");
+  }
+  return rc;
+}
+#endif

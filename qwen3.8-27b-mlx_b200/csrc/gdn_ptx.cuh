@@ -116,6 +116,17 @@ __device__ __forceinline__ uint32_t kmajor_offset(int r, int k, int elem_bytes, 
   return static_cast<uint32_t>(r >> 3) * sbo + (kb >> 4) * 128u + static_cast<uint32_t>(r & 7) * 16u + (kb & 15u);
 }
 
+// MN-major, no-swizzle: a core matrix is 8 K-rows x 16 bytes along M/N,
+// stored contiguously; M/N groups of 16 bytes are `sbo` apart, groups of 8
+// K-rows `lbo` apart.  Element (mn, k) sits at
+//     (mn * E / 16) * sbo + (k / 8) * lbo + (k % 8) * 16 + (mn * E) % 16.
+// An MMA's K step (8 tf32 = one K group, 16 bf16 = two) advances the
+// descriptor start address by that many `lbo`.
+__device__ __forceinline__ uint32_t mnmajor_offset(int mn, int k, int elem_bytes, uint32_t sbo, uint32_t lbo) {
+  const uint32_t mb = static_cast<uint32_t>(mn * elem_bytes);
+  return (mb >> 4) * sbo + static_cast<uint32_t>(k >> 3) * lbo + static_cast<uint32_t>(k & 7) * 16u + (mb & 15u);
+}
+
 // Shared-memory matrix descriptor (sm_100 "version 1"), no swizzle.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -128,13 +139,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 
 enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };
 
-// Instruction descriptor of kind::f16 / kind::tf32 with an fp32 accumulator,
-// both operands K-major.
-__host__ __device__ constexpr uint32_t instr_desc(Kind ab, int M, int N, bool neg_a = false, bool neg_b = false) {
+// Instruction descriptor of kind::f16 / kind::tf32 with an fp32 accumulator;
+// a_mn / b_mn select the MN-major layout for A / B (default K-major).
+__host__ __device__ constexpr uint32_t instr_desc(Kind ab, int M, int N, bool neg_a = false, bool neg_b = false,
+                                                  bool a_mn = false, bool b_mn = false) {
   return (1u << 4)                                   // D format: f32
          | (static_cast<uint32_t>(ab) << 7)          // A format
          | (static_cast<uint32_t>(ab) << 10)         // B format
          | ((neg_a ? 1u : 0u) << 13) | ((neg_b ? 1u : 0u) << 14)
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }

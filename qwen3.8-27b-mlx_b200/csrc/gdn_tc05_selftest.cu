@@ -30,15 +30,20 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
 
+  // K-major: sbo per 8 rows, lbo 128.  MN-major: sbo 128 per 16 bytes of
+  // M/N, lbo per 8 K-rows = the whole M/N extent.
+  const bool a_mn = (mode & 8) != 0, b_mn = (mode & 16) != 0;
+  const uint32_t lboA_mn = static_cast<uint32_t>(128 * E / 16) * 128;
+  const uint32_t lboB_mn = static_cast<uint32_t>(N * E / 16) * 128;
   for (int idx = tid; idx < 128 * K; idx += 128) {
     const int r = idx / K, k = idx - r * K;
-    const uint32_t off = tc::kmajor_offset(r, k, E, sbo);
+    const uint32_t off = a_mn ? tc::mnmajor_offset(r, k, E, 128, lboA_mn) : tc::kmajor_offset(r, k, E, sbo);
     if (bf) *reinterpret_cast<__nv_bfloat16*>(sA + off) = __float2bfloat16_rn(A[idx]);
     else *reinterpret_cast<float*>(sA + off) = A[idx];
   }
   for (int idx = tid; idx < N * K; idx += 128) {
     const int r = idx / K, k = idx - r * K;
-    const uint32_t off = tc::kmajor_offset(r, k, E, sbo);
+    const uint32_t off = b_mn ? tc::mnmajor_offset(r, k, E, 128, lboB_mn) : tc::kmajor_offset(r, k, E, sbo);
     if (bf) *reinterpret_cast<__nv_bfloat16*>(sB + off) = __float2bfloat16_rn(B[idx]);
     else *reinterpret_cast<float*>(sB + off) = B[idx];
   }
@@ -72,14 +77,17 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   }
 
   if (tid == 0) {
-    const uint32_t idesc = tc::instr_desc(bf ? tc::kBF16 : tc::kTF32, 128, N, (mode & 2) != 0);
+    const uint32_t idesc = tc::instr_desc(bf ? tc::kBF16 : tc::kTF32, 128, N, (mode & 2) != 0, false, a_mn, b_mn);
     const int steps = static_cast<int>(kbytes / 32);
+    const int kgroups = bf ? 2 : 1;                 // K groups of 8 per MMA
     for (int j = 0; j < steps; ++j) {
-      const uint64_t bd = tc::smem_desc(ptx::smem_u32(sB) + j * 256, 128, sbo);
+      const uint64_t bd = b_mn ? tc::smem_desc(ptx::smem_u32(sB) + j * kgroups * lboB_mn, lboB_mn, 128)
+                               : tc::smem_desc(ptx::smem_u32(sB) + j * 256, 128, sbo);
       if (mode & 4) {
         tc::mma_ts_tf32(tD, tA + j * 8, bd, idesc, j > 0);
       } else {
-        const uint64_t ad = tc::smem_desc(ptx::smem_u32(sA) + j * 256, 128, sbo);
+        const uint64_t ad = a_mn ? tc::smem_desc(ptx::smem_u32(sA) + j * kgroups * lboA_mn, lboA_mn, 128)
+                                 : tc::smem_desc(ptx::smem_u32(sA) + j * 256, 128, sbo);
         if (bf) tc::mma_ss<tc::kBF16>(tD, ad, bd, idesc, j > 0);
         else tc::mma_ss<tc::kTF32>(tD, ad, bd, idesc, j > 0);
       }
@@ -113,8 +121,9 @@ using namespace gdn;
 extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                                  int* status, void* stream) {
   clear_error();
-  if (mode & ~7) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~7);
+  if (mode & ~31) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~31);
   if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
+  if ((mode & 4) && (mode & 8)) return fail(GDN_ERR_FLAGS, "A from tensor memory has no MN-major form");
   if (N < 16 || N > 128 || N % 16 || K < 16 || K > 128 || K % 16)
     return fail(GDN_ERR_SHAPE, "N=%d K=%d: need multiples of 16 in [16, 128]", N, K);
   if (!A || !B || !D || !status) return fail(GDN_ERR_NULL, "A, B, D and status are required");

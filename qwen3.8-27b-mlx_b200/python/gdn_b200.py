@@ -180,14 +180,15 @@ def recurrent_fwd_from_ckpt(q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src,
     return o, state_out, ckpt
 
 
-def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False):
+def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=False, b_mn=False):
     """D = op(A) @ B.T on one CTA through tcgen05 (diagnostic).  A (128,K),
     B (N,K) fp32 CUDA tensors.  Returns (D, status)."""
     dev = _dev(A, B)
     N, K = B.shape
     D = torch.empty((128, N), dtype=torch.float32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    mode = (1 if bf16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0)
+    mode = (1 if bf16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0) | (8 if a_mn else 0) | \
+        (16 if b_mn else 0)
     check(lib().gdn_tc05_selftest(ptr(A), ptr(B), ptr(D), N, K, mode, ptr(status), stream_ptr(dev)))
     return D, status
 

@@ -18,16 +18,18 @@ def tf32(x):
 
 
 @pytest.mark.parametrize("N,K", [(64, 64), (128, 128), (64, 128), (16, 16)])
-@pytest.mark.parametrize("mode", ["tf32", "bf16", "neg", "tmem"])
+@pytest.mark.parametrize("mode", ["tf32", "bf16", "neg", "tmem", "a_mn", "b_mn", "ab_mn", "bf16_ab_mn", "tmem_b_mn"])
 def test_tc05_gemm(N, K, mode):
     g = torch.Generator(device="cuda").manual_seed(N * 1000 + K)
     A = torch.randn((128, K), generator=g, device="cuda")
     B = torch.randn((N, K), generator=g, device="cuda")
-    if mode == "bf16":
+    if mode.startswith("bf16"):
         A, B = A.bfloat16().float(), B.bfloat16().float()
     else:
         A, B = tf32(A), tf32(B)
-    D, st = G.tc05_selftest(A, B, bf16=(mode == "bf16"), negate_a=(mode == "neg"), a_in_tmem=(mode == "tmem"))
+    D, st = G.tc05_selftest(A, B, bf16=mode.startswith("bf16"), negate_a=(mode == "neg"),
+                            a_in_tmem=mode.startswith("tmem"), a_mn=mode in ("a_mn", "ab_mn", "bf16_ab_mn"),
+                            b_mn=mode in ("b_mn", "ab_mn", "bf16_ab_mn", "tmem_b_mn"))
     torch.cuda.synchronize()
     ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
     if mode == "neg":
