@@ -525,7 +525,7 @@ def run_prefill(args, lib, device, world):
     hk, hv = shard.hk, shard.hv
     res = {}
     cases = [("config3", [args.prefill_T])]
-    if args.config4:
+    if not args.no_config4:
         cases.append(("config4", config4_lengths()))
     for name, lens in cases:
         X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
@@ -661,7 +661,7 @@ def main():
     ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-T", type=int, default=4096)
-    ap.add_argument("--config4", action="store_true", help="also time one layer of config 4 (B=8 varlen 16K-64K)")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     args = ap.parse_args()
     if args.small:

@@ -21,7 +21,8 @@ namespace {
 constexpr int kConvK = 4;            // linear_conv_kernel_dim (python/qwen35.py:92)
 constexpr int kConvVec = 8;          // channels per thread (one 16-byte bf16 vector)
 constexpr int kConvThreads = 128;
-constexpr int kConvRun = 32;         // tokens per thread
+constexpr int kConvRun = 64;         // tokens per thread
+constexpr int kConvBatch = 8;        // rows loaded ahead of use (bytes in flight per thread)
 
 struct alignas(16) Bf16x8 {
   __nv_bfloat162 h[4];
@@ -70,17 +71,23 @@ struct ConvParams {
   unsigned flags;
 };
 
-// One thread: 8 channels x a run of up to 32 consecutive packed tokens, with
+// One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
 // the 3-row causal window in registers, so every x element is read once
-// (plus a 3-row halo at the start of the run).
-__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvParams p) {
-  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * kConvVec;
-  if (c0 >= p.C) return;
+// (plus a 3-row halo at the start of the run); rows are fetched 8 at a time
+// ahead of use so that each thread keeps 128 bytes of loads in flight.
+template <bool BF16_OPS>
+__global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParams p) {
   const long long t_begin = static_cast<long long>(blockIdx.y) * kConvRun;
   if (t_begin >= p.total) return;
+  // one binary search of cu_seqlens per block, shared through shared memory
+  __shared__ int s_seq;
+  if (p.cu && threadIdx.x == 0) s_seq = seq_of(p.cu, p.B, t_begin);
+  __syncthreads();
+  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * kConvVec;
+  if (c0 >= p.C) return;
   const long long t_end = t_begin + kConvRun < p.total ? t_begin + kConvRun : p.total;
   const bool silu = !(p.flags & GDN_F_CONV_NO_SILU);
-  const bool bf16_ops = (p.flags & GDN_F_CONV_BF16_OPS) != 0;
+  constexpr bool bf16_ops = BF16_OPS;
 
   float w[kConvK][kConvVec];
   {
@@ -101,7 +108,7 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvParams p
   // token range of sequence `seq`: packed offsets, or seq*T .. seq*T+T
   auto seq_begin = [&](int sq) -> long long { return p.cu ? p.cu[sq] : static_cast<long long>(sq) * p.T; };
   auto seq_end = [&](int sq) -> long long { return p.cu ? p.cu[sq + 1] : static_cast<long long>(sq + 1) * p.T; };
-  int seq = p.cu ? seq_of(p.cu, p.B, t_begin) : static_cast<int>(t_begin / p.T);
+  int seq = p.cu ? s_seq : static_cast<int>(t_begin / p.T);
   long long s_begin = seq_begin(seq);
   long long s_end = seq_end(seq);
 
@@ -126,49 +133,59 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvParams p
   };
   load_window(t_begin);
 
-  for (long long t = t_begin; t < t_end; ++t) {
-    if (t >= s_end && seq < p.B - 1) {   // crossed into the next sequence
-      ++seq;
-      s_begin = seq_begin(seq);
-      s_end = seq_end(seq);
-      while (t >= s_end && seq < p.B - 1) {   // skip empty packed sequences
+  for (long long tb = t_begin; tb < t_end; tb += kConvBatch) {
+    // issue the batch's row loads before any of them is used
+    Bf16x8 xr[kConvBatch];
+#pragma unroll
+    for (int u = 0; u < kConvBatch; ++u)
+      if (tb + u < t_end) xr[u] = *reinterpret_cast<const Bf16x8*>(p.x + (tb + u) * p.C + c0);
+#pragma unroll
+    for (int u = 0; u < kConvBatch; ++u) {
+      const long long t = tb + u;
+      if (t >= t_end) break;
+      if (t >= s_end && seq < p.B - 1) {   // crossed into the next sequence
         ++seq;
         s_begin = seq_begin(seq);
         s_end = seq_end(seq);
+        while (t >= s_end && seq < p.B - 1) {   // skip empty packed sequences
+          ++seq;
+          s_begin = seq_begin(seq);
+          s_end = seq_end(seq);
+        }
+        load_window(t);
       }
-      load_window(t);
-    }
-    float xv[kConvVec];
-    unpack8(*reinterpret_cast<const Bf16x8*>(p.x + t * p.C + c0), xv);
-    float out[kConvVec];
+      float xv[kConvVec];
+      unpack8(xr[u], xv);
+      float out[kConvVec];
 #pragma unroll
-    for (int e = 0; e < kConvVec; ++e) {
-      float acc;
-      if (bf16_ops) {   // MLX per-op bf16: each product and each partial sum rounded
-        acc = bf16r(win[0][e] * w[0][e]);
-        acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
-        acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
-        acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
-        if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
-      } else {
-        acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
-        if (silu) acc = acc * sigmoid_f(acc);
+      for (int e = 0; e < kConvVec; ++e) {
+        float acc;
+        if constexpr (bf16_ops) {   // MLX per-op bf16: each product and each partial sum rounded
+          acc = bf16r(win[0][e] * w[0][e]);
+          acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
+          acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
+          acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
+          if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
+        } else {          // fp32 accumulation; the bf16 output rounding dwarfs the fast-exp error
+          acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
+          if (silu) acc = __fdividef(acc, 1.f + __expf(-acc));
+        }
+        out[e] = acc;
       }
-      out[e] = acc;
-    }
-    *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = pack8(out);
+      *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = pack8(out);
 #pragma unroll
-    for (int e = 0; e < kConvVec; ++e) {
-      win[0][e] = win[1][e];
-      win[1][e] = win[2][e];
-      win[2][e] = xv[e];
-    }
-    if (p.state_out && t == s_end - 1) {
-      // the carried window: the last K-1 rows of [state; x]
+      for (int e = 0; e < kConvVec; ++e) {
+        win[0][e] = win[1][e];
+        win[1][e] = win[2][e];
+        win[2][e] = xv[e];
+      }
+      if (p.state_out && t == s_end - 1) {
+        // the carried window: the last K-1 rows of [state; x]
 #pragma unroll
-      for (int j = 0; j < kConvK - 1; ++j)
-        *reinterpret_cast<Bf16x8*>(p.state_out + (static_cast<long long>(seq) * (kConvK - 1) + j) * p.C + c0) =
-            pack8(win[j]);
+        for (int j = 0; j < kConvK - 1; ++j)
+          *reinterpret_cast<Bf16x8*>(p.state_out + (static_cast<long long>(seq) * (kConvK - 1) + j) * p.C + c0) =
+              pack8(win[j]);
+      }
     }
   }
 }
@@ -298,7 +315,8 @@ extern "C" int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in
     if (gy > 65535LL * 1024) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
     // grid.y is limited to 65535: fold extra runs into grid.z is not needed below 2M tokens
     if (gy > 65535) return fail(GDN_ERR_SHAPE, "at most %d tokens per call", 65535 * kConvRun);
-    conv1d_kernel<<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
+    if (flags & GDN_F_CONV_BF16_OPS) conv1d_kernel<true><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
+    else conv1d_kernel<false><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
     int rc = cuda_status(cudaGetLastError(), "conv1d launch");
     if (rc != GDN_OK) return rc;
   }

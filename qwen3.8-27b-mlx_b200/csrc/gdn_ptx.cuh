@@ -57,7 +57,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-// ---- bulk copies through the TMA engine (no tensor map, no multicast) --------
+// ---- bulk copies through the TMA engine (no tensor map, this CTA only) -------
 
 // global -> shared, completion counted in bytes on `bar`.  16-byte aligned
 // addresses, size a multiple of 16.

@@ -124,6 +124,10 @@ extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N
   if (mode & ~31) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~31);
   if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
   if ((mode & 4) && (mode & 8)) return fail(GDN_ERR_FLAGS, "A from tensor memory has no MN-major form");
+  // MN-major operands are exercised with bf16 only: on sm_100a with this
+  // toolchain kind::tf32 with an MN-major operand completed with an all-zero
+  // result, so no kernel of this library uses that combination.
+  if ((mode & 24) && !(mode & 1)) return fail(GDN_ERR_FLAGS, "MN-major operands are tested with bf16 only");
   if (N < 16 || N > 128 || N % 16 || K < 16 || K > 128 || K % 16)
     return fail(GDN_ERR_SHAPE, "N=%d K=%d: need multiples of 16 in [16, 128]", N, K);
   if (!A || !B || !D || !status) return fail(GDN_ERR_NULL, "A, B, D and status are required");

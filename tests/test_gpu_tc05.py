@@ -18,7 +18,7 @@ def tf32(x):
 
 
 @pytest.mark.parametrize("N,K", [(64, 64), (128, 128), (64, 128), (16, 16)])
-@pytest.mark.parametrize("mode", ["tf32", "bf16", "neg", "tmem", "a_mn", "b_mn", "ab_mn", "bf16_ab_mn", "tmem_b_mn"])
+@pytest.mark.parametrize("mode", ["tf32", "bf16", "neg", "tmem", "bf16_a_mn", "bf16_b_mn", "bf16_ab_mn"])
 def test_tc05_gemm(N, K, mode):
     g = torch.Generator(device="cuda").manual_seed(N * 1000 + K)
     A = torch.randn((128, K), generator=g, device="cuda")
@@ -28,11 +28,19 @@ def test_tc05_gemm(N, K, mode):
     else:
         A, B = tf32(A), tf32(B)
     D, st = G.tc05_selftest(A, B, bf16=mode.startswith("bf16"), negate_a=(mode == "neg"),
-                            a_in_tmem=mode.startswith("tmem"), a_mn=mode in ("a_mn", "ab_mn", "bf16_ab_mn"),
-                            b_mn=mode in ("b_mn", "ab_mn", "bf16_ab_mn", "tmem_b_mn"))
+                            a_in_tmem=mode.startswith("tmem"), a_mn=mode in ("bf16_a_mn", "bf16_ab_mn"),
+                            b_mn=mode in ("bf16_b_mn", "bf16_ab_mn"))
     torch.cuda.synchronize()
     ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
     if mode == "neg":
         ref = -ref
     assert int(st.item()) == 0
     assert O.rel_err(D.cpu().numpy(), ref) < 1e-5
+
+
+def test_tf32_mn_major_is_refused():
+    A = torch.zeros((128, 16), device="cuda")
+    B = torch.zeros((16, 16), device="cuda")
+    with pytest.raises(G.GdnError) as e:
+        G.tc05_selftest(A, B, a_mn=True)
+    assert e.value.code == G.GDN_ERR_FLAGS
