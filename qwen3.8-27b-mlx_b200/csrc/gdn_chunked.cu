@@ -295,27 +295,36 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     __syncthreads();
     GDN_TICK(1);
 
-    // ---- columns: K^T diag(beta g r_k) (threads 0-127 -> dk), V^T diag(beta)
-    //      (threads 128-255 -> dv), read column-wise from global, row-wise stores
+    // ---- columns: K^T diag(beta g r_k) and V^T diag(beta), read column-wise
+    //      from global two columns per 4-byte load (threads 0-63: K columns
+    //      2p, 2p+1 for tokens of half th; threads 128-191 likewise for V),
+    //      stored row-wise
     {
-      const int c = tid & 127;
+      const int pr = tid & 63;                   // column pair
+      const int th = (tid >> 6) & 1;             // token half
       const bool is_k = tid < 128;
-      const __nv_bfloat16* src = (is_k ? p.k + kh * kD + c : p.v + h * kD + c) + t0 * (is_k ? p.k_stride : p.v_stride);
+      const int c = 2 * pr;
       const long long stride = is_k ? p.k_stride : p.v_stride;
+      const __nv_bfloat16* src = (is_k ? p.k + kh * kD : p.v + h * kD) + c + (t0 + th * 32) * stride;
       unsigned char* dst = is_k ? sKt : sVt;
-      __nv_bfloat16 raw[kC];                    // all 64 loads in flight before any use
+      const int nv = nvalid - th * 32;
+      __nv_bfloat162 raw[32];                   // all loads in flight before any use
 #pragma unroll
-      for (int j = 0; j < kC; ++j) raw[j] = j < nvalid ? src[j * stride] : __float2bfloat16_rn(0.f);
+      for (int j = 0; j < 32; ++j)
+        raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * stride) : __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < kC; j += 4) {
-        float x[4];
+      for (int j = 0; j < 32; j += 4) {
+        float x0[4], x1[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int jj = j + e;
+          const int jj = th * 32 + j + e;
           const float sc_ = is_k ? s_beta[jj] * s_g[jj] * s_rk[jj] : s_beta[jj];
-          x[e] = tc::to_tf32(__bfloat162float(raw[jj]) * sc_);
+          const float2 f = __bfloat1622float2(raw[j + e]);
+          x0[e] = tc::to_tf32(f.x * sc_);
+          x1[e] = tc::to_tf32(f.y * sc_);
         }
-        *reinterpret_cast<float4*>(at(dst, c, j, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
+        *reinterpret_cast<float4*>(at(dst, c, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+        *reinterpret_cast<float4*>(at(dst, c + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
       }
     }
     ptx::fence_proxy_async_smem();
@@ -492,17 +501,29 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
         *reinterpret_cast<float4*>(at(sW, i, half * 64 + e, kSbo128)) =
             make_float4(tc::to_tf32(w[e]), tc::to_tf32(w[e + 1]), tc::to_tf32(w[e + 2]), tc::to_tf32(w[e + 3]));
     } else {
-      const int dk = (tid & 63) + 64 * half;
-      const __nv_bfloat16* src = p.k + kh * kD + dk + t0 * p.k_stride;
-      __nv_bfloat16 raw[kC];
+      const int lt = (tid & 63) + 64 * half;     // 0..127 over the four warps on lanes 64-127
+      const int pr = lt & 63;
+      const int th = lt >> 6;
+      const int c = 2 * pr;
+      const __nv_bfloat16* src = p.k + kh * kD + c + (t0 + th * 32) * p.k_stride;
+      const int nv = nvalid - th * 32;
+      __nv_bfloat162 raw[32];
 #pragma unroll
-      for (int j = 0; j < kC; ++j) raw[j] = j < nvalid ? src[j * p.k_stride] : __float2bfloat16_rn(0.f);
+      for (int j = 0; j < 32; ++j)
+        raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * p.k_stride) : __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < kC; j += 4) {
-        float x[4];
+      for (int j = 0; j < 32; j += 4) {
+        float x0[4], x1[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] = tc::to_tf32(__bfloat162float(raw[j + e]) * s_ratio[j + e] * s_rk[j + e]);
-        *reinterpret_cast<float4*>(at(sKt, dk, j, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
+        for (int e = 0; e < 4; ++e) {
+          const int jj = th * 32 + j + e;
+          const float sc_ = s_ratio[jj] * s_rk[jj];
+          const float2 f = __bfloat1622float2(raw[j + e]);
+          x0[e] = tc::to_tf32(f.x * sc_);
+          x1[e] = tc::to_tf32(f.y * sc_);
+        }
+        *reinterpret_cast<float4*>(at(sKt, c, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+        *reinterpret_cast<float4*>(at(sKt, c + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
       }
     }
     ptx::fence_proxy_async_smem();
