@@ -407,7 +407,7 @@ class PrefillLayer:
     bf16 projection output (C = 2*hk*128 + hv*128), conv weights, z, gamma,
     gate inputs.  `lens` packs sequences of those lengths (cu_seqlens)."""
 
-    def __init__(self, lens, device, seed, hk=HK, hv=HV):
+    def __init__(self, lens, device, seed, hk=HK, hv=HV, split=False):
         g = torch.Generator(device=device)
         g.manual_seed(seed)
         C = 2 * hk * D + hv * D
@@ -430,6 +430,19 @@ class PrefillLayer:
         self.o = torch.empty((self.N, hv, D), dtype=torch.float32, device=device)
         self.S = torch.empty((self.B, hv, D, D), dtype=torch.float32, device=device)
         self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
+        self.split = False
+        self.ws = None
+        if split:
+            self.use_split(True)
+
+    def use_split(self, on):
+        """Run the chunked step as gdn_chunked_fwd_ws (prep + scan launches on a
+        workspace allocated here, outside any timed region) or gdn_chunked_fwd."""
+        import gdn_b200 as G
+        self.split = bool(on)
+        if self.split and self.ws is None:
+            need = G.chunked_workspace_bytes(self.B, self.T, self.hv, not self.uniform)
+            self.ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
 
     def _cu(self):
         return None if self.uniform else ctypes.c_void_p(self.cu.data_ptr())
@@ -450,9 +463,14 @@ class PrefillLayer:
         q = ctypes.c_void_p(base)
         k = ctypes.c_void_p(base + hk * D * 2)
         v = ctypes.c_void_p(base + 2 * hk * D * 2)
-        rc = lib.gdn_chunked_fwd(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
-                                 None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
-                                 G.F_QK_L2NORM, h)
+        if self.split:
+            rc = lib.gdn_chunked_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
+                                        None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
+                                        G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
+        else:
+            rc = lib.gdn_chunked_fwd(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
+                                     None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
+                                     G.F_QK_L2NORM, h)
         if rc:
             raise RuntimeError(lib.gdn_last_error().decode())
 
@@ -527,22 +545,32 @@ def run_prefill(args, lib, device, world):
     cases = [("config3", [args.prefill_T])]
     if not args.no_config4:
         cases.append(("config4", config4_lengths()))
+    schedules = ["fused", "split"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
     for name, lens in cases:
         X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
         gathered = None
         if world > 1:
             gathered = torch.empty((world,) + tuple(X.out.shape), dtype=torch.bfloat16, device=device)
         steps = max(2, args.steps // 10) if name == "config4" else max(3, args.steps // 5)
-        ms, kms = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1) if name == "config4"
-                                     else max(args.warmup, 3), gathered)
+        timed = {}
+        for sched in schedules:          # every rank times every schedule, in the same order
+            X.use_split(sched == "split")
+            timed[sched] = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1)
+                                              if name == "config4" else max(args.warmup, 3), gathered)
+        best = min(timed, key=lambda k: timed[k][0])
+        ms, kms = timed[best]
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
+        kernel = "chunk_prep_kernel + chunk_scan_kernel" if best == "split" else "chunked_kernel"
         res[name] = {
+            "schedule": best,
+            "ms_per_layer_by_schedule": {k: round(v[0], 4) for k, v in timed.items()},
+            "workspace_bytes": int(X.ws.numel()) if X.ws is not None else 0,
             "workload": (f"{name}: {X.B} seq, {X.N} tokens, conv(C={X.C}, K=4)+SiLU -> chunked C=64 "
                          f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
                          + (" -> NCCL all-gather" if world > 1 else "")),
             "tokens_per_s": round(X.N / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
             "kernel_ms": {k: round(v, 4) for k, v in kms.items()},
-            "roofline": {"bound": "tensor", "kernel": "chunked_kernel", "achieved": round(achieved, 2),
+            "roofline": {"bound": "tensor", "kernel": kernel, "achieved": round(achieved, 2),
                          "peak": tf_peak, "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
                          "peak_kind": peak_kind + " bf16 dense (the kernel runs tf32)",
                          "flop_per_launch": X.flops(), "flop_per_token_head": FLOP_PER_TOKEN_HEAD}}
@@ -662,6 +690,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
+    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split"], default="auto",
+                    help="chunked schedule for configs 3/4; auto times both and reports the faster")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     args = ap.parse_args()
     if args.small:

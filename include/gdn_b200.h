@@ -161,6 +161,34 @@ int gdn_chunked_fwd(const void* q, const void* k, const void* v,
                     unsigned flags, void* stream);
 
 /*
+ * gdn_chunked_workspace_bytes -- device workspace that gdn_chunked_fwd_ws
+ * needs for B sequences of T tokens (packed = 0), or for B packed sequences
+ * of T tokens in all (packed != 0, an upper bound that holds for any
+ * cu_seqlens).  About 113 KiB per (64-token chunk, value head).  0 for bad
+ * sizes.
+ */
+size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed);
+
+/*
+ * gdn_chunked_fwd_ws -- gdn_chunked_fwd split in two launches: the
+ * state-independent part of every (chunk, value head) in parallel, written
+ * to `workspace`, then the state chain per (sequence, value head) reading it
+ * back.  Same arguments, results and flags as gdn_chunked_fwd (the same
+ * function of the inputs as chunked_delta, python/qwen35.py:365-431); the
+ * split exposes (chunks x heads) of parallel work where gdn_chunked_fwd
+ * has (sequences x heads).  workspace: device memory, 256-byte aligned, at
+ * least gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) bytes,
+ * no initial contents needed, not overlapping the states or o; calls that
+ * share one workspace must be ordered on a stream.
+ */
+int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
+                       long long q_stride, long long k_stride, long long v_stride,
+                       const float* a, const float* b, const float* A_log, const float* dt_bias,
+                       const float* state_in, float* state_out, void* o,
+                       const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                       unsigned flags, void* workspace, size_t workspace_size, void* stream);
+
+/*
  * gdn_conv1d_fwd -- causal depthwise conv1d (kernel K = 4, no bias) over the
  * concatenated q|k|v channels, then SiLU: the front end of
  * GatedDeltaNet::operator() (DepthwiseConv::operator(), cpp/src/model.cpp:

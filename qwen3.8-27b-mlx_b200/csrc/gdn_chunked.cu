@@ -11,23 +11,28 @@
 //   A[i,j] = beta_i r_ki r_kj e^{Gam_i-Gam_j} G[i,j]          (j < i)
 //   T^-1   = (I + A)^-1                          (blocked forward substitution)
 //   U0^T   = V^T diag(beta) T^-T                 (MMA)
-//   W^T    = K^T diag(beta g r_k) T^-T           (MMA)
-//   U^T    = U0^T - R W^T                        (MMA, R from tensor memory)
+//   W      = T^-1 diag(beta g r_k) K             (MMA)
 //   M[i,j] = r_qi r_kj e^{Gam_i-Gam_j} P[i,j]                  (j <= i)
+//   ---- everything above is independent of the state ("prep") ----
+//   U^T    = U0^T - R W^T                        (MMA, R from tensor memory)
 //   y^T    = R (diag(g r_q) Q)^T + U^T M^T       (MMAs)      -> o
 //   R     <- g_last R + U^T diag(e^{Gam_last-Gam} r_k) K       (MMA)
 //
 // which is the reference's y = M U0 + Qeff S, U = U0 - Kt S,
 // S <- cumg_last S + k^T (ratio U) regrouped so that every product has
-// M = 128 rows (Dv, Dk or the 128 rows of [K; Q]) and the state never leaves
-// the chip between chunks.  One CTA (4 warps, thread t <-> TMEM lane t) owns
-// one (sequence, value head); the 512 tensor-memory columns hold
-//   [0,128)   R rounded to tf32 (A operand of U and y)
-//   [128,256) R in full fp32, also the accumulator of the state update
-//   [256,320) G (lanes 0-63) and P (lanes 64-127)
-//   [320,384) W^T    [384,448) U^T    [448,512) y^T
-// All MMAs are kind::tf32 with fp32 accumulation: the bf16 inputs are exact
-// in tf32, derived operands are rounded to nearest tf32 once.
+// M = 128 rows and the state stays on chip between chunks.  All MMAs are
+// kind::tf32 with fp32 accumulation: the bf16 inputs are exact in tf32,
+// derived operands are rounded to nearest tf32 once.
+//
+// Two schedules share the phase functions below:
+//   * fused (gdn_chunked_fwd): one CTA per (sequence, value head) runs prep
+//     and state update chunk after chunk; no scratch memory.
+//   * split (gdn_chunked_fwd_ws): a prep kernel runs the state-independent
+//     work of every (chunk, value head) in parallel and writes its operands,
+//     in the shared-memory layouts the tensor cores read, to a workspace; a
+//     scan kernel per (sequence, value head) bulk-copies them in and runs
+//     only the state chain, so the serial work per chunk shrinks to the
+//     state-dependent MMAs and their epilogues.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -42,10 +47,10 @@ namespace gdn {
 __device__ long long g_chunk_timing[16];
 #define GDN_TICK(slot)                                                          \
   do {                                                                          \
-    if (blockIdx.x == 0 && threadIdx.x == 0) {                                  \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {               \
       const long long now_ = clock64();                                         \
-      g_chunk_timing[slot] += now_ - tick_;                                     \
-      tick_ = now_;                                                             \
+      g_chunk_timing[slot] += now_ - c.tick;                                    \
+      c.tick = now_;                                                            \
     }                                                                           \
   } while (0)
 #else
@@ -59,8 +64,9 @@ namespace {
 constexpr int kC = 64;          // tokens per chunk (python/qwen35.py:365)
 constexpr int kThreads = 256;   // 8 warps: warp w owns TMEM lane quarter w % 4, column half w / 4
 
-// shared memory map, bytes; tensor-core operands in the K-major no-swizzle
-// layout (LBO 128 B), written row-wise so that a warp's stores hit distinct banks
+// shared memory map of the fused and prep kernels, bytes; tensor-core operands
+// in the K-major no-swizzle layout (LBO 128 B), written row-wise so that a
+// warp's stores hit distinct banks
 constexpr uint32_t kSbo128 = (kD * 4 / 16) * 128;   // 8-row group stride of 128-wide fp32 rows
 constexpr uint32_t kSbo64 = (kC * 4 / 16) * 128;    // ... of 64-wide fp32 rows
 constexpr int kPad = kC + 1;                        // row stride of the plain solve arrays
@@ -72,15 +78,39 @@ constexpr uint32_t kOffM = kOffTi + kC * kC * 4;    // M (must follow T^-1)    6
 constexpr uint32_t kOffW = kOffM + kC * kC * 4;     // W rows 64 x 128 (32 KiB); X during the solve
 constexpr uint32_t kOffA = kOffW + kC * kD * 4;     // A, plain, row stride 65
 constexpr uint32_t kOffY = kOffA + kC * kPad * 4;   // solve temporaries 3 x 16 x 16
-constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 8 x 64
-constexpr uint32_t kOffBar = kOffSc + 8 * kC * 4;   // mbarrier, TMEM base
+constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 10 x 64
+constexpr uint32_t kOffBar = kOffSc + 10 * kC * 4;  // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
 
+// shared memory map of the scan kernel
+constexpr uint32_t kScanW = 0;                      // W        64 x 128 (32 KiB)
+constexpr uint32_t kScanKh = kScanW + kC * kD * 4;  // K-hat^T 128 x 64  (32 KiB)
+constexpr uint32_t kScanM = kScanKh + kD * kC * 4;  // M        64 x 64  (16 KiB)
+constexpr uint32_t kScanQ = kScanM + kC * kC * 4;   // Qs       64 x 128 (32 KiB)
+constexpr uint32_t kScanU = kScanQ + kC * kD * 4;   // U^T     128 x 64  (32 KiB)
+constexpr uint32_t kScanSc = kScanU + kD * kC * 4;  // gq[64], g_last
+constexpr uint32_t kScanBar = kScanSc + 2 * kC * 4; // 3 mbarriers, TMEM base
+constexpr uint32_t kScanSmem = kScanBar + 64;
+
 constexpr uint32_t kTmemCols = 512;
-// [0,128) R (tf32), [128,256) R (fp32 master, state-update accumulator),
-// [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
+// fused / prep: [0,128) R (tf32), [128,256) R (fp32 master, state-update
+// accumulator), [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
 // [384,448) U^T; [448,512) y^T
 constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 384, kColY = 448;
+
+// One workspace record per (chunk, value head): the prep kernel's outputs in
+// the byte layout of the scan kernel's shared memory.
+constexpr uint32_t kRecW = 0;                       // W, K-major 64 x 128, SBO 4096
+constexpr uint32_t kRecKh = kRecW + kC * kD * 4;    // K-hat^T, K-major 128 x 64, SBO 2048
+constexpr uint32_t kRecM = kRecKh + kD * kC * 4;    // M, K-major 64 x 64, SBO 2048
+constexpr uint32_t kRecU = kRecM + kC * kC * 4;     // U0^T, plain row-major 128 x 64
+constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // gq[64] = g_i r_qi, [64] = g_last
+constexpr uint32_t kRecBytes = kRecSc + 1024;       // multiple of 256
+constexpr size_t kWsHeader = 256;                   // then the chunk prefix (B+1 int32), then records
+
+__host__ __device__ constexpr size_t records_offset(int B) {
+  return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
+}
 
 struct ChunkParams {
   const __nv_bfloat16* q;
@@ -98,6 +128,11 @@ struct ChunkParams {
   int B, T, Hk, Hv;
   unsigned flags;
   int* err;
+  // split schedule
+  unsigned char* ws;              // workspace (256-byte aligned)
+  int32_t* chunk_prefix;          // (B+1) first record slot of each sequence (packed batches)
+  long long n_slots;              // record slots (chunks over all sequences, or an upper bound)
+  int nch_uniform;                // chunks per sequence when cu == null
 };
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
@@ -133,40 +168,12 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
   tc::tmem_ld_wait();
 }
 
-__global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams p) {
-  extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* sKQ = sm + kOffKQ;
-  unsigned char* sKt = sm + kOffKt;
-  unsigned char* sVt = sm + kOffVt;   // V^T diag(beta), later U^T
-  unsigned char* sTi = sm + kOffTi;
-  unsigned char* sM = sm + kOffM;
-  unsigned char* sW = sm + kOffW;
-  float* sX = reinterpret_cast<float*>(sm + kOffW);   // T^-1 in plain form while solving
-  float* sA = reinterpret_cast<float*>(sm + kOffA);
-  float* sY = reinterpret_cast<float*>(sm + kOffY);
-  float* sc = reinterpret_cast<float*>(sm + kOffSc);
-  float* s_pre = sc;            // warp-local prefix of log-decay
-  float* s_gam = sc + 64;       // Gam_i
-  float* s_g = sc + 128;        // exp(Gam_i)
-  float* s_ratio = sc + 192;    // exp(Gam_last - Gam_i)
-  float* s_beta = sc + 256;
-  float* s_rk = sc + 320;
-  float* s_rq = sc + 384;
-  float* s_misc = sc + 448;     // [0] g_last
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kOffBar + 8);
+__device__ __forceinline__ uint64_t desc(const unsigned char* base, uint32_t byte_off, uint32_t sbo) {
+  return tc::smem_desc(ptx::smem_u32(base) + byte_off, 128, sbo);
+}
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int quarter = warp & 3;       // TMEM lanes 32*quarter ..
-  const int half = warp >> 2;         // column half of the epilogues
-  const int row = quarter * 32 + lane;  // TMEM lane of this thread
-  const int bh = blockIdx.x;
-  const int b = bh / p.Hv;
-  const int h = bh - b * p.Hv;
-  const int kh = h / (p.Hv / p.Hk);
-  long long s0, s1;
+// Token range of sequence b.
+__device__ __forceinline__ void seq_range(const ChunkParams& p, int b, long long& s0, long long& s1) {
   if (p.cu) {
     s0 = p.cu[b];
     s1 = p.cu[b + 1];
@@ -175,470 +182,828 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     s0 = static_cast<long long>(b) * p.T;
     s1 = s0 + p.T;
   }
-  const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
-  const bool l2 = (p.flags & GDN_F_QK_L2NORM) != 0;
-  const float A_h = expf(__ldg(p.A_log + h));
-  const float dtb = __ldg(p.dt_bias + h);
-  const float log_clip = logf(1e-6f);          // log(clip(alpha, 1e-6, 1)), python/qwen35.py:400
-  const float qscale = rsqrtf(static_cast<float>(kD));
+}
 
-  if (warp == 0) {
+// Per-CTA state shared by the phase functions.
+struct Ctx {
+  unsigned char *sKQ, *sKt, *sVt, *sTi, *sM, *sW;
+  float *sX, *sA, *sY;
+  float *s_pre, *s_gam, *s_g, *s_ratio, *s_beta, *s_rk, *s_rq, *s_misc, *s_kw, *s_kh;
+  uint64_t* bar;
+  int tid, warp, lane, quarter, half, row;
+  int h, kh;
+  float A_h, dtb, log_clip, qscale;
+  bool l2;
+  uint32_t tb, my;   // TMEM base, this warp's lane quarter
+  uint32_t phase;
+#ifdef GDN_CHUNK_TIMING
+  long long tick;
+#endif
+};
+
+__device__ __forceinline__ void ctx_init(Ctx& c, const ChunkParams& p, unsigned char* sm, int h) {
+  c.sKQ = sm + kOffKQ;
+  c.sKt = sm + kOffKt;
+  c.sVt = sm + kOffVt;
+  c.sTi = sm + kOffTi;
+  c.sM = sm + kOffM;
+  c.sW = sm + kOffW;
+  c.sX = reinterpret_cast<float*>(sm + kOffW);
+  c.sA = reinterpret_cast<float*>(sm + kOffA);
+  c.sY = reinterpret_cast<float*>(sm + kOffY);
+  float* sc = reinterpret_cast<float*>(sm + kOffSc);
+  c.s_pre = sc;
+  c.s_gam = sc + 64;
+  c.s_g = sc + 128;
+  c.s_ratio = sc + 192;
+  c.s_beta = sc + 256;
+  c.s_rk = sc + 320;
+  c.s_rq = sc + 384;
+  c.s_misc = sc + 448;
+  c.s_kw = sc + 512;      // beta g r_k: the K columns of W's right-hand side
+  c.s_kh = sc + 576;      // e^{Gam_last-Gam} r_k: the K columns of the state update
+  c.bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  c.tid = threadIdx.x;
+  c.warp = c.tid >> 5;
+  c.lane = c.tid & 31;
+  c.quarter = c.warp & 3;
+  c.half = c.warp >> 2;
+  c.row = c.quarter * 32 + c.lane;
+  c.h = h;
+  c.kh = h / (p.Hv / p.Hk);
+  c.l2 = (p.flags & GDN_F_QK_L2NORM) != 0;
+  c.A_h = expf(__ldg(p.A_log + h));
+  c.dtb = __ldg(p.dt_bias + h);
+  c.log_clip = logf(1e-6f);                  // log(clip(alpha, 1e-6, 1)), python/qwen35.py:400
+  c.qscale = rsqrtf(static_cast<float>(kD));
+  c.phase = 0;
+  c.my = static_cast<uint32_t>(c.quarter * 32) << 16;
+#ifdef GDN_CHUNK_TIMING
+  c.tick = clock64();
+#endif
+}
+
+// Allocate the CTA's tensor memory and initialise its mbarriers.
+__device__ __forceinline__ void tmem_setup(Ctx& c, uint32_t* tslot, uint64_t* bars, int n_bars) {
+  if (c.warp == 0) {
     tc::tmem_alloc(tslot, kTmemCols);
     tc::tmem_relinquish();
   }
-  if (tid == 0) {
-    ptx::mbar_init(bar, 1);
+  if (c.tid == 0) {
+    for (int i = 0; i < n_bars; ++i) ptx::mbar_init(bars + i, 1);
     ptx::fence_mbar_init();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tb = *tslot;
-  const uint32_t my = static_cast<uint32_t>(quarter * 32) << 16;      // this warp's lane quarter
-  const uint32_t tR = tb + kColR + my, tDR = tb + kColDR + my, tGP = tb + kColGP + my;
-  const uint32_t tW = tb + kColW + my, tU = tb + kColU + my, tY = tb + kColY + my;
+  c.tb = *tslot;
+}
 
-  // initial state: row dv = row, columns [64*half, 64*half+64), into the fp32 master
-  {
-    const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + row) * kD + half * 64 : nullptr;
-    for (int c = 0; c < 64; c += 16) {
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        const float4 f = src ? *reinterpret_cast<const float4*>(src + c + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
-      }
-      tc::tmem_st16(tDR + half * 64 + c, v);
+// One warp polls the MMA barrier, the others wait at the CTA barrier; false if
+// the bounded wait gave up or warp 0 passes ok_in = false (then every thread
+// sees false).
+__device__ __forceinline__ bool mma_wait(Ctx& c, bool ok_in = true) {
+  bool ok = true;
+  if (c.warp == 0) ok = ptx::mbar_wait(c.bar, c.phase) && ok_in;
+  c.phase ^= 1u;
+  const bool all_ok = !__syncthreads_or(!ok);
+  tc::fence_after_sync();
+  return all_ok;
+}
+
+// ---- prep phases (state-independent) -----------------------------------------
+
+// Gates and the in-chunk decay prefix.  s_g, s_ratio, s_misc[0] are written by
+// threads 0-63 without a trailing barrier (the next phase ends with one).
+__device__ __forceinline__ void phase_gates(const ChunkParams& p, Ctx& c, long long t0, int nvalid) {
+  if (c.tid < kC) {
+    float lg = 0.f, beta = 0.f;
+    if (c.tid < nvalid) {
+      const size_t gi = static_cast<size_t>(t0 + c.tid) * p.Hv + c.h;
+      lg = fmaxf(-(c.A_h * softplus_f(__ldg(p.a + gi) + c.dtb)), c.log_clip);
+      beta = 1.f / (1.f + expf(-__ldg(p.b + gi)));
     }
-    tc::tmem_st_wait();
+    float x = lg;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, off);
+      if (c.lane >= off) x += y;
+    }
+    c.s_pre[c.tid] = x;
+    c.s_beta[c.tid] = beta;
   }
+  __syncthreads();
+  if (c.tid < kC) c.s_gam[c.tid] = c.s_pre[c.tid] + (c.tid >= 32 ? c.s_pre[31] : 0.f);
+  __syncthreads();
+  if (c.tid < kC) {
+    const float gl = c.s_gam[kC - 1];
+    c.s_g[c.tid] = expf(c.s_gam[c.tid]);
+    c.s_ratio[c.tid] = expf(gl - c.s_gam[c.tid]);
+    if (c.tid == 0) c.s_misc[0] = expf(gl);
+  }
+}
 
-  uint32_t phase = 0;
-  bool failed = false;
-#ifdef GDN_CHUNK_TIMING
-  long long tick_ = clock64();
-#endif
-  // one warp polls the MMA barrier, the others wait at the CTA barrier
-  auto mma_wait = [&]() -> bool {
-    bool ok = true;
-    if (warp == 0) ok = ptx::mbar_wait(bar, phase);
-    phase ^= 1u;
-    const bool all_ok = !__syncthreads_or(!ok);
+// Rows of K and Q (thread -> token i, 32-dim quarter) into [K; Q], and their norms.
+__device__ __forceinline__ void phase_rows(const ChunkParams& p, Ctx& c, long long t0, long long s0, int nvalid) {
+  const int i = c.tid >> 2;
+  const int qd = c.tid & 3;
+  const bool valid = i < nvalid;
+  const long long tok = valid ? t0 + i : s0;
+  float f[32];
+  load32(p.k + tok * p.k_stride + c.kh * kD + qd * 32, valid, f);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4)
+    *reinterpret_cast<float4*>(at(c.sKQ, i, qd * 32 + e, kSbo128)) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+  if (qd == 0) c.s_rk[i] = c.l2 ? rsqrtf(ss + 1e-6f) : 1.f;
+  load32(p.q + tok * p.q_stride + c.kh * kD + qd * 32, valid, f);
+  ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4)
+    *reinterpret_cast<float4*>(at(c.sKQ, kC + i, qd * 32 + e, kSbo128)) =
+        make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+  if (qd == 0) c.s_rq[i] = c.l2 ? rsqrtf(ss + 1e-6f) * c.qscale : 1.f;
+  __syncthreads();
+}
+
+// Columns of K (or V) read from global two at a time (4-byte loads), scaled
+// per token by scale[], stored as rows of the transposed operand (K-major, 64
+// tokens wide) at dst.  lt in [0,128): column pair lt & 63, token half lt >> 6.
+// The caller selects K or V at run time so that all warps share one copy of
+// this code.
+__device__ __forceinline__ void columns(const ChunkParams& p, const Ctx& c, long long t0, int nvalid, int lt,
+                                        bool is_k, const float* scale, unsigned char* dst) {
+  const int pr = lt & 63;
+  const int th = lt >> 6;
+  const int cc = 2 * pr;
+  const long long stride = is_k ? p.k_stride : p.v_stride;
+  const __nv_bfloat16* src = (is_k ? p.k + c.kh * kD : p.v + c.h * kD) + cc + (t0 + th * 32) * stride;
+  const int nv = nvalid - th * 32;
+  __nv_bfloat162 raw[32];                   // all loads in flight before any use
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * stride) : __floats2bfloat162_rn(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    float x0[4], x1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int jj = th * 32 + j + e;
+      const float s = scale[jj];
+      const float2 f = __bfloat1622float2(raw[j + e]);
+      x0[e] = tc::to_tf32(f.x * s);
+      x1[e] = tc::to_tf32(f.y * s);
+    }
+    *reinterpret_cast<float4*>(at(dst, cc, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+    *reinterpret_cast<float4*>(at(dst, cc + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+  }
+}
+
+// K^T diag(beta g r_k) (threads 0-127) and V^T diag(beta) (threads 128-255).
+__device__ __forceinline__ void phase_cols(const ChunkParams& p, Ctx& c, long long t0, int nvalid) {
+  if (c.tid < kC) {
+    c.s_kw[c.tid] = c.s_beta[c.tid] * c.s_g[c.tid] * c.s_rk[c.tid];
+    c.s_kh[c.tid] = c.s_ratio[c.tid] * c.s_rk[c.tid];
+  }
+  __syncthreads();
+  const bool is_k = c.tid < 128;
+  columns(p, c, t0, nvalid, c.tid & 127, is_k, is_k ? c.s_kw : c.s_beta, is_k ? c.sKt : c.sVt);
+  ptx::fence_proxy_async_smem();
+}
+
+// (a) [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127).
+__device__ __forceinline__ bool phase_mma_a(Ctx& c) {
+  if (c.tid == 0) {
     tc::fence_after_sync();
-    return all_ok;
-  };
-  auto desc = [](const unsigned char* base, uint32_t byte_off, uint32_t sbo) {
-    return tc::smem_desc(ptx::smem_u32(base) + byte_off, 128, sbo);
-  };
-
-  for (int ch = 0; ch < n_chunks; ++ch) {
-    const long long t0 = s0 + static_cast<long long>(ch) * kC;
-    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-
-    // ---- per-token gates and the in-chunk decay prefix ----------------------
-    if (tid < kC) {
-      float lg = 0.f, beta = 0.f;
-      if (tid < nvalid) {
-        const size_t gi = static_cast<size_t>(t0 + tid) * p.Hv + h;
-        lg = fmaxf(-(A_h * softplus_f(__ldg(p.a + gi) + dtb)), log_clip);
-        beta = 1.f / (1.f + expf(-__ldg(p.b + gi)));
-      }
-      float x = lg;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += y;
-      }
-      s_pre[tid] = x;
-      s_beta[tid] = beta;
-    }
-    __syncthreads();
-    if (tid < kC) s_gam[tid] = s_pre[tid] + (tid >= 32 ? s_pre[31] : 0.f);
-    __syncthreads();
-    if (tid < kC) {
-      const float gl = s_gam[kC - 1];
-      s_g[tid] = expf(s_gam[tid]);
-      s_ratio[tid] = expf(gl - s_gam[tid]);
-      if (tid == 0) s_misc[0] = expf(gl);
-    }
-    GDN_TICK(0);
-
-    // ---- rows of K and Q (thread -> token i, 32-dim quarter qd) and their norms
-    {
-      const int i = tid >> 2;
-      const int qd = tid & 3;
-      const bool valid = i < nvalid;
-      const long long tok = valid ? t0 + i : s0;
-      float f[32];
-      load32(p.k + tok * p.k_stride + kh * kD + qd * 32, valid, f);
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-#pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(at(sKQ, i, qd * 32 + e, kSbo128)) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-      if (qd == 0) s_rk[i] = l2 ? rsqrtf(ss + 1e-6f) : 1.f;
-      load32(p.q + tok * p.q_stride + kh * kD + qd * 32, valid, f);
-      ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) ss += f[e] * f[e];
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-#pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(at(sKQ, kC + i, qd * 32 + e, kSbo128)) =
-            make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-      if (qd == 0) s_rq[i] = l2 ? rsqrtf(ss + 1e-6f) * qscale : 1.f;
-    }
-    __syncthreads();
-    GDN_TICK(1);
-
-    // ---- columns: K^T diag(beta g r_k) and V^T diag(beta), read column-wise
-    //      from global two columns per 4-byte load (threads 0-63: K columns
-    //      2p, 2p+1 for tokens of half th; threads 128-191 likewise for V),
-    //      stored row-wise
-    {
-      const int pr = tid & 63;                   // column pair
-      const int th = (tid >> 6) & 1;             // token half
-      const bool is_k = tid < 128;
-      const int c = 2 * pr;
-      const long long stride = is_k ? p.k_stride : p.v_stride;
-      const __nv_bfloat16* src = (is_k ? p.k + kh * kD : p.v + h * kD) + c + (t0 + th * 32) * stride;
-      unsigned char* dst = is_k ? sKt : sVt;
-      const int nv = nvalid - th * 32;
-      __nv_bfloat162 raw[32];                   // all loads in flight before any use
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * stride) : __floats2bfloat162_rn(0.f, 0.f);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float x0[4], x1[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int jj = th * 32 + j + e;
-          const float sc_ = is_k ? s_beta[jj] * s_g[jj] * s_rk[jj] : s_beta[jj];
-          const float2 f = __bfloat1622float2(raw[j + e]);
-          x0[e] = tc::to_tf32(f.x * sc_);
-          x1[e] = tc::to_tf32(f.y * sc_);
-        }
-        *reinterpret_cast<float4*>(at(dst, c, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-        *reinterpret_cast<float4*>(at(dst, c + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
-      }
-    }
-    ptx::fence_proxy_async_smem();
-    GDN_TICK(2);
-
-    // ---- state operand for this chunk: tR = tf32(R), tDR = g_last * R ---------
-    {
-      const float gl = s_misc[0];
-      for (int c = 0; c < 64; c += 16) {
-        float v[16], r[16];
-        tc::tmem_ld16(tDR + half * 64 + c, v);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          r[i] = tc::to_tf32(v[i]);
-          v[i] *= gl;
-        }
-        tc::tmem_st16(tR + half * 64 + c, r);
-        tc::tmem_st16(tDR + half * 64 + c, v);
-      }
-      tc::tmem_st_wait();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(3);
-
-    // ---- (a)  [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127) --------------------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
-      for (int j = 0; j < kD / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tb + kColGP, desc(sKQ, j * 256, kSbo128), desc(sKQ, j * 256, kSbo128), id, j > 0);
-      tc::mma_commit(bar);
-    }
-    if (!mma_wait()) {
-      failed = true;
-      break;
-    }
-    GDN_TICK(4);
-
-    // ---- A (strictly lower, plain), M (lower), Q rows rescaled by g r_q --------
-    {
-      float gp[32];
-      tmem_ld<32>(tGP + half * 32, gp);
-      if (quarter < 2) {
-        const int i = row;
-        const float fi = s_beta[i] * s_rk[i];
-        const float gi = s_gam[i];
-        float* Ar = sA + i * kPad + half * 32;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = half * 32 + e;
-          Ar[e] = (j < i) ? fi * s_rk[j] * expf(gi - s_gam[j]) * gp[e] : 0.f;
-        }
-      } else {
-        const int i = row - kC;
-        const float fi = s_rq[i];
-        const float gi = s_gam[i];
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          float m[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = half * 32 + e + u;
-            m[u] = (j <= i) ? tc::to_tf32(fi * s_rk[j] * expf(gi - s_gam[j]) * gp[e + u]) : 0.f;
-          }
-          *reinterpret_cast<float4*>(at(sM, i, half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
-        }
-        const float sq = s_g[i] * s_rq[i];
-        for (int c = half * 64; c < half * 64 + 64; c += 4) {
-          float4* qp = reinterpret_cast<float4*>(at(sKQ, kC + i, c, kSbo128));
-          float4 v = *qp;
-          v.x = tc::to_tf32(v.x * sq);
-          v.y = tc::to_tf32(v.y * sq);
-          v.z = tc::to_tf32(v.z * sq);
-          v.w = tc::to_tf32(v.w * sq);
-          *qp = v;
-        }
-      }
-    }
-    __syncthreads();
-    GDN_TICK(5);
-
-    // ---- T^-1 = (I + A)^-1: 16x16 diagonal blocks by substitution, then block
-    //      diagonals X_ij = -X_ii sum_{k=j}^{i-1} A_ik X_kj; plain arrays, row stride 65
-    if (tid < kC) {
-      const int blk = tid >> 4, c = tid & 15;
-      const float* Ab = sA + (blk * 16) * kPad + blk * 16;
-      float col[16];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) col[r] = (r == c) ? 1.f : 0.f;
-#pragma unroll
-      for (int r = 1; r < 16; ++r) {
-        if (r > c) {
-          float s = 0.f;
-#pragma unroll
-          for (int m = 0; m < r; ++m)
-            if (m >= c) s += Ab[r * kPad + m] * col[m];
-          col[r] = -s;
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) sX[(blk * 16 + r) * kPad + blk * 16 + c] = col[r];
-    }
-    __syncthreads();
-    for (int d = 1; d < 4; ++d) {
-      const int nt = 4 - d;
-      for (int e = tid; e < nt * 256; e += kThreads) {
-        const int t = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int bj = t, bi = t + d;
-        const float* Ar = sA + (bi * 16 + r) * kPad;
-        float y = 0.f;
-        for (int kb = bj; kb < bi; ++kb) {
-#pragma unroll
-          for (int m = 0; m < 16; ++m) y += Ar[kb * 16 + m] * sX[(kb * 16 + m) * kPad + bj * 16 + c];
-        }
-        sY[e] = y;
-      }
-      __syncthreads();
-      for (int e = tid; e < nt * 256; e += kThreads) {
-        const int t = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int bj = t, bi = t + d;
-        const float* Xr = sX + (bi * 16 + r) * kPad + bi * 16;
-        float x = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) x += Xr[m] * sY[(t << 8) + (m << 4) + c];
-        sX[(bi * 16 + r) * kPad + bj * 16 + c] = -x;
-      }
-      __syncthreads();
-    }
-    // T^-1 into the operand layout, rounded to tf32, zeros above the diagonal blocks
-    {
-      const int i = tid >> 2;
-      const int c0 = (tid & 3) * 16;
-#pragma unroll
-      for (int c = c0; c < c0 + 16; c += 4) {
-        float x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = ((c + u) >> 4) <= (i >> 4) ? tc::to_tf32(sX[i * kPad + c + u]) : 0.f;
-        *reinterpret_cast<float4*>(at(sTi, i, c, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
-      }
-    }
-    ptx::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(6);
-
-    // ---- (b) U0^T = V^T diag(beta) T^-T;  (c) W = [T^-1; *] (K^T diag(beta g r_k))^T
-    //      (M = 128: rows 64-127 of A read the M buffer and are discarded)
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
-      const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
-      for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tb + kColU, desc(sVt, j * 256, kSbo64), desc(sTi, j * 256, kSbo64), id64, j > 0);
-      for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tb + kColW, desc(sTi, j * 256, kSbo64), desc(sKt, j * 256, kSbo64), id128, j > 0);
-      tc::mma_commit(bar);
-    }
-    if (!mma_wait()) {
-      failed = true;
-      break;
-    }
-    GDN_TICK(7);
-
-    // ---- W rows into the operand buffer (warps on lanes 0-63); K^T rescaled
-    //      by ratio r_k for the state update (warps on lanes 64-127)
-    if (quarter < 2) {
-      float w[64];
-      tmem_ld<64>(tW + half * 64, w);
-      const int i = row;
-#pragma unroll
-      for (int e = 0; e < 64; e += 4)
-        *reinterpret_cast<float4*>(at(sW, i, half * 64 + e, kSbo128)) =
-            make_float4(tc::to_tf32(w[e]), tc::to_tf32(w[e + 1]), tc::to_tf32(w[e + 2]), tc::to_tf32(w[e + 3]));
-    } else {
-      const int lt = (tid & 63) + 64 * half;     // 0..127 over the four warps on lanes 64-127
-      const int pr = lt & 63;
-      const int th = lt >> 6;
-      const int c = 2 * pr;
-      const __nv_bfloat16* src = p.k + kh * kD + c + (t0 + th * 32) * p.k_stride;
-      const int nv = nvalid - th * 32;
-      __nv_bfloat162 raw[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * p.k_stride) : __floats2bfloat162_rn(0.f, 0.f);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float x0[4], x1[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int jj = th * 32 + j + e;
-          const float sc_ = s_ratio[jj] * s_rk[jj];
-          const float2 f = __bfloat1622float2(raw[j + e]);
-          x0[e] = tc::to_tf32(f.x * sc_);
-          x1[e] = tc::to_tf32(f.y * sc_);
-        }
-        *reinterpret_cast<float4*>(at(sKt, c, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-        *reinterpret_cast<float4*>(at(sKt, c + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
-      }
-    }
-    ptx::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(8);
-
-    // ---- (d) U^T = U0^T - R W^T ----------------------------------------------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
-      for (int j = 0; j < kD / 8; ++j) tc::mma_ts_tf32(tb + kColU, tb + kColR + j * 8, desc(sW, j * 256, kSbo128), id, 1);
-      tc::mma_commit(bar);
-    }
-    if (!mma_wait()) {
-      failed = true;
-      break;
-    }
-    GDN_TICK(9);
-
-    // ---- U^T rows into shared memory (the V^T buffer) -------------------------
-    {
-      float u[32];
-      tmem_ld<32>(tU + half * 32, u);
-#pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(at(sVt, row, half * 32 + e, kSbo64)) =
-            make_float4(tc::to_tf32(u[e]), tc::to_tf32(u[e + 1]), tc::to_tf32(u[e + 2]), tc::to_tf32(u[e + 3]));
-    }
-    ptx::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(10);
-
-    // ---- (e) y^T = R Qs^T + U^T M^T,  (f) R += U^T diag(ratio r_k) K ---------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
-      const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
-      for (int j = 0; j < kD / 8; ++j)
-        tc::mma_ts_tf32(tb + kColY, tb + kColR + j * 8, desc(sKQ, 8 * kSbo128 + j * 256, kSbo128), id64, j > 0);
-      for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tb + kColY, desc(sVt, j * 256, kSbo64), desc(sM, j * 256, kSbo64), id64, 1);
-      for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(tb + kColDR, desc(sVt, j * 256, kSbo64), desc(sKt, j * 256, kSbo64), id128, 1);
-      tc::mma_commit(bar);
-    }
-    if (!mma_wait()) {
-      failed = true;
-      break;
-    }
-    GDN_TICK(11);
-
-    // ---- o rows of the chunk: thread -> (dv = row, tokens of its half) --------
-    {
-      float y[32];
-      tmem_ld<32>(tY + half * 32, y);
-      const size_t orow = static_cast<size_t>(p.Hv) * kD;
-      const size_t base = (static_cast<size_t>(t0 + half * 32) * p.Hv + h) * kD + row;
-      const int nv = nvalid - half * 32;
-      if (p.flags & GDN_F_O_BF16) {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nv) o[i * orow] = __float2bfloat16_rn(y[i]);
-      } else {
-        float* o = static_cast<float*>(p.o) + base;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nv) o[i * orow] = y[i];
-      }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(12);
+    const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
+    for (int j = 0; j < kD / 8; ++j)
+      tc::mma_ss<tc::kTF32>(c.tb + kColGP, desc(c.sKQ, j * 256, kSbo128), desc(c.sKQ, j * 256, kSbo128), id, j > 0);
+    tc::mma_commit(c.bar);
   }
+  return mma_wait(c);
+}
 
-  if (failed) {
-    if (tid == 0) atomicExch(p.err, 1);
-    ptx::mbar_wait(bar, phase);      // one more bounded chance for an MMA in flight
-  } else if (p.state_out) {
-    float* dst = p.state_out + (static_cast<size_t>(bh) * kD + row) * kD + half * 64;
-    for (int c = 0; c < 64; c += 16) {
-      float v[16];
-      tc::tmem_ld16(tDR + half * 64 + c, v);
-      tc::tmem_ld_wait();
+// A (strictly lower, plain) for the solve; M (lower) in the operand layout at
+// m_dst (shared memory or a workspace record); optionally the Q rows of
+// [K; Q] rescaled by g r_q for the fused schedule's y product.
+__device__ __forceinline__ void phase_epi_a(Ctx& c, unsigned char* m_dst, bool rescale_q) {
+  float gp[32];
+  tmem_ld<32>(c.tb + kColGP + c.my + c.half * 32, gp);
+  if (c.quarter < 2) {
+    const int i = c.row;
+    const float fi = c.s_beta[i] * c.s_rk[i];
+    const float gi = c.s_gam[i];
+    float* Ar = c.sA + i * kPad + c.half * 32;
 #pragma unroll
-      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    for (int e = 0; e < 32; ++e) {
+      const int j = c.half * 32 + e;
+      Ar[e] = (j < i) ? fi * c.s_rk[j] * __expf(gi - c.s_gam[j]) * gp[e] : 0.f;
     }
+  } else {
+    const int i = c.row - kC;
+    const float fi = c.s_rq[i];
+    const float gi = c.s_gam[i];
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      float m[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = c.half * 32 + e + u;
+        m[u] = (j <= i) ? tc::to_tf32(fi * c.s_rk[j] * __expf(gi - c.s_gam[j]) * gp[e + u]) : 0.f;
+      }
+      *reinterpret_cast<float4*>(at(m_dst, i, c.half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
+    }
+    if (rescale_q) {
+      const float sq = c.s_g[i] * c.s_rq[i];
+      for (int cc = c.half * 64; cc < c.half * 64 + 64; cc += 4) {
+        float4* qp = reinterpret_cast<float4*>(at(c.sKQ, kC + i, cc, kSbo128));
+        float4 v = *qp;
+        v.x = tc::to_tf32(v.x * sq);
+        v.y = tc::to_tf32(v.y * sq);
+        v.z = tc::to_tf32(v.z * sq);
+        v.w = tc::to_tf32(v.w * sq);
+        *qp = v;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// T^-1 = (I + A)^-1: 16x16 diagonal blocks by substitution, then block
+// diagonals X_ij = -X_ii sum_{k=j}^{i-1} A_ik X_kj on plain arrays (row
+// stride 65), finally rounded to tf32 into the operand layout.
+__device__ __forceinline__ void phase_solve(Ctx& c) {
+  float* sA = c.sA;
+  float* sX = c.sX;
+  float* sY = c.sY;
+  if (c.tid < kC) {
+    const int blk = c.tid >> 4, cc = c.tid & 15;
+    const float* Ab = sA + (blk * 16) * kPad + blk * 16;
+    float col[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) col[r] = (r == cc) ? 1.f : 0.f;
+#pragma unroll
+    for (int r = 1; r < 16; ++r) {
+      if (r > cc) {
+        float s = 0.f;
+#pragma unroll
+        for (int m = 0; m < r; ++m)
+          if (m >= cc) s += Ab[r * kPad + m] * col[m];
+        col[r] = -s;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sX[(blk * 16 + r) * kPad + blk * 16 + cc] = col[r];
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int nt = 4 - d;
+    for (int e = c.tid; e < nt * 256; e += kThreads) {
+      const int t = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bj = t, bi = t + d;
+      const float* Ar = sA + (bi * 16 + r) * kPad;
+      float y = 0.f;
+      for (int kb = bj; kb < bi; ++kb) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m) y += Ar[kb * 16 + m] * sX[(kb * 16 + m) * kPad + bj * 16 + cc];
+      }
+      sY[e] = y;
+    }
+    __syncthreads();
+    for (int e = c.tid; e < nt * 256; e += kThreads) {
+      const int t = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bj = t, bi = t + d;
+      const float* Xr = sX + (bi * 16 + r) * kPad + bi * 16;
+      float x = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) x += Xr[m] * sY[(t << 8) + (m << 4) + cc];
+      sX[(bi * 16 + r) * kPad + bj * 16 + cc] = -x;
+    }
+    __syncthreads();
+  }
+  {
+    const int i = c.tid >> 2;
+    const int c0 = (c.tid & 3) * 16;
+#pragma unroll
+    for (int cc = c0; cc < c0 + 16; cc += 4) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = ((cc + u) >> 4) <= (i >> 4) ? tc::to_tf32(sX[i * kPad + cc + u]) : 0.f;
+      *reinterpret_cast<float4*>(at(c.sTi, i, cc, kSbo64)) = make_float4(x[0], x[1], x[2], x[3]);
+    }
+  }
+  ptx::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+}
+
+// (b) U0^T = V^T diag(beta) T^-T;  (c) W = [T^-1; *] (K^T diag(beta g r_k))^T
+// (M = 128: rows 64-127 of A read the next 16 KiB of shared memory and are
+// discarded).
+__device__ __forceinline__ bool phase_mma_bc(Ctx& c) {
+  if (c.tid == 0) {
+    tc::fence_after_sync();
+    const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
+    const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
+    for (int j = 0; j < kC / 8; ++j)
+      tc::mma_ss<tc::kTF32>(c.tb + kColU, desc(c.sVt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id64, j > 0);
+    for (int j = 0; j < kC / 8; ++j)
+      tc::mma_ss<tc::kTF32>(c.tb + kColW, desc(c.sTi, j * 256, kSbo64), desc(c.sKt, j * 256, kSbo64), id128, j > 0);
+    tc::mma_commit(c.bar);
+  }
+  return mma_wait(c);
+}
+
+// W rows (warps on lanes 0-63) into w_dst; K^T diag(ratio r_k) (warps on lanes
+// 64-127) into kh_dst; both in the operand layouts, in shared memory or a
+// workspace record.
+__device__ __forceinline__ void phase_epi_c(const ChunkParams& p, Ctx& c, long long t0, int nvalid,
+                                            unsigned char* w_dst, unsigned char* kh_dst) {
+  if (c.quarter < 2) {
+    float w[64];
+    tmem_ld<64>(c.tb + kColW + c.my + c.half * 64, w);
+    const int i = c.row;
+#pragma unroll
+    for (int e = 0; e < 64; e += 4)
+      *reinterpret_cast<float4*>(at(w_dst, i, c.half * 64 + e, kSbo128)) =
+          make_float4(tc::to_tf32(w[e]), tc::to_tf32(w[e + 1]), tc::to_tf32(w[e + 2]), tc::to_tf32(w[e + 3]));
+  } else {
+    const int lt = (c.tid & 63) + 64 * c.half;     // 0..127 over the four warps on lanes 64-127
+    columns(p, c, t0, nvalid, lt, true, c.s_kh, kh_dst);
+  }
+  ptx::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+}
+
+// ---- state phases --------------------------------------------------------------
+
+// tR = tf32(R), tDR = g_last * R (the state update accumulates onto it).
+__device__ __forceinline__ void phase_r_update(Ctx& c, float gl, uint32_t col_r, uint32_t col_dr) {
+  for (int cc = 0; cc < 64; cc += 16) {
+    float v[16], r[16];
+    tc::tmem_ld16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      r[i] = tc::to_tf32(v[i]);
+      v[i] *= gl;
+    }
+    tc::tmem_st16(c.tb + col_r + c.my + c.half * 64 + cc, r);
+    tc::tmem_st16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+  }
+  tc::tmem_st_wait();
+}
+
+// U^T (TMEM) -> rows of the U^T operand in shared memory.
+__device__ __forceinline__ void phase_epi_d(Ctx& c, uint32_t col_u, unsigned char* ut) {
+  float u[32];
+  tmem_ld<32>(c.tb + col_u + c.my + c.half * 32, u);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4)
+    *reinterpret_cast<float4*>(at(ut, c.row, c.half * 32 + e, kSbo64)) =
+        make_float4(tc::to_tf32(u[e]), tc::to_tf32(u[e + 1]), tc::to_tf32(u[e + 2]), tc::to_tf32(u[e + 3]));
+  ptx::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+}
+
+// y^T (TMEM) -> o rows of the chunk: thread -> (dv = row, tokens of its half).
+__device__ __forceinline__ void phase_epi_e(const ChunkParams& p, Ctx& c, uint32_t col_y, long long t0, int nvalid) {
+  float y[32];
+  tmem_ld<32>(c.tb + col_y + c.my + c.half * 32, y);
+  const size_t orow = static_cast<size_t>(p.Hv) * kD;
+  const size_t base = (static_cast<size_t>(t0 + c.half * 32) * p.Hv + c.h) * kD + c.row;
+  const int nv = nvalid - c.half * 32;
+  if (p.flags & GDN_F_O_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < nv) o[i * orow] = __float2bfloat16_rn(y[i]);
+  } else {
+    float* o = static_cast<float*>(p.o) + base;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < nv) o[i * orow] = y[i];
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tb, kTmemCols);
 }
 
-}  // namespace
-}  // namespace gdn
+// Initial state row dv = row (columns of this warp's half) into the fp32 master.
+__device__ __forceinline__ void state_load(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr) {
+  const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + c.row) * kD + c.half * 64 : nullptr;
+  for (int cc = 0; cc < 64; cc += 16) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 f = src ? *reinterpret_cast<const float4*>(src + cc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+    }
+    tc::tmem_st16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+  }
+  tc::tmem_st_wait();
+}
 
-using namespace gdn;
+__device__ __forceinline__ void state_store(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr) {
+  if (!p.state_out) return;
+  float* dst = p.state_out + (static_cast<size_t>(bh) * kD + c.row) * kD + c.half * 64;
+  for (int cc = 0; cc < 64; cc += 16) {
+    float v[16];
+    tc::tmem_ld16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; i += 4)
+      *reinterpret_cast<float4*>(dst + cc + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  }
+}
 
-extern "C" int gdn_chunked_fwd(const void* q, const void* k, const void* v, long long q_stride, long long k_stride,
-                               long long v_stride, const float* a, const float* b, const float* A_log,
-                               const float* dt_bias, const float* state_in, float* state_out, void* o,
-                               const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
-                               unsigned flags, void* stream) {
-  clear_error();
+// ---- the fused schedule -----------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams p) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const int bh = blockIdx.x;
+  const int b = bh / p.Hv;
+  Ctx c;
+  ctx_init(c, p, sm, bh - b * p.Hv);
+  long long s0, s1;
+  seq_range(p, b, s0, s1);
+  const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1);
+  state_load(p, c, bh, kColDR);
+
+  bool failed = false;
+  for (int ch = 0; ch < n_chunks; ++ch) {
+    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    phase_gates(p, c, t0, nvalid);
+    GDN_TICK(0);
+    phase_rows(p, c, t0, s0, nvalid);
+    GDN_TICK(1);
+    phase_cols(p, c, t0, nvalid);
+    GDN_TICK(2);
+    phase_r_update(c, c.s_misc[0], kColR, kColDR);
+    tc::fence_before_sync();
+    __syncthreads();
+    GDN_TICK(3);
+    if (!phase_mma_a(c)) { failed = true; break; }
+    GDN_TICK(4);
+    phase_epi_a(c, c.sM, /*rescale_q=*/true);
+    GDN_TICK(5);
+    phase_solve(c);
+    GDN_TICK(6);
+    if (!phase_mma_bc(c)) { failed = true; break; }
+    GDN_TICK(7);
+    phase_epi_c(p, c, t0, nvalid, c.sW, c.sKt);
+    GDN_TICK(8);
+    // (d) U^T = U0^T - R W^T
+    if (c.tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
+      for (int j = 0; j < kD / 8; ++j)
+        tc::mma_ts_tf32(c.tb + kColU, c.tb + kColR + j * 8, desc(c.sW, j * 256, kSbo128), id, 1);
+      tc::mma_commit(c.bar);
+    }
+    if (!mma_wait(c)) { failed = true; break; }
+    GDN_TICK(9);
+    phase_epi_d(c, kColU, c.sVt);
+    GDN_TICK(10);
+    // (e) y^T = R Qs^T + U^T M^T,  (f) R += U^T diag(ratio r_k) K
+    if (c.tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
+      const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
+      for (int j = 0; j < kD / 8; ++j)
+        tc::mma_ts_tf32(c.tb + kColY, c.tb + kColR + j * 8, desc(c.sKQ, 8 * kSbo128 + j * 256, kSbo128), id64, j > 0);
+      for (int j = 0; j < kC / 8; ++j)
+        tc::mma_ss<tc::kTF32>(c.tb + kColY, desc(c.sVt, j * 256, kSbo64), desc(c.sM, j * 256, kSbo64), id64, 1);
+      for (int j = 0; j < kC / 8; ++j)
+        tc::mma_ss<tc::kTF32>(c.tb + kColDR, desc(c.sVt, j * 256, kSbo64), desc(c.sKt, j * 256, kSbo64), id128, 1);
+      tc::mma_commit(c.bar);
+    }
+    if (!mma_wait(c)) { failed = true; break; }
+    GDN_TICK(11);
+    phase_epi_e(p, c, kColY, t0, nvalid);
+    GDN_TICK(12);
+  }
+  if (failed) {
+    if (c.tid == 0) atomicExch(p.err, 1);
+    ptx::mbar_wait(c.bar, c.phase);      // one more bounded chance for an MMA in flight
+  } else {
+    state_store(p, c, bh, kColDR);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
+}
+
+// ---- the split schedule: prep (parallel over chunks) -------------------------------
+
+// Record of (slot, value head) in the workspace (256-byte aligned).
+__device__ __forceinline__ unsigned char* record(const ChunkParams& p, long long slot, int h) {
+  return p.ws + records_offset(p.B) + (static_cast<size_t>(slot) * p.Hv + h) * kRecBytes;
+}
+
+// Sequence and chunk of a record slot; false for an unused slot.
+__device__ __forceinline__ bool slot_to_chunk(const ChunkParams& p, long long slot, int& b, int& ch) {
+  if (!p.cu) {
+    b = static_cast<int>(slot / p.nch_uniform);
+    ch = static_cast<int>(slot - static_cast<long long>(b) * p.nch_uniform);
+    return b < p.B;
+  }
+  if (slot >= p.chunk_prefix[p.B]) return false;
+  int lo = 0, hi = p.B - 1;                 // last sequence whose first slot is <= slot
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.chunk_prefix[mid] <= slot) lo = mid;
+    else hi = mid - 1;
+  }
+  b = lo;
+  ch = static_cast<int>(slot - p.chunk_prefix[lo]);
+  return true;
+}
+
+// First record slot of sequence b.
+__device__ __forceinline__ long long seq_first_slot(const ChunkParams& p, int b) {
+  return p.cu ? static_cast<long long>(p.chunk_prefix[b]) : static_cast<long long>(b) * p.nch_uniform;
+}
+
+// prefix[b] = number of 64-token chunks of packed sequences 0 .. b-1 (one block).
+__global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, int B, int32_t* prefix) {
+  __shared__ int32_t carry;
+  __shared__ int32_t buf[1024];
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < B; base += 1024) {
+    const int b = base + threadIdx.x;
+    int32_t n = 0;
+    if (b < B) {
+      const int32_t len = cu[b + 1] - cu[b];
+      n = len > 0 ? (len + kC - 1) / kC : 0;
+    }
+    buf[threadIdx.x] = n;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {       // inclusive scan
+      const int32_t add = threadIdx.x >= off ? buf[threadIdx.x - off] : 0;
+      __syncthreads();
+      buf[threadIdx.x] += add;
+      __syncthreads();
+    }
+    if (b < B) prefix[b] = carry + buf[threadIdx.x] - n;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += buf[1023];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) prefix[B] = carry;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) chunk_prep_kernel(const ChunkParams p) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const long long slot = blockIdx.x;
+  int* s_bc = reinterpret_cast<int*>(sm + kOffBar + 16);
+  if (threadIdx.x == 0) {
+    int b = 0, ch = 0;
+    const bool used = slot_to_chunk(p, slot, b, ch);
+    s_bc[0] = used ? b : -1;
+    s_bc[1] = ch;
+  }
+  __syncthreads();
+  const int b = s_bc[0];
+  if (b < 0) return;
+  const int ch = s_bc[1];
+  Ctx c;
+  ctx_init(c, p, sm, blockIdx.y);
+  long long s0, s1;
+  seq_range(p, b, s0, s1);
+  const long long t0 = s0 + static_cast<long long>(ch) * kC;
+  const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+  unsigned char* rec = record(p, slot, c.h);
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1);
+
+  phase_gates(p, c, t0, nvalid);
+  phase_rows(p, c, t0, s0, nvalid);
+  phase_cols(p, c, t0, nvalid);
+  tc::fence_before_sync();
+  __syncthreads();
+  bool ok = phase_mma_a(c);
+  if (ok) {
+    phase_epi_a(c, rec + kRecM, /*rescale_q=*/false);
+    phase_solve(c);
+    ok = phase_mma_bc(c);
+  }
+  if (ok) {
+    // U0^T rows (plain) and the per-token factors the scan kernel needs
+    float u[32];
+    tmem_ld<32>(c.tb + kColU + c.my + c.half * 32, u);
+    float* ud = reinterpret_cast<float*>(rec + kRecU) + c.row * kC + c.half * 32;
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(ud + e) = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+    float* sc = reinterpret_cast<float*>(rec + kRecSc);
+    if (c.tid < kC) sc[c.tid] = c.s_g[c.tid] * c.s_rq[c.tid];
+    if (c.tid == 0) sc[kC] = c.s_misc[0];
+    phase_epi_c(p, c, t0, nvalid, rec + kRecW, rec + kRecKh);
+  } else {
+    if (c.tid == 0) atomicExch(p.err, 1);
+    ptx::mbar_wait(c.bar, c.phase);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
+}
+
+// ---- the split schedule: scan (serial over chunks, per sequence and head) ---------
+
+__global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkParams p) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  unsigned char* sW = sm + kScanW;
+  unsigned char* sKh = sm + kScanKh;
+  unsigned char* sMm = sm + kScanM;
+  unsigned char* sQ = sm + kScanQ;
+  unsigned char* sU = sm + kScanU;
+  float* s_gq = reinterpret_cast<float*>(sm + kScanSc);          // [0,64) g r_q, [64] g_last
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);   // [0] MMA, [1] W, [2] K-hat + M
+  const int bh = blockIdx.x;
+  const int b = bh / p.Hv;
+  Ctx c;
+  ctx_init(c, p, sm, bh - b * p.Hv);
+  c.bar = bars;
+  long long s0, s1;
+  seq_range(p, b, s0, s1);
+  const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
+  const long long slot0 = seq_first_slot(p, b);
+  // TMEM: R tf32 [0,128), R fp32 [128,256), U^T [256,320), y^T [320,384)
+  constexpr uint32_t cR = 0, cDR = 128, cU = 256, cY = 320;
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 3);
+  state_load(p, c, bh, cDR);
+
+  auto load_w = [&](int ch) {           // thread 0: W of chunk ch (bulk copies)
+    const unsigned char* rec = record(p, slot0 + ch, c.h);
+    ptx::mbar_arrive_expect_tx(&bars[1], kC * kD * 4);
+    for (uint32_t off = 0; off < kC * kD * 4; off += 16384) ptx::bulk_g2s(sW + off, rec + kRecW + off, 16384, &bars[1]);
+  };
+  auto load_kh_m = [&](int ch) {        // thread 0: K-hat^T and M of chunk ch
+    const unsigned char* rec = record(p, slot0 + ch, c.h);
+    ptx::mbar_arrive_expect_tx(&bars[2], kD * kC * 4 + kC * kC * 4);
+    for (uint32_t off = 0; off < kD * kC * 4; off += 16384)
+      ptx::bulk_g2s(sKh + off, rec + kRecKh + off, 16384, &bars[2]);
+    ptx::bulk_g2s(sMm, rec + kRecM, kC * kC * 4, &bars[2]);
+  };
+  // W and K-hat/M loads issued and waited for (counted by every thread, the
+  // waits by warp 0 only: their difference is what a failed exit waits for)
+  int w_issued = 0, w_done = 0, k_issued = 0, k_done = 0;
+  if (n_chunks > 0) {
+    if (c.tid == 0) {
+      load_w(0);
+      load_kh_m(0);
+    }
+    w_issued = k_issued = 1;
+  }
+
+  bool failed = false;
+  for (int ch = 0; ch < n_chunks; ++ch) {
+    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    const unsigned char* rec = record(p, slot0 + ch, c.h);
+    // per-token factors; U0^T into TMEM as the accumulator of U^T
+    if (c.tid <= kC) s_gq[c.tid] = reinterpret_cast<const float*>(rec + kRecSc)[c.tid];
+    {
+      const float* ur = reinterpret_cast<const float*>(rec + kRecU) + c.row * kC + c.half * 32;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float u[16];
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) {
+          const float4 f = *reinterpret_cast<const float4*>(ur + h2 * 16 + e);
+          u[e] = f.x; u[e + 1] = f.y; u[e + 2] = f.z; u[e + 3] = f.w;
+        }
+        tc::tmem_st16(c.tb + cU + c.my + c.half * 32 + h2 * 16, u);
+      }
+      tc::tmem_st_wait();
+    }
+    __syncthreads();
+    // Qs = diag(g r_q) Q rows (thread -> token i, 32-dim quarter)
+    {
+      const int i = c.tid >> 2;
+      const int qd = c.tid & 3;
+      const bool valid = i < nvalid;
+      float f[32];
+      load32(p.q + (valid ? t0 + i : s0) * p.q_stride + c.kh * kD + qd * 32, valid, f);
+      const float sq = s_gq[i];
+#pragma unroll
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(at(sQ, i, qd * 32 + e, kSbo128)) =
+            make_float4(tc::to_tf32(f[e] * sq), tc::to_tf32(f[e + 1] * sq), tc::to_tf32(f[e + 2] * sq),
+                        tc::to_tf32(f[e + 3] * sq));
+    }
+    ptx::fence_proxy_async_smem();
+    phase_r_update(c, s_gq[kC], cR, cDR);
+    tc::fence_before_sync();
+    __syncthreads();
+    // (d) U^T = U0^T - R W^T and (e1) y^T = R Qs^T, once W has landed
+    bool landed = true;
+    if (c.warp == 0) {
+      landed = ptx::mbar_wait(&bars[1], ch & 1);
+      w_done += landed;
+      if (c.lane == 0) {
+        if (landed) {
+          tc::fence_after_sync();
+          const uint32_t idd = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
+          const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
+          for (int j = 0; j < kD / 8; ++j)
+            tc::mma_ts_tf32(c.tb + cU, c.tb + cR + j * 8, desc(sW, j * 256, kSbo128), idd, 1);
+          for (int j = 0; j < kD / 8; ++j)
+            tc::mma_ts_tf32(c.tb + cY, c.tb + cR + j * 8, desc(sQ, j * 256, kSbo128), id64, j > 0);
+        }
+        tc::mma_commit(c.bar);       // with no MMA issued it arrives at once
+      }
+    }
+    if (!mma_wait(c, landed)) { failed = true; break; }
+    if (ch + 1 < n_chunks) {
+      if (c.tid == 0) load_w(ch + 1);
+      ++w_issued;
+    }
+    phase_epi_d(c, cU, sU);
+    // (e2) y^T += U^T M^T,  (f) R += U^T K-hat
+    landed = true;
+    if (c.warp == 0) {
+      landed = ptx::mbar_wait(&bars[2], ch & 1);
+      k_done += landed;
+      if (c.lane == 0) {
+        if (landed) {
+          tc::fence_after_sync();
+          const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
+          const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
+          for (int j = 0; j < kC / 8; ++j)
+            tc::mma_ss<tc::kTF32>(c.tb + cY, desc(sU, j * 256, kSbo64), desc(sMm, j * 256, kSbo64), id64, 1);
+          for (int j = 0; j < kC / 8; ++j)
+            tc::mma_ss<tc::kTF32>(c.tb + cDR, desc(sU, j * 256, kSbo64), desc(sKh, j * 256, kSbo64), id128, 1);
+        }
+        tc::mma_commit(c.bar);
+      }
+    }
+    if (!mma_wait(c, landed)) { failed = true; break; }
+    if (ch + 1 < n_chunks) {
+      if (c.tid == 0) load_kh_m(ch + 1);
+      ++k_issued;
+    }
+    phase_epi_e(p, c, cY, t0, nvalid);
+  }
+  if (failed) {
+    // bounded waits for the MMA and the bulk copies still in flight
+    if (c.tid == 0) atomicExch(p.err, 1);
+    if (c.warp == 0) {
+      ptx::mbar_wait(c.bar, c.phase);
+      if (w_issued > w_done) ptx::mbar_wait(&bars[1], w_done & 1);
+      if (k_issued > k_done) ptx::mbar_wait(&bars[2], k_done & 1);
+    }
+  } else {
+    state_store(p, c, bh, cDR);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
+}
+
+// ---- host side ----------------------------------------------------------------
+
+int set_smem_attr(const void* fn, uint32_t bytes, bool (&done)[64]) {
+  static std::mutex mu;
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != GDN_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev & 63]) {
+    rc = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+                     "chunked kernel smem attribute");
+    if (rc != GDN_OK) return rc;
+    done[dev & 63] = true;
+  }
+  return GDN_OK;
+}
+
+// Argument checks shared by the chunked entry points; fills p without the
+// workspace fields.
+int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, long long q_stride, long long k_stride,
+                 long long v_stride, const float* a, const float* b, const float* A_log, const float* dt_bias,
+                 const float* state_in, float* state_out, void* o, const int32_t* cu_seqlens, int B, int T, int Hk,
+                 int Hv, int Dk, int Dv, unsigned flags) {
   if (flags & ~(GDN_F_O_BF16 | GDN_F_QK_L2NORM)) return fail(GDN_ERR_FLAGS, "unknown flag bits 0x%x", flags);
   if (B < 0 || T < 0 || Hk <= 0 || Hv <= 0) return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d Hk=%d Hv=%d", B, T, Hk, Hv);
   if (Dk != kD || Dv != kD) return fail(GDN_ERR_SHAPE, "Dk=%d Dv=%d: only 128x128 heads are built", Dk, Dv);
   if (Hv % Hk) return fail(GDN_ERR_SHAPE, "Hv=%d is not a multiple of Hk=%d", Hv, Hk);
   if (static_cast<long long>(B) * Hv >= (1LL << 31)) return fail(GDN_ERR_SHAPE, "B*Hv too large");
-  if (B == 0) return GDN_OK;
   const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
-  if (total > 0 && (!q || !k || !v || !a || !b || !o)) return fail(GDN_ERR_NULL, "q, k, v, a, b and o are required");
-  if (!A_log || !dt_bias) return fail(GDN_ERR_NULL, "A_log and dt_bias are required");
+  if (B > 0 && total > 0 && (!q || !k || !v || !a || !b || !o))
+    return fail(GDN_ERR_NULL, "q, k, v, a, b and o are required");
+  if (B > 0 && (!A_log || !dt_bias)) return fail(GDN_ERR_NULL, "A_log and dt_bias are required");
   if (q_stride < static_cast<long long>(Hk) * kD || k_stride < static_cast<long long>(Hk) * kD ||
       v_stride < static_cast<long long>(Hv) * kD)
     return fail(GDN_ERR_SHAPE, "token strides too small for the heads");
@@ -656,26 +1021,101 @@ extern "C" int gdn_chunked_fwd(const void* q, const void* k, const void* v, long
   int* err = nullptr;
   int rc = device_error_ptr(&err);
   if (rc != GDN_OK) return rc;
-  {
-    static bool attr_set[64] = {false};
-    static std::mutex mu;
-    int dev = 0;
-    rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+  p = ChunkParams{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                  static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
+                  state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err,
+                  nullptr, nullptr, 0, 0};
+  return GDN_OK;
+}
+
+// Record slots for (B, T): exact for uniform batches, an upper bound (one
+// partial chunk per sequence) for packed ones.
+long long chunk_slots(int B, int T, bool packed) {
+  return packed ? (static_cast<long long>(T) + kC - 1) / kC + B
+                : static_cast<long long>(B) * ((static_cast<long long>(T) + kC - 1) / kC);
+}
+
+size_t workspace_bytes(int B, int T, int Hv, bool packed) {
+  return records_offset(B) + static_cast<size_t>(chunk_slots(B, T, packed)) * Hv * kRecBytes;
+}
+
+// Launch the split schedule on a workspace of at least workspace_bytes().
+int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
+  const bool packed = p.cu != nullptr;
+  p.ws = ws;
+  p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
+  p.nch_uniform = packed ? 0 : (p.T + kC - 1) / kC;
+  static bool attr_prep[64] = {false}, attr_scan[64] = {false};
+  int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kSmemBytes, attr_prep);
+  if (rc != GDN_OK) return rc;
+  rc = set_smem_attr(reinterpret_cast<const void*>(chunk_scan_kernel), kScanSmem, attr_scan);
+  if (rc != GDN_OK) return rc;
+  if (packed) {
+    chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.chunk_prefix);
+    rc = cuda_status(cudaGetLastError(), "chunk prefix launch");
     if (rc != GDN_OK) return rc;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!attr_set[dev & 63]) {
-      rc = cuda_status(cudaFuncSetAttribute(chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(kSmemBytes)),
-                       "chunked kernel smem attribute");
-      if (rc != GDN_OK) return rc;
-      attr_set[dev & 63] = true;
-    }
   }
-  ChunkParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
-                state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err};
+  if (p.n_slots > 0) {
+    chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kSmemBytes,
+                        st>>>(p);
+    rc = cuda_status(cudaGetLastError(), "chunk prep launch");
+    if (rc != GDN_OK) return rc;
+  }
+  chunk_scan_kernel<<<static_cast<unsigned>(p.B * p.Hv), kThreads, kScanSmem, st>>>(p);
+  return cuda_status(cudaGetLastError(), "chunk scan launch");
+}
+
+}  // namespace
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_chunked_fwd(const void* q, const void* k, const void* v, long long q_stride, long long k_stride,
+                               long long v_stride, const float* a, const float* b, const float* A_log,
+                               const float* dt_bias, const float* state_in, float* state_out, void* o,
+                               const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                               unsigned flags, void* stream) {
+  clear_error();
+  ChunkParams p;
+  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, o,
+                        cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags);
+  if (rc != GDN_OK || B == 0) return rc;
+  static bool attr[64] = {false};
+  rc = set_smem_attr(reinterpret_cast<const void*>(chunked_kernel), kSmemBytes, attr);
+  if (rc != GDN_OK) return rc;
   chunked_kernel<<<static_cast<unsigned>(B * Hv), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_status(cudaGetLastError(), "chunked kernel launch");
+}
+
+extern "C" size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed) {
+  if (B < 0 || T < 0 || Hv <= 0) return 0;
+  return workspace_bytes(B, T, Hv, packed != 0);
+}
+
+extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
+                                  long long k_stride, long long v_stride, const float* a, const float* b,
+                                  const float* A_log, const float* dt_bias, const float* state_in,
+                                  float* state_out, void* o, const int32_t* cu_seqlens, int B, int T, int Hk,
+                                  int Hv, int Dk, int Dv, unsigned flags, void* workspace,
+                                  size_t workspace_size, void* stream) {
+  clear_error();
+  ChunkParams p;
+  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, o,
+                        cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags);
+  if (rc != GDN_OK || B == 0) return rc;
+  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
+  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes)", need);
+  if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");
+  if (workspace_size < need) return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, %zu needed", workspace_size, need);
+  const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * 4;
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  const size_t obytes = static_cast<size_t>(total) * Hv * kD * ((flags & GDN_F_O_BF16) ? 2 : 4);
+  if (overlap(workspace, need, state_in, sbytes) || overlap(workspace, need, state_out, sbytes) ||
+      overlap(workspace, need, o, obytes))
+    return fail(GDN_ERR_ALIAS, "workspace overlaps a state or o");
+  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
+  if (p.n_slots > 0x7fffffffLL || Hv > 65535) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+  return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 #ifdef GDN_CHUNK_TIMING

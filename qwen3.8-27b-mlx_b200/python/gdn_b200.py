@@ -54,9 +54,15 @@ SIGNATURES = {
     "gdn_tc05_selftest": [_vp] * 3 + [_i] * 3 + [_vp, _vp],
     "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
+    "gdn_chunked_workspace_bytes": [_i] * 4,
+    "gdn_chunked_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6
+                          + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_conv_commit": [_vp] * 5 + [_i] * 4 + [_vp],
     "gdn_gated_rmsnorm_fwd": [_vp] * 4 + [ctypes.c_longlong, _i, ctypes.c_float, _u, _vp],
 }
+
+# return types other than int
+RESTYPES = {"gdn_last_error": ctypes.c_char_p, "gdn_chunked_workspace_bytes": ctypes.c_size_t}
 
 _lib = None
 
@@ -77,7 +83,7 @@ def lib():
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_char_p if name == "gdn_last_error" else ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = L
     return _lib
 
@@ -237,11 +243,19 @@ def gated_rmsnorm_fwd(o, z, gamma, out=None, eps=1e-6, out_dtype=torch.bfloat16)
     return out
 
 
+def chunked_workspace_bytes(B, T, Hv, packed=False) -> int:
+    """Workspace bytes gdn_chunked_fwd_ws needs (gdn_chunked_workspace_bytes)."""
+    return int(lib().gdn_chunked_workspace_bytes(B, T, Hv, 1 if packed else 0))
+
+
 def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=None, cu_seqlens=None, *,
-                l2norm=True, o_dtype=torch.float32, B=None, T=None):
-    """Chunked prefill (gdn_chunked_fwd).  q, k: (..., Hk, 128) bf16 views of
-    token-major rows (any token stride); v: (..., Hv, 128).  Leading dims are
-    (B, T) or, with cu_seqlens, (total,).  Returns (o, state_out)."""
+                l2norm=True, o_dtype=torch.float32, B=None, T=None, split=False, workspace=None):
+    """Chunked prefill.  q, k: (..., Hk, 128) bf16 views of token-major rows
+    (any token stride); v: (..., Hv, 128).  Leading dims are (B, T) or, with
+    cu_seqlens, (total,).  split=False runs gdn_chunked_fwd (one launch, no
+    scratch); split=True runs gdn_chunked_fwd_ws on `workspace` (a uint8 CUDA
+    tensor of at least chunked_workspace_bytes(...) bytes, allocated here
+    when None).  Returns (o, state_out)."""
     Hk, Hv = q.shape[-2], v.shape[-2]
     for t in (q, k, v):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
@@ -262,7 +276,17 @@ def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=
     if state_out is None:
         state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
     flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0)
-    check(lib().gdn_chunked_fwd(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
-                                ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,
-                                flags, stream_ptr(dev)))
+    if not split:
+        check(lib().gdn_chunked_fwd(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                    ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,
+                                    flags, stream_ptr(dev)))
+        return o, state_out
+    need = chunked_workspace_bytes(B, T, Hv, cu_seqlens is not None)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    elif workspace.dtype != torch.uint8 or not workspace.is_contiguous():
+        raise ValueError("workspace must be a contiguous uint8 tensor")
+    check(lib().gdn_chunked_fwd_ws(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                   ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,
+                                   flags, ptr(workspace), workspace.numel(), stream_ptr(dev)))
     return o, state_out

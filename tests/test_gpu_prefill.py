@@ -151,36 +151,42 @@ def oracle_chunked(inp, sl=slice(None)):
     return O.chunked_delta(O.expand_heads(q, Hv), O.expand_heads(k, Hv), inp["v"][sl], al, bt, S0)
 
 
-def run_chunked(inp, cu=None, o_dtype=torch.float32):
+def run_chunked(inp, cu=None, o_dtype=torch.float32, split=False):
     t = lambda n: dev(inp[n], torch.bfloat16)  # noqa: E731
     S0 = None if inp["S0"] is None else dev(inp["S0"])
     return G.chunked_fwd(t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]),
-                         dev(inp["dt_bias"]), state_in=S0, cu_seqlens=cu, o_dtype=o_dtype)
+                         dev(inp["dt_bias"]), state_in=S0, cu_seqlens=cu, o_dtype=o_dtype, split=split)
 
 
+SCHEDULES = [pytest.param(False, id="fused"), pytest.param(True, id="split")]
+
+
+@pytest.mark.parametrize("split", SCHEDULES)
 @pytest.mark.parametrize("T", [1, 63, 64, 65, 130, 200, 300])
 @pytest.mark.parametrize("slow", [False, True])
-def test_chunked_vs_oracle(T, slow):
+def test_chunked_vs_oracle(T, slow, split):
     rng = np.random.default_rng(40 + T + (1000 if slow else 0))
     inp = chunk_inputs(rng, 1, T, 2, 6, slow_decay=slow)
-    o, S = run_chunked(inp)
+    o, S = run_chunked(inp, split=split)
     ro, rS = oracle_chunked(inp)
     assert O.rel_l2(host(o), ro) < PREFILL_TOL, O.rel_l2(host(o), ro)
     assert O.rel_l2(host(S), rS) < PREFILL_TOL, O.rel_l2(host(S), rS)
     assert G.take_device_error() == 0
 
 
-def test_chunked_zero_state_batch_and_bf16_out():
+@pytest.mark.parametrize("split", SCHEDULES)
+def test_chunked_zero_state_batch_and_bf16_out(split):
     rng = np.random.default_rng(50)
     inp = chunk_inputs(rng, 3, 97, 1, 3, slow_decay=True, state=False)
-    o, S = run_chunked(inp, o_dtype=torch.bfloat16)
+    o, S = run_chunked(inp, o_dtype=torch.bfloat16, split=split)
     ro, rS = oracle_chunked(inp)
     assert o.dtype == torch.bfloat16
     assert O.rel_l2(host(o), ro) < PREFILL_TOL + 2e-3
     assert O.rel_l2(host(S), rS) < PREFILL_TOL
 
 
-def test_chunked_varlen_packed():
+@pytest.mark.parametrize("split", SCHEDULES)
+def test_chunked_varlen_packed(split):
     rng = np.random.default_rng(51)
     lens = [100, 0, 257, 64, 3]
     Hk, Hv = 2, 6
@@ -190,7 +196,7 @@ def test_chunked_varlen_packed():
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
     o, S = G.chunked_fwd(t("q"), t("k"), t("v"), dev(inp["a"][0]), dev(inp["b"][0]), dev(inp["A_log"]),
-                         dev(inp["dt_bias"]), state_in=dev(S0), cu_seqlens=dev(cu, torch.int32))
+                         dev(inp["dt_bias"]), state_in=dev(S0), cu_seqlens=dev(cu, torch.int32), split=split)
     oh, Sh = host(o), host(S)
     for s, L in enumerate(lens):
         sub = dict(inp)
@@ -203,6 +209,45 @@ def test_chunked_varlen_packed():
         ro, rS = oracle_chunked(sub)
         assert O.rel_l2(oh[cu[s]:cu[s + 1]], ro[0]) < PREFILL_TOL, s
         assert O.rel_l2(Sh[s:s + 1], rS) < PREFILL_TOL, s
+
+
+@pytest.mark.parametrize("lens", [[300], [130, 130, 130], [100, 0, 257, 64, 3, 1, 640]])
+def test_split_schedule_is_bit_identical_to_fused(lens):
+    """The split schedule runs the same products in the same order on the same
+    tf32 operands as the fused kernel, so o and the state agree bit for bit;
+    a second call on the same (reused, unzeroed) workspace does too."""
+    rng = np.random.default_rng(60 + len(lens))
+    total = sum(lens)
+    inp = chunk_inputs(rng, 1, total, 2, 6, slow_decay=False)
+    S0 = dev(rng.standard_normal((len(lens), 6, 128, 128), dtype=np.float32) * np.float32(0.05))
+    cu = None if len(lens) == 1 else dev(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), torch.int32)
+    t = lambda n: dev(inp[n][0], torch.bfloat16) if cu is not None else dev(inp[n], torch.bfloat16)  # noqa: E731
+    g = lambda n: dev(inp[n][0]) if cu is not None else dev(inp[n])  # noqa: E731
+    args = (t("q"), t("k"), t("v"), g("a"), g("b"), dev(inp["A_log"]), dev(inp["dt_bias"]))
+    o_f, S_f = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu)
+    need = G.chunked_workspace_bytes(len(lens), total if cu is not None else lens[0], 6, cu is not None)
+    ws = torch.full((need,), 0xAB, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        o_s, S_s = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
+        assert torch.equal(o_s, o_f)
+        assert torch.equal(S_s, S_f)
+    assert G.take_device_error() == 0
+
+
+def test_split_schedule_rejects_a_short_or_misaligned_workspace():
+    rng = np.random.default_rng(61)
+    inp = chunk_inputs(rng, 1, 130, 2, 6)
+    t = lambda n: dev(inp[n], torch.bfloat16)  # noqa: E731
+    args = (t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]), dev(inp["dt_bias"]))
+    need = G.chunked_workspace_bytes(1, 130, 6)
+    assert need == G.chunked_workspace_bytes(1, 129, 6) > 0
+    ws = torch.empty(need + 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(G.GdnError) as e:
+        G.chunked_fwd(*args, split=True, workspace=ws[:need - 1])
+    assert e.value.code == G.GDN_ERR_SHAPE
+    with pytest.raises(G.GdnError) as e:
+        G.chunked_fwd(*args, split=True, workspace=ws[16:16 + need])
+    assert e.value.code == G.GDN_ERR_ALIGN
 
 
 def test_chunked_matches_decode_kernel_run_token_by_token():
@@ -218,7 +263,8 @@ def test_chunked_matches_decode_kernel_run_token_by_token():
     assert O.rel_l2(host(S_c), host(S_d)) < PREFILL_TOL
 
 
-def test_config3_pipeline_conv_chunked_norm():
+@pytest.mark.parametrize("split", SCHEDULES)
+def test_config3_pipeline_conv_chunked_norm(split):
     """B=1, T=4096, conv over 10240 channels -> chunked
     recurrence (16 K / 48 V heads, zero start state) -> gated RMSNorm."""
     T = 4096
@@ -236,7 +282,7 @@ def test_config3_pipeline_conv_chunked_norm():
     q = y[..., :2048].view(1, T, 16, 128)
     k = y[..., 2048:4096].view(1, T, 16, 128)
     v = y[..., 4096:].view(1, T, 48, 128)
-    o, S = G.chunked_fwd(q, k, v, dev(a), dev(b), dev(A_log), dev(dt))
+    o, S = G.chunked_fwd(q, k, v, dev(a), dev(b), dev(A_log), dev(dt), split=split)
     out = G.gated_rmsnorm_fwd(o, dev(z, torch.bfloat16), dev(gamma), out_dtype=torch.float32)
 
     yo, _ = O.depthwise_conv(x, w)
