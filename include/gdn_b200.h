@@ -188,6 +188,34 @@ int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
                        const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
                        unsigned flags, void* workspace, size_t workspace_size, void* stream);
 
+/* Size of the fixed device scratch that gdn_chunked_fwd_static uses. */
+#define GDN_CHUNKED_STATIC_SCRATCH_BYTES (64ull << 20)
+
+/*
+ * gdn_chunked_fwd_static -- gdn_chunked_fwd_ws without a caller workspace:
+ * the same two launches and results, with the scratch in a fixed 64 MiB
+ * device array of the library (GDN_CHUNKED_STATIC_SCRATCH_BYTES), so the call
+ * allocates no memory.  No counterpart in the reference; it serves callers
+ * that cannot allocate device memory at call time.
+ *   Arguments, flags and results as gdn_chunked_fwd.
+ *   Limit: gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) must not
+ *   exceed GDN_CHUNKED_STATIC_SCRATCH_BYTES (about 580 (64-token chunk, value
+ *   head) pairs, e.g. 768 tokens x 48 heads or 6144 tokens x 6 heads); larger
+ *   calls return GDN_ERR_SHAPE and touch nothing.
+ *   The first call on each device looks up the scratch's address
+ *   (cudaGetSymbolAddress, with that device current) and sets the kernels'
+ *   shared-memory attributes; make that first call before any stream capture.
+ *   Nothing in the scratch needs to start at zero.  There is one scratch per
+ *   device: calls on the same device that overlap in time (different streams
+ *   or host threads without ordering between them) race on it.
+ */
+int gdn_chunked_fwd_static(const void* q, const void* k, const void* v,
+                           long long q_stride, long long k_stride, long long v_stride,
+                           const float* a, const float* b, const float* A_log, const float* dt_bias,
+                           const float* state_in, float* state_out, void* o,
+                           const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                           unsigned flags, void* stream);
+
 /*
  * gdn_conv1d_fwd -- causal depthwise conv1d (kernel K = 4, no bias) over the
  * concatenated q|k|v channels, then SiLU: the front end of

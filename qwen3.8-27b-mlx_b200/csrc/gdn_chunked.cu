@@ -1118,6 +1118,62 @@ extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, l
   return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
+// Scratch of gdn_chunked_fwd_static: a fixed device array, so that the call
+// allocates nothing.  Nothing in it needs to start at zero: the prefix kernel
+// writes the chunk prefix and the prep kernel every record before the scan
+// kernel reads them.  One per device; overlapping calls on a device race on it.
+static __device__ __align__(256) unsigned char g_chunked_static_scratch[GDN_CHUNKED_STATIC_SCRATCH_BYTES];
+
+namespace gdn {
+namespace {
+
+// Address of g_chunked_static_scratch on the current device, looked up once per
+// device (cudaGetSymbolAddress with that device current) and cached.
+int static_scratch_ptr(unsigned char** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != GDN_OK) return rc;
+  if (dev < 0 || dev >= 64) return fail(GDN_ERR_CUDA, "device ordinal %d beyond the 64 the library tracks", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* a = nullptr;
+    rc = cuda_status(cudaGetSymbolAddress(&a, g_chunked_static_scratch), "cudaGetSymbolAddress(static scratch)");
+    if (rc != GDN_OK) return rc;
+    addr[dev] = a;
+  }
+  *out = static_cast<unsigned char*>(addr[dev]);
+  return GDN_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_chunked_fwd_static(const void* q, const void* k, const void* v, long long q_stride,
+                                      long long k_stride, long long v_stride, const float* a, const float* b,
+                                      const float* A_log, const float* dt_bias, const float* state_in,
+                                      float* state_out, void* o, const int32_t* cu_seqlens, int B, int T, int Hk,
+                                      int Hv, int Dk, int Dv, unsigned flags, void* stream) {
+  clear_error();
+  ChunkParams p;
+  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, o,
+                        cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags);
+  if (rc != GDN_OK || B == 0) return rc;
+  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
+  if (need > GDN_CHUNKED_STATIC_SCRATCH_BYTES)
+    return fail(GDN_ERR_SHAPE,
+                "gdn_chunked_fwd_static: B=%d T=%d Hv=%d needs %zu bytes of scratch, more than the %llu of the "
+                "static scratch; split the call or use gdn_chunked_fwd_ws",
+                B, T, Hv, need, static_cast<unsigned long long>(GDN_CHUNKED_STATIC_SCRATCH_BYTES));
+  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
+  if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
+  unsigned char* ws = nullptr;
+  rc = static_scratch_ptr(&ws);
+  if (rc != GDN_OK) return rc;
+  return run_split(p, ws, static_cast<cudaStream_t>(stream));
+}
+
 #ifdef GDN_CHUNK_TIMING
 extern "C" int gdn_debug_chunk_timing(long long* out, int reset) {
   int rc = cuda_status(cudaMemcpyFromSymbol(out, gdn::g_chunk_timing, sizeof(long long) * 16), "timing read");

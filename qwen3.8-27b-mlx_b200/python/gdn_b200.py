@@ -55,6 +55,7 @@ SIGNATURES = {
     "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_workspace_bytes": [_i] * 4,
+    "gdn_chunked_fwd_static": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6
                           + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_conv_commit": [_vp] * 5 + [_i] * 4 + [_vp],
