@@ -164,7 +164,7 @@ int gdn_chunked_fwd(const void* q, const void* k, const void* v,
  * gdn_chunked_workspace_bytes -- device workspace that gdn_chunked_fwd_ws
  * needs for B sequences of T tokens (packed = 0), or for B packed sequences
  * of T tokens in all (packed != 0, an upper bound that holds for any
- * cu_seqlens).  About 113 KiB per (64-token chunk, value head).  0 for bad
+ * cu_seqlens).  145 KiB per (64-token chunk, value head).  0 for bad
  * sizes.
  */
 size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed);
@@ -199,8 +199,8 @@ int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
  * that cannot allocate device memory at call time.
  *   Arguments, flags and results as gdn_chunked_fwd.
  *   Limit: gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) must not
- *   exceed GDN_CHUNKED_STATIC_SCRATCH_BYTES (about 580 (64-token chunk, value
- *   head) pairs, e.g. 768 tokens x 48 heads or 6144 tokens x 6 heads); larger
+ *   exceed GDN_CHUNKED_STATIC_SCRATCH_BYTES (about 450 (64-token chunk, value
+ *   head) pairs, e.g. 576 tokens x 48 heads or 4800 tokens x 6 heads); larger
  *   calls return GDN_ERR_SHAPE and touch nothing.
  *   The first call on each device looks up the scratch's address
  *   (cudaGetSymbolAddress, with that device current) and sets the kernels'

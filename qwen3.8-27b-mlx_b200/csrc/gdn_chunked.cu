@@ -64,9 +64,9 @@ namespace {
 constexpr int kC = 64;          // tokens per chunk (python/qwen35.py:365)
 constexpr int kThreads = 256;   // 8 warps: warp w owns TMEM lane quarter w % 4, column half w / 4
 
-// shared memory map of the fused and prep kernels, bytes; tensor-core operands
-// in the K-major no-swizzle layout (LBO 128 B), written row-wise so that a
-// warp's stores hit distinct banks
+// shared memory map of the fused kernel, bytes; tensor-core operands in the
+// K-major no-swizzle layout (LBO 128 B), written row-wise so that a warp's
+// stores hit distinct banks
 constexpr uint32_t kSbo128 = (kD * 4 / 16) * 128;   // 8-row group stride of 128-wide fp32 rows
 constexpr uint32_t kSbo64 = (kC * 4 / 16) * 128;    // ... of 64-wide fp32 rows
 constexpr int kPad = kC + 1;                        // row stride of the plain solve arrays
@@ -82,31 +82,47 @@ constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 10 x 6
 constexpr uint32_t kOffBar = kOffSc + 10 * kC * 4;  // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
 
-// shared memory map of the scan kernel
-constexpr uint32_t kScanW = 0;                      // W        64 x 128 (32 KiB)
-constexpr uint32_t kScanKh = kScanW + kC * kD * 4;  // K-hat^T 128 x 64  (32 KiB)
-constexpr uint32_t kScanM = kScanKh + kD * kC * 4;  // M        64 x 64  (16 KiB)
-constexpr uint32_t kScanQ = kScanM + kC * kC * 4;   // Qs       64 x 128 (32 KiB)
-constexpr uint32_t kScanU = kScanQ + kC * kD * 4;   // U^T     128 x 64  (32 KiB)
-constexpr uint32_t kScanSc = kScanU + kD * kC * 4;  // gq[64], g_last
-constexpr uint32_t kScanBar = kScanSc + 2 * kC * 4; // 3 mbarriers, TMEM base
-constexpr uint32_t kScanSmem = kScanBar + 64;
+// shared memory map of the prep kernel: regions are reused as the phases go,
+// so that two CTAs fit on an SM
+constexpr uint32_t kPKQ = 0;                        // [K; Q] rows 128 x 128, until (a) and its epilogue
+constexpr uint32_t kPA = 0;                         // A, plain, over the K rows once (a) has run
+constexpr uint32_t kPY = kPA + kC * kPad * 4;       // solve temporaries
+constexpr uint32_t kPX = 32768;                     // X, plain, over the Q rows once they are read
+constexpr uint32_t kPKt = 0;                        // K^T diag(beta g r_k) 128 x 64, after the solve
+constexpr uint32_t kPVt = 32768;                    // V^T diag(beta) 128 x 64, after the solve
+constexpr uint32_t kPTi = 65536;                    // T^-1 64 x 64
+constexpr uint32_t kPSc = kPTi + kC * kC * 4;       // per-token scalars, 10 x 64
+constexpr uint32_t kPBar = kPSc + 10 * kC * 4;      // mbarrier, TMEM base, slot broadcast
+constexpr uint32_t kPrepSmem = kPBar + 64;
+static_assert(kPY + 3 * 256 * 4 <= kPX, "prep: solve temporaries overlap X");
+static_assert(kPX + kC * kPad * 4 <= kPTi, "prep: X overlaps T^-1");
+static_assert(2 * (kPrepSmem + 1024) <= 233472, "prep: two CTAs per SM");
 
 constexpr uint32_t kTmemCols = 512;
-// fused / prep: [0,128) R (tf32), [128,256) R (fp32 master, state-update
+// fused: [0,128) R (tf32), [128,256) R (fp32 master, state-update
 // accumulator), [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
 // [384,448) U^T; [448,512) y^T
 constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 384, kColY = 448;
+// prep: [0,64) G|P, [64,128) U0^T, [128,192) W^T
+constexpr uint32_t kPrepTmemCols = 256;
+constexpr uint32_t kPColGP = 0, kPColU = 64, kPColWt = 128;
 
 // One workspace record per (chunk, value head): the prep kernel's outputs in
-// the byte layout of the scan kernel's shared memory.
-constexpr uint32_t kRecW = 0;                       // W, K-major 64 x 128, SBO 4096
-constexpr uint32_t kRecKh = kRecW + kC * kD * 4;    // K-hat^T, K-major 128 x 64, SBO 2048
-constexpr uint32_t kRecM = kRecKh + kD * kC * 4;    // M, K-major 64 x 64, SBO 2048
-constexpr uint32_t kRecU = kRecM + kC * kC * 4;     // U0^T, plain row-major 128 x 64
-constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // gq[64] = g_i r_qi, [64] = g_last
+// the byte layout of the scan kernel's shared memory (same offsets), in three
+// groups that the scan kernel bulk-copies one chunk ahead of their use.
+constexpr uint32_t kRecW = 0;                       // W, K-major 64 x 128, SBO 4096        group 1
+constexpr uint32_t kRecQ = kRecW + kC * kD * 4;     // diag(g r_q) Q, K-major 64 x 128      group 1
+constexpr uint32_t kRecKh = kRecQ + kC * kD * 4;    // K-hat^T, K-major 128 x 64, SBO 2048  group 2
+constexpr uint32_t kRecM = kRecKh + kD * kC * 4;    // M, K-major 64 x 64, SBO 2048         group 2
+constexpr uint32_t kRecU = kRecM + kC * kC * 4;     // U0^T by column quads: (c/4, row, c%4)  group 3
+constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // [0] = g_last                         group 3
 constexpr uint32_t kRecBytes = kRecSc + 1024;       // multiple of 256
 constexpr size_t kWsHeader = 256;                   // then the chunk prefix (B+1 int32), then records
+
+// shared memory map of the scan kernel: the record, then U^T and the barriers
+constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
+constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
+constexpr uint32_t kScanSmem = kScanBar + 64;
 
 __host__ __device__ constexpr size_t records_offset(int B) {
   return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
@@ -201,17 +217,8 @@ struct Ctx {
 #endif
 };
 
-__device__ __forceinline__ void ctx_init(Ctx& c, const ChunkParams& p, unsigned char* sm, int h) {
-  c.sKQ = sm + kOffKQ;
-  c.sKt = sm + kOffKt;
-  c.sVt = sm + kOffVt;
-  c.sTi = sm + kOffTi;
-  c.sM = sm + kOffM;
-  c.sW = sm + kOffW;
-  c.sX = reinterpret_cast<float*>(sm + kOffW);
-  c.sA = reinterpret_cast<float*>(sm + kOffA);
-  c.sY = reinterpret_cast<float*>(sm + kOffY);
-  float* sc = reinterpret_cast<float*>(sm + kOffSc);
+// Per-token scalar arrays at sc (10 x 64 floats).
+__device__ __forceinline__ void ctx_scalars(Ctx& c, float* sc) {
   c.s_pre = sc;
   c.s_gam = sc + 64;
   c.s_g = sc + 128;
@@ -222,7 +229,40 @@ __device__ __forceinline__ void ctx_init(Ctx& c, const ChunkParams& p, unsigned 
   c.s_misc = sc + 448;
   c.s_kw = sc + 512;      // beta g r_k: the K columns of W's right-hand side
   c.s_kh = sc + 576;      // e^{Gam_last-Gam} r_k: the K columns of the state update
+}
+
+// Shared-memory pointers of the fused kernel's layout.
+__device__ __forceinline__ void ctx_fused_layout(Ctx& c, unsigned char* sm) {
+  c.sKQ = sm + kOffKQ;
+  c.sKt = sm + kOffKt;
+  c.sVt = sm + kOffVt;
+  c.sTi = sm + kOffTi;
+  c.sM = sm + kOffM;
+  c.sW = sm + kOffW;
+  c.sX = reinterpret_cast<float*>(sm + kOffW);
+  c.sA = reinterpret_cast<float*>(sm + kOffA);
+  c.sY = reinterpret_cast<float*>(sm + kOffY);
+  ctx_scalars(c, reinterpret_cast<float*>(sm + kOffSc));
   c.bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+}
+
+// Shared-memory pointers of the prep kernel's layout (M and W go to the record).
+__device__ __forceinline__ void ctx_prep_layout(Ctx& c, unsigned char* sm) {
+  c.sKQ = sm + kPKQ;
+  c.sKt = sm + kPKt;
+  c.sVt = sm + kPVt;
+  c.sTi = sm + kPTi;
+  c.sM = nullptr;
+  c.sW = nullptr;
+  c.sX = reinterpret_cast<float*>(sm + kPX);
+  c.sA = reinterpret_cast<float*>(sm + kPA);
+  c.sY = reinterpret_cast<float*>(sm + kPY);
+  ctx_scalars(c, reinterpret_cast<float*>(sm + kPSc));
+  c.bar = reinterpret_cast<uint64_t*>(sm + kPBar);
+}
+
+// Thread geometry and per-head constants (pointers are set by a layout function).
+__device__ __forceinline__ void ctx_init(Ctx& c, const ChunkParams& p, int h) {
   c.tid = threadIdx.x;
   c.warp = c.tid >> 5;
   c.lane = c.tid & 31;
@@ -243,10 +283,10 @@ __device__ __forceinline__ void ctx_init(Ctx& c, const ChunkParams& p, unsigned 
 #endif
 }
 
-// Allocate the CTA's tensor memory and initialise its mbarriers.
-__device__ __forceinline__ void tmem_setup(Ctx& c, uint32_t* tslot, uint64_t* bars, int n_bars) {
+// Allocate ncols columns of tensor memory and initialise the CTA's mbarriers.
+__device__ __forceinline__ void tmem_setup(Ctx& c, uint32_t* tslot, uint64_t* bars, int n_bars, uint32_t ncols) {
   if (c.warp == 0) {
-    tc::tmem_alloc(tslot, kTmemCols);
+    tc::tmem_alloc(tslot, ncols);
     tc::tmem_relinquish();
   }
   if (c.tid == 0) {
@@ -331,16 +371,18 @@ __device__ __forceinline__ void phase_rows(const ChunkParams& p, Ctx& c, long lo
     *reinterpret_cast<float4*>(at(c.sKQ, kC + i, qd * 32 + e, kSbo128)) =
         make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
   if (qd == 0) c.s_rq[i] = c.l2 ? rsqrtf(ss + 1e-6f) * c.qscale : 1.f;
+  ptx::fence_proxy_async_smem();
   __syncthreads();
 }
 
 // Columns of K (or V) read from global two at a time (4-byte loads), scaled
 // per token by scale[], stored as rows of the transposed operand (K-major, 64
-// tokens wide) at dst.  lt in [0,128): column pair lt & 63, token half lt >> 6.
-// The caller selects K or V at run time so that all warps share one copy of
-// this code.
+// tokens wide) at dst, and when dst2 is set scaled by scale2[] into dst2 too.
+// lt in [0,128): column pair lt & 63, token half lt >> 6.  The caller selects
+// K or V at run time so that all warps share one copy of this code.
 __device__ __forceinline__ void columns(const ChunkParams& p, const Ctx& c, long long t0, int nvalid, int lt,
-                                        bool is_k, const float* scale, unsigned char* dst) {
+                                        bool is_k, const float* scale, unsigned char* dst,
+                                        const float* scale2 = nullptr, unsigned char* dst2 = nullptr) {
   const int pr = lt & 63;
   const int th = lt >> 6;
   const int cc = 2 * pr;
@@ -364,39 +406,54 @@ __device__ __forceinline__ void columns(const ChunkParams& p, const Ctx& c, long
     }
     *reinterpret_cast<float4*>(at(dst, cc, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
     *reinterpret_cast<float4*>(at(dst, cc + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+    if (dst2) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float s = scale2[th * 32 + j + e];
+        const float2 f = __bfloat1622float2(raw[j + e]);
+        x0[e] = tc::to_tf32(f.x * s);
+        x1[e] = tc::to_tf32(f.y * s);
+      }
+      *reinterpret_cast<float4*>(at(dst2, cc, th * 32 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+      *reinterpret_cast<float4*>(at(dst2, cc + 1, th * 32 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+    }
   }
 }
 
-// K^T diag(beta g r_k) (threads 0-127) and V^T diag(beta) (threads 128-255).
-__device__ __forceinline__ void phase_cols(const ChunkParams& p, Ctx& c, long long t0, int nvalid) {
+// K^T diag(beta g r_k) (threads 0-127) and V^T diag(beta) (threads 128-255);
+// with kh_dst set, K^T diag(e^{Gam_last-Gam} r_k) into kh_dst as well.
+__device__ __forceinline__ void phase_cols(const ChunkParams& p, Ctx& c, long long t0, int nvalid,
+                                           unsigned char* kh_dst = nullptr) {
   if (c.tid < kC) {
     c.s_kw[c.tid] = c.s_beta[c.tid] * c.s_g[c.tid] * c.s_rk[c.tid];
     c.s_kh[c.tid] = c.s_ratio[c.tid] * c.s_rk[c.tid];
   }
   __syncthreads();
   const bool is_k = c.tid < 128;
-  columns(p, c, t0, nvalid, c.tid & 127, is_k, is_k ? c.s_kw : c.s_beta, is_k ? c.sKt : c.sVt);
+  columns(p, c, t0, nvalid, c.tid & 127, is_k, is_k ? c.s_kw : c.s_beta, is_k ? c.sKt : c.sVt, c.s_kh,
+          is_k ? kh_dst : nullptr);
   ptx::fence_proxy_async_smem();
 }
 
-// (a) [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127).
-__device__ __forceinline__ bool phase_mma_a(Ctx& c) {
+// (a) [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127) at TMEM column col.
+__device__ __forceinline__ bool phase_mma_a(Ctx& c, uint32_t col) {
   if (c.tid == 0) {
     tc::fence_after_sync();
     const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
     for (int j = 0; j < kD / 8; ++j)
-      tc::mma_ss<tc::kTF32>(c.tb + kColGP, desc(c.sKQ, j * 256, kSbo128), desc(c.sKQ, j * 256, kSbo128), id, j > 0);
+      tc::mma_ss<tc::kTF32>(c.tb + col, desc(c.sKQ, j * 256, kSbo128), desc(c.sKQ, j * 256, kSbo128), id, j > 0);
     tc::mma_commit(c.bar);
   }
   return mma_wait(c);
 }
 
 // A (strictly lower, plain) for the solve; M (lower) in the operand layout at
-// m_dst (shared memory or a workspace record); optionally the Q rows of
-// [K; Q] rescaled by g r_q for the fused schedule's y product.
-__device__ __forceinline__ void phase_epi_a(Ctx& c, unsigned char* m_dst, bool rescale_q) {
+// m_dst; the Q rows of [K; Q] scaled by g r_q in the operand layout at q_dst
+// (the fused kernel rescales them in place).  Destinations are shared memory
+// or a workspace record.
+__device__ __forceinline__ void phase_epi_a(Ctx& c, uint32_t col, unsigned char* m_dst, unsigned char* q_dst) {
   float gp[32];
-  tmem_ld<32>(c.tb + kColGP + c.my + c.half * 32, gp);
+  tmem_ld<32>(c.tb + col + c.my + c.half * 32, gp);
   if (c.quarter < 2) {
     const int i = c.row;
     const float fi = c.s_beta[i] * c.s_rk[i];
@@ -421,17 +478,14 @@ __device__ __forceinline__ void phase_epi_a(Ctx& c, unsigned char* m_dst, bool r
       }
       *reinterpret_cast<float4*>(at(m_dst, i, c.half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
     }
-    if (rescale_q) {
-      const float sq = c.s_g[i] * c.s_rq[i];
-      for (int cc = c.half * 64; cc < c.half * 64 + 64; cc += 4) {
-        float4* qp = reinterpret_cast<float4*>(at(c.sKQ, kC + i, cc, kSbo128));
-        float4 v = *qp;
-        v.x = tc::to_tf32(v.x * sq);
-        v.y = tc::to_tf32(v.y * sq);
-        v.z = tc::to_tf32(v.z * sq);
-        v.w = tc::to_tf32(v.w * sq);
-        *qp = v;
-      }
+    const float sq = c.s_g[i] * c.s_rq[i];
+    for (int cc = c.half * 64; cc < c.half * 64 + 64; cc += 4) {
+      float4 v = *reinterpret_cast<const float4*>(at(c.sKQ, kC + i, cc, kSbo128));
+      v.x = tc::to_tf32(v.x * sq);
+      v.y = tc::to_tf32(v.y * sq);
+      v.z = tc::to_tf32(v.z * sq);
+      v.w = tc::to_tf32(v.w * sq);
+      *reinterpret_cast<float4*>(at(q_dst, i, cc, kSbo128)) = v;
     }
   }
   __syncthreads();
@@ -577,6 +631,7 @@ __device__ __forceinline__ void phase_epi_d(Ctx& c, uint32_t col_u, unsigned cha
 }
 
 // y^T (TMEM) -> o rows of the chunk: thread -> (dv = row, tokens of its half).
+// No barrier at the end: the caller orders it with what follows.
 __device__ __forceinline__ void phase_epi_e(const ChunkParams& p, Ctx& c, uint32_t col_y, long long t0, int nvalid) {
   float y[32];
   tmem_ld<32>(c.tb + col_y + c.my + c.half * 32, y);
@@ -594,8 +649,6 @@ __device__ __forceinline__ void phase_epi_e(const ChunkParams& p, Ctx& c, uint32
     for (int i = 0; i < 32; ++i)
       if (i < nv) o[i * orow] = y[i];
   }
-  tc::fence_before_sync();
-  __syncthreads();
 }
 
 // Initial state row dv = row (columns of this warp's half) into the fp32 master.
@@ -633,11 +686,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   const int bh = blockIdx.x;
   const int b = bh / p.Hv;
   Ctx c;
-  ctx_init(c, p, sm, bh - b * p.Hv);
+  ctx_init(c, p, bh - b * p.Hv);
+  ctx_fused_layout(c, sm);
   long long s0, s1;
   seq_range(p, b, s0, s1);
   const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
-  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1);
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1, kTmemCols);
   state_load(p, c, bh, kColDR);
 
   bool failed = false;
@@ -654,9 +708,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     tc::fence_before_sync();
     __syncthreads();
     GDN_TICK(3);
-    if (!phase_mma_a(c)) { failed = true; break; }
+    if (!phase_mma_a(c, kColGP)) { failed = true; break; }
     GDN_TICK(4);
-    phase_epi_a(c, c.sM, /*rescale_q=*/true);
+    phase_epi_a(c, kColGP, c.sM, c.sKQ + 8 * kSbo128);
     GDN_TICK(5);
     phase_solve(c);
     GDN_TICK(6);
@@ -692,11 +746,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     if (!mma_wait(c)) { failed = true; break; }
     GDN_TICK(11);
     phase_epi_e(p, c, kColY, t0, nvalid);
+    tc::fence_before_sync();
+    __syncthreads();
     GDN_TICK(12);
   }
   if (failed) {
     if (c.tid == 0) atomicExch(p.err, 1);
-    ptx::mbar_wait(c.bar, c.phase);      // one more bounded chance for an MMA in flight
+    ptx::mbar_wait(c.bar, c.phase ^ 1u);   // the phase mma_wait gave up on: one more bounded wait
   } else {
     state_store(p, c, bh, kColDR);
   }
@@ -765,10 +821,40 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
   if (threadIdx.x == 0) prefix[B] = carry;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) chunk_prep_kernel(const ChunkParams p) {
+// (b) U0^T = V^T diag(beta) T^-T and (c) W^T = K^T diag(beta g r_k) T^-T, both
+// M = 128 (Dv resp. Dk rows) x N = 64 tokens with T^-1 as the B operand.
+__device__ __forceinline__ bool phase_mma_bc_prep(Ctx& c) {
+  if (c.tid == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
+    for (int j = 0; j < kC / 8; ++j)
+      tc::mma_ss<tc::kTF32>(c.tb + kPColU, desc(c.sVt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
+    for (int j = 0; j < kC / 8; ++j)
+      tc::mma_ss<tc::kTF32>(c.tb + kPColWt, desc(c.sKt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
+    tc::mma_commit(c.bar);
+  }
+  return mma_wait(c);
+}
+
+// U0^T rows into the record by column quads (conflict-free reads for the scan
+// kernel's threads) and W^T columns into the record's K-major W (token rows).
+__device__ __forceinline__ void phase_epi_prep(Ctx& c, unsigned char* rec) {
+  float u[32];
+  tmem_ld<32>(c.tb + kPColU + c.my + c.half * 32, u);
+  float4* ud = reinterpret_cast<float4*>(rec + kRecU);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4)
+    ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+  tmem_ld<32>(c.tb + kPColWt + c.my + c.half * 32, u);
+#pragma unroll
+  for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = tc::to_tf32(u[e]);
+  if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
+}
+
+__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const long long slot = blockIdx.x;
-  int* s_bc = reinterpret_cast<int*>(sm + kOffBar + 16);
+  int* s_bc = reinterpret_cast<int*>(sm + kPBar + 16);
   if (threadIdx.x == 0) {
     int b = 0, ch = 0;
     const bool used = slot_to_chunk(p, slot, b, ch);
@@ -780,60 +866,59 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_prep_kernel(const ChunkPara
   if (b < 0) return;
   const int ch = s_bc[1];
   Ctx c;
-  ctx_init(c, p, sm, blockIdx.y);
+  ctx_init(c, p, blockIdx.y);
+  ctx_prep_layout(c, sm);
   long long s0, s1;
   seq_range(p, b, s0, s1);
   const long long t0 = s0 + static_cast<long long>(ch) * kC;
   const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
   unsigned char* rec = record(p, slot, c.h);
-  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1);
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kPBar + 8), c.bar, 1, kPrepTmemCols);
 
   phase_gates(p, c, t0, nvalid);
   phase_rows(p, c, t0, s0, nvalid);
-  phase_cols(p, c, t0, nvalid);
-  tc::fence_before_sync();
-  __syncthreads();
-  bool ok = phase_mma_a(c);
+  bool ok = phase_mma_a(c, kPColGP);
   if (ok) {
-    phase_epi_a(c, rec + kRecM, /*rescale_q=*/false);
-    phase_solve(c);
-    ok = phase_mma_bc(c);
+    phase_epi_a(c, kPColGP, rec + kRecM, rec + kRecQ);   // A over the K rows; M, Qs to the record
+    phase_solve(c);                                       // X over the Q rows
+    phase_cols(p, c, t0, nvalid, rec + kRecKh);           // K^T, V^T over A and X; K-hat^T to the record
+    tc::fence_before_sync();
+    __syncthreads();
+    ok = phase_mma_bc_prep(c);
   }
   if (ok) {
-    // U0^T rows (plain) and the per-token factors the scan kernel needs
-    float u[32];
-    tmem_ld<32>(c.tb + kColU + c.my + c.half * 32, u);
-    float* ud = reinterpret_cast<float*>(rec + kRecU) + c.row * kC + c.half * 32;
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(ud + e) = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
-    float* sc = reinterpret_cast<float*>(rec + kRecSc);
-    if (c.tid < kC) sc[c.tid] = c.s_g[c.tid] * c.s_rq[c.tid];
-    if (c.tid == 0) sc[kC] = c.s_misc[0];
-    phase_epi_c(p, c, t0, nvalid, rec + kRecW, rec + kRecKh);
+    phase_epi_prep(c, rec);
   } else {
     if (c.tid == 0) atomicExch(p.err, 1);
-    ptx::mbar_wait(c.bar, c.phase);
+    ptx::mbar_wait(c.bar, c.phase ^ 1u);
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
+  if (c.warp == 0) tc::tmem_dealloc(c.tb, kPrepTmemCols);
 }
 
 // ---- the split schedule: scan (serial over chunks, per sequence and head) ---------
 
+// Bytes [begin, end) of record group g (1: W | Qs, 2: K-hat^T | M, 3: U0^T | g_last).
+__device__ __forceinline__ void group_range(int g, uint32_t& begin, uint32_t& end) {
+  begin = g == 1 ? kRecW : g == 2 ? kRecKh : kRecU;
+  end = g == 1 ? kRecKh : g == 2 ? kRecU : kRecBytes;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* sW = sm + kScanW;
-  unsigned char* sKh = sm + kScanKh;
-  unsigned char* sMm = sm + kScanM;
-  unsigned char* sQ = sm + kScanQ;
+  unsigned char* sW = sm + kRecW;
+  unsigned char* sQ = sm + kRecQ;
+  unsigned char* sKh = sm + kRecKh;
+  unsigned char* sMm = sm + kRecM;
+  const float4* sU0 = reinterpret_cast<const float4*>(sm + kRecU);
+  const float* sSc = reinterpret_cast<const float*>(sm + kRecSc);
   unsigned char* sU = sm + kScanU;
-  float* s_gq = reinterpret_cast<float*>(sm + kScanSc);          // [0,64) g r_q, [64] g_last
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);   // [0] MMA, [1] W, [2] K-hat + M
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);   // [0] MMA, [1..3] record groups
   const int bh = blockIdx.x;
   const int b = bh / p.Hv;
   Ctx c;
-  ctx_init(c, p, sm, bh - b * p.Hv);
+  ctx_init(c, p, bh - b * p.Hv);
   c.bar = bars;
   long long s0, s1;
   seq_range(p, b, s0, s1);
@@ -841,79 +926,76 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
   const long long slot0 = seq_first_slot(p, b);
   // TMEM: R tf32 [0,128), R fp32 [128,256), U^T [256,320), y^T [320,384)
   constexpr uint32_t cR = 0, cDR = 128, cU = 256, cY = 320;
-  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 3);
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 4, kTmemCols);
   state_load(p, c, bh, cDR);
 
-  auto load_w = [&](int ch) {           // thread 0: W of chunk ch (bulk copies)
-    const unsigned char* rec = record(p, slot0 + ch, c.h);
-    ptx::mbar_arrive_expect_tx(&bars[1], kC * kD * 4);
-    for (uint32_t off = 0; off < kC * kD * 4; off += 16384) ptx::bulk_g2s(sW + off, rec + kRecW + off, 16384, &bars[1]);
-  };
-  auto load_kh_m = [&](int ch) {        // thread 0: K-hat^T and M of chunk ch
-    const unsigned char* rec = record(p, slot0 + ch, c.h);
-    ptx::mbar_arrive_expect_tx(&bars[2], kD * kC * 4 + kC * kC * 4);
-    for (uint32_t off = 0; off < kD * kC * 4; off += 16384)
-      ptx::bulk_g2s(sKh + off, rec + kRecKh + off, 16384, &bars[2]);
-    ptx::bulk_g2s(sMm, rec + kRecM, kC * kC * 4, &bars[2]);
-  };
-  // W and K-hat/M loads issued and waited for (counted by every thread, the
-  // waits by warp 0 only: their difference is what a failed exit waits for)
-  int w_issued = 0, w_done = 0, k_issued = 0, k_done = 0;
-  if (n_chunks > 0) {
+  // record groups issued and waited for (issued counted by every thread, waits
+  // by warp 0: their difference is what a failed exit still waits for)
+  int issued[4] = {0, 0, 0, 0}, done[4] = {0, 0, 0, 0};
+  auto load = [&](int g, int ch) {      // group g of chunk ch into the same offsets of shared memory
     if (c.tid == 0) {
-      load_w(0);
-      load_kh_m(0);
+      uint32_t begin, end;
+      group_range(g, begin, end);
+      const unsigned char* rec = record(p, slot0 + ch, c.h);
+      ptx::mbar_arrive_expect_tx(&bars[g], end - begin);
+      for (uint32_t off = begin; off < end; off += 16384)
+        ptx::bulk_g2s(sm + off, rec + off, end - off < 16384 ? end - off : 16384, &bars[g]);
     }
-    w_issued = k_issued = 1;
-  }
+    ++issued[g];
+  };
+  // warp 0 waits for group g of chunk ch; the CTA agrees on the outcome
+  auto landed = [&](int g, int ch) -> bool {
+    bool ok = true;
+    if (c.warp == 0) {
+      ok = ptx::mbar_wait(&bars[g], ch & 1);
+      done[g] += ok;
+    }
+    const bool all = !__syncthreads_or(!ok);
+    return all;
+  };
+  // U0^T of chunk ch into the U^T accumulator, R -> tf32 operand and g_last R
+  auto stage = [&]() {
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      float u[16];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 f = sU0[(c.half * 8 + h2 * 4 + e) * kD + c.row];
+        u[4 * e] = f.x; u[4 * e + 1] = f.y; u[4 * e + 2] = f.z; u[4 * e + 3] = f.w;
+      }
+      tc::tmem_st16(c.tb + cU + c.my + c.half * 32 + h2 * 16, u);
+    }
+    phase_r_update(c, sSc[0], cR, cDR);      // ends with tcgen05.wait::st
+  };
 
   bool failed = false;
-  for (int ch = 0; ch < n_chunks; ++ch) {
-    const long long t0 = s0 + static_cast<long long>(ch) * kC;
-    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-    const unsigned char* rec = record(p, slot0 + ch, c.h);
-    // per-token factors; U0^T into TMEM as the accumulator of U^T
-    if (c.tid <= kC) s_gq[c.tid] = reinterpret_cast<const float*>(rec + kRecSc)[c.tid];
-    {
-      const float* ur = reinterpret_cast<const float*>(rec + kRecU) + c.row * kC + c.half * 32;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        float u[16];
-#pragma unroll
-        for (int e = 0; e < 16; e += 4) {
-          const float4 f = *reinterpret_cast<const float4*>(ur + h2 * 16 + e);
-          u[e] = f.x; u[e + 1] = f.y; u[e + 2] = f.z; u[e + 3] = f.w;
-        }
-        tc::tmem_st16(c.tb + cU + c.my + c.half * 32 + h2 * 16, u);
-      }
-      tc::tmem_st_wait();
+  if (n_chunks > 0) {
+    load(1, 0);
+    load(2, 0);
+    load(3, 0);
+    if (landed(3, 0)) {
+      tc::fence_after_sync();
+      stage();
+    } else {
+      failed = true;
     }
-    __syncthreads();
-    // Qs = diag(g r_q) Q rows (thread -> token i, 32-dim quarter)
-    {
-      const int i = c.tid >> 2;
-      const int qd = c.tid & 3;
-      const bool valid = i < nvalid;
-      float f[32];
-      load32(p.q + (valid ? t0 + i : s0) * p.q_stride + c.kh * kD + qd * 32, valid, f);
-      const float sq = s_gq[i];
-#pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(at(sQ, i, qd * 32 + e, kSbo128)) =
-            make_float4(tc::to_tf32(f[e] * sq), tc::to_tf32(f[e + 1] * sq), tc::to_tf32(f[e + 2] * sq),
-                        tc::to_tf32(f[e + 3] * sq));
-    }
-    ptx::fence_proxy_async_smem();
-    phase_r_update(c, s_gq[kC], cR, cDR);
     tc::fence_before_sync();
     __syncthreads();
-    // (d) U^T = U0^T - R W^T and (e1) y^T = R Qs^T, once W has landed
-    bool landed = true;
+    if (!failed && n_chunks > 1) {
+      if (c.tid == 0) ptx::fence_proxy_async_smem();
+      load(3, 1);
+    }
+  }
+  for (int ch = 0; ch < n_chunks && !failed; ++ch) {
+    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    // (d) U^T = U0^T - R W^T,  (e1) y^T = R Qs^T
+    bool ok = true;
     if (c.warp == 0) {
-      landed = ptx::mbar_wait(&bars[1], ch & 1);
-      w_done += landed;
+      ok = ptx::mbar_wait(&bars[1], ch & 1);
+      done[1] += ok;
       if (c.lane == 0) {
-        if (landed) {
+        if (ok) {
           tc::fence_after_sync();
           const uint32_t idd = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
           const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
@@ -925,19 +1007,16 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
         tc::mma_commit(c.bar);       // with no MMA issued it arrives at once
       }
     }
-    if (!mma_wait(c, landed)) { failed = true; break; }
-    if (ch + 1 < n_chunks) {
-      if (c.tid == 0) load_w(ch + 1);
-      ++w_issued;
-    }
+    if (!mma_wait(c, ok)) { failed = true; break; }
+    if (ch + 1 < n_chunks) load(1, ch + 1);
     phase_epi_d(c, cU, sU);
     // (e2) y^T += U^T M^T,  (f) R += U^T K-hat
-    landed = true;
+    ok = true;
     if (c.warp == 0) {
-      landed = ptx::mbar_wait(&bars[2], ch & 1);
-      k_done += landed;
+      ok = ptx::mbar_wait(&bars[2], ch & 1);
+      done[2] += ok;
       if (c.lane == 0) {
-        if (landed) {
+        if (ok) {
           tc::fence_after_sync();
           const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
           const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
@@ -949,20 +1028,29 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
         tc::mma_commit(c.bar);
       }
     }
-    if (!mma_wait(c, landed)) { failed = true; break; }
-    if (ch + 1 < n_chunks) {
-      if (c.tid == 0) load_kh_m(ch + 1);
-      ++k_issued;
-    }
+    if (!mma_wait(c, ok)) { failed = true; break; }
+    if (ch + 1 < n_chunks) load(2, ch + 1);
+    // o of this chunk; U0^T and the state operands of the next
     phase_epi_e(p, c, cY, t0, nvalid);
+    if (ch + 1 < n_chunks) {
+      if (!landed(3, ch + 1)) { failed = true; break; }
+      tc::fence_after_sync();
+      stage();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (ch + 2 < n_chunks) {
+      if (c.tid == 0) ptx::fence_proxy_async_smem();
+      load(3, ch + 2);
+    }
   }
   if (failed) {
     // bounded waits for the MMA and the bulk copies still in flight
     if (c.tid == 0) atomicExch(p.err, 1);
     if (c.warp == 0) {
-      ptx::mbar_wait(c.bar, c.phase);
-      if (w_issued > w_done) ptx::mbar_wait(&bars[1], w_done & 1);
-      if (k_issued > k_done) ptx::mbar_wait(&bars[2], k_done & 1);
+      ptx::mbar_wait(c.bar, c.phase ^ 1u);
+      for (int g = 1; g <= 3; ++g)
+        if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
     }
   } else {
     state_store(p, c, bh, cDR);
@@ -1046,7 +1134,7 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
   p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
   p.nch_uniform = packed ? 0 : (p.T + kC - 1) / kC;
   static bool attr_prep[64] = {false}, attr_scan[64] = {false};
-  int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kSmemBytes, attr_prep);
+  int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kPrepSmem, attr_prep);
   if (rc != GDN_OK) return rc;
   rc = set_smem_attr(reinterpret_cast<const void*>(chunk_scan_kernel), kScanSmem, attr_scan);
   if (rc != GDN_OK) return rc;
@@ -1056,7 +1144,7 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
     if (rc != GDN_OK) return rc;
   }
   if (p.n_slots > 0) {
-    chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kSmemBytes,
+    chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kPrepSmem,
                         st>>>(p);
     rc = cuda_status(cudaGetLastError(), "chunk prep launch");
     if (rc != GDN_OK) return rc;

@@ -212,10 +212,11 @@ def test_chunked_varlen_packed(split):
 
 
 @pytest.mark.parametrize("lens", [[300], [130, 130, 130], [100, 0, 257, 64, 3, 1, 640]])
-def test_split_schedule_is_bit_identical_to_fused(lens):
-    """The split schedule runs the same products in the same order on the same
-    tf32 operands as the fused kernel, so o and the state agree bit for bit;
-    a second call on the same (reused, unzeroed) workspace does too."""
+def test_split_schedule_matches_fused(lens):
+    """The split schedule forms the same tf32 operands as the fused kernel (W
+    as W^T = K^T diag(beta g r_k) T^-T, the other products unchanged), so the
+    two agree far inside the oracle bound (1e-5 relative L2); a second call on
+    the same reused, unzeroed workspace gives the same bits as the first."""
     rng = np.random.default_rng(60 + len(lens))
     total = sum(lens)
     inp = chunk_inputs(rng, 1, total, 2, 6, slow_decay=False)
@@ -227,10 +228,11 @@ def test_split_schedule_is_bit_identical_to_fused(lens):
     o_f, S_f = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu)
     need = G.chunked_workspace_bytes(len(lens), total if cu is not None else lens[0], 6, cu is not None)
     ws = torch.full((need,), 0xAB, dtype=torch.uint8, device="cuda")
-    for _ in range(2):
-        o_s, S_s = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
-        assert torch.equal(o_s, o_f)
-        assert torch.equal(S_s, S_f)
+    o_1, S_1 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
+    o_2, S_2 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
+    assert O.rel_l2(host(o_1), host(o_f)) < 1e-5, O.rel_l2(host(o_1), host(o_f))
+    assert O.rel_l2(host(S_1), host(S_f)) < 1e-5, O.rel_l2(host(S_1), host(S_f))
+    assert torch.equal(o_1, o_2) and torch.equal(S_1, S_2)
     assert G.take_device_error() == 0
 
 

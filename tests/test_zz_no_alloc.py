@@ -107,7 +107,7 @@ def test_static_scratch_matches_workspace_entry_on_two_calls_in_a_row():
 
 
 def test_static_scratch_rejects_a_call_beyond_its_size():
-    """768 (chunk, head) records (16 chunks x 48 heads, 86 MiB) exceed the
+    """768 (chunk, head) records (16 chunks x 48 heads, 109 MiB) exceed the
     64 MiB scratch: GDN_ERR_SHAPE, outputs untouched.  The buffers have the
     call's full size, so nothing could be out of bounds either way."""
     L = G.lib()
