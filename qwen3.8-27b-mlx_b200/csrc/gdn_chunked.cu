@@ -44,7 +44,7 @@
 namespace gdn {
 
 #ifdef GDN_CHUNK_TIMING
-__device__ long long g_chunk_timing[16];
+__device__ long long g_chunk_timing[32];   // [0,13) fused, [16,24) prep, [24,29) scan
 #define GDN_TICK(slot)                                                          \
   do {                                                                          \
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {               \
@@ -876,18 +876,26 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kPBar + 8), c.bar, 1, kPrepTmemCols);
 
   phase_gates(p, c, t0, nvalid);
+  GDN_TICK(16);
   phase_rows(p, c, t0, s0, nvalid);
+  GDN_TICK(17);
   bool ok = phase_mma_a(c, kPColGP);
+  GDN_TICK(18);
   if (ok) {
     phase_epi_a(c, kPColGP, rec + kRecM, rec + kRecQ);   // A over the K rows; M, Qs to the record
+    GDN_TICK(19);
     phase_solve(c);                                       // X over the Q rows
+    GDN_TICK(20);
     phase_cols(p, c, t0, nvalid, rec + kRecKh);           // K^T, V^T over A and X; K-hat^T to the record
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(21);
     ok = phase_mma_bc_prep(c);
+    GDN_TICK(22);
   }
   if (ok) {
     phase_epi_prep(c, rec);
+    GDN_TICK(23);
   } else {
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);
@@ -1008,8 +1016,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
       }
     }
     if (!mma_wait(c, ok)) { failed = true; break; }
+    GDN_TICK(24);
     if (ch + 1 < n_chunks) load(1, ch + 1);
     phase_epi_d(c, cU, sU);
+    GDN_TICK(25);
     // (e2) y^T += U^T M^T,  (f) R += U^T K-hat
     ok = true;
     if (c.warp == 0) {
@@ -1029,9 +1039,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
       }
     }
     if (!mma_wait(c, ok)) { failed = true; break; }
+    GDN_TICK(26);
     if (ch + 1 < n_chunks) load(2, ch + 1);
     // o of this chunk; U0^T and the state operands of the next
     phase_epi_e(p, c, cY, t0, nvalid);
+    GDN_TICK(27);
     if (ch + 1 < n_chunks) {
       if (!landed(3, ch + 1)) { failed = true; break; }
       tc::fence_after_sync();
@@ -1039,6 +1051,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
     }
     tc::fence_before_sync();
     __syncthreads();
+    GDN_TICK(28);
     if (ch + 2 < n_chunks) {
       if (c.tid == 0) ptx::fence_proxy_async_smem();
       load(3, ch + 2);
@@ -1264,9 +1277,9 @@ extern "C" int gdn_chunked_fwd_static(const void* q, const void* k, const void* 
 
 #ifdef GDN_CHUNK_TIMING
 extern "C" int gdn_debug_chunk_timing(long long* out, int reset) {
-  int rc = cuda_status(cudaMemcpyFromSymbol(out, gdn::g_chunk_timing, sizeof(long long) * 16), "timing read");
+  int rc = cuda_status(cudaMemcpyFromSymbol(out, gdn::g_chunk_timing, sizeof(long long) * 32), "timing read");
   if (rc == GDN_OK && reset) {
-    long long z[16] = {0};
+    long long z[32] = {0};
     rc = cuda_status(cudaMemcpyToSymbol(gdn::g_chunk_timing, z, sizeof(z)), "timing reset");
   }
   return rc;
