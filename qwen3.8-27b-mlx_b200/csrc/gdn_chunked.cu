@@ -107,19 +107,25 @@ constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 3
 constexpr uint32_t kPrepTmemCols = 256;
 constexpr uint32_t kPColGP = 0, kPColU = 64, kPColWt = 128;
 
-// One workspace record per (chunk, value head): the prep kernel's outputs in
-// the byte layout of the scan kernel's shared memory (same offsets), in three
-// groups that the scan kernel bulk-copies one chunk ahead of their use.
-constexpr uint32_t kRecW = 0;                       // W, K-major 64 x 128, SBO 4096        group 1
-constexpr uint32_t kRecQ = kRecW + kC * kD * 4;     // diag(g r_q) Q, K-major 64 x 128      group 1
-constexpr uint32_t kRecKh = kRecQ + kC * kD * 4;    // K-hat^T, K-major 128 x 64, SBO 2048  group 2
-constexpr uint32_t kRecM = kRecKh + kD * kC * 4;    // M, K-major 64 x 64, SBO 2048         group 2
-constexpr uint32_t kRecU = kRecM + kC * kC * 4;     // U0^T by column quads: (c/4, row, c%4)  group 3
+// One workspace record per (chunk, value head): the prep kernel's outputs as
+// tensor-core operands (K-major, no swizzle) in three groups that the scan
+// kernel bulk-copies into shared memory a chunk ahead of their use.  -W and
+// Qs form one 128-row B operand, M and K-hat^T one 192-row B operand.
+constexpr uint32_t kRecW = 0;                       // -W, 64 x 128, SBO 4096               group 1
+constexpr uint32_t kRecQ = kRecW + kC * kD * 4;     // diag(g r_q) Q, 64 x 128, SBO 4096    group 1
+constexpr uint32_t kRecM = kRecQ + kC * kD * 4;     // M, 64 x 64, SBO 2048                 group 2
+constexpr uint32_t kRecKh = kRecM + kC * kC * 4;    // K-hat^T, 128 x 64, SBO 2048          group 2
+constexpr uint32_t kRecU = kRecKh + kD * kC * 4;    // U0^T by column quads: (c/4, row, c%4)  group 3
 constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // [0] = g_last                         group 3
 constexpr uint32_t kRecBytes = kRecSc + 1024;       // multiple of 256
 constexpr size_t kWsHeader = 256;                   // then the chunk prefix (B+1 int32), then records
 
 // shared memory map of the scan kernel: the record, then U^T and the barriers
+// shared memory map of the scan kernel: group 1 at [0, 64K) and group 2 at
+// [64K, 112K), each with its two operands in chunk-parity order (see the
+// kernel); group 3 at the record's own offsets; then U^T and the barriers
+constexpr uint32_t kScanG1 = 0;
+constexpr uint32_t kScanG2 = kRecM;
 constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
 constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
 constexpr uint32_t kScanSmem = kScanBar + 64;
@@ -651,27 +657,28 @@ __device__ __forceinline__ void phase_epi_e(const ChunkParams& p, Ctx& c, uint32
   }
 }
 
-// Initial state row dv = row (columns of this warp's half) into the fp32 master.
-__device__ __forceinline__ void state_load(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr) {
-  const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + c.row) * kD + c.half * 64 : nullptr;
-  for (int cc = 0; cc < 64; cc += 16) {
+// Initial state row dv = row, columns [col0, col0 + ncols), into the fp32 master.
+__device__ __forceinline__ void state_load(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr, int col0, int ncols) {
+  const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + c.row) * kD + col0 : nullptr;
+  for (int cc = 0; cc < ncols; cc += 16) {
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; i += 4) {
       const float4 f = src ? *reinterpret_cast<const float4*>(src + cc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
     }
-    tc::tmem_st16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+    tc::tmem_st16(c.tb + col_dr + c.my + col0 + cc, v);
   }
   tc::tmem_st_wait();
 }
 
-__device__ __forceinline__ void state_store(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr) {
+__device__ __forceinline__ void state_store(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr, int col0,
+                                            int ncols) {
   if (!p.state_out) return;
-  float* dst = p.state_out + (static_cast<size_t>(bh) * kD + c.row) * kD + c.half * 64;
-  for (int cc = 0; cc < 64; cc += 16) {
+  float* dst = p.state_out + (static_cast<size_t>(bh) * kD + c.row) * kD + col0;
+  for (int cc = 0; cc < ncols; cc += 16) {
     float v[16];
-    tc::tmem_ld16(c.tb + col_dr + c.my + c.half * 64 + cc, v);
+    tc::tmem_ld16(c.tb + col_dr + c.my + col0 + cc, v);
     tc::tmem_ld_wait();
 #pragma unroll
     for (int i = 0; i < 16; i += 4)
@@ -692,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   seq_range(p, b, s0, s1);
   const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1, kTmemCols);
-  state_load(p, c, bh, kColDR);
+  state_load(p, c, bh, kColDR, c.half * 64, 64);
 
   bool failed = false;
   for (int ch = 0; ch < n_chunks; ++ch) {
@@ -754,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);   // the phase mma_wait gave up on: one more bounded wait
   } else {
-    state_store(p, c, bh, kColDR);
+    state_store(p, c, bh, kColDR, c.half * 64, 64);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -837,7 +844,8 @@ __device__ __forceinline__ bool phase_mma_bc_prep(Ctx& c) {
 }
 
 // U0^T rows into the record by column quads (conflict-free reads for the scan
-// kernel's threads) and W^T columns into the record's K-major W (token rows).
+// kernel's threads) and W^T columns, negated, into the record's K-major W
+// (token rows).
 __device__ __forceinline__ void phase_epi_prep(Ctx& c, unsigned char* rec) {
   float u[32];
   tmem_ld<32>(c.tb + kPColU + c.my + c.half * 32, u);
@@ -847,7 +855,7 @@ __device__ __forceinline__ void phase_epi_prep(Ctx& c, unsigned char* rec) {
     ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
   tmem_ld<32>(c.tb + kPColWt + c.my + c.half * 32, u);
 #pragma unroll
-  for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = tc::to_tf32(u[e]);
+  for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = -tc::to_tf32(u[e]);
   if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
 }
 
@@ -907,73 +915,139 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
 
 // ---- the split schedule: scan (serial over chunks, per sequence and head) ---------
 
-// Bytes [begin, end) of record group g (1: W | Qs, 2: K-hat^T | M, 3: U0^T | g_last).
-__device__ __forceinline__ void group_range(int g, uint32_t& begin, uint32_t& end) {
-  begin = g == 1 ? kRecW : g == 2 ? kRecKh : kRecU;
-  end = g == 1 ? kRecKh : g == 2 ? kRecU : kRecBytes;
-}
+// 17 warps: warps 0-15 are the epilogue workers -- warp w reaches TMEM lanes
+// 32 (w % 4) .. +31 and owns column group w / 4 (a quarter of each
+// accumulator's columns); warp 16 waits for the bulk copies and the MMAs, and
+// its lane 0 issues both, so that its issue stalls never delay the workers.
+constexpr int kScanWorkers = 512;
+constexpr int kScanThreads = kScanWorkers + 32;
 
-__global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkParams p) {
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* sW = sm + kRecW;
-  unsigned char* sQ = sm + kRecQ;
-  unsigned char* sKh = sm + kRecKh;
-  unsigned char* sMm = sm + kRecM;
   const float4* sU0 = reinterpret_cast<const float4*>(sm + kRecU);
   const float* sSc = reinterpret_cast<const float*>(sm + kRecSc);
   unsigned char* sU = sm + kScanU;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);   // [0] MMA, [1..3] record groups
+  // [0] MMA; record groups [1] -W | Qs, [2] M | K-hat^T, [3] U0^T | g_last
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);
   const int bh = blockIdx.x;
   const int b = bh / p.Hv;
   Ctx c;
   ctx_init(c, p, bh - b * p.Hv);
   c.bar = bars;
+  const bool mw = c.warp == kScanWorkers / 32;     // the MMA / copy warp
+  const bool issuer = mw && c.lane == 0;
+  const int cg = (c.warp >> 2) & 3;                // column group of a worker
   long long s0, s1;
   seq_range(p, b, s0, s1);
   const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
   const long long slot0 = seq_first_slot(p, b);
-  // TMEM: R tf32 [0,128), R fp32 [128,256), U^T [256,320), y^T [320,384)
-  constexpr uint32_t cR = 0, cDR = 128, cU = 256, cY = 320;
+  // TMEM columns: R tf32 [0,128) | U (even) | y (even) | R fp32 [256,384) | y (odd) | U (odd).
+  // The first MMA batch writes [U | y] (even) or [y | U] (odd) in one N = 128
+  // product, the second [y | R] or [R | y] in one N = 192 product; odd chunks
+  // mirror the order of the stacked B operands in shared memory to match.
+  constexpr uint32_t cR = 0, cDR = 256;
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 4, kTmemCols);
-  state_load(p, c, bh, cDR);
+  if (!mw) state_load(p, c, bh, cDR, cg * 32, 32);
+  const uint32_t lane_cols = c.tb + c.my + cg * 32;   // a worker's 32 columns of R / R fp32
 
-  // record groups issued and waited for (issued counted by every thread, waits
-  // by warp 0: their difference is what a failed exit still waits for)
+  // record groups issued and waited for, counted by the copy warp only
   int issued[4] = {0, 0, 0, 0}, done[4] = {0, 0, 0, 0};
-  auto load = [&](int g, int ch) {      // group g of chunk ch into the same offsets of shared memory
-    if (c.tid == 0) {
-      uint32_t begin, end;
-      group_range(g, begin, end);
+  // group g of chunk ch; groups 1, 2 put their two operands in chunk-parity order
+  auto load = [&](int g, int ch) {
+    if (issuer) {
       const unsigned char* rec = record(p, slot0 + ch, c.h);
-      ptx::mbar_arrive_expect_tx(&bars[g], end - begin);
-      for (uint32_t off = begin; off < end; off += 16384)
-        ptx::bulk_g2s(sm + off, rec + off, end - off < 16384 ? end - off : 16384, &bars[g]);
+      const bool odd = ch & 1;
+      if (g == 1) {
+        ptx::mbar_arrive_expect_tx(&bars[1], 2 * kC * kD * 4);
+        unsigned char* dw = sm + kScanG1 + (odd ? kC * kD * 4 : 0);
+        unsigned char* dq = sm + kScanG1 + (odd ? 0 : kC * kD * 4);
+        for (uint32_t off = 0; off < kC * kD * 4; off += 16384) {
+          ptx::bulk_g2s(dw + off, rec + kRecW + off, 16384, &bars[1]);
+          ptx::bulk_g2s(dq + off, rec + kRecQ + off, 16384, &bars[1]);
+        }
+      } else if (g == 2) {
+        ptx::mbar_arrive_expect_tx(&bars[2], kC * kC * 4 + kD * kC * 4);
+        unsigned char* dm = sm + kScanG2 + (odd ? kD * kC * 4 : 0);
+        unsigned char* dk = sm + kScanG2 + (odd ? 0 : kC * kC * 4);
+        ptx::bulk_g2s(dm, rec + kRecM, kC * kC * 4, &bars[2]);
+        for (uint32_t off = 0; off < kD * kC * 4; off += 16384)
+          ptx::bulk_g2s(dk + off, rec + kRecKh + off, 16384, &bars[2]);
+      } else {
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive_expect_tx(&bars[3], kRecBytes - kRecU);
+        for (uint32_t off = kRecU; off < kRecBytes; off += 16384)
+          ptx::bulk_g2s(sm + off, rec + off, kRecBytes - off < 16384 ? kRecBytes - off : 16384, &bars[3]);
+      }
     }
-    ++issued[g];
+    if (mw) ++issued[g];
   };
-  // warp 0 waits for group g of chunk ch; the CTA agrees on the outcome
-  auto landed = [&](int g, int ch) -> bool {
-    bool ok = true;
-    if (c.warp == 0) {
-      ok = ptx::mbar_wait(&bars[g], ch & 1);
-      done[g] += ok;
-    }
+  // the copy warp waits for group g of chunk ch (true elsewhere)
+  auto wait_group = [&](int g, int ch) -> bool {
+    if (!mw) return true;
+    const bool ok = ptx::mbar_wait(&bars[g], ch & 1);
+    done[g] += ok;
+    return ok;
+  };
+  // MMA completion: the copy warp polls, the CTA agrees (false if it gave up)
+  auto mma_done = [&](bool ok_in) -> bool {
+    bool ok = ok_in;
+    if (mw) ok = ptx::mbar_wait(c.bar, c.phase) && ok;
+    c.phase ^= 1u;
     const bool all = !__syncthreads_or(!ok);
+    tc::fence_after_sync();
     return all;
   };
-  // U0^T of chunk ch into the U^T accumulator, R -> tf32 operand and g_last R
-  auto stage = [&]() {
+  // R (fp32 master) -> tf32 operand copy, or R *= gl in place (a worker's 32 columns)
+  auto r_pass = [&](bool to_tf32, float gl) {
+    float v[16], w[16];
+    tc::tmem_ld16(lane_cols + cDR, v);
+    tc::tmem_ld16(lane_cols + cDR + 16, w);
+    tc::tmem_ld_wait();
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      float u[16];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float4 f = sU0[(c.half * 8 + h2 * 4 + e) * kD + c.row];
-        u[4 * e] = f.x; u[4 * e + 1] = f.y; u[4 * e + 2] = f.z; u[4 * e + 3] = f.w;
-      }
-      tc::tmem_st16(c.tb + cU + c.my + c.half * 32 + h2 * 16, u);
+    for (int i = 0; i < 16; ++i) {
+      v[i] = to_tf32 ? tc::to_tf32(v[i]) : v[i] * gl;
+      w[i] = to_tf32 ? tc::to_tf32(w[i]) : w[i] * gl;
     }
-    phase_r_update(c, sSc[0], cR, cDR);      // ends with tcgen05.wait::st
+    tc::tmem_st16(lane_cols + (to_tf32 ? cR : cDR), v);
+    tc::tmem_st16(lane_cols + (to_tf32 ? cR : cDR) + 16, w);
+  };
+  // U^T = (R (-W)^T from TMEM) + U0^T (shared memory) -> tf32 rows of the U^T operand
+  auto epi_u = [&](uint32_t col_u) {
+    float u[16];
+    tc::tmem_ld16(c.tb + col_u + c.my + cg * 16, u);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 f = sU0[(cg * 4 + e / 4) * kD + c.row];
+      *reinterpret_cast<float4*>(at(sU, c.row, cg * 16 + e, kSbo64)) =
+          make_float4(tc::to_tf32(u[e] + f.x), tc::to_tf32(u[e + 1] + f.y), tc::to_tf32(u[e + 2] + f.z),
+                      tc::to_tf32(u[e + 3] + f.w));
+    }
+    ptx::fence_proxy_async_smem();
+  };
+  // o rows of chunk ch from y^T: a worker's dv = row, tokens cg*16 + part*8 .. +7
+  auto epi_o = [&](int ch, int part) {
+    const uint32_t col_y = (ch & 1) ? 384 : 192;
+    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    float y[8];
+    tc::tmem_ld8(c.tb + col_y + c.my + cg * 16 + part * 8, y);
+    tc::tmem_ld_wait();
+    const size_t orow = static_cast<size_t>(p.Hv) * kD;
+    const int tok = cg * 16 + part * 8;
+    const size_t base = (static_cast<size_t>(t0 + tok) * p.Hv + c.h) * kD + c.row;
+    const int nv = nvalid - tok;
+    if (p.flags & GDN_F_O_BF16) {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < nv) o[i * orow] = __float2bfloat16_rn(y[i]);
+    } else {
+      float* o = static_cast<float*>(p.o) + base;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < nv) o[i * orow] = y[i];
+    }
   };
 
   bool failed = false;
@@ -981,92 +1055,81 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ChunkPara
     load(1, 0);
     load(2, 0);
     load(3, 0);
-    if (landed(3, 0)) {
-      tc::fence_after_sync();
-      stage();
-    } else {
-      failed = true;
+    if (!mw) {
+      r_pass(true, 1.f);                  // tf32(R_0)
+      tc::tmem_st_wait();
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (!failed && n_chunks > 1) {
-      if (c.tid == 0) ptx::fence_proxy_async_smem();
-      load(3, 1);
-    }
   }
   for (int ch = 0; ch < n_chunks && !failed; ++ch) {
-    const long long t0 = s0 + static_cast<long long>(ch) * kC;
-    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-    // (d) U^T = U0^T - R W^T,  (e1) y^T = R Qs^T
-    bool ok = true;
-    if (c.warp == 0) {
-      ok = ptx::mbar_wait(&bars[1], ch & 1);
-      done[1] += ok;
-      if (c.lane == 0) {
-        if (ok) {
-          tc::fence_after_sync();
-          const uint32_t idd = tc::instr_desc(tc::kTF32, 128, kC, /*neg_a=*/true);
-          const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
-          for (int j = 0; j < kD / 8; ++j)
-            tc::mma_ts_tf32(c.tb + cU, c.tb + cR + j * 8, desc(sW, j * 256, kSbo128), idd, 1);
-          for (int j = 0; j < kD / 8; ++j)
-            tc::mma_ts_tf32(c.tb + cY, c.tb + cR + j * 8, desc(sQ, j * 256, kSbo128), id64, j > 0);
-        }
-        tc::mma_commit(c.bar);       // with no MMA issued it arrives at once
-      }
+    const bool odd = ch & 1;
+    const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
+    const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
+    const uint32_t col_u = odd ? 448 : 128;
+    // -W | Qs and U0^T | g_last of this chunk in shared memory
+    bool ok = wait_group(1, ch);
+    ok = wait_group(3, ch) && ok;
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc::fence_after_sync();
+    GDN_TICK(29);
+    if (issuer) {              // first batch: [U | y] = R [-W; Qs]^T (U0^T is added in the epilogue)
+      const uint32_t id = tc::instr_desc(tc::kTF32, 128, 2 * kC);
+      for (int j = 0; j < kD / 8; ++j)
+        tc::mma_ts_tf32(c.tb + col_b1, c.tb + cR + j * 8, desc(sm + kScanG1, j * 256, kSbo128), id, j > 0);
+      tc::mma_commit(c.bar);
+    } else if (!mw) {          // under it: R *= g_last(ch) for the update, half of the previous o
+      r_pass(false, sSc[0]);
+      if (ch > 0) epi_o(ch - 1, 0);
+      tc::tmem_st_wait();
     }
-    if (!mma_wait(c, ok)) { failed = true; break; }
+    tc::fence_before_sync();
+    if (!mma_done(true)) { failed = true; break; }
     GDN_TICK(24);
     if (ch + 1 < n_chunks) load(1, ch + 1);
-    phase_epi_d(c, cU, sU);
+    if (!mw) epi_u(col_u);
+    ok = wait_group(2, ch);
+    tc::fence_before_sync();
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc::fence_after_sync();
     GDN_TICK(25);
-    // (e2) y^T += U^T M^T,  (f) R += U^T K-hat
-    ok = true;
-    if (c.warp == 0) {
-      ok = ptx::mbar_wait(&bars[2], ch & 1);
-      done[2] += ok;
-      if (c.lane == 0) {
-        if (ok) {
-          tc::fence_after_sync();
-          const uint32_t id64 = tc::instr_desc(tc::kTF32, 128, kC);
-          const uint32_t id128 = tc::instr_desc(tc::kTF32, 128, kD);
-          for (int j = 0; j < kC / 8; ++j)
-            tc::mma_ss<tc::kTF32>(c.tb + cY, desc(sU, j * 256, kSbo64), desc(sMm, j * 256, kSbo64), id64, 1);
-          for (int j = 0; j < kC / 8; ++j)
-            tc::mma_ss<tc::kTF32>(c.tb + cDR, desc(sU, j * 256, kSbo64), desc(sKh, j * 256, kSbo64), id128, 1);
-        }
-        tc::mma_commit(c.bar);
-      }
+    if (issuer) {              // second batch: [y | R] += U^T [M; K-hat^T]^T
+      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC + kD);
+      for (int j = 0; j < kC / 8; ++j)
+        tc::mma_ss<tc::kTF32>(c.tb + col_b2, desc(sU, j * 256, kSbo64), desc(sm + kScanG2, j * 256, kSbo64), id, 1);
+      tc::mma_commit(c.bar);
+    } else if (!mw && ch > 0) {
+      epi_o(ch - 1, 1);        // under it: the other half of the previous o
     }
-    if (!mma_wait(c, ok)) { failed = true; break; }
+    if (ch + 1 < n_chunks) load(3, ch + 1);
+    tc::fence_before_sync();
+    if (!mma_done(true)) { failed = true; break; }
     GDN_TICK(26);
-    if (ch + 1 < n_chunks) load(2, ch + 1);
-    // o of this chunk; U0^T and the state operands of the next
-    phase_epi_e(p, c, cY, t0, nvalid);
-    GDN_TICK(27);
     if (ch + 1 < n_chunks) {
-      if (!landed(3, ch + 1)) { failed = true; break; }
-      tc::fence_after_sync();
-      stage();
+      load(2, ch + 1);
+      if (!mw) {
+        r_pass(true, 1.f);                // tf32(R_{ch+1}) for the next first batch
+        tc::tmem_st_wait();
+      }
     }
     tc::fence_before_sync();
     __syncthreads();
-    GDN_TICK(28);
-    if (ch + 2 < n_chunks) {
-      if (c.tid == 0) ptx::fence_proxy_async_smem();
-      load(3, ch + 2);
-    }
+    GDN_TICK(27);
+  }
+  if (!failed && n_chunks > 0 && !mw) {
+    epi_o(n_chunks - 1, 0);
+    epi_o(n_chunks - 1, 1);
   }
   if (failed) {
     // bounded waits for the MMA and the bulk copies still in flight
     if (c.tid == 0) atomicExch(p.err, 1);
-    if (c.warp == 0) {
+    if (mw) {
       ptx::mbar_wait(c.bar, c.phase ^ 1u);
       for (int g = 1; g <= 3; ++g)
         if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
     }
-  } else {
-    state_store(p, c, bh, cDR);
+  } else if (!mw) {
+    state_store(p, c, bh, cDR, cg * 32, 32);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1162,7 +1225,7 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
     rc = cuda_status(cudaGetLastError(), "chunk prep launch");
     if (rc != GDN_OK) return rc;
   }
-  chunk_scan_kernel<<<static_cast<unsigned>(p.B * p.Hv), kThreads, kScanSmem, st>>>(p);
+  chunk_scan_kernel<<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
   return cuda_status(cudaGetLastError(), "chunk scan launch");
 }
 

@@ -3,7 +3,8 @@
 // N x K) through tcgen05.mma with the accumulator in tensor memory, using the
 // same shared-memory layout, descriptors and TMEM load/store helpers as the
 // prefill kernel.  Modes: tf32 or bf16 operands, A negated by the instruction
-// descriptor, A read from tensor memory instead of shared memory.
+// descriptor, A read from tensor memory instead of shared memory, MN-major
+// operands, D at a column offset of 64 and/or 128 (N up to 256).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -13,7 +14,7 @@
 namespace gdn {
 namespace {
 
-constexpr int kSelfTestCols = 256;   // TMEM columns: D in [0,128), A in [128,256)
+constexpr int kSelfTestCols = 512;   // TMEM columns: D from column 0, 64, 128 or 192; A in [384,512)
 
 __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                             float* __restrict__ D, int N, int K, int mode,
@@ -60,8 +61,8 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t base = *slot;
-  const uint32_t tD = base;
-  const uint32_t tA = base + 128;
+  const uint32_t tD = base + ((mode & 32) ? 64 : 0) + ((mode & 64) ? 128 : 0);
+  const uint32_t tA = base + 384;
 
   if (mode & 4) {       // A into tensor memory: row r = lane r, one tf32 per column
     for (int c = 0; c < K; c += 16) {
@@ -121,15 +122,17 @@ using namespace gdn;
 extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                                  int* status, void* stream) {
   clear_error();
-  if (mode & ~31) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~31);
+  if (mode & ~127) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~127);
   if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
   if ((mode & 4) && (mode & 8)) return fail(GDN_ERR_FLAGS, "A from tensor memory has no MN-major form");
   // MN-major operands are exercised with bf16 only: on sm_100a with this
   // toolchain kind::tf32 with an MN-major operand completed with an all-zero
   // result, so no kernel of this library uses that combination.
   if ((mode & 24) && !(mode & 1)) return fail(GDN_ERR_FLAGS, "MN-major operands are tested with bf16 only");
-  if (N < 16 || N > 128 || N % 16 || K < 16 || K > 128 || K % 16)
-    return fail(GDN_ERR_SHAPE, "N=%d K=%d: need multiples of 16 in [16, 128]", N, K);
+  const int dcol = ((mode & 32) ? 64 : 0) + ((mode & 64) ? 128 : 0);
+  if (N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16 || dcol + N > 384)
+    return fail(GDN_ERR_SHAPE, "N=%d K=%d at column %d: need multiples of 16, N <= 256, K <= 128, D below column 384",
+                N, K, dcol);
   if (!A || !B || !D || !status) return fail(GDN_ERR_NULL, "A, B, D and status are required");
   if (!aligned(A, 4) || !aligned(B, 4) || !aligned(D, 4) || !aligned(status, 4))
     return fail(GDN_ERR_ALIGN, "buffers must be 4-byte aligned");

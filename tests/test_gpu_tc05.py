@@ -44,3 +44,18 @@ def test_tf32_mn_major_is_refused():
     with pytest.raises(G.GdnError) as e:
         G.tc05_selftest(A, B, a_mn=True)
     assert e.value.code == G.GDN_ERR_FLAGS
+
+
+@pytest.mark.parametrize("N,K,mode,d_col", [(128, 128, "tmem", 128), (192, 64, "tf32", 192), (192, 64, "tf32", 0),
+                                            (256, 32, "tf32", 128), (128, 128, "tmem", 0), (64, 128, "tmem", 192)])
+def test_tc05_wide_n_and_column_offsets(N, K, mode, d_col):
+    """The accumulator shapes of the split prefill's scan kernel: N = 128 with
+    A from tensor memory and N = 192 from shared memory, at column offsets."""
+    g = torch.Generator(device="cuda").manual_seed(N * 7 + K + d_col)
+    A = tf32(torch.randn((128, K), generator=g, device="cuda"))
+    B = tf32(torch.randn((N, K), generator=g, device="cuda"))
+    D, st = G.tc05_selftest(A, B, a_in_tmem=(mode == "tmem"), d_col=d_col)
+    torch.cuda.synchronize()
+    ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
+    assert int(st.item()) == 0
+    assert O.rel_err(D.cpu().numpy(), ref) < 1e-5
