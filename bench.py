@@ -44,6 +44,9 @@ import torch  # noqa: E402
 METRIC = "GDN decode state HBM GB/s vs ~8 TB/s; chunked prefill tokens/s at 1/2/4/8 GPU"
 D = 128
 HK, HV = 16, 48
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one recurrent_kernel launch
+# at B = 256, 48 value heads (810,676,992 + 748,824,832 bytes)
+DECODE_TRAFFIC_B256 = 810676992 + 748824832
 STATE_BYTES = D * D * 4                   # one (Dv, Dk) fp32 head state
 
 
@@ -282,11 +285,17 @@ def run_ours(args, world, rank, local):
     launch_ms = statistics.mean(durs)
     per_launch = 2 * Bg * hv * STATE_BYTES
     achieved = per_launch / (launch_ms * 1e-3) / 1e9
+    # dram bytes of one launch from an ncu capture (--traffic overrides): the
+    # B = 256 value was measured on this kernel at this shape (profile
+    # recurrent_kernel_decode_b256_traffic.md); other shapes report null
+    traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
+    if traffic is None and Bg == 256 and hv == HV:
+        traffic, traffic_src = DECODE_TRAFFIC_B256, "ncu dram__bytes_read.sum + dram__bytes_write.sum, B=256 launch"
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
                 "frac_of_8TBps": round(achieved / 8000.0, 4),
                 "kernel": "recurrent_kernel", "bytes_per_launch": per_launch,
-                "launch_ms": round(launch_ms, 5), "traffic": args.traffic}
+                "launch_ms": round(launch_ms, 5), "traffic": traffic, "traffic_source": traffic_src}
 
     # --- batch sweep (B in {1, 16, 64, 256})
     sweep = {}
