@@ -286,10 +286,10 @@ def run_ours(args, world, rank, local):
     per_launch = 2 * Bg * hv * STATE_BYTES
     achieved = per_launch / (launch_ms * 1e-3) / 1e9
     # dram bytes of one launch from an ncu capture (--traffic overrides): the
-    # B = 256 value was measured on this kernel at this shape (profile
-    # recurrent_kernel_decode_b256_traffic.md); other shapes report null
+    # value for 256 sequences x 48 heads of state per launch was measured on
+    # this kernel at that shape; other shapes report null
     traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
-    if traffic is None and Bg == 256 and hv == HV:
+    if traffic is None and per_launch == 2 * 256 * HV * STATE_BYTES:   # same bytes at every shard split
         traffic, traffic_src = DECODE_TRAFFIC_B256, "ncu dram__bytes_read.sum + dram__bytes_write.sum, B=256 launch"
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
