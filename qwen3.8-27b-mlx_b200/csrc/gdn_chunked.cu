@@ -497,57 +497,46 @@ __device__ __forceinline__ void phase_epi_a(Ctx& c, uint32_t col, unsigned char*
   __syncthreads();
 }
 
-// T^-1 = (I + A)^-1: 16x16 diagonal blocks by substitution, then block
-// diagonals X_ij = -X_ii sum_{k=j}^{i-1} A_ik X_kj on plain arrays (row
-// stride 65), finally rounded to tf32 into the operand layout.
+// T^-1 = (I + A)^-1 by forward substitution on all 64 columns at once:
+// warps 2s, 2s+1 hold rows 16s .. 16s+15 of the 64 columns (one column per
+// thread, in registers).  Row segments are solved in order -- an in-block
+// substitution, then the rows go to X -- and as soon as segment s is in X
+// every later segment subtracts its contribution, so the critical path is
+// four 16-step substitutions and three 16 x 16 updates.  fp32 throughout;
+// X is exactly lower triangular with a unit diagonal.
 __device__ __forceinline__ void phase_solve(Ctx& c) {
-  float* sA = c.sA;
+  const float* sA = c.sA;
   float* sX = c.sX;
-  float* sY = c.sY;
-  if (c.tid < kC) {
-    const int blk = c.tid >> 4, cc = c.tid & 15;
-    const float* Ab = sA + (blk * 16) * kPad + blk * 16;
-    float col[16];
+  const int seg = c.warp >> 1;
+  const int j = ((c.warp & 1) << 5) + c.lane;
+  float b[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) col[r] = (r == cc) ? 1.f : 0.f;
+  for (int r = 0; r < 16; ++r) b[r] = (seg * 16 + r == j) ? 1.f : 0.f;
+  for (int step = 0; step < 4; ++step) {
+    if (seg == step) {
+      const float* Ab = sA + (seg * 16) * kPad + seg * 16;
 #pragma unroll
-    for (int r = 1; r < 16; ++r) {
-      if (r > cc) {
-        float s = 0.f;
+      for (int r = 0; r < 16; ++r) {
 #pragma unroll
-        for (int m = 0; m < r; ++m)
-          if (m >= cc) s += Ab[r * kPad + m] * col[m];
-        col[r] = -s;
+        for (int i = r + 1; i < 16; ++i) b[i] -= Ab[i * kPad + r] * b[r];
       }
-    }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) sX[(blk * 16 + r) * kPad + blk * 16 + cc] = col[r];
-  }
-  __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    const int nt = 4 - d;
-    for (int e = c.tid; e < nt * 256; e += kThreads) {
-      const int t = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bj = t, bi = t + d;
-      const float* Ar = sA + (bi * 16 + r) * kPad;
-      float y = 0.f;
-      for (int kb = bj; kb < bi; ++kb) {
-#pragma unroll
-        for (int m = 0; m < 16; ++m) y += Ar[kb * 16 + m] * sX[(kb * 16 + m) * kPad + bj * 16 + cc];
-      }
-      sY[e] = y;
+      for (int r = 0; r < 16; ++r) sX[(seg * 16 + r) * kPad + j] = b[r];
     }
     __syncthreads();
-    for (int e = c.tid; e < nt * 256; e += kThreads) {
-      const int t = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bj = t, bi = t + d;
-      const float* Xr = sX + (bi * 16 + r) * kPad + bi * 16;
-      float x = 0.f;
+    if (seg > step) {
+      float x[16];
 #pragma unroll
-      for (int m = 0; m < 16; ++m) x += Xr[m] * sY[(t << 8) + (m << 4) + cc];
-      sX[(bi * 16 + r) * kPad + bj * 16 + cc] = -x;
+      for (int m = 0; m < 16; ++m) x[m] = sX[(step * 16 + m) * kPad + j];
+      const float* Ab = sA + (seg * 16) * kPad + step * 16;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc += Ab[r * kPad + m] * x[m];
+        b[r] -= acc;
+      }
     }
-    __syncthreads();
   }
   {
     const int i = c.tid >> 2;
