@@ -69,15 +69,16 @@ constexpr int kThreads = 256;   // 8 warps: warp w owns TMEM lane quarter w % 4,
 // stores hit distinct banks
 constexpr uint32_t kSbo128 = (kD * 4 / 16) * 128;   // 8-row group stride of 128-wide fp32 rows
 constexpr uint32_t kSbo64 = (kC * 4 / 16) * 128;    // ... of 64-wide fp32 rows
-constexpr int kPad = kC + 1;                        // row stride of the plain solve arrays
+constexpr int kPad = kC + 1;                        // row stride of X (plain)
+constexpr int kPadA = kC + 4;                       // row stride of A^T (plain, 16-byte rows)
 constexpr uint32_t kOffKQ = 0;                      // [K; Q] rows            128 x 128 (64 KiB)
 constexpr uint32_t kOffKt = kOffKQ + 128 * kD * 4;  // K^T, scaled            128 x 64  (32 KiB)
 constexpr uint32_t kOffVt = kOffKt + kD * kC * 4;   // V^T diag(beta), U^T    128 x 64  (32 KiB)
 constexpr uint32_t kOffTi = kOffVt + kD * kC * 4;   // T^-1                    64 x 64  (16 KiB)
 constexpr uint32_t kOffM = kOffTi + kC * kC * 4;    // M (must follow T^-1)    64 x 64  (16 KiB)
 constexpr uint32_t kOffW = kOffM + kC * kC * 4;     // W rows 64 x 128 (32 KiB); X during the solve
-constexpr uint32_t kOffA = kOffW + kC * kD * 4;     // A, plain, row stride 65
-constexpr uint32_t kOffY = kOffA + kC * kPad * 4;   // solve temporaries 3 x 16 x 16
+constexpr uint32_t kOffA = kOffW + kC * kD * 4;     // A^T, plain, row stride 68
+constexpr uint32_t kOffY = kOffA + kC * kPadA * 4;  // solve temporaries 3 x 16 x 16
 constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 10 x 64
 constexpr uint32_t kOffBar = kOffSc + 10 * kC * 4;  // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
@@ -85,8 +86,8 @@ constexpr uint32_t kSmemBytes = kOffBar + 64;
 // shared memory map of the prep kernel: regions are reused as the phases go,
 // so that two CTAs fit on an SM
 constexpr uint32_t kPKQ = 0;                        // [K; Q] rows 128 x 128, until (a) and its epilogue
-constexpr uint32_t kPA = 0;                         // A, plain, over the K rows once (a) has run
-constexpr uint32_t kPY = kPA + kC * kPad * 4;       // solve temporaries
+constexpr uint32_t kPA = 0;                         // A^T, plain, over the K rows once (a) has run
+constexpr uint32_t kPY = kPA + kC * kPadA * 4;      // solve temporaries
 constexpr uint32_t kPX = 32768;                     // X, plain, over the Q rows once they are read
 constexpr uint32_t kPKt = 0;                        // K^T diag(beta g r_k) 128 x 64, after the solve
 constexpr uint32_t kPVt = 32768;                    // V^T diag(beta) 128 x 64, after the solve
@@ -464,11 +465,11 @@ __device__ __forceinline__ void phase_epi_a(Ctx& c, uint32_t col, unsigned char*
     const int i = c.row;
     const float fi = c.s_beta[i] * c.s_rk[i];
     const float gi = c.s_gam[i];
-    float* Ar = c.sA + i * kPad + c.half * 32;
+    float* Ac = c.sA + (c.half * 32) * kPadA + i;     // A^T: column i of row j at j * kPadA + i
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       const int j = c.half * 32 + e;
-      Ar[e] = (j < i) ? fi * c.s_rk[j] * __expf(gi - c.s_gam[j]) * gp[e] : 0.f;
+      Ac[e * kPadA] = (j < i) ? fi * c.s_rk[j] * __expf(gi - c.s_gam[j]) * gp[e] : 0.f;
     }
   } else {
     const int i = c.row - kC;
@@ -514,27 +515,37 @@ __device__ __forceinline__ void phase_solve(Ctx& c) {
   for (int r = 0; r < 16; ++r) b[r] = (seg * 16 + r == j) ? 1.f : 0.f;
   for (int step = 0; step < 4; ++step) {
     if (seg == step) {
-      const float* Ab = sA + (seg * 16) * kPad + seg * 16;
+      // A[16 seg + i][16 seg + r] = A^T[16 seg + r][16 seg + i], read 4 rows i at a time
+      const float* At = sA + (seg * 16) * kPadA + seg * 16;
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
+        float a[16];
 #pragma unroll
-        for (int i = r + 1; i < 16; ++i) b[i] -= Ab[i * kPad + r] * b[r];
+        for (int q = 0; q < 4; ++q) {
+          const float4 f = *reinterpret_cast<const float4*>(At + r * kPadA + 4 * q);
+          a[4 * q] = f.x; a[4 * q + 1] = f.y; a[4 * q + 2] = f.z; a[4 * q + 3] = f.w;
+        }
+#pragma unroll
+        for (int i = r + 1; i < 16; ++i) b[i] -= a[i] * b[r];
       }
 #pragma unroll
       for (int r = 0; r < 16; ++r) sX[(seg * 16 + r) * kPad + j] = b[r];
     }
     __syncthreads();
     if (seg > step) {
-      float x[16];
+      // b_r -= sum_m A[16 seg + r][16 step + m] X[16 step + m][j], A^T rows m read 4 r at a time
+      const float* At = sA + (step * 16) * kPadA + seg * 16;
 #pragma unroll
-      for (int m = 0; m < 16; ++m) x[m] = sX[(step * 16 + m) * kPad + j];
-      const float* Ab = sA + (seg * 16) * kPad + step * 16;
+      for (int m = 0; m < 16; ++m) {
+        const float x = sX[(step * 16 + m) * kPad + j];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) acc += Ab[r * kPad + m] * x[m];
-        b[r] -= acc;
+        for (int q = 0; q < 4; ++q) {
+          const float4 f = *reinterpret_cast<const float4*>(At + m * kPadA + 4 * q);
+          b[4 * q] -= f.x * x;
+          b[4 * q + 1] -= f.y * x;
+          b[4 * q + 2] -= f.z * x;
+          b[4 * q + 3] -= f.w * x;
+        }
       }
     }
   }
