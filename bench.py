@@ -439,19 +439,24 @@ class PrefillLayer:
         self.o = torch.empty((self.N, hv, D), dtype=torch.float32, device=device)
         self.S = torch.empty((self.B, hv, D, D), dtype=torch.float32, device=device)
         self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
-        self.split = False
+        self.schedule = "fused"
         self.ws = None
         if split:
-            self.use_split(True)
+            self.use_schedule("split")
 
-    def use_split(self, on):
-        """Run the chunked step as gdn_chunked_fwd_ws (prep + scan launches on a
-        workspace allocated here, outside any timed region) or gdn_chunked_fwd."""
+    def use_schedule(self, schedule):
+        """fused: gdn_chunked_fwd then the gated norm; split: gdn_chunked_fwd_ws
+        (prep + scan on a workspace allocated here, outside any timed region)
+        then the norm; split_norm: gdn_chunked_norm_fwd_ws, the norm fused
+        into the scan (no separate norm launch)."""
         import gdn_b200 as G
-        self.split = bool(on)
-        if self.split and self.ws is None:
+        self.schedule = schedule
+        if schedule != "fused" and self.ws is None:
             need = G.chunked_workspace_bytes(self.B, self.T, self.hv, not self.uniform)
             self.ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
+
+    def use_split(self, on):
+        self.use_schedule("split" if on else "fused")
 
     def _cu(self):
         return None if self.uniform else ctypes.c_void_p(self.cu.data_ptr())
@@ -472,7 +477,13 @@ class PrefillLayer:
         q = ctypes.c_void_p(base)
         k = ctypes.c_void_p(base + hk * D * 2)
         v = ctypes.c_void_p(base + 2 * hk * D * 2)
-        if self.split:
+        if self.schedule == "split_norm":
+            rc = lib.gdn_chunked_norm_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log),
+                                             P(self.dt_bias), None, P(self.S), P(self.z), self.hv * D,
+                                             P(self.gamma), ctypes.c_float(1e-6), P(self.out), self.hv * D, 0,
+                                             self._cu(), self.B, self.T, hk, self.hv, D, D, G.F_QK_L2NORM,
+                                             P(self.ws), self.ws.numel(), h)
+        elif self.schedule == "split":
             rc = lib.gdn_chunked_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
                                         None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
                                         G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
@@ -484,6 +495,8 @@ class PrefillLayer:
             raise RuntimeError(lib.gdn_last_error().decode())
 
     def norm(self, lib, h):
+        if self.schedule == "split_norm":
+            return                         # fused into the scan
         P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         rc = lib.gdn_gated_rmsnorm_fwd(P(self.o), P(self.z), P(self.gamma), P(self.out),
                                        self.N * self.hv, D, ctypes.c_float(1e-6), 0, h)
@@ -538,7 +551,18 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
         durs["conv"].append(ev[0].elapsed_time(ev[1]))
         durs["chunked"].append(ev[1].elapsed_time(ev[2]))
         durs["norm"].append(ev[2].elapsed_time(ev[3]))
-    return ms, {k: statistics.mean(v) for k, v in durs.items()}
+    kms = {k: statistics.mean(v) for k, v in durs.items()}
+    if gathered is not None:
+        # the same layer without the all-gather (recurrence throughput alone), max over ranks
+        barrier(world)
+        e0.record(st)
+        for _ in range(steps):
+            X.step(lib, h)
+        e1.record(st)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        kms["layer_without_gather"] = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    return ms, kms
 
 
 def run_prefill(args, lib, device, world):
@@ -554,7 +578,7 @@ def run_prefill(args, lib, device, world):
     cases = [("config3", [args.prefill_T])]
     if not args.no_config4:
         cases.append(("config4", config4_lengths()))
-    schedules = ["fused", "split"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
+    schedules = ["fused", "split", "split_norm"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
     for name, lens in cases:
         X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
         gathered = None
@@ -563,13 +587,14 @@ def run_prefill(args, lib, device, world):
         steps = max(2, args.steps // 10) if name == "config4" else max(3, args.steps // 5)
         timed = {}
         for sched in schedules:          # every rank times every schedule, in the same order
-            X.use_split(sched == "split")
+            X.use_schedule(sched)
             timed[sched] = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1)
                                               if name == "config4" else max(args.warmup, 3), gathered)
         best = min(timed, key=lambda k: timed[k][0])
         ms, kms = timed[best]
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
-        kernel = "chunk_prep_kernel + chunk_scan_kernel" if best == "split" else "chunked_kernel"
+        kernel = {"fused": "chunked_kernel", "split": "chunk_prep_kernel + chunk_scan_kernel",
+                  "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>"}[best]
         res[name] = {
             "schedule": best,
             "ms_per_layer_by_schedule": {k: round(v[0], 4) for k, v in timed.items()},
@@ -578,6 +603,8 @@ def run_prefill(args, lib, device, world):
                          f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
                          + (" -> NCCL all-gather" if world > 1 else "")),
             "tokens_per_s": round(X.N / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+            **({"tokens_per_s_without_gather": round(X.N / (kms["layer_without_gather"] * 1e-3), 1)}
+               if "layer_without_gather" in kms else {}),
             "kernel_ms": {k: round(v, 4) for k, v in kms.items()},
             "roofline": {"bound": "tensor", "kernel": kernel, "achieved": round(achieved, 2),
                          "peak": tf_peak, "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
@@ -699,7 +726,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
-    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split"], default="auto",
+    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm"], default="auto",
                     help="chunked schedule for configs 3/4; auto times both and reports the faster")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     args = ap.parse_args()

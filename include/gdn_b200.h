@@ -188,6 +188,27 @@ int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
                        const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
                        unsigned flags, void* workspace, size_t workspace_size, void* stream);
 
+/*
+ * gdn_chunked_norm_fwd_ws -- gdn_chunked_fwd_ws with the gated RMSNorm of
+ * gdn_gated_rmsnorm_fwd fused into the scan's epilogue: writes
+ *     out[t*out_stride + (out_head0 + h)*128 + d]
+ *         = bf16( o[t,h,d] * rsqrt(mean_d o[t,h,:]^2 + eps) * gamma[d] * silu(z[t,h,d]) )
+ * instead of o (the reference's norm(o, z), cpp/src/model.cpp:350-354 and
+ * :625-627, python/qwen35.py:159-180).  z: bf16, element (t, h, d) at
+ * z[t*z_stride + h*128 + d]; gamma (128) fp32.  out_stride / out_head0 place
+ * this call's Hv heads inside a wider row (e.g. the all-heads output of a
+ * head-sharded layer).  Flags: GDN_F_QK_L2NORM only.  Other arguments and
+ * the workspace as gdn_chunked_fwd_ws.
+ */
+int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v,
+                            long long q_stride, long long k_stride, long long v_stride,
+                            const float* a, const float* b, const float* A_log, const float* dt_bias,
+                            const float* state_in, float* state_out,
+                            const void* z, long long z_stride, const float* gamma, float eps,
+                            void* out, long long out_stride, int out_head0,
+                            const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                            unsigned flags, void* workspace, size_t workspace_size, void* stream);
+
 /* Size of the fixed device scratch that gdn_chunked_fwd_static uses. */
 #define GDN_CHUNKED_STATIC_SCRATCH_BYTES (64ull << 20)
 

@@ -129,7 +129,8 @@ constexpr uint32_t kScanG1 = 0;
 constexpr uint32_t kScanG2 = kRecM;
 constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
 constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
-constexpr uint32_t kScanSmem = kScanBar + 64;
+constexpr uint32_t kScanNorm = kScanBar + 64;       // fused norm: partial sums of squares, 4 x 64 floats
+constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
 
 __host__ __device__ constexpr size_t records_offset(int B) {
   return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
@@ -156,6 +157,14 @@ struct ChunkParams {
   int32_t* chunk_prefix;          // (B+1) first record slot of each sequence (packed batches)
   long long n_slots;              // record slots (chunks over all sequences, or an upper bound)
   int nch_uniform;                // chunks per sequence when cu == null
+  // gated RMSNorm fused into the scan's epilogue (o is then the bf16 output):
+  // out[t * out_stride + (out_head0 + h) * 128 + d] = rms_norm(o)[d] gamma[d] silu(z[t, h, d])
+  const __nv_bfloat16* z;
+  long long z_stride;             // elements between consecutive tokens of z
+  const float* gamma;
+  float eps;
+  long long out_stride;
+  int out_head0;
 };
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
@@ -922,6 +931,7 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
 constexpr int kScanWorkers = 512;
 constexpr int kScanThreads = kScanWorkers + 32;
 
+template <bool NORM>
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const float4* sU0 = reinterpret_cast<const float4*>(sm + kRecU);
@@ -1025,18 +1035,69 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     }
     ptx::fence_proxy_async_smem();
   };
+  float* s_part = reinterpret_cast<float*>(sm + kScanNorm);   // [lane quarter][token] sums of y^2
+  const float gam = NORM ? __ldg(p.gamma + c.row) : 0.f;
+  // fused norm: z of a worker's 16 tokens of a chunk, loaded a chunk before its
+  // use and left untouched until then (so the loads never stall the chunk)
+  unsigned short z_next[16];
+  uint32_t z_prev[8];                             // packed pairs, filled at the end of the chunk
+  auto load_z = [&](int ch) {
+    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const int nv = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC) - cg * 16;
+    const unsigned short* zp = reinterpret_cast<const unsigned short*>(p.z) + (t0 + cg * 16) * p.z_stride +
+                               c.h * kD + c.row;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) z_next[i] = i < nv ? __ldg(zp + i * p.z_stride) : 0;
+  };
   // o rows of chunk ch from y^T: a worker's dv = row, tokens cg*16 + part*8 .. +7
   auto epi_o = [&](int ch, int part) {
     const uint32_t col_y = (ch & 1) ? 384 : 192;
     const long long t0 = s0 + static_cast<long long>(ch) * kC;
     const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    const int tok = cg * 16 + part * 8;
+    const int nv = nvalid - tok;
     float y[8];
-    tc::tmem_ld8(c.tb + col_y + c.my + cg * 16 + part * 8, y);
+    if constexpr (NORM) {
+      float zz[8];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const uint32_t w = part ? z_prev[4 + i / 2] : z_prev[i / 2];
+        zz[i] = __uint_as_float(w << 16);
+        zz[i + 1] = __uint_as_float(w & 0xffff0000u);
+      }
+      tc::tmem_ld8(c.tb + col_y + c.my + tok, y);
+      tc::tmem_ld_wait();
+      // sum of y^2 over this warp's 32 rows for each of the 8 tokens: halve the
+      // token set per exchange (4 + 2 + 1 shuffles), then finish with 2
+      float s4[4], s2[2], s1v;
+      const bool b4 = c.lane & 16, b3 = c.lane & 8, b2 = c.lane & 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = y[i] * y[i], hi = y[i + 4] * y[i + 4];
+        s4[i] = (b4 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b4 ? lo : hi, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) s2[i] = (b3 ? s4[i + 2] : s4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? s4[i] : s4[i + 2], 8);
+      s1v = (b2 ? s2[1] : s2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s2[0] : s2[1], 4);
+      s1v += __shfl_xor_sync(0xffffffffu, s1v, 2);
+      s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
+      if ((c.lane & 3) == 0) s_part[c.quarter * kC + tok + (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0)] = s1v;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");   // the 4 warps of this column group
+      const size_t base = static_cast<size_t>(t0 + tok) * p.out_stride + static_cast<size_t>(p.out_head0 + c.h) * kD + c.row;
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float ss = s_part[tok + i] + s_part[kC + tok + i] + s_part[2 * kC + tok + i] + s_part[3 * kC + tok + i];
+        const float r = rsqrtf(ss / static_cast<float>(kD) + p.eps);
+        const float sg = __fdividef(1.f, 1.f + __expf(-zz[i]));
+        if (i < nv) o[i * p.out_stride] = __float2bfloat16_rn((y[i] * r * gam) * (zz[i] * sg));
+      }
+      return;
+    }
+    tc::tmem_ld8(c.tb + col_y + c.my + tok, y);
     tc::tmem_ld_wait();
     const size_t orow = static_cast<size_t>(p.Hv) * kD;
-    const int tok = cg * 16 + part * 8;
     const size_t base = (static_cast<size_t>(t0 + tok) * p.Hv + c.h) * kD + c.row;
-    const int nv = nvalid - tok;
     if (p.flags & GDN_F_O_BF16) {
       __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
 #pragma unroll
@@ -1063,6 +1124,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     __syncthreads();
   }
   for (int ch = 0; ch < n_chunks && !failed; ++ch) {
+    if (NORM && !mw) load_z(ch);
     const bool odd = ch & 1;
     const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
     const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
@@ -1115,6 +1177,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     tc::fence_before_sync();
     __syncthreads();
     GDN_TICK(27);
+    if (NORM) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        z_prev[i] = static_cast<uint32_t>(z_next[2 * i]) | (static_cast<uint32_t>(z_next[2 * i + 1]) << 16);
+    }
   }
   if (!failed && n_chunks > 0 && !mw) {
     epi_o(n_chunks - 1, 0);
@@ -1188,7 +1255,7 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
   p = ChunkParams{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                   static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
                   state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err,
-                  nullptr, nullptr, 0, 0};
+                  nullptr, nullptr, 0, 0, nullptr, 0, nullptr, 0.f, 0, 0};
   return GDN_OK;
 }
 
@@ -1212,7 +1279,10 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
   static bool attr_prep[64] = {false}, attr_scan[64] = {false};
   int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kPrepSmem, attr_prep);
   if (rc != GDN_OK) return rc;
-  rc = set_smem_attr(reinterpret_cast<const void*>(chunk_scan_kernel), kScanSmem, attr_scan);
+  static bool attr_scan_norm[64] = {false};
+  const void* scan = p.z ? reinterpret_cast<const void*>(chunk_scan_kernel<true>)
+                         : reinterpret_cast<const void*>(chunk_scan_kernel<false>);
+  rc = set_smem_attr(scan, kScanSmem, p.z ? attr_scan_norm : attr_scan);
   if (rc != GDN_OK) return rc;
   if (packed) {
     chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.chunk_prefix);
@@ -1225,7 +1295,8 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
     rc = cuda_status(cudaGetLastError(), "chunk prep launch");
     if (rc != GDN_OK) return rc;
   }
-  chunk_scan_kernel<<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
+  if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
+  else chunk_scan_kernel<false><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
   return cuda_status(cudaGetLastError(), "chunk scan launch");
 }
 
@@ -1279,6 +1350,45 @@ extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, l
     return fail(GDN_ERR_ALIAS, "workspace overlaps a state or o");
   p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
   if (p.n_slots > 0x7fffffffLL || Hv > 65535) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+  return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
+                                       long long k_stride, long long v_stride, const float* a, const float* b,
+                                       const float* A_log, const float* dt_bias, const float* state_in,
+                                       float* state_out, const void* z, long long z_stride, const float* gamma,
+                                       float eps, void* out, long long out_stride, int out_head0,
+                                       const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                                       unsigned flags, void* workspace, size_t workspace_size, void* stream) {
+  clear_error();
+  if (flags & ~GDN_F_QK_L2NORM) return fail(GDN_ERR_FLAGS, "only GDN_F_QK_L2NORM applies (out is bf16)");
+  ChunkParams p;
+  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, out,
+                        cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags | GDN_F_O_BF16);
+  if (rc != GDN_OK || B == 0) return rc;
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  if (total > 0 && (!z || !gamma)) return fail(GDN_ERR_NULL, "z and gamma are required");
+  if (out_head0 < 0 || out_stride < (static_cast<long long>(out_head0) + Hv) * kD || z_stride < static_cast<long long>(Hv) * kD)
+    return fail(GDN_ERR_SHAPE, "out_stride / out_head0 / z_stride do not fit Hv heads of 128");
+  if (!aligned(z, 2) || !aligned(gamma, 4) || !(eps >= 0.f)) return fail(GDN_ERR_ALIGN, "z, gamma misaligned or eps < 0");
+  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
+  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes)", need);
+  if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");
+  if (workspace_size < need) return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, %zu needed", workspace_size, need);
+  const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * 4;
+  const size_t obytes = total > 0 ? static_cast<size_t>(total - 1) * out_stride * 2 + (out_head0 + Hv) * kD * 2 : 0;
+  if (overlap(workspace, need, state_in, sbytes) || overlap(workspace, need, state_out, sbytes) ||
+      overlap(workspace, need, out, obytes) || overlap(out, obytes, state_in, sbytes) ||
+      overlap(out, obytes, state_out, sbytes))
+    return fail(GDN_ERR_ALIAS, "workspace, out and the states must not overlap");
+  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
+  if (p.n_slots > 0x7fffffffLL || Hv > 65535) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+  p.z = static_cast<const __nv_bfloat16*>(z);
+  p.z_stride = z_stride;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.out_stride = out_stride;
+  p.out_head0 = out_head0;
   return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
 }
 

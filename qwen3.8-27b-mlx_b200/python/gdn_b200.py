@@ -56,6 +56,9 @@ SIGNATURES = {
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_workspace_bytes": [_i] * 4,
     "gdn_chunked_fwd_static": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
+    "gdn_chunked_norm_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 7 + [ctypes.c_longlong, _vp,
+                               ctypes.c_float, _vp, ctypes.c_longlong, _i, _vp] + [_i] * 6
+                               + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_chunked_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6
                           + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_conv_commit": [_vp] * 5 + [_i] * 4 + [_vp],
@@ -201,6 +204,43 @@ def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=Fal
         (16 if b_mn else 0) | (32 if d_col & 64 else 0) | (64 if d_col & 128 else 0)
     check(lib().gdn_tc05_selftest(ptr(A), ptr(B), ptr(D), N, K, mode, ptr(status), stream_ptr(dev)))
     return D, status
+
+
+def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, state_out=None, out=None,
+                     cu_seqlens=None, *, eps=1e-6, l2norm=True, out_head0=0, workspace=None):
+    """Chunked prefill with the gated RMSNorm fused in (gdn_chunked_norm_fwd_ws).
+    q, k, v as chunked_fwd; z (..., Hv, 128) bf16 with contiguous heads;
+    gamma (128,) fp32.  out: bf16 (..., H_out, 128) with H_out >= out_head0 +
+    Hv (allocated as (..., Hv, 128) when None).  Returns (out, state_out)."""
+    Hk, Hv = q.shape[-2], v.shape[-2]
+    for t in (q, k, v, z):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
+            raise ValueError("q, k, v, z must be bf16 with contiguous 128-wide heads")
+    if cu_seqlens is not None:
+        B, T = cu_seqlens.numel() - 1, q.shape[0]
+        lead = (T,)
+    else:
+        B, T = q.shape[0], q.shape[1]
+        lead = (B, T)
+        if B > 1 and (q.stride(0) != T * q.stride(-3) or k.stride(0) != T * k.stride(-3)
+                      or v.stride(0) != T * v.stride(-3) or z.stride(0) != T * z.stride(-3)):
+            raise ValueError("batch rows must follow each other (token-major storage)")
+    dev = _dev(a, b, A_log, dt_bias, z, gamma, state_in, state_out, out, cu_seqlens)
+    if out is None:
+        out = torch.empty(lead + (Hv, D), dtype=torch.bfloat16, device=dev)
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1 or out.stride(-2) != 128:
+        raise ValueError("out must be bf16 with contiguous 128-wide heads")
+    if state_out is None:
+        state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
+    need = chunked_workspace_bytes(B, T, Hv, cu_seqlens is not None)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    check(lib().gdn_chunked_norm_fwd_ws(ptr(q), ptr(k), ptr(v), q.stride(-3), k.stride(-3), v.stride(-3), ptr(a),
+                                        ptr(b), ptr(A_log), ptr(dt_bias), ptr(state_in), ptr(state_out), ptr(z),
+                                        z.stride(-3), ptr(gamma), eps, ptr(out), out.stride(-3), out_head0,
+                                        ptr(cu_seqlens), B, T, Hk, Hv, D, D, F_QK_L2NORM if l2norm else 0,
+                                        ptr(workspace), workspace.numel(), stream_ptr(dev)))
+    return out, state_out
 
 
 def conv1d_fwd(x, w, state_in=None, state_out=None, y=None, cu_seqlens=None, *, bf16_ops=False, silu=True):

@@ -301,3 +301,75 @@ def test_config3_pipeline_conv_chunked_norm(split):
     assert O.rel_l2(host(S), rS) < PREFILL_TOL
     assert O.rel_l2(host(out), rout) < PREFILL_TOL
     assert G.take_device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# chunked recurrence with the gated RMSNorm fused into the scan
+# ---------------------------------------------------------------------------
+
+def norm_inputs(rng, shape):
+    z = O.bf16_round(rng.standard_normal(shape, dtype=np.float32))
+    gamma = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    return z, gamma
+
+
+@pytest.mark.parametrize("lens", [[200, 200], [100, 0, 257, 64, 3]])
+def test_chunked_norm_matches_chunked_then_norm(lens):
+    """gdn_chunked_norm_fwd_ws against gdn_chunked_fwd_ws followed by
+    gdn_gated_rmsnorm_fwd (bf16 out): the same arithmetic but for the order of
+    the sum of squares, so within one bf16 rounding; and against the oracle."""
+    rng = np.random.default_rng(80 + len(lens))
+    Hk, Hv = 2, 6
+    total = sum(lens)
+    packed = len(set(lens)) > 1
+    inp = chunk_inputs(rng, 1, total, Hk, Hv, slow_decay=False)
+    z, gamma = norm_inputs(rng, (total, Hv, 128))
+    S0 = rng.standard_normal((len(lens), Hv, 128, 128), dtype=np.float32) * np.float32(0.05)
+    if packed:
+        cu = dev(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), torch.int32)
+        t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0])  # noqa: E731
+        zz = dev(z, torch.bfloat16)
+    else:
+        cu = None
+        B, T = len(lens), lens[0]
+        t = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]), torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]))  # noqa: E731
+        zz = dev(z.reshape(B, T, Hv, 128), torch.bfloat16)
+    args = (t("q"), t("k"), t("v"), g("a"), g("b"), dev(inp["A_log"]), dev(inp["dt_bias"]))
+    o, S = G.chunked_fwd(*args, state_in=dev(S0), cu_seqlens=cu, split=True)
+    ref = G.gated_rmsnorm_fwd(o, zz, dev(gamma))
+    out, S2 = G.chunked_norm_fwd(*args, zz, dev(gamma), state_in=dev(S0), cu_seqlens=cu)
+    torch.cuda.synchronize()
+    a, r = host(out), host(ref)
+    assert np.max(np.abs(a - r)) <= 2 ** -8 * np.max(np.abs(r)) + 1e-6
+    assert torch.equal(S2, S)
+    # oracle: chunked_delta then the gated norm, per sequence
+    cuh = np.concatenate([[0], np.cumsum(lens)])
+    for s_, L in enumerate(lens):
+        if L == 0:
+            continue
+        sub = {n: inp[n][:, cuh[s_]:cuh[s_ + 1]] for n in ("q", "k", "v", "a", "b")}
+        sub.update(A_log=inp["A_log"], dt_bias=inp["dt_bias"], S0=S0[s_:s_ + 1])
+        ro, _ = oracle_chunked(sub)
+        rout = O.gated_rmsnorm(ro, z[None, cuh[s_]:cuh[s_ + 1]], gamma)
+        got = a.reshape(total, Hv, 128)[cuh[s_]:cuh[s_ + 1]]
+        assert O.rel_l2(got, rout[0]) < PREFILL_TOL + 4e-3, s_
+    assert G.take_device_error() == 0
+
+
+def test_chunked_norm_writes_its_heads_inside_wider_rows():
+    """out_head0 / out_stride place the call's heads inside a wider output row
+    (the head-sharded layout); the other heads of the row are left alone."""
+    rng = np.random.default_rng(90)
+    T, Hk, Hv = 130, 1, 3
+    inp = chunk_inputs(rng, 1, T, Hk, Hv)
+    z, gamma = norm_inputs(rng, (1, T, Hv, 128))
+    t = lambda n: dev(inp[n], torch.bfloat16)  # noqa: E731
+    args = (t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]), dev(inp["dt_bias"]))
+    own, _ = G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]))
+    wide = torch.full((1, T, 12, 128), 3.0, dtype=torch.bfloat16, device="cuda")
+    G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]), out=wide, out_head0=6)
+    torch.cuda.synchronize()
+    assert torch.equal(wide[:, :, 6:9], own)
+    assert bool((wide[:, :, :6] == 3.0).all()) and bool((wide[:, :, 9:] == 3.0).all())
