@@ -315,6 +315,10 @@ def run_ours(args, world, rank, local):
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(seconds=args.cpu_seconds)
 
+    verify = None
+    if not args.no_verify:
+        verify = run_verify_chain(args, lib, device, world, hk, hv, hbm_peak)
+
     prefill = None
     if not args.no_prefill:
         del X
@@ -336,9 +340,114 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
                    "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
-        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu, "prefill": prefill,
+        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill,
     }
     return line
+
+
+VOCAB = 248320          # Qwen3.5/3.8 vocabulary (the verify pass's distributions are over it)
+
+
+def run_verify_chain(args, lib, device, world, hk, hv, hbm_peak, B=32, k=3):
+    """BASELINE config 2 as a device-resident chain per step: the (k+1)-token
+    verify block with checkpoints (gdn_recurrent_fwd), the acceptance test on
+    seeded target/draft distributions over the vocabulary (gdn_spec_verify),
+    the conv-window rollback (gdn_conv_commit) and the next decode step from
+    the accepted checkpoint (gdn_recurrent_fwd_from_ckpt) -- no host read.
+    Reports ms per step (max over ranks), the checkpoint-write bandwidth of
+    the verify kernel and the acceptance kernel's read rate."""
+    import gdn_b200 as G
+    g = torch.Generator(device=device)
+    g.manual_seed(31)
+    T = k + 1
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    def bf(*shape):
+        return torch.randn(shape, generator=g, device=device).bfloat16()
+    q, kk, v = bf(B, T, hk, D), bf(B, T, hk, D), bf(B, T, hv, D)
+    q1, k1, v1 = bf(B, 1, hk, D), bf(B, 1, hk, D), bf(B, 1, hv, D)
+    a = torch.randn((B, T, hv), generator=g, device=device)
+    b = torch.randn((B, T, hv), generator=g, device=device)
+    a1, b1 = torch.randn((B, 1, hv), generator=g, device=device), torch.randn((B, 1, hv), generator=g, device=device)
+    A_log = torch.rand((hv,), generator=g, device=device) * float(np.log(16.0))
+    dtb = torch.rand((hv,), generator=g, device=device)
+    S = torch.randn((B, hv, D, D), generator=g, device=device) * 0.05
+    S_next = torch.empty_like(S)
+    ckpt = torch.empty((B, hv, T, D, D), device=device)
+    o = torch.empty((B, T, hv, D), dtype=torch.bfloat16, device=device)
+    o1 = torch.empty((B, 1, hv, D), dtype=torch.bfloat16, device=device)
+    C = 2 * hk * D + hv * D
+    xw, xb = bf(B, 3, C), bf(B, T, C)
+    conv_next = torch.empty_like(xw)
+    # target and draft distributions that overlap like a real MTP head's (the
+    # draft's logits are the target's plus noise): a few drafts get accepted
+    logits = torch.randn((B, T, VOCAB), generator=g, device=device) * 4
+    pr = torch.softmax(logits, -1)
+    qr = torch.softmax(logits[:, :k] + torch.randn((B, k, VOCAB), generator=g, device=device) * 0.5, -1)
+    draft = torch.multinomial(qr.reshape(-1, VOCAB), 1, generator=g).reshape(B, k).int()
+    ua = torch.rand((B, k), generator=g, device=device)
+    us = torch.rand((B,), generator=g, device=device)
+    acc, commit, tok = (torch.empty(B, dtype=torch.int32, device=device) for _ in range(3))
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    st = torch.cuda.current_stream(device)
+    h = ctypes.c_void_p(st.cuda_stream)
+    flags = G.F_O_BF16
+
+    def chk(rc):
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+
+    def verify():
+        chk(lib.gdn_recurrent_fwd(P(q), P(kk), P(v), P(a), P(b), P(A_log), P(dtb), P(S), None, P(o), P(ckpt),
+                                  B, T, hk, hv, D, D, flags, h))
+
+    def accept():
+        chk(lib.gdn_spec_verify(P(pr), P(qr), P(draft), P(ua), P(us), B, k, VOCAB, P(acc), P(commit), P(tok),
+                                P(err), h))
+
+    def rollback_and_decode():
+        chk(lib.gdn_conv_commit(P(xw), P(xb), P(commit), P(conv_next), P(err), B, T, C, 4, h))
+        chk(lib.gdn_recurrent_fwd_from_ckpt(P(q1), P(k1), P(v1), P(a1), P(b1),
+                                            P(A_log), P(dtb), P(S), P(ckpt), P(commit), T, P(S_next), P(o1), None,
+                                            P(err), B, 1, hk, hv, D, D, flags, h))
+
+    def chain():
+        verify()
+        accept()
+        rollback_and_decode()
+
+    steps = max(5, args.steps // 10)
+    for _ in range(max(args.warmup, 3)):
+        chain()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record(st)
+    for _ in range(steps):
+        chain()
+    e[1].record(st)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(e[0].elapsed_time(e[1]) / steps, world, device)
+    tv, ta = [], []
+    for _ in range(3):
+        e[0].record(st); verify(); e[1].record(st); accept(); e[2].record(st)
+        torch.cuda.synchronize(device)
+        tv.append(e[0].elapsed_time(e[1]))
+        ta.append(e[1].elapsed_time(e[2]))
+    tv, ta = statistics.mean(tv), statistics.mean(ta)
+    state = B * hv * D * D * 4
+    verify_bytes = state * (1 + T)                         # read S, write T checkpoints (S_out aliases the last)
+    j = acc.cpu().numpy()
+    accept_bytes = int(sum((2 if jj < k else 1) * VOCAB * 4 for jj in j))   # residual row pair or p_k row
+    if int(err.item()):
+        raise RuntimeError("verify chain raised the device error flag")
+    return {"workload": f"config2: B={B}, k+1={T} verify with checkpoints -> on-device accept over V={VOCAB} "
+                        f"-> conv rollback -> decode from the accepted checkpoint (Hk={hk} Hv={hv} per GPU)",
+            "ms_per_step": round(ms, 4), "verify_ms": round(tv, 4),
+            "verify_gbs": round(verify_bytes / (tv * 1e-3) / 1e9, 1),
+            "verify_frac": round(verify_bytes / (tv * 1e-3) / 1e9 / hbm_peak, 4),
+            "accept_ms": round(ta, 4), "accept_gbs": round(accept_bytes / (ta * 1e-3) / 1e9, 1),
+            "mean_accepted": round(float(j.mean()), 3), "gpu_launches_per_step": 4}
 
 
 def run_e2e(args, lib, X, Bg, device, world):
@@ -724,6 +833,7 @@ def main():
                     help="dram bytes per launch from an ncu capture, reported as roofline.traffic")
     ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-verify", action="store_true", help="skip the config-2 verify/accept/rollback chain")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
     ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm"], default="auto",
@@ -732,7 +842,7 @@ def main():
     args = ap.parse_args()
     if args.small:
         args.batch, args.layers, args.sweep = 64, 2, ""
-        args.no_e2e = args.no_cpu_baseline = args.no_prefill = True
+        args.no_e2e = args.no_cpu_baseline = args.no_prefill = args.no_verify = True
     args.warmup = max(args.warmup, 0)
 
     world, rank, local = dist_env()

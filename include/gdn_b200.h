@@ -209,6 +209,27 @@ int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v,
                             const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
                             unsigned flags, void* workspace, size_t workspace_size, void* stream);
 
+/*
+ * gdn_spec_verify -- the acceptance step of an MTP speculative-verify block
+ * on the device (python/speculative.py:161-190, cpp/src/session.cpp:495-511),
+ * so the rollback index feeds gdn_recurrent_fwd_from_ckpt and
+ * gdn_conv_commit without a host round trip.  Per sequence b:
+ *   accept_i = q_i[d_i] > 0 ? u_accept[b,i] * q_i[d_i] <= p_i[d_i] : p_i[d_i] > 0
+ *   accept_len[b] = j = number of leading accepted drafts, commit_n[b] = j + 1
+ *   token[b] = inverse-CDF draw with uniform u_sample[b] from p_k (j == k)
+ *              or from normalize(max(p_j - q_j, 0)) (p_j when that is empty),
+ *              i.e. the smallest v with u * sum(r) < sum_{x<=v} r[x]
+ *   p (B, k+1, V) fp32 target distributions of the verify pass
+ *   q (B, k, V) fp32 draft distributions; draft (B, k) int32 draft tokens
+ *   u_accept (B, k), u_sample (B) fp32 uniforms in [0, 1)
+ * 1 <= k <= 32, V <= 4,194,304.  A draft token outside [0, V) is treated as
+ * rejected and sets *err_flag.
+ */
+int gdn_spec_verify(const float* p, const float* q, const int32_t* draft,
+                    const float* u_accept, const float* u_sample, int B, int k, long long V,
+                    int32_t* accept_len, int32_t* commit_n, int32_t* token, int32_t* err_flag,
+                    void* stream);
+
 /* Size of the fixed device scratch that gdn_chunked_fwd_static uses. */
 #define GDN_CHUNKED_STATIC_SCRATCH_BYTES (64ull << 20)
 

@@ -146,6 +146,44 @@ def commit_index(n: int, T: int) -> int:
     return n - 1
 
 
+def spec_residual(p, q):
+    """Normalised max(0, p - q), or p / sum(p) when that is empty
+    (python/speculative.py:100-106)."""
+    r = np.maximum(np.asarray(p, np.float64) - np.asarray(q, np.float64), 0.0)
+    tot = r.sum()
+    if tot <= 1e-12:
+        return np.asarray(p, np.float64) / np.sum(p, dtype=np.float64)
+    return r / tot
+
+
+def spec_verify(p, q, draft, u_accept, u_sample):
+    """Acceptance step of a speculative block for one sequence, as
+    python/speculative.py:170-190 (cpp/src/session.cpp:495-511): accept draft
+    i iff q_i[d_i] > 0 ? u_i q_i[d_i] <= p_i[d_i] : p_i[d_i] > 0; j = leading
+    accepted drafts; the corrected token is drawn from p_k (j == k) or from
+    the residual of row j -- here by inverse CDF with the uniform u_sample
+    (the reference draws with MLX's categorical sampler).  p (k+1, V), q
+    (k, V) fp32.  Returns (j, commit_n = j + 1, token)."""
+    k = len(draft)
+    j = 0
+    while j < k:
+        d = int(draft[j])
+        pd, qd = np.float32(p[j][d]), np.float32(q[j][d])
+        acc = (np.float32(u_accept[j]) * qd <= pd) if qd > 0 else (pd > 0)
+        if not acc:
+            break
+        j += 1
+    r = np.asarray(p[k], np.float64) if j == k else np.maximum(
+        np.asarray(p[j], np.float64) - np.asarray(q[j], np.float64), 0.0)
+    if j < k and not r.sum() > 1e-12:
+        r = np.asarray(p[j], np.float64)
+    cdf = np.cumsum(r)
+    v = int(np.searchsorted(cdf, float(u_sample) * cdf[-1], side="right"))
+    if v >= len(r):
+        v = int(np.nonzero(r > 0)[0][-1])
+    return j, j + 1, v
+
+
 # ---------------------------------------------------------------------------
 # the chunked (WY / UT) form, the oracle of the prefill kernel
 # ---------------------------------------------------------------------------

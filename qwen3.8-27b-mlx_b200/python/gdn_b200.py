@@ -56,6 +56,7 @@ SIGNATURES = {
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_workspace_bytes": [_i] * 4,
     "gdn_chunked_fwd_static": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
+    "gdn_spec_verify": [_vp] * 5 + [_i, _i, ctypes.c_longlong] + [_vp] * 5,
     "gdn_chunked_norm_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 7 + [ctypes.c_longlong, _vp,
                                ctypes.c_float, _vp, ctypes.c_longlong, _i, _vp] + [_i] * 6
                                + [_u, _vp, ctypes.c_size_t, _vp],
@@ -241,6 +242,25 @@ def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, sta
                                         ptr(cu_seqlens), B, T, Hk, Hv, D, D, F_QK_L2NORM if l2norm else 0,
                                         ptr(workspace), workspace.numel(), stream_ptr(dev)))
     return out, state_out
+
+
+def spec_verify(p, q, draft, u_accept, u_sample, err_flag=None):
+    """On-device acceptance of a speculative block (gdn_spec_verify).  p
+    (B, k+1, V), q (B, k, V) fp32; draft (B, k) int32; u_accept (B, k),
+    u_sample (B,) fp32.  Returns (accept_len, commit_n, token), int32 (B,)."""
+    B, k1, V = p.shape
+    k = k1 - 1
+    if q.shape != (B, k, V) or draft.shape != (B, k) or u_accept.shape != (B, k) or u_sample.shape != (B,):
+        raise ValueError("shapes: p (B,k+1,V), q (B,k,V), draft (B,k), u_accept (B,k), u_sample (B,)")
+    if draft.dtype != torch.int32:
+        raise ValueError("draft must be int32")
+    dev = _dev(p, q, draft, u_accept, u_sample, err_flag)
+    outs = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(3)]
+    if err_flag is None:
+        err_flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib().gdn_spec_verify(ptr(p), ptr(q), ptr(draft), ptr(u_accept), ptr(u_sample), B, k, V,
+                                ptr(outs[0]), ptr(outs[1]), ptr(outs[2]), ptr(err_flag), stream_ptr(dev)))
+    return tuple(outs)
 
 
 def conv1d_fwd(x, w, state_in=None, state_out=None, y=None, cu_seqlens=None, *, bf16_ops=False, silu=True):

@@ -21,6 +21,8 @@ What is pinned (all functions are the reference's own, unmodified):
   that BUILD_LOG.md:314 reports, with test-style gates and with model-style
   gates (alpha = exp(-exp(A_log)*softplus(a+dt_bias)), A_log ~ U(0, ln 16),
   which underflows below the 1e-6 clip).
+* ``spec_residual.npz`` ``residual`` (python/speculative.py:100-106) of the
+  speculative acceptance step on seeded softmax pairs.
 * ``block_*.npz``       ``GatedDeltaNet.__call__`` (python/qwen35.py:572-639)
   with the input/output projections replaced by fixed tensors, driving a
   ``DeltaCache`` (python/qwen35.py:291-328) through prefill (chunked path),
@@ -184,11 +186,46 @@ def gen_block(mx, qwen35, dtype_name, seed, name):
     np.savez_compressed(os.path.join(HERE, name), **out)
 
 
+def gen_spec(mx, seed, name):
+    """``residual`` of the speculative acceptance step (python/speculative.py:
+    100-106), the reference's own function, on seeded softmax pairs (V = 6 as
+    its selftest, and V = 50), plus p == q (empty residual -> p) and a
+    one-hot p (greedy)."""
+    import speculative  # noqa: E402  (the reference; imports qwen35, generate, tokenizer)
+    rng = np.random.default_rng(seed)
+    ps, qs, rs = [], [], []
+
+    def softmax(x):
+        e = np.exp(x - x.max())
+        return (e / e.sum()).astype(np.float32)
+
+    for V in (6, 50):
+        for _ in range(8):
+            p = softmax(rng.standard_normal(V).astype(np.float32) * 2)
+            q = softmax(rng.standard_normal(V).astype(np.float32) * 2)
+            ps.append(p), qs.append(q)
+    p = softmax(rng.standard_normal(50).astype(np.float32))
+    ps.append(p), qs.append(p.copy())
+    oh = np.zeros(50, np.float32)
+    oh[7] = 1
+    ps.append(oh), qs.append(softmax(rng.standard_normal(50).astype(np.float32)))
+    for p, q in zip(ps, qs):
+        rs.append(np.asarray(speculative.residual(mx.array(p), mx.array(q)), np.float32))
+    out = {}
+    for i, (p, q, r) in enumerate(zip(ps, qs, rs)):
+        out[f"p{i}"], out[f"q{i}"], out[f"r{i}"] = p, q, r
+    np.savez_compressed(os.path.join(HERE, name), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("GDN_REFERENCE_PY", "/root/reference/python"))
+    ap.add_argument("--only", choices=["spec"], default=None, help="regenerate one file set only")
     args = ap.parse_args()
     mx, qwen35 = load_reference(args.ref)
+    if args.only == "spec":
+        gen_spec(mx, 1008, "spec_residual.npz")
+        return
     gen_recurrent(mx, qwen35, 32, [(1, 1, 4), (1, 4, 4), (1, 9, 4), (2, 3, 2), (1, 64, 2)],
                   1001, "recurrent_d32.npz")
     gen_recurrent(mx, qwen35, 128, [(1, 1, 3), (1, 4, 1), (2, 3, 1), (1, 9, 1)],
@@ -199,6 +236,7 @@ def main():
     gen_chunked(mx, qwen35, 128, 1, [130], 1005, "chunked_d128.npz", model_style=True)
     gen_block(mx, qwen35, "f32", 1006, "block_f32.npz")
     gen_block(mx, qwen35, "bf16", 1007, "block_bf16.npz")
+    gen_spec(mx, 1008, "spec_residual.npz")
     print("golden vectors written to", HERE)
 
 
