@@ -161,13 +161,24 @@ int gdn_chunked_fwd(const void* q, const void* k, const void* v,
                     unsigned flags, void* stream);
 
 /*
- * gdn_chunked_workspace_bytes -- device workspace that gdn_chunked_fwd_ws
- * needs for B sequences of T tokens (packed = 0), or for B packed sequences
- * of T tokens in all (packed != 0, an upper bound that holds for any
- * cu_seqlens).  145 KiB per (64-token chunk, value head).  0 for bad
- * sizes.
+ * gdn_chunked_workspace_bytes -- device workspace with which
+ * gdn_chunked_fwd_ws runs B sequences of T tokens (packed = 0), or B packed
+ * sequences of T tokens in all (packed != 0, an upper bound that holds for
+ * any cu_seqlens), in one pass: 145 KiB per (64-token chunk, value head).
+ * 0 for bad sizes.
  */
 size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed);
+
+/*
+ * gdn_chunked_workspace_min_bytes -- the smallest workspace gdn_chunked_fwd_ws
+ * accepts for B sequences and Hv value heads: one chunk per sequence per
+ * window, plus B*Hv*64 KiB for the state carried between windows when the
+ * call has no state_out (has_state_out == 0).  Smaller-than-one-pass
+ * workspaces run the call window by window (chunks [c0, c0 + w) of every
+ * sequence per window, w as large as the workspace allows), with the same
+ * results.  0 for bad sizes.
+ */
+size_t gdn_chunked_workspace_min_bytes(int B, int Hv, int has_state_out);
 
 /*
  * gdn_chunked_fwd_ws -- gdn_chunked_fwd split in two launches: the
@@ -177,9 +188,10 @@ size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed);
  * function of the inputs as chunked_delta, python/qwen35.py:365-431); the
  * split exposes (chunks x heads) of parallel work where gdn_chunked_fwd
  * has (sequences x heads).  workspace: device memory, 256-byte aligned, at
- * least gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) bytes,
- * no initial contents needed, not overlapping the states or o; calls that
- * share one workspace must be ordered on a stream.
+ * least gdn_chunked_workspace_min_bytes(B, Hv, state_out != NULL) bytes
+ * (gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) for one pass;
+ * less runs in windows), no initial contents needed, not overlapping the
+ * states or o; calls that share one workspace must be ordered on a stream.
  */
 int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
                        long long q_stride, long long k_stride, long long v_stride,

@@ -156,7 +156,10 @@ struct ChunkParams {
   unsigned char* ws;              // workspace (256-byte aligned)
   int32_t* chunk_prefix;          // (B+1) first record slot of each sequence (packed batches)
   long long n_slots;              // record slots (chunks over all sequences, or an upper bound)
-  int nch_uniform;                // chunks per sequence when cu == null
+  int nch_uniform;                // chunks per sequence in this window when cu == null
+  size_t rec_off;                 // byte offset of the records in the workspace
+  int win_c0, win_len;            // window: chunks [win_c0, win_c0 + win_len) of every sequence
+  float* carry;                   // state between windows (state_out, a workspace region, or null)
   // gated RMSNorm fused into the scan's epilogue (o is then the bf16 output):
   // out[t * out_stride + (out_head0 + h) * 128 + d] = rms_norm(o)[d] gamma[d] silu(z[t, h, d])
   const __nv_bfloat16* z;
@@ -667,8 +670,8 @@ __device__ __forceinline__ void phase_epi_e(const ChunkParams& p, Ctx& c, uint32
 }
 
 // Initial state row dv = row, columns [col0, col0 + ncols), into the fp32 master.
-__device__ __forceinline__ void state_load(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr, int col0, int ncols) {
-  const float* src = p.state_in ? p.state_in + (static_cast<size_t>(bh) * kD + c.row) * kD + col0 : nullptr;
+__device__ __forceinline__ void state_load(const float* state, Ctx& c, int bh, uint32_t col_dr, int col0, int ncols) {
+  const float* src = state ? state + (static_cast<size_t>(bh) * kD + c.row) * kD + col0 : nullptr;
   for (int cc = 0; cc < ncols; cc += 16) {
     float v[16];
 #pragma unroll
@@ -681,10 +684,9 @@ __device__ __forceinline__ void state_load(const ChunkParams& p, Ctx& c, int bh,
   tc::tmem_st_wait();
 }
 
-__device__ __forceinline__ void state_store(const ChunkParams& p, Ctx& c, int bh, uint32_t col_dr, int col0,
-                                            int ncols) {
-  if (!p.state_out) return;
-  float* dst = p.state_out + (static_cast<size_t>(bh) * kD + c.row) * kD + col0;
+__device__ __forceinline__ void state_store(float* state, Ctx& c, int bh, uint32_t col_dr, int col0, int ncols) {
+  if (!state) return;
+  float* dst = state + (static_cast<size_t>(bh) * kD + c.row) * kD + col0;
   for (int cc = 0; cc < ncols; cc += 16) {
     float v[16];
     tc::tmem_ld16(c.tb + col_dr + c.my + col0 + cc, v);
@@ -708,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
   seq_range(p, b, s0, s1);
   const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kOffBar + 8), c.bar, 1, kTmemCols);
-  state_load(p, c, bh, kColDR, c.half * 64, 64);
+  state_load(p.state_in, c, bh, kColDR, c.half * 64, 64);
 
   bool failed = false;
   for (int ch = 0; ch < n_chunks; ++ch) {
@@ -770,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);   // the phase mma_wait gave up on: one more bounded wait
   } else {
-    state_store(p, c, bh, kColDR, c.half * 64, 64);
+    state_store(p.state_out, c, bh, kColDR, c.half * 64, 64);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -781,14 +783,15 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const ChunkParams 
 
 // Record of (slot, value head) in the workspace (256-byte aligned).
 __device__ __forceinline__ unsigned char* record(const ChunkParams& p, long long slot, int h) {
-  return p.ws + records_offset(p.B) + (static_cast<size_t>(slot) * p.Hv + h) * kRecBytes;
+  return p.ws + p.rec_off + (static_cast<size_t>(slot) * p.Hv + h) * kRecBytes;
 }
 
-// Sequence and chunk of a record slot; false for an unused slot.
+// Sequence and (absolute) chunk of a record slot of the current window;
+// false for an unused slot.
 __device__ __forceinline__ bool slot_to_chunk(const ChunkParams& p, long long slot, int& b, int& ch) {
   if (!p.cu) {
     b = static_cast<int>(slot / p.nch_uniform);
-    ch = static_cast<int>(slot - static_cast<long long>(b) * p.nch_uniform);
+    ch = p.win_c0 + static_cast<int>(slot - static_cast<long long>(b) * p.nch_uniform);
     return b < p.B;
   }
   if (slot >= p.chunk_prefix[p.B]) return false;
@@ -799,7 +802,7 @@ __device__ __forceinline__ bool slot_to_chunk(const ChunkParams& p, long long sl
     else hi = mid - 1;
   }
   b = lo;
-  ch = static_cast<int>(slot - p.chunk_prefix[lo]);
+  ch = p.win_c0 + static_cast<int>(slot - p.chunk_prefix[lo]);
   return true;
 }
 
@@ -808,8 +811,10 @@ __device__ __forceinline__ long long seq_first_slot(const ChunkParams& p, int b)
   return p.cu ? static_cast<long long>(p.chunk_prefix[b]) : static_cast<long long>(b) * p.nch_uniform;
 }
 
-// prefix[b] = number of 64-token chunks of packed sequences 0 .. b-1 (one block).
-__global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, int B, int32_t* prefix) {
+// prefix[b] = number of 64-token chunks of packed sequences 0 .. b-1 that fall
+// in the window [c0, c0 + wlen) (one block).
+__global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, int B, int c0, int wlen,
+                                                            int32_t* prefix) {
   __shared__ int32_t carry;
   __shared__ int32_t buf[1024];
   if (threadIdx.x == 0) carry = 0;
@@ -819,7 +824,8 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
     int32_t n = 0;
     if (b < B) {
       const int32_t len = cu[b + 1] - cu[b];
-      n = len > 0 ? (len + kC - 1) / kC : 0;
+      n = len > 0 ? (len + kC - 1) / kC - c0 : 0;
+      n = n < 0 ? 0 : (n > wlen ? wlen : n);
     }
     buf[threadIdx.x] = n;
     __syncthreads();
@@ -949,7 +955,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   const int cg = (c.warp >> 2) & 3;                // column group of a worker
   long long s0, s1;
   seq_range(p, b, s0, s1);
-  const int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC);
+  // this window's chunks of the sequence
+  int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC) - p.win_c0;
+  n_chunks = n_chunks < 0 ? 0 : (n_chunks > p.win_len ? p.win_len : n_chunks);
+  if (p.win_c0 > 0 && n_chunks == 0) return;       // finished in an earlier window: its state is in place
   const long long slot0 = seq_first_slot(p, b);
   // TMEM columns: R tf32 [0,128) | U (even) | y (even) | R fp32 [256,384) | y (odd) | U (odd).
   // The first MMA batch writes [U | y] (even) or [y | U] (odd) in one N = 128
@@ -957,7 +966,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   // mirror the order of the stacked B operands in shared memory to match.
   constexpr uint32_t cR = 0, cDR = 256;
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 4, kTmemCols);
-  if (!mw) state_load(p, c, bh, cDR, cg * 32, 32);
+  if (!mw) state_load(p.win_c0 == 0 ? p.state_in : p.carry, c, bh, cDR, cg * 32, 32);
   const uint32_t lane_cols = c.tb + c.my + cg * 32;   // a worker's 32 columns of R / R fp32
 
   // record groups issued and waited for, counted by the copy warp only
@@ -1042,7 +1051,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   unsigned short z_next[16];
   uint32_t z_prev[8];                             // packed pairs, filled at the end of the chunk
   auto load_z = [&](int ch) {
-    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
     const int nv = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC) - cg * 16;
     const unsigned short* zp = reinterpret_cast<const unsigned short*>(p.z) + (t0 + cg * 16) * p.z_stride +
                                c.h * kD + c.row;
@@ -1052,7 +1061,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   // o rows of chunk ch from y^T: a worker's dv = row, tokens cg*16 + part*8 .. +7
   auto epi_o = [&](int ch, int part) {
     const uint32_t col_y = (ch & 1) ? 384 : 192;
-    const long long t0 = s0 + static_cast<long long>(ch) * kC;
+    const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
     const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
     const int tok = cg * 16 + part * 8;
     const int nv = nvalid - tok;
@@ -1196,7 +1205,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
         if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
     }
   } else if (!mw) {
-    state_store(p, c, bh, cDR, cg * 32, 32);
+    state_store(p.carry, c, bh, cDR, cg * 32, 32);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1255,27 +1264,76 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
   p = ChunkParams{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                   static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
                   state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err,
-                  nullptr, nullptr, 0, 0, nullptr, 0, nullptr, 0.f, 0, 0};
+                  nullptr, nullptr, 0, 0, 0, 0, 0, nullptr, nullptr, 0, nullptr, 0.f, 0, 0};
   return GDN_OK;
 }
 
-// Record slots for (B, T): exact for uniform batches, an upper bound (one
-// partial chunk per sequence) for packed ones.
-long long chunk_slots(int B, int T, bool packed) {
-  return packed ? (static_cast<long long>(T) + kC - 1) / kC + B
-                : static_cast<long long>(B) * ((static_cast<long long>(T) + kC - 1) / kC);
+// Record slots of a window of `w` chunks per sequence: exact for uniform
+// batches, an upper bound for packed ones (at most w chunks per sequence, at
+// most one partial chunk per sequence overall).
+long long window_slots(int B, int T, bool packed, long long w) {
+  const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
+  const long long ww = w < nch ? w : nch;
+  if (!packed) return static_cast<long long>(B) * ww;
+  const long long cap = nch + B;
+  return static_cast<long long>(B) * ww < cap ? static_cast<long long>(B) * ww : cap;
 }
 
+long long chunk_slots(int B, int T, bool packed) { return window_slots(B, T, packed, 1LL << 40); }
+
+size_t records_base(int B) { return records_offset(B); }
+
+// The whole call in one window.
 size_t workspace_bytes(int B, int T, int Hv, bool packed) {
-  return records_offset(B) + static_cast<size_t>(chunk_slots(B, T, packed)) * Hv * kRecBytes;
+  return records_base(B) + static_cast<size_t>(chunk_slots(B, T, packed)) * Hv * kRecBytes;
 }
 
-// Launch the split schedule on a workspace of at least workspace_bytes().
-int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
+// Smallest workspace: one chunk per sequence per window, plus the state
+// carried between windows when the caller keeps no state_out.
+size_t workspace_min_bytes(int B, int Hv, bool carry) {
+  return records_base(B) + (carry ? static_cast<size_t>(B) * Hv * kD * kD * 4 : 0) +
+         static_cast<size_t>(B) * Hv * kRecBytes;
+}
+
+struct SplitPlan {
+  int win_len = 0, n_windows = 0;
+  size_t carry_off = 0, rec_off = 0;
+};
+
+// Windows that fit `ws_size` bytes: one if the whole call fits, else the
+// largest window of chunks per sequence that does.
+bool plan_split(int B, int T, int Hv, bool packed, bool has_state_out, size_t ws_size, SplitPlan& pl) {
+  const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
+  if (ws_size >= workspace_bytes(B, T, Hv, packed)) {
+    pl.win_len = static_cast<int>(nch > 0 ? nch : 1);
+    pl.n_windows = 1;
+    pl.rec_off = records_base(B);
+    return true;
+  }
+  pl.carry_off = records_base(B);
+  pl.rec_off = pl.carry_off + (has_state_out ? 0 : static_cast<size_t>(B) * Hv * kD * kD * 4);
+  if (ws_size < pl.rec_off) return false;
+  const size_t per_chunk = static_cast<size_t>(B) * Hv * kRecBytes;
+  const long long w = static_cast<long long>((ws_size - pl.rec_off) / per_chunk);
+  if (w < 1) return false;
+  pl.win_len = static_cast<int>(w < nch ? w : nch);
+  pl.n_windows = static_cast<int>((nch + pl.win_len - 1) / pl.win_len);
+  return true;
+}
+
+// Launch the split schedule, window by window, on a workspace of ws_size bytes
+// (at least workspace_min_bytes()).
+int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStream_t st) {
   const bool packed = p.cu != nullptr;
+  SplitPlan pl;
+  if (!plan_split(p.B, T, p.Hv, packed, p.state_out != nullptr, ws_size, pl))
+    return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, at least %zu needed (%zu for one window)", ws_size,
+                workspace_min_bytes(p.B, p.Hv, p.state_out == nullptr), workspace_bytes(p.B, T, p.Hv, packed));
   p.ws = ws;
   p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
-  p.nch_uniform = packed ? 0 : (p.T + kC - 1) / kC;
+  p.rec_off = pl.rec_off;
+  p.carry = p.state_out ? p.state_out : (pl.n_windows > 1 ? reinterpret_cast<float*>(ws + pl.carry_off) : nullptr);
+  p.win_len = pl.win_len;
   static bool attr_prep[64] = {false}, attr_scan[64] = {false};
   int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kPrepSmem, attr_prep);
   if (rc != GDN_OK) return rc;
@@ -1284,20 +1342,30 @@ int run_split(ChunkParams p, unsigned char* ws, cudaStream_t st) {
                          : reinterpret_cast<const void*>(chunk_scan_kernel<false>);
   rc = set_smem_attr(scan, kScanSmem, p.z ? attr_scan_norm : attr_scan);
   if (rc != GDN_OK) return rc;
-  if (packed) {
-    chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.chunk_prefix);
-    rc = cuda_status(cudaGetLastError(), "chunk prefix launch");
+  const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
+  for (int w = 0; w < pl.n_windows; ++w) {
+    p.win_c0 = w * pl.win_len;
+    const long long left = nch - p.win_c0;
+    p.nch_uniform = packed ? 0 : static_cast<int>(left < pl.win_len ? left : pl.win_len);
+    p.n_slots = packed ? window_slots(p.B, T, true, pl.win_len) : static_cast<long long>(p.B) * p.nch_uniform;
+    if (p.n_slots > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+    if (packed) {
+      chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.win_c0, pl.win_len, p.chunk_prefix);
+      rc = cuda_status(cudaGetLastError(), "chunk prefix launch");
+      if (rc != GDN_OK) return rc;
+    }
+    if (p.n_slots > 0) {
+      chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kPrepSmem,
+                          st>>>(p);
+      rc = cuda_status(cudaGetLastError(), "chunk prep launch");
+      if (rc != GDN_OK) return rc;
+    }
+    if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
+    else chunk_scan_kernel<false><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
+    rc = cuda_status(cudaGetLastError(), "chunk scan launch");
     if (rc != GDN_OK) return rc;
   }
-  if (p.n_slots > 0) {
-    chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kPrepSmem,
-                        st>>>(p);
-    rc = cuda_status(cudaGetLastError(), "chunk prep launch");
-    if (rc != GDN_OK) return rc;
-  }
-  if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
-  else chunk_scan_kernel<false><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
-  return cuda_status(cudaGetLastError(), "chunk scan launch");
+  return GDN_OK;
 }
 
 }  // namespace
@@ -1327,6 +1395,11 @@ extern "C" size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed) 
   return workspace_bytes(B, T, Hv, packed != 0);
 }
 
+extern "C" size_t gdn_chunked_workspace_min_bytes(int B, int Hv, int has_state_out) {
+  if (B < 0 || Hv <= 0) return 0;
+  return workspace_min_bytes(B, Hv, has_state_out == 0);
+}
+
 extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
                                   long long k_stride, long long v_stride, const float* a, const float* b,
                                   const float* A_log, const float* dt_bias, const float* state_in,
@@ -1338,19 +1411,17 @@ extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, l
   int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, o,
                         cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags);
   if (rc != GDN_OK || B == 0) return rc;
-  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
-  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes)", need);
+  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes for one window)",
+                              workspace_bytes(B, T, Hv, cu_seqlens != nullptr));
   if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");
-  if (workspace_size < need) return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, %zu needed", workspace_size, need);
   const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * 4;
   const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
   const size_t obytes = static_cast<size_t>(total) * Hv * kD * ((flags & GDN_F_O_BF16) ? 2 : 4);
-  if (overlap(workspace, need, state_in, sbytes) || overlap(workspace, need, state_out, sbytes) ||
-      overlap(workspace, need, o, obytes))
+  if (overlap(workspace, workspace_size, state_in, sbytes) || overlap(workspace, workspace_size, state_out, sbytes) ||
+      overlap(workspace, workspace_size, o, obytes))
     return fail(GDN_ERR_ALIAS, "workspace overlaps a state or o");
-  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
-  if (p.n_slots > 0x7fffffffLL || Hv > 65535) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
-  return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
+  if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
+  return run_split(p, T, static_cast<unsigned char*>(workspace), workspace_size, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
@@ -1371,25 +1442,23 @@ extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void*
   if (out_head0 < 0 || out_stride < (static_cast<long long>(out_head0) + Hv) * kD || z_stride < static_cast<long long>(Hv) * kD)
     return fail(GDN_ERR_SHAPE, "out_stride / out_head0 / z_stride do not fit Hv heads of 128");
   if (!aligned(z, 2) || !aligned(gamma, 4) || !(eps >= 0.f)) return fail(GDN_ERR_ALIGN, "z, gamma misaligned or eps < 0");
-  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
-  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes)", need);
+  if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes for one window)",
+                              workspace_bytes(B, T, Hv, cu_seqlens != nullptr));
   if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");
-  if (workspace_size < need) return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, %zu needed", workspace_size, need);
   const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * 4;
   const size_t obytes = total > 0 ? static_cast<size_t>(total - 1) * out_stride * 2 + (out_head0 + Hv) * kD * 2 : 0;
-  if (overlap(workspace, need, state_in, sbytes) || overlap(workspace, need, state_out, sbytes) ||
-      overlap(workspace, need, out, obytes) || overlap(out, obytes, state_in, sbytes) ||
+  if (overlap(workspace, workspace_size, state_in, sbytes) || overlap(workspace, workspace_size, state_out, sbytes) ||
+      overlap(workspace, workspace_size, out, obytes) || overlap(out, obytes, state_in, sbytes) ||
       overlap(out, obytes, state_out, sbytes))
     return fail(GDN_ERR_ALIAS, "workspace, out and the states must not overlap");
-  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
-  if (p.n_slots > 0x7fffffffLL || Hv > 65535) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+  if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
   p.z = static_cast<const __nv_bfloat16*>(z);
   p.z_stride = z_stride;
   p.gamma = gamma;
   p.eps = eps;
   p.out_stride = out_stride;
   p.out_head0 = out_head0;
-  return run_split(p, static_cast<unsigned char*>(workspace), static_cast<cudaStream_t>(stream));
+  return run_split(p, T, static_cast<unsigned char*>(workspace), workspace_size, static_cast<cudaStream_t>(stream));
 }
 
 // Scratch of gdn_chunked_fwd_static: a fixed device array, so that the call
@@ -1440,12 +1509,11 @@ extern "C" int gdn_chunked_fwd_static(const void* q, const void* k, const void* 
                 "gdn_chunked_fwd_static: B=%d T=%d Hv=%d needs %zu bytes of scratch, more than the %llu of the "
                 "static scratch; split the call or use gdn_chunked_fwd_ws",
                 B, T, Hv, need, static_cast<unsigned long long>(GDN_CHUNKED_STATIC_SCRATCH_BYTES));
-  p.n_slots = chunk_slots(B, T, cu_seqlens != nullptr);
   if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
   unsigned char* ws = nullptr;
   rc = static_scratch_ptr(&ws);
   if (rc != GDN_OK) return rc;
-  return run_split(p, ws, static_cast<cudaStream_t>(stream));
+  return run_split(p, T, ws, need, static_cast<cudaStream_t>(stream));
 }
 
 #ifdef GDN_CHUNK_TIMING

@@ -55,6 +55,7 @@ SIGNATURES = {
     "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_workspace_bytes": [_i] * 4,
+    "gdn_chunked_workspace_min_bytes": [_i] * 3,
     "gdn_chunked_fwd_static": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_spec_verify": [_vp] * 5 + [_i, _i, ctypes.c_longlong] + [_vp] * 5,
     "gdn_chunked_norm_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 7 + [ctypes.c_longlong, _vp,
@@ -67,7 +68,8 @@ SIGNATURES = {
 }
 
 # return types other than int
-RESTYPES = {"gdn_last_error": ctypes.c_char_p, "gdn_chunked_workspace_bytes": ctypes.c_size_t}
+RESTYPES = {"gdn_last_error": ctypes.c_char_p, "gdn_chunked_workspace_bytes": ctypes.c_size_t,
+            "gdn_chunked_workspace_min_bytes": ctypes.c_size_t}
 
 _lib = None
 
@@ -308,8 +310,13 @@ def gated_rmsnorm_fwd(o, z, gamma, out=None, eps=1e-6, out_dtype=torch.bfloat16)
 
 
 def chunked_workspace_bytes(B, T, Hv, packed=False) -> int:
-    """Workspace bytes gdn_chunked_fwd_ws needs (gdn_chunked_workspace_bytes)."""
+    """Workspace bytes for one pass of gdn_chunked_fwd_ws (gdn_chunked_workspace_bytes)."""
     return int(lib().gdn_chunked_workspace_bytes(B, T, Hv, 1 if packed else 0))
+
+
+def chunked_workspace_min_bytes(B, Hv, has_state_out=True) -> int:
+    """Smallest workspace gdn_chunked_fwd_ws accepts; smaller than one pass runs in windows."""
+    return int(lib().gdn_chunked_workspace_min_bytes(B, Hv, 1 if has_state_out else 0))
 
 
 def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=None, cu_seqlens=None, *,

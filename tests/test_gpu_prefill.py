@@ -243,9 +243,11 @@ def test_split_schedule_rejects_a_short_or_misaligned_workspace():
     args = (t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]), dev(inp["dt_bias"]))
     need = G.chunked_workspace_bytes(1, 130, 6)
     assert need == G.chunked_workspace_bytes(1, 129, 6) > 0
+    least = G.chunked_workspace_min_bytes(1, 6, True)
+    assert 0 < least < need
     ws = torch.empty(need + 256, dtype=torch.uint8, device="cuda")
     with pytest.raises(G.GdnError) as e:
-        G.chunked_fwd(*args, split=True, workspace=ws[:need - 1])
+        G.chunked_fwd(*args, split=True, workspace=ws[:least - 1])
     assert e.value.code == G.GDN_ERR_SHAPE
     with pytest.raises(G.GdnError) as e:
         G.chunked_fwd(*args, split=True, workspace=ws[16:16 + need])
@@ -373,3 +375,57 @@ def test_chunked_norm_writes_its_heads_inside_wider_rows():
     torch.cuda.synchronize()
     assert torch.equal(wide[:, :, 6:9], own)
     assert bool((wide[:, :, :6] == 3.0).all()) and bool((wide[:, :, 9:] == 3.0).all())
+
+
+@pytest.mark.parametrize("lens", [[300, 300], [100, 0, 257, 64, 3, 1, 640]])
+@pytest.mark.parametrize("with_state_out", [True, False])
+def test_split_schedule_in_windows_matches_one_pass(lens, with_state_out):
+    """A workspace smaller than one pass runs the call in windows of w chunks
+    per sequence (state carried in state_out, or in the workspace when the
+    call keeps none): o and the final state are bit-identical to one pass,
+    for w = 1, 2, 3; below the minimum the call is rejected."""
+    import ctypes
+    rng = np.random.default_rng(70 + len(lens))
+    Hk, Hv = 2, 6
+    total = sum(lens)
+    packed = len(set(lens)) > 1
+    inp = chunk_inputs(rng, 1, total, Hk, Hv)
+    S0 = dev(rng.standard_normal((len(lens), Hv, 128, 128), dtype=np.float32) * np.float32(0.05))
+    if packed:
+        cu = dev(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), torch.int32)
+        B, T = len(lens), total
+        t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0])  # noqa: E731
+    else:
+        cu = None
+        B, T = len(lens), lens[0]
+        t = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]), torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]))  # noqa: E731
+    q, k, v, a, b = t("q"), t("k"), t("v"), g("a"), g("b")
+    A_log, dtb = dev(inp["A_log"]), dev(inp["dt_bias"])      # kept alive across the asynchronous calls
+    o_ref, S_ref = G.chunked_fwd(q, k, v, a, b, A_log, dtb, state_in=S0, cu_seqlens=cu, split=True)
+    L = G.lib()
+    rec = L.gdn_chunked_workspace_bytes(1, 64, 1, 0) - L.gdn_chunked_workspace_bytes(1, 0, 1, 0)
+    base = G.chunked_workspace_min_bytes(B, Hv, with_state_out)
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    for w in (1, 2, 3):
+        size = base + (w - 1) * B * Hv * rec
+        ws = torch.empty(size, dtype=torch.uint8, device="cuda")
+        o = torch.empty_like(o_ref)
+        S = torch.empty_like(S_ref) if with_state_out else None
+        rc = L.gdn_chunked_fwd_ws(P(q), P(k), P(v), q.stride(-3), k.stride(-3), v.stride(-3), P(a), P(b),
+                                  P(A_log), P(dtb), P(S0), P(S), P(o), P(cu), B, T, Hk,
+                                  Hv, 128, 128, G.F_QK_L2NORM, P(ws), ctypes.c_size_t(size),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == G.GDN_OK, L.gdn_last_error().decode()
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref), w
+        if with_state_out:
+            assert torch.equal(S, S_ref), w
+    ws = torch.empty(base - 1, dtype=torch.uint8, device="cuda")
+    rc = L.gdn_chunked_fwd_ws(P(q), P(k), P(v), q.stride(-3), k.stride(-3), v.stride(-3), P(a), P(b),
+                              P(A_log), P(dtb), P(S0), P(S), P(o_ref), P(cu), B, T,
+                              Hk, Hv, 128, 128, G.F_QK_L2NORM, P(ws), ctypes.c_size_t(base - 1),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == G.GDN_ERR_SHAPE
+    assert G.take_device_error() == 0
