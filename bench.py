@@ -550,6 +550,7 @@ class PrefillLayer:
         self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
         self.schedule = "fused"
         self.ws = None
+        self.ws_cap = 0
         if split:
             self.use_schedule("split")
 
@@ -562,6 +563,8 @@ class PrefillLayer:
         self.schedule = schedule
         if schedule != "fused" and self.ws is None:
             need = G.chunked_workspace_bytes(self.B, self.T, self.hv, not self.uniform)
+            if self.ws_cap:            # bounded workspace: the library runs the call in windows
+                need = max(min(need, self.ws_cap), G.chunked_workspace_min_bytes(self.B, self.hv, True))
             self.ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
 
     def use_split(self, on):
@@ -690,6 +693,7 @@ def run_prefill(args, lib, device, world):
     schedules = ["fused", "split", "split_norm"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
     for name, lens in cases:
         X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
+        X.ws_cap = int(args.prefill_ws_gb * 1e9)
         gathered = None
         if world > 1:
             gathered = torch.empty((world,) + tuple(X.out.shape), dtype=torch.bfloat16, device=device)
@@ -839,6 +843,8 @@ def main():
     ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm"], default="auto",
                     help="chunked schedule for configs 3/4; auto times both and reports the faster")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
+    ap.add_argument("--prefill-ws-gb", type=float, default=0.0,
+                    help="cap the split schedule's workspace (GB); smaller than one pass runs in windows")
     args = ap.parse_args()
     if args.small:
         args.batch, args.layers, args.sweep = 64, 2, ""
