@@ -92,8 +92,9 @@ constexpr uint32_t kPX = 32768;                     // X, plain, over the Q rows
 constexpr uint32_t kPKt = 0;                        // K^T diag(beta g r_k) 128 x 64, after the solve
 constexpr uint32_t kPVt = 32768;                    // V^T diag(beta) 128 x 64, after the solve
 constexpr uint32_t kPTi = 65536;                    // T^-1 64 x 64
-constexpr uint32_t kPSc = kPTi + kC * kC * 4;       // per-token scalars, 10 x 64
-constexpr uint32_t kPBar = kPSc + 10 * kC * 4;      // mbarrier, TMEM base, slot broadcast
+constexpr int kPrepHeads = 4;                       // value heads per prep CTA at most (one key head's)
+constexpr uint32_t kPSc = kPTi + kC * kC * 4;       // per-token scalars, 10 x 64 per value head
+constexpr uint32_t kPBar = kPSc + kPrepHeads * 10 * kC * 4;   // mbarrier, TMEM base, slot broadcast
 constexpr uint32_t kPrepSmem = kPBar + 64;
 static_assert(kPY + 3 * 256 * 4 <= kPX, "prep: solve temporaries overlap X");
 static_assert(kPX + kC * kPad * 4 <= kPTi, "prep: X overlaps T^-1");
@@ -497,17 +498,36 @@ __device__ __forceinline__ void phase_epi_a(Ctx& c, uint32_t col, unsigned char*
       }
       *reinterpret_cast<float4*>(at(m_dst, i, c.half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
     }
-    const float sq = c.s_g[i] * c.s_rq[i];
-    for (int cc = c.half * 64; cc < c.half * 64 + 64; cc += 4) {
-      float4 v = *reinterpret_cast<const float4*>(at(c.sKQ, kC + i, cc, kSbo128));
-      v.x = tc::to_tf32(v.x * sq);
-      v.y = tc::to_tf32(v.y * sq);
-      v.z = tc::to_tf32(v.z * sq);
-      v.w = tc::to_tf32(v.w * sq);
-      *reinterpret_cast<float4*>(at(q_dst, i, cc, kSbo128)) = v;
+    if (q_dst) {
+      const float sq = c.s_g[i] * c.s_rq[i];
+      for (int cc = c.half * 64; cc < c.half * 64 + 64; cc += 4) {
+        float4 v = *reinterpret_cast<const float4*>(at(c.sKQ, kC + i, cc, kSbo128));
+        v.x = tc::to_tf32(v.x * sq);
+        v.y = tc::to_tf32(v.y * sq);
+        v.z = tc::to_tf32(v.z * sq);
+        v.w = tc::to_tf32(v.w * sq);
+        *reinterpret_cast<float4*>(at(q_dst, i, cc, kSbo128)) = v;
+      }
     }
   }
   __syncthreads();
+}
+
+// diag(g r_q) Q rows of [K; Q] into q_dst with the decay g of scalar block
+// s_g (all 256 threads: thread -> token i, 32-dim quarter).  No barrier.
+__device__ __forceinline__ void phase_qtilde(const Ctx& c, const float* s_g, unsigned char* q_dst) {
+  const int i = c.tid >> 2;
+  const int c0 = (c.tid & 3) * 32;
+  const float sq = s_g[i] * c.s_rq[i];
+#pragma unroll
+  for (int cc = c0; cc < c0 + 32; cc += 4) {
+    float4 v = *reinterpret_cast<const float4*>(at(c.sKQ, kC + i, cc, kSbo128));
+    v.x = tc::to_tf32(v.x * sq);
+    v.y = tc::to_tf32(v.y * sq);
+    v.z = tc::to_tf32(v.z * sq);
+    v.w = tc::to_tf32(v.w * sq);
+    *reinterpret_cast<float4*>(at(q_dst, i, cc, kSbo128)) = v;
+  }
 }
 
 // T^-1 = (I + A)^-1 by forward substitution on all 64 columns at once:
@@ -874,7 +894,11 @@ __device__ __forceinline__ void phase_epi_prep(Ctx& c, unsigned char* rec) {
   if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
 }
 
-__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkParams p) {
+// One CTA per (chunk, key head) handles the hpc value heads that share that
+// key head (hpc = Hv / Hk when it is at most kPrepHeads, else one): the K / Q
+// rows, their norms and [K; Q] K^T are formed once; gates, A, the solve, M,
+// the columns and U0 / W per value head.
+__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkParams p, int hpc) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const long long slot = blockIdx.x;
   int* s_bc = reinterpret_cast<int*>(sm + kPBar + 16);
@@ -888,38 +912,63 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
   const int b = s_bc[0];
   if (b < 0) return;
   const int ch = s_bc[1];
+  const int h0 = blockIdx.y * hpc;
   Ctx c;
-  ctx_init(c, p, blockIdx.y);
+  ctx_init(c, p, h0);
   ctx_prep_layout(c, sm);
+  float* sc0 = reinterpret_cast<float*>(sm + kPSc);
+  auto head_scalars = [&](int j) {             // scalar block of head j; the norms live in block 0
+    ctx_scalars(c, sc0 + j * 10 * kC);
+    c.s_rk = sc0 + 320;
+    c.s_rq = sc0 + 384;
+  };
+  auto head_gates = [&](int j) {               // per-head constants of value head h0 + j
+    c.h = h0 + j;
+    c.A_h = expf(__ldg(p.A_log + c.h));
+    c.dtb = __ldg(p.dt_bias + c.h);
+  };
   long long s0, s1;
   seq_range(p, b, s0, s1);
   const long long t0 = s0 + static_cast<long long>(ch) * kC;
   const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-  unsigned char* rec = record(p, slot, c.h);
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kPBar + 8), c.bar, 1, kPrepTmemCols);
 
-  phase_gates(p, c, t0, nvalid);
+  for (int j = 0; j < hpc; ++j) {              // gates of every value head first
+    head_scalars(j);
+    head_gates(j);
+    phase_gates(p, c, t0, nvalid);
+  }
   GDN_TICK(16);
-  phase_rows(p, c, t0, s0, nvalid);
+  head_scalars(0);
+  phase_rows(p, c, t0, s0, nvalid);            // shared K / Q rows and norms (ends with a barrier)
   GDN_TICK(17);
-  bool ok = phase_mma_a(c, kPColGP);
+  bool ok = phase_mma_a(c, kPColGP);           // G | P, shared, kept in TMEM for every head
   GDN_TICK(18);
-  if (ok) {
-    phase_epi_a(c, kPColGP, rec + kRecM, rec + kRecQ);   // A over the K rows; M, Qs to the record
+  for (int j = 0; j < hpc && ok; ++j) {
+    head_scalars(j);
+    head_gates(j);
+    unsigned char* rec = record(p, slot, c.h);
+    if (j == 0) {                              // Q rows are overwritten by the first solve: Qs for all heads now
+      for (int jj = 0; jj < hpc; ++jj) phase_qtilde(c, sc0 + jj * 10 * kC + 128, record(p, slot, h0 + jj) + kRecQ);
+    }
+    phase_epi_a(c, kPColGP, rec + kRecM, nullptr);     // A over the K rows; M to the record
     GDN_TICK(19);
-    phase_solve(c);                                       // X over the Q rows
+    phase_solve(c);                                    // X over the Q rows
     GDN_TICK(20);
-    phase_cols(p, c, t0, nvalid, rec + kRecKh);           // K^T, V^T over A and X; K-hat^T to the record
+    phase_cols(p, c, t0, nvalid, rec + kRecKh);        // K^T, V^T over A and X; K-hat^T to the record
     tc::fence_before_sync();
     __syncthreads();
     GDN_TICK(21);
     ok = phase_mma_bc_prep(c);
     GDN_TICK(22);
+    if (ok) {
+      phase_epi_prep(c, rec);
+      tc::fence_before_sync();
+      __syncthreads();
+      GDN_TICK(23);
+    }
   }
-  if (ok) {
-    phase_epi_prep(c, rec);
-    GDN_TICK(23);
-  } else {
+  if (!ok) {
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);
   }
@@ -1355,8 +1404,10 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
       if (rc != GDN_OK) return rc;
     }
     if (p.n_slots > 0) {
-      chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv)), kThreads, kPrepSmem,
-                          st>>>(p);
+      const int ratio = p.Hv / p.Hk;
+      const int hpc = ratio <= kPrepHeads ? ratio : 1;
+      chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv / hpc)), kThreads,
+                          kPrepSmem, st>>>(p, hpc);
       rc = cuda_status(cudaGetLastError(), "chunk prep launch");
       if (rc != GDN_OK) return rc;
     }

@@ -225,8 +225,8 @@ def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, sta
     else:
         B, T = q.shape[0], q.shape[1]
         lead = (B, T)
-        if B > 1 and (q.stride(0) != T * q.stride(-3) or k.stride(0) != T * k.stride(-3)
-                      or v.stride(0) != T * v.stride(-3) or z.stride(0) != T * z.stride(-3)):
+        if B > 1 and T > 0 and (q.stride(0) != T * q.stride(-3) or k.stride(0) != T * k.stride(-3)
+                                or v.stride(0) != T * v.stride(-3) or z.stride(0) != T * z.stride(-3)):
             raise ValueError("batch rows must follow each other (token-major storage)")
     dev = _dev(a, b, A_log, dt_bias, z, gamma, state_in, state_out, out, cu_seqlens)
     if out is None:
@@ -339,7 +339,7 @@ def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=
     else:
         B, T = q.shape[0], q.shape[1]
         lead = (B, T)
-        if B > 1 and (q.stride(0) != T * qs or k.stride(0) != T * ks or v.stride(0) != T * vs):
+        if B > 1 and T > 0 and (q.stride(0) != T * qs or k.stride(0) != T * ks or v.stride(0) != T * vs):
             raise ValueError("batch rows must follow each other (token-major storage)")
     dev = _dev(a, b, A_log, dt_bias, state_in, state_out, o, cu_seqlens)
     if o is None:

@@ -429,3 +429,43 @@ def test_split_schedule_in_windows_matches_one_pass(lens, with_state_out):
                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == G.GDN_ERR_SHAPE
     assert G.take_device_error() == 0
+
+
+@pytest.mark.parametrize("split", SCHEDULES)
+def test_chunked_empty_batch_copies_the_state(split):
+    """T = 0 (uniform) and all-empty packed sequences: o is empty and the final
+    state equals the start state (zeros when none is given)."""
+    rng = np.random.default_rng(95)
+    Hk, Hv = 1, 3
+    S0 = rng.standard_normal((2, Hv, 128, 128), dtype=np.float32) * np.float32(0.05)
+    q = torch.empty((2, 0, Hk, 128), dtype=torch.bfloat16, device="cuda")
+    v = torch.empty((2, 0, Hv, 128), dtype=torch.bfloat16, device="cuda")
+    g = torch.empty((2, 0, Hv), device="cuda")
+    A_log, dtb = dev(np.zeros(Hv, np.float32)), dev(np.zeros(Hv, np.float32))
+    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, state_in=dev(S0), split=split)
+    torch.cuda.synchronize()
+    assert o.numel() == 0 and np.array_equal(host(S), S0)
+    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, split=split)
+    torch.cuda.synchronize()
+    assert not host(S).any()
+    cu = dev(np.zeros(4, np.int32), torch.int32)             # three empty packed sequences
+    qp = torch.empty((0, Hk, 128), dtype=torch.bfloat16, device="cuda")
+    vp = torch.empty((0, Hv, 128), dtype=torch.bfloat16, device="cuda")
+    gp = torch.empty((0, Hv), device="cuda")
+    S3 = rng.standard_normal((3, Hv, 128, 128), dtype=np.float32)
+    o, S = G.chunked_fwd(qp, qp, vp, gp, gp, A_log, dtb, state_in=dev(S3), cu_seqlens=cu, split=split)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(S), S3)
+    assert G.take_device_error() == 0
+
+
+@pytest.mark.parametrize("split", SCHEDULES)
+@pytest.mark.parametrize("Hk,Hv", [(1, 1), (2, 2), (4, 8), (1, 6)])
+def test_chunked_head_ratios(Hk, Hv, split):
+    """GQA ratios other than 16:48 (key head i serves value heads i*r .. i*r+r-1)."""
+    rng = np.random.default_rng(96 + Hk * 10 + Hv)
+    inp = chunk_inputs(rng, 2, 130, Hk, Hv)
+    o, S = run_chunked(inp, split=split)
+    ro, rS = oracle_chunked(inp)
+    assert O.rel_l2(host(o), ro) < PREFILL_TOL
+    assert O.rel_l2(host(S), rS) < PREFILL_TOL
