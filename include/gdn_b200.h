@@ -209,8 +209,9 @@ int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
  * :625-627, python/qwen35.py:159-180).  z: bf16, element (t, h, d) at
  * z[t*z_stride + h*128 + d]; gamma (128) fp32.  out_stride / out_head0 place
  * this call's Hv heads inside a wider row (e.g. the all-heads output of a
- * head-sharded layer).  Flags: GDN_F_QK_L2NORM only.  Other arguments and
- * the workspace as gdn_chunked_fwd_ws.
+ * head-sharded layer); out 16-byte aligned, out_stride a multiple of 8.
+ * Flags: GDN_F_QK_L2NORM only.  Other arguments and the workspace as
+ * gdn_chunked_fwd_ws.
  */
 int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v,
                             long long q_stride, long long k_stride, long long v_stride,
@@ -241,6 +242,53 @@ int gdn_spec_verify(const float* p, const float* q, const int32_t* draft,
                     const float* u_accept, const float* u_sample, int B, int k, long long V,
                     int32_t* accept_len, int32_t* commit_n, int32_t* token, int32_t* err_flag,
                     void* stream);
+
+/*
+ * gdn_chunked_norm_gather_ws -- gdn_chunked_norm_fwd_ws of one rank of a
+ * head-sharded layer whose epilogue writes the normed rows straight into the
+ * all-heads output buffer of every rank over NVLink (the reference's layer
+ * boundary, cpp/src/model.cpp:625-641, with the per-head outputs gathered):
+ * compute and the all-gather are one kernel, no separate collective.
+ *   out_ranks[r]  device pointer of rank r's output buffer (this process's
+ *                 view of it, e.g. a CUDA IPC / symmetric-memory mapping),
+ *                 out_elems bf16 elements each, 16-byte aligned; this rank's
+ *                 heads land at head offset out_head0 of every row
+ *   flag_ranks[r] rank r's array of `world` uint32 counters (same kind of
+ *                 mapping); after its scan this call adds 1 to
+ *                 flag_ranks[r][rank] for every r (release, system scope)
+ * 1 <= world <= 8.  The host arrays are read during the call.  A consumer
+ * waits with gdn_gather_wait before reading its buffer; buffers must not be
+ * read by a consumer while a later call writes them (alternate two).
+ */
+int gdn_chunked_norm_gather_ws(const void* q, const void* k, const void* v,
+                               long long q_stride, long long k_stride, long long v_stride,
+                               const float* a, const float* b, const float* A_log, const float* dt_bias,
+                               const float* state_in, float* state_out,
+                               const void* z, long long z_stride, const float* gamma, float eps,
+                               void* const* out_ranks, uint32_t* const* flag_ranks, int world, int rank,
+                               long long out_elems, long long out_stride, int out_head0,
+                               const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                               unsigned flags, void* workspace, size_t workspace_size, void* stream);
+
+/*
+ * gdn_gather_wait -- stream-ordered wait until every rank r < world has
+ * signalled at least `expected` calls in flags[r] (this rank's counter array
+ * of gdn_chunked_norm_gather_ws), with acquire semantics at system scope.
+ * Bounded: after about 4 s it sets *err_flag and returns.
+ */
+int gdn_gather_wait(const uint32_t* flags, int world, unsigned expected, int32_t* err_flag, void* stream);
+
+/*
+ * gdn_ipc_export / gdn_ipc_open / gdn_ipc_close -- share a device buffer with
+ * the other processes of a head-sharded layer for gdn_chunked_norm_gather_ws:
+ * export writes the 64-byte CUDA IPC handle of the allocation holding `ptr`
+ * and ptr's offset in it; a peer opens it with its own device current (peer
+ * access from that device is enabled lazily) and gets the mapping's base
+ * (for gdn_ipc_close) and the buffer's address.  Plain peer mappings.
+ */
+int gdn_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+int gdn_ipc_open(const void* handle, size_t offset, void** base_out, void** ptr_out);
+int gdn_ipc_close(void* base);
 
 /* Size of the fixed device scratch that gdn_chunked_fwd_static uses. */
 #define GDN_CHUNKED_STATIC_SCRATCH_BYTES (64ull << 20)

@@ -131,7 +131,8 @@ constexpr uint32_t kScanG2 = kRecM;
 constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
 constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
 constexpr uint32_t kScanNorm = kScanBar + 64;       // fused norm: partial sums of squares, 4 x 64 floats
-constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
+constexpr uint32_t kScanOut = kScanNorm + 4 * kC * 4;   // fused norm: the chunk's bf16 output rows, 64 x 128
+constexpr uint32_t kScanSmem = kScanOut + kC * kD * 2;
 
 __host__ __device__ constexpr size_t records_offset(int B) {
   return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
@@ -169,6 +170,12 @@ struct ChunkParams {
   float eps;
   long long out_stride;
   int out_head0;
+  // fused norm output destinations: this rank's rows go to every buffer in
+  // dst (the caller's own first or not; one per rank of a head-sharded
+  // layer, same layout in each), out_elems elements each
+  __nv_bfloat16* dst[8];
+  int n_dst;
+  long long out_elems;
 };
 
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
@@ -1141,14 +1148,28 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
       s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
       if ((c.lane & 3) == 0) s_part[c.quarter * kC + tok + (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0)] = s1v;
       asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");   // the 4 warps of this column group
-      const size_t base = static_cast<size_t>(t0 + tok) * p.out_stride + static_cast<size_t>(p.out_head0 + c.h) * kD + c.row;
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
+      // normalised rows into the shared tile, then 16-byte pieces of the 8 rows to every destination
+      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(sm + kScanOut);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float ss = s_part[tok + i] + s_part[kC + tok + i] + s_part[2 * kC + tok + i] + s_part[3 * kC + tok + i];
         const float r = rsqrtf(ss / static_cast<float>(kD) + p.eps);
         const float sg = __fdividef(1.f, 1.f + __expf(-zz[i]));
-        if (i < nv) o[i * p.out_stride] = __float2bfloat16_rn((y[i] * r * gam) * (zz[i] * sg));
+        tile[(tok + i) * kD + c.row] = __float2bfloat16_rn((y[i] * r * gam) * (zz[i] * sg));
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");
+      const int tt = c.quarter * 32 + c.lane;          // 128 threads: 8 rows x 16 pieces of 16 bytes
+      const int ti = tt >> 4, seg = (tt & 15) * 8;
+      if (ti < nv) {
+        const uint4 piece = *reinterpret_cast<const uint4*>(tile + (tok + ti) * kD + seg);
+        const long long off = (t0 + tok + ti) * p.out_stride + static_cast<long long>(p.out_head0 + c.h) * kD + seg;
+        if (off + 8 <= p.out_elems) {
+#pragma unroll
+          for (int d = 0; d < 8; ++d)
+            if (d < p.n_dst) *reinterpret_cast<uint4*>(p.dst[d] + off) = piece;
+        } else if (c.lane == 0) {
+          atomicExch(p.err, 1);
+        }
       }
       return;
     }
@@ -1256,6 +1277,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   } else if (!mw) {
     state_store(p.carry, c, bh, cDR, cg * 32, 32);
   }
+  if (NORM && p.n_dst > 1) __threadfence_system();  // peer stores performed before the call's signal
   tc::fence_before_sync();
   __syncthreads();
   if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
@@ -1313,7 +1335,8 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
   p = ChunkParams{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                   static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
                   state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err,
-                  nullptr, nullptr, 0, 0, 0, 0, 0, nullptr, nullptr, 0, nullptr, 0.f, 0, 0};
+                  nullptr, nullptr, 0, 0, 0, 0, 0, nullptr, nullptr, 0, nullptr, 0.f, 0, 0,
+                  {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr}, 0, 0};
   return GDN_OK;
 }
 
@@ -1475,32 +1498,41 @@ extern "C" int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v, l
   return run_split(p, T, static_cast<unsigned char*>(workspace), workspace_size, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
-                                       long long k_stride, long long v_stride, const float* a, const float* b,
-                                       const float* A_log, const float* dt_bias, const float* state_in,
-                                       float* state_out, const void* z, long long z_stride, const float* gamma,
-                                       float eps, void* out, long long out_stride, int out_head0,
-                                       const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
-                                       unsigned flags, void* workspace, size_t workspace_size, void* stream) {
-  clear_error();
+namespace gdn {
+namespace {
+
+// Shared checks and launch of the fused-norm split schedule writing to n_dst
+// destinations of out_elems elements each.
+int run_norm(const void* q, const void* k, const void* v, long long q_stride, long long k_stride,
+             long long v_stride, const float* a, const float* b, const float* A_log, const float* dt_bias,
+             const float* state_in, float* state_out, const void* z, long long z_stride, const float* gamma,
+             float eps, void* const* dst, int n_dst, long long out_elems, long long out_stride, int out_head0,
+             const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv, unsigned flags,
+             void* workspace, size_t workspace_size, cudaStream_t stream) {
   if (flags & ~GDN_F_QK_L2NORM) return fail(GDN_ERR_FLAGS, "only GDN_F_QK_L2NORM applies (out is bf16)");
+  if (n_dst < 1 || n_dst > 8 || !dst) return fail(GDN_ERR_SHAPE, "1 to 8 output destinations");
   ChunkParams p;
-  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, out,
+  int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, dst[0],
                         cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags | GDN_F_O_BF16);
   if (rc != GDN_OK || B == 0) return rc;
   const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
   if (total > 0 && (!z || !gamma)) return fail(GDN_ERR_NULL, "z and gamma are required");
   if (out_head0 < 0 || out_stride < (static_cast<long long>(out_head0) + Hv) * kD || z_stride < static_cast<long long>(Hv) * kD)
     return fail(GDN_ERR_SHAPE, "out_stride / out_head0 / z_stride do not fit Hv heads of 128");
+  const long long used = total > 0 ? (total - 1) * out_stride + (static_cast<long long>(out_head0) + Hv) * kD : 0;
+  if (out_elems < used) return fail(GDN_ERR_SHAPE, "output of %lld elements, %lld needed", out_elems, used);
+  if (out_stride % 8) return fail(GDN_ERR_ALIGN, "out_stride must be a multiple of 8 elements (16 bytes)");
+  for (int d = 0; d < n_dst; ++d)
+    if (!dst[d] || !aligned(dst[d], 16)) return fail(GDN_ERR_ALIGN, "output %d is null or not 16-byte aligned", d);
   if (!aligned(z, 2) || !aligned(gamma, 4) || !(eps >= 0.f)) return fail(GDN_ERR_ALIGN, "z, gamma misaligned or eps < 0");
   if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes for one window)",
                               workspace_bytes(B, T, Hv, cu_seqlens != nullptr));
   if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");
   const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * 4;
-  const size_t obytes = total > 0 ? static_cast<size_t>(total - 1) * out_stride * 2 + (out_head0 + Hv) * kD * 2 : 0;
+  const size_t obytes = static_cast<size_t>(used) * 2;
   if (overlap(workspace, workspace_size, state_in, sbytes) || overlap(workspace, workspace_size, state_out, sbytes) ||
-      overlap(workspace, workspace_size, out, obytes) || overlap(out, obytes, state_in, sbytes) ||
-      overlap(out, obytes, state_out, sbytes))
+      overlap(workspace, workspace_size, dst[0], obytes) || overlap(dst[0], obytes, state_in, sbytes) ||
+      overlap(dst[0], obytes, state_out, sbytes))
     return fail(GDN_ERR_ALIAS, "workspace, out and the states must not overlap");
   if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
   p.z = static_cast<const __nv_bfloat16*>(z);
@@ -1509,7 +1541,103 @@ extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void*
   p.eps = eps;
   p.out_stride = out_stride;
   p.out_head0 = out_head0;
-  return run_split(p, T, static_cast<unsigned char*>(workspace), workspace_size, static_cast<cudaStream_t>(stream));
+  for (int d = 0; d < n_dst; ++d) p.dst[d] = static_cast<__nv_bfloat16*>(dst[d]);
+  p.n_dst = n_dst;
+  p.out_elems = out_elems;
+  return run_split(p, T, static_cast<unsigned char*>(workspace), workspace_size, stream);
+}
+
+struct FlagPtrs {
+  uint32_t* f[8];
+};
+
+// One thread per destination rank: after the call's scan kernels (which
+// fenced their peer stores at system scope), count one more finished call
+// in every rank's flag word of this rank.
+__global__ void gather_signal_kernel(FlagPtrs fp, int rank, int world) {
+  const int r = threadIdx.x;
+  if (r < world) {
+    __threadfence_system();
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(fp.f[r] + rank) : "memory");
+  }
+}
+
+// Wait until every rank has signalled `expected` calls (bounded: about 4 s of
+// polling, then *err = 1 and return).
+__global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t expected, int32_t* err) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+    if (static_cast<int32_t>(v - expected) >= 0) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 4000000000ull) {
+      atomicExch(err, 1);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_chunked_norm_fwd_ws(const void* q, const void* k, const void* v, long long q_stride,
+                                       long long k_stride, long long v_stride, const float* a, const float* b,
+                                       const float* A_log, const float* dt_bias, const float* state_in,
+                                       float* state_out, const void* z, long long z_stride, const float* gamma,
+                                       float eps, void* out, long long out_stride, int out_head0,
+                                       const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                                       unsigned flags, void* workspace, size_t workspace_size, void* stream) {
+  clear_error();
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  const long long used = total > 0 ? (total - 1) * out_stride + (static_cast<long long>(out_head0) + Hv) * 128 : 0;
+  void* dst[1] = {out};
+  return run_norm(q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, z, z_stride,
+                  gamma, eps, dst, 1, used, out_stride, out_head0, cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags, workspace,
+                  workspace_size, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gdn_chunked_norm_gather_ws(const void* q, const void* k, const void* v, long long q_stride,
+                                          long long k_stride, long long v_stride, const float* a, const float* b,
+                                          const float* A_log, const float* dt_bias, const float* state_in,
+                                          float* state_out, const void* z, long long z_stride, const float* gamma,
+                                          float eps, void* const* out_ranks, uint32_t* const* flag_ranks, int world,
+                                          int rank, long long out_elems, long long out_stride, int out_head0,
+                                          const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                                          unsigned flags, void* workspace, size_t workspace_size, void* stream) {
+  clear_error();
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || !out_ranks || !flag_ranks)
+    return fail(GDN_ERR_SHAPE, "world %d, rank %d: need 1 <= world <= 8, 0 <= rank < world, pointer arrays", world,
+                rank);
+  FlagPtrs fp{};
+  for (int r = 0; r < world; ++r) {
+    if (!flag_ranks[r] || !aligned(flag_ranks[r], 4)) return fail(GDN_ERR_ALIGN, "flag word array %d", r);
+    fp.f[r] = flag_ranks[r];
+  }
+  // this rank's own buffer first, so the output checks apply to it
+  void* dst[8];
+  for (int r = 0; r < world; ++r) dst[r] = out_ranks[(rank + r) % world];
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = run_norm(q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, z, z_stride,
+                    gamma, eps, dst, world, out_elems, out_stride, out_head0, cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags,
+                    workspace, workspace_size, st);
+  if (rc != GDN_OK) return rc;
+  gather_signal_kernel<<<1, 32, 0, st>>>(fp, rank, world);
+  return cuda_status(cudaGetLastError(), "gather signal launch");
+}
+
+extern "C" int gdn_gather_wait(const uint32_t* flags, int world, unsigned expected, int32_t* err_flag, void* stream) {
+  clear_error();
+  if (world < 1 || world > 8) return fail(GDN_ERR_SHAPE, "world %d: need 1 <= world <= 8", world);
+  if (!flags || !err_flag) return fail(GDN_ERR_NULL, "flags and err_flag are required");
+  if (!aligned(flags, 4) || !aligned(err_flag, 4)) return fail(GDN_ERR_ALIGN, "flags, err_flag 4-byte aligned");
+  gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, expected, err_flag);
+  return cuda_status(cudaGetLastError(), "gather wait launch");
 }
 
 // Scratch of gdn_chunked_fwd_static: a fixed device array, so that the call

@@ -57,6 +57,13 @@ SIGNATURES = {
     "gdn_chunked_workspace_bytes": [_i] * 4,
     "gdn_chunked_workspace_min_bytes": [_i] * 3,
     "gdn_chunked_fwd_static": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
+    "gdn_chunked_norm_gather_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 7 + [ctypes.c_longlong, _vp,
+                                  ctypes.c_float, _vp, _vp, _i, _i, ctypes.c_longlong, ctypes.c_longlong, _i, _vp]
+                                  + [_i] * 6 + [_u, _vp, ctypes.c_size_t, _vp],
+    "gdn_gather_wait": [_vp, _i, _u, _vp, _vp],
+    "gdn_ipc_export": [_vp, _vp, _vp],
+    "gdn_ipc_open": [_vp, ctypes.c_size_t, _vp, _vp],
+    "gdn_ipc_close": [_vp],
     "gdn_spec_verify": [_vp] * 5 + [_i, _i, ctypes.c_longlong] + [_vp] * 5,
     "gdn_chunked_norm_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 7 + [ctypes.c_longlong, _vp,
                                ctypes.c_float, _vp, ctypes.c_longlong, _i, _vp] + [_i] * 6

@@ -1,0 +1,31 @@
+"""Multi-GPU checks, each run as one process per GPU under torch.distributed
+(skipped when fewer than 2 GPUs are visible): the gathered norm of
+gdn_chunked_norm_gather_ws against the single-GPU path
+(tests/mgpu/norm_gather_check.py)."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_norm_gather_over_nvlink_matches_single_gpu():
+    n = 2 if torch.cuda.device_count() < 4 else 4
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(HERE, "mgpu", "norm_gather_check.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[:4000] + "\n...\n" + r.stdout[-2000:] + r.stderr[:6000]
