@@ -525,7 +525,7 @@ class PrefillLayer:
     bf16 projection output (C = 2*hk*128 + hv*128), conv weights, z, gamma,
     gate inputs.  `lens` packs sequences of those lengths (cu_seqlens)."""
 
-    def __init__(self, lens, device, seed, hk=HK, hv=HV, split=False):
+    def __init__(self, lens, device, seed, hk=HK, hv=HV, split=False, head0=0, hv_total=None):
         g = torch.Generator(device=device)
         g.manual_seed(seed)
         C = 2 * hk * D + hv * D
@@ -551,6 +551,8 @@ class PrefillLayer:
         self.schedule = "fused"
         self.ws = None
         self.ws_cap = 0
+        self.head0, self.hv_total = head0, hv_total if hv_total is not None else hv
+        self.pgs, self.pg_i, self.pg_last = None, 0, None
         if split:
             self.use_schedule("split")
 
@@ -558,9 +560,16 @@ class PrefillLayer:
         """fused: gdn_chunked_fwd then the gated norm; split: gdn_chunked_fwd_ws
         (prep + scan on a workspace allocated here, outside any timed region)
         then the norm; split_norm: gdn_chunked_norm_fwd_ws, the norm fused
-        into the scan (no separate norm launch)."""
+        into the scan (no separate norm launch); split_gather (head-sharded
+        ranks): gdn_chunked_norm_gather_ws, the scan also storing every
+        chunk's rows into all ranks' (tokens, Hv_total, 128) outputs over
+        NVLink, then gdn_gather_wait -- no separate all-gather.  Two
+        PeerGather buffers alternate across layers."""
         import gdn_b200 as G
         self.schedule = schedule
+        if schedule == "split_gather" and self.pgs is None:
+            import gdn_shard
+            self.pgs = [gdn_shard.PeerGather(self.N, self.hv_total, self.x.device) for _ in range(2)]
         if schedule != "fused" and self.ws is None:
             need = G.chunked_workspace_bytes(self.B, self.T, self.hv, not self.uniform)
             if self.ws_cap:            # bounded workspace: the library runs the call in windows
@@ -589,6 +598,14 @@ class PrefillLayer:
         q = ctypes.c_void_p(base)
         k = ctypes.c_void_p(base + hk * D * 2)
         v = ctypes.c_void_p(base + 2 * hk * D * 2)
+        if self.schedule == "split_gather":
+            pg = self.pgs[self.pg_i]
+            self.pg_i ^= 1
+            pg.run(lib, q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias), None, P(self.S),
+                   P(self.z), self.hv * D, P(self.gamma), 1e-6, self.head0, self._cu(), self.B, self.T, hk,
+                   self.hv, G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
+            self.pg_last = pg
+            return
         if self.schedule == "split_norm":
             rc = lib.gdn_chunked_norm_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log),
                                              P(self.dt_bias), None, P(self.S), P(self.z), self.hv * D,
@@ -607,6 +624,9 @@ class PrefillLayer:
             raise RuntimeError(lib.gdn_last_error().decode())
 
     def norm(self, lib, h):
+        if self.schedule == "split_gather":
+            self.pg_last.wait(lib, h)      # norm and gather fused into the scan; wait for every rank
+            return
         if self.schedule == "split_norm":
             return                         # fused into the scan
         P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
@@ -623,6 +643,17 @@ class PrefillLayer:
     def flops(self):
         return FLOP_PER_TOKEN_HEAD * self.N * self.hv
 
+    def gather_errors(self):
+        """Timeouts recorded by gdn_gather_wait (0 when every wait completed)."""
+        return sum(int(pg.err.item()) for pg in self.pgs) if self.pgs else 0
+
+    def close(self):
+        """Unmap the PeerGather buffers (collective)."""
+        if self.pgs:
+            for pg in self.pgs:
+                pg.close()
+            self.pgs = None
+
 
 def config4_lengths(seed=4, B=8, lo=16384, hi=65536):
     """B=8 sequences of seeded lengths uniform in [16384, 65536]."""
@@ -636,9 +667,11 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
     st = torch.cuda.current_stream(device)
     h = ctypes.c_void_p(st.cuda_stream)
 
+    fused_gather = X.schedule == "split_gather"
+
     def layer():
         X.step(lib, h)
-        if gathered is not None:
+        if gathered is not None and not fused_gather:
             torch.distributed.all_gather_into_tensor(gathered, X.out)
 
     for _ in range(warmup):
@@ -664,7 +697,11 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
         durs["chunked"].append(ev[1].elapsed_time(ev[2]))
         durs["norm"].append(ev[2].elapsed_time(ev[3]))
     kms = {k: statistics.mean(v) for k, v in durs.items()}
-    if gathered is not None:
+    if fused_gather:
+        torch.cuda.synchronize(device)
+        if max_over_ranks(float(X.gather_errors()), world, device):   # every rank raises together
+            raise RuntimeError("gdn_gather_wait timed out on a rank: peer gather incomplete")
+    if gathered is not None and not fused_gather:
         # the same layer without the all-gather (recurrence throughput alone), max over ranks
         barrier(world)
         e0.record(st)
@@ -679,7 +716,8 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
 
 def run_prefill(args, lib, device, world):
     """Configs 3 and 4 on this rank's K-head shard (16/N key, 48/N value heads);
-    for N > 1 each layer ends with the NCCL all-gather of the bf16 outputs.
+    for N > 1 each layer ends with the NCCL all-gather of the bf16 outputs, or
+    (split_gather) the scan itself stores them into every rank's output.
     tokens/s counts the layer's tokens once (all heads) per max-over-ranks second."""
     import gdn_shard
     _, tf_peak, peak_kind = peaks()
@@ -691,8 +729,10 @@ def run_prefill(args, lib, device, world):
     if not args.no_config4:
         cases.append(("config4", config4_lengths()))
     schedules = ["fused", "split", "split_norm"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
+    if world > 1 and args.prefill_schedule == "auto" and not args.no_peer_gather:
+        schedules.append("split_gather")
     for name, lens in cases:
-        X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv)
+        X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv, head0=shard.v0, hv_total=HV)
         X.ws_cap = int(args.prefill_ws_gb * 1e9)
         gathered = None
         if world > 1:
@@ -703,18 +743,21 @@ def run_prefill(args, lib, device, world):
             X.use_schedule(sched)
             timed[sched] = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1)
                                               if name == "config4" else max(args.warmup, 3), gathered)
+        X.close()
         best = min(timed, key=lambda k: timed[k][0])
         ms, kms = timed[best]
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
         kernel = {"fused": "chunked_kernel", "split": "chunk_prep_kernel + chunk_scan_kernel",
-                  "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>"}[best]
+                  "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>",
+                  "split_gather": "chunk_prep_kernel + chunk_scan_kernel<norm, peer stores>"}[best]
         res[name] = {
             "schedule": best,
             "ms_per_layer_by_schedule": {k: round(v[0], 4) for k, v in timed.items()},
             "workspace_bytes": int(X.ws.numel()) if X.ws is not None else 0,
             "workload": (f"{name}: {X.B} seq, {X.N} tokens, conv(C={X.C}, K=4)+SiLU -> chunked C=64 "
                          f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
-                         + (" -> NCCL all-gather" if world > 1 else "")),
+                         + ((" -> all-gather fused into the scan (NVLink peer stores)" if best == "split_gather"
+                             else " -> NCCL all-gather") if world > 1 else "")),
             "tokens_per_s": round(X.N / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
             **({"tokens_per_s_without_gather": round(X.N / (kms["layer_without_gather"] * 1e-3), 1)}
                if "layer_without_gather" in kms else {}),
@@ -840,8 +883,11 @@ def main():
     ap.add_argument("--no-verify", action="store_true", help="skip the config-2 verify/accept/rollback chain")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
-    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm"], default="auto",
-                    help="chunked schedule for configs 3/4; auto times both and reports the faster")
+    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather"],
+                    default="auto", help="chunked schedule for configs 3/4; auto times each and reports the fastest "
+                    "(split_gather: N > 1 only)")
+    ap.add_argument("--no-peer-gather", action="store_true",
+                    help="N > 1: leave out the schedule whose scan stores into every rank's output over NVLink")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     ap.add_argument("--prefill-ws-gb", type=float, default=0.0,
                     help="cap the split schedule's workspace (GB); smaller than one pass runs in windows")
