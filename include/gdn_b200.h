@@ -123,6 +123,38 @@ int gdn_recurrent_fwd_from_ckpt(const void* q, const void* k, const void* v,
                                 unsigned flags, void* stream);
 
 /*
+ * gdn_recurrent_fwd_pool -- the decode / verify step over a serving batch whose
+ * states live in a slot pool instead of a dense (B, Hv, D, D) array: sequence
+ * b reads and writes slot slots[b] (device int32) of pool (n_slots, Hv, D, D)
+ * fp32, so a continuous-batching engine changes the batch by rewriting
+ * `slots` (a CUDA graph of the step stays valid) and never compacts states.
+ * This is the HBM layout of DeltaCache::state across a batch
+ * (cpp/src/model.hpp:211-227 keeps one dense state per sequence).
+ *   start     pool[slot]; with commit_n / ckpt_src (both or neither) as in
+ *             gdn_recurrent_fwd_from_ckpt: n == 0 -> pool[slot], 1..Tsrc ->
+ *             ckpt_src[b, :, n-1] ((B, Hv, Tsrc, D, D), the previous block's).
+ *   pool_write GDN_POOL_FINAL: pool[slot] := the state after position T-1;
+ *             GDN_POOL_START: pool[slot] := the start state (a committed
+ *             checkpoint materialised -- DeltaCache::commit, cpp/src/model.cpp:
+ *             439-457 -- before a new record-mode block; with T = 0 it is only
+ *             that); GDN_POOL_KEEP: the pool is not written (record mode).
+ * Slots must be distinct within a call.  A slot outside [0, n_slots) gets a
+ * zero start state, its o and ckpt are written, the pool is not, and
+ * *err_flag (may be NULL) is set to 1.  Other arguments as gdn_recurrent_fwd.
+ */
+#define GDN_POOL_KEEP  0
+#define GDN_POOL_FINAL 1
+#define GDN_POOL_START 2
+int gdn_recurrent_fwd_pool(const void* q, const void* k, const void* v,
+                           const float* a, const float* b,
+                           const float* A_log, const float* dt_bias,
+                           float* pool, const int32_t* slots, int n_slots,
+                           const float* ckpt_src, const int32_t* commit_n, int Tsrc,
+                           int pool_write, void* o, float* ckpt, int32_t* err_flag,
+                           int B, int T, int Hk, int Hv, int Dk, int Dv,
+                           unsigned flags, void* stream);
+
+/*
  * gdn_delta_run -- literal swap for delta::run (cpp/src/delta.hpp:66-68):
  * fp32, head-expanded q, k (B,L,H,Dk), v (B,L,H,Dv), precomputed alpha, beta
  * (B,L,H); S NULL for zeros; states (B,H,L,Dv,Dk) or NULL (collect = false).
@@ -347,6 +379,31 @@ int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in, void* sta
  */
 int gdn_conv_commit(const void* state_prev, const void* x, const int32_t* commit_n, void* state_out,
                     int32_t* err_flag, int B, int T, int C, int K, void* stream);
+
+/*
+ * gdn_conv1d_fwd_pool / gdn_conv_ring_append -- the conv window of a serving
+ * batch as a ring per pool slot (no counterpart in the reference, whose
+ * DeltaCache::conv is one dense (1, K-1, C) window per sequence rebuilt by
+ * concatenation, cpp/src/model.cpp:385-395, 446-447).  ring is (n_slots, K-1,
+ * C) bf16 and ring_pos (n_slots) int32 the row of each slot's oldest entry.
+ * gdn_conv1d_fwd_pool is gdn_conv1d_fwd reading sequence b's carried window
+ * from slot slots[b] (oldest first from ring_pos) and writing no state.
+ * gdn_conv_ring_append then moves the first n_b tokens of each sequence into
+ * its ring (n_b = counts[b], or the sequence's length when counts is NULL;
+ * 0 <= n_b <= length): a decode step writes one row instead of shifting K-1,
+ * and after a speculative block counts = commit_n is the conv half of
+ * DeltaCache::commit.  Call append after every conv reading the same slots
+ * (stream order).  Slots must be distinct within a call; a slot outside
+ * [0, n_slots) or an n_b out of range reads a zero window / appends nothing
+ * and sets *err_flag (may be NULL).  A fresh slot needs a zeroed ring and
+ * ring_pos = 0.
+ */
+int gdn_conv1d_fwd_pool(const void* x, const void* w, const void* ring, const int32_t* ring_pos,
+                        const int32_t* slots, int n_slots, void* y, const int32_t* cu_seqlens,
+                        int B, int T, int C, int K, unsigned flags, int32_t* err_flag, void* stream);
+int gdn_conv_ring_append(const void* x, void* ring, int32_t* ring_pos, const int32_t* slots, int n_slots,
+                         const int32_t* counts, const int32_t* cu_seqlens, int B, int T, int C, int K,
+                         int32_t* err_flag, void* stream);
 
 /*
  * gdn_gated_rmsnorm_fwd -- normalise, then gate (GatedRMSNorm,

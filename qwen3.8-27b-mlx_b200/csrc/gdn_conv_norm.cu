@@ -69,6 +69,12 @@ struct ConvParams {
   long long total;                 // tokens
   int B, T, C;
   unsigned flags;
+  // ring pool mode: state_in is (n_slots, K-1, C), sequence b's window is
+  // slot slots[b] read oldest first from row ring_pos[slot]
+  const int32_t* slots;
+  const int32_t* ring_pos;
+  int n_slots;
+  int32_t* err;
 };
 
 // One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
@@ -122,9 +128,26 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
       if (pos >= 0 && row >= 0 && row < p.total) {
         unpack8(*reinterpret_cast<const Bf16x8*>(p.x + row * p.C + c0), win[j]);
       } else if (p.state_in && pos < 0 && pos >= -(kConvK - 1)) {
-        const long long srow = (kConvK - 1) + pos;               // 0 .. K-2
-        unpack8(*reinterpret_cast<const Bf16x8*>(p.state_in + (static_cast<long long>(seq) * (kConvK - 1) + srow) * p.C + c0),
-                win[j]);
+        const long long srow = (kConvK - 1) + pos;               // 0 .. K-2, oldest first
+        const __nv_bfloat16* sp = nullptr;
+        if (p.slots) {
+          const int sl = p.slots[seq];
+          if (sl >= 0 && sl < p.n_slots) {
+            int hd = p.ring_pos[sl] % (kConvK - 1);
+            if (hd < 0) hd += kConvK - 1;
+            sp = p.state_in + (static_cast<long long>(sl) * (kConvK - 1) + (hd + srow) % (kConvK - 1)) * p.C + c0;
+          } else if (p.err) {
+            atomicExch(p.err, 1);
+          }
+        } else {
+          sp = p.state_in + (static_cast<long long>(seq) * (kConvK - 1) + srow) * p.C + c0;
+        }
+        if (sp) {
+          unpack8(*reinterpret_cast<const Bf16x8*>(sp), win[j]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
@@ -236,6 +259,42 @@ __global__ void conv_commit_kernel(const __nv_bfloat16* state_prev, const __nv_b
   }
 }
 
+// Ring append: the first n_b tokens of sequence b (n_b = counts[b], or its
+// length) enter the ring of slot slots[b]: token i goes to row
+// (ring_pos + i) % (K-1), only the last K-1 of them matter, and ring_pos
+// advances by n_b.  One block per sequence, so the position is read by every
+// thread before thread 0 moves it.
+__global__ void __launch_bounds__(256) conv_ring_append_kernel(const __nv_bfloat16* x, __nv_bfloat16* ring,
+                                                              int32_t* ring_pos, const int32_t* slots, int n_slots,
+                                                              const int32_t* counts, const int32_t* cu, int T, int C,
+                                                              int32_t* err) {
+  constexpr int W = kConvK - 1;
+  const int b = blockIdx.x;
+  const long long s_begin = cu ? static_cast<long long>(cu[b]) : static_cast<long long>(b) * T;
+  const long long len = cu ? static_cast<long long>(cu[b + 1]) - cu[b] : T;
+  const int sl = slots[b];
+  const long long n = counts ? static_cast<long long>(counts[b]) : len;
+  if (!(sl >= 0 && sl < n_slots && n >= 0 && n <= len)) {        // uniform over the block
+    if (threadIdx.x == 0 && err) atomicExch(err, 1);
+    return;
+  }
+  if (n == 0) return;
+  int hd = ring_pos[sl] % W;
+  if (hd < 0) hd += W;
+  __syncthreads();
+  const long long first = n > W ? n - W : 0;
+  const int nv = C / kConvVec;
+  const long long work = (n - first) * nv;
+  for (long long idx = threadIdx.x; idx < work; idx += blockDim.x) {
+    const long long i = first + idx / nv;
+    const int c0 = static_cast<int>(idx % nv) * kConvVec;
+    const int r = static_cast<int>((hd + i) % W);
+    *reinterpret_cast<Bf16x8*>(ring + (static_cast<size_t>(sl) * W + r) * C + c0) =
+        *reinterpret_cast<const Bf16x8*>(x + (s_begin + i) * C + c0);
+  }
+  if (threadIdx.x == 0) ring_pos[sl] = static_cast<int32_t>((hd + n) % W);
+}
+
 // Gated RMSNorm: one warp per (token, head) row of 128; lane j holds 4
 // consecutive elements.  out = o * rsqrt(mean(o^2) + eps) * gamma * silu(z).
 __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const void* o, const __nv_bfloat16* z, const float* gamma,
@@ -279,6 +338,8 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const void* o, const
   }
 }
 
+int run_conv(const ConvParams& p, void* stream);
+
 }  // namespace
 }  // namespace gdn
 
@@ -307,7 +368,17 @@ extern "C" int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in
     return fail(GDN_ERR_ALIAS, "state_out overlaps an input or y");
   ConvParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
                static_cast<const __nv_bfloat16*>(state_in), static_cast<__nv_bfloat16*>(state_out),
-               static_cast<__nv_bfloat16*>(y), cu_seqlens, total, B, cu_seqlens ? 0 : T, C, flags};
+               static_cast<__nv_bfloat16*>(y), cu_seqlens, total, B, cu_seqlens ? 0 : T, C, flags,
+               nullptr, nullptr, 0, nullptr};
+  return run_conv(p, stream);
+}
+
+namespace gdn {
+namespace {
+
+int run_conv(const ConvParams& p, void* stream) {
+  const int C = p.C, B = p.B;
+  const long long total = p.total;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned gx = static_cast<unsigned>((C / kConvVec + kConvThreads - 1) / kConvThreads);
   if (total > 0) {
@@ -315,18 +386,72 @@ extern "C" int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in
     if (gy > 65535LL * 1024) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
     // grid.y is limited to 65535: fold extra runs into grid.z is not needed below 2M tokens
     if (gy > 65535) return fail(GDN_ERR_SHAPE, "at most %d tokens per call", 65535 * kConvRun);
-    if (flags & GDN_F_CONV_BF16_OPS) conv1d_kernel<true><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
+    if (p.flags & GDN_F_CONV_BF16_OPS) conv1d_kernel<true><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
     else conv1d_kernel<false><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
     int rc = cuda_status(cudaGetLastError(), "conv1d launch");
     if (rc != GDN_OK) return rc;
   }
-  if (state_out) {
+  if (p.state_out) {
     if (B > 65535) return fail(GDN_ERR_SHAPE, "B=%d too large", B);
     conv_empty_kernel<<<dim3(gx, static_cast<unsigned>(B)), kConvThreads, 0, st>>>(p);
     int rc = cuda_status(cudaGetLastError(), "conv1d empty-sequence launch");
     if (rc != GDN_OK) return rc;
   }
   return GDN_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_conv1d_fwd_pool(const void* x, const void* w, const void* ring, const int32_t* ring_pos,
+                                   const int32_t* slots, int n_slots, void* y, const int32_t* cu_seqlens, int B,
+                                   int T, int C, int K, unsigned flags, int32_t* err_flag, void* stream) {
+  clear_error();
+  if (flags & ~(GDN_F_CONV_BF16_OPS | GDN_F_CONV_NO_SILU))
+    return fail(GDN_ERR_FLAGS, "unknown conv flag bits 0x%x", flags);
+  if (K != kConvK) return fail(GDN_ERR_SHAPE, "K=%d: only the model's kernel size 4 is built", K);
+  if (B < 0 || T < 0 || C <= 0 || C % kConvVec || n_slots <= 0)
+    return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d C=%d n_slots=%d", B, T, C, n_slots);
+  if (B == 0) return GDN_OK;
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  if (!w || !ring || !ring_pos || !slots || (total > 0 && (!x || !y)))
+    return fail(GDN_ERR_NULL, "w, ring, ring_pos, slots, and x and y when there are tokens, are required");
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !aligned(ring, 16) || !aligned(ring_pos, 4) ||
+      !aligned(slots, 4) || !aligned(err_flag, 4))
+    return fail(GDN_ERR_ALIGN, "x, w, y, ring 16-byte aligned; ring_pos, slots, err_flag 4-byte");
+  const size_t xbytes = static_cast<size_t>(total) * C * 2;
+  const size_t rbytes = static_cast<size_t>(n_slots) * (kConvK - 1) * C * 2;
+  if (total > 0 && (y == x || overlap(y, xbytes, x, xbytes)))
+    return fail(GDN_ERR_ALIAS, "y must not overlap x (the halo rows are re-read)");
+  if (overlap(y, xbytes, ring, rbytes)) return fail(GDN_ERR_ALIAS, "y overlaps the ring pool");
+  ConvParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+               static_cast<const __nv_bfloat16*>(ring), nullptr, static_cast<__nv_bfloat16*>(y), cu_seqlens, total, B,
+               cu_seqlens ? 0 : T, C, flags, slots, ring_pos, n_slots, err_flag};
+  return run_conv(p, stream);
+}
+
+extern "C" int gdn_conv_ring_append(const void* x, void* ring, int32_t* ring_pos, const int32_t* slots, int n_slots,
+                                    const int32_t* counts, const int32_t* cu_seqlens, int B, int T, int C, int K,
+                                    int32_t* err_flag, void* stream) {
+  clear_error();
+  if (K != kConvK) return fail(GDN_ERR_SHAPE, "K=%d: only 4 is built", K);
+  if (B < 0 || T < 0 || C <= 0 || C % kConvVec || n_slots <= 0)
+    return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d C=%d n_slots=%d", B, T, C, n_slots);
+  if (B == 0) return GDN_OK;
+  const long long total = cu_seqlens ? static_cast<long long>(T) : static_cast<long long>(B) * T;
+  if (!ring || !ring_pos || !slots || (total > 0 && !x))
+    return fail(GDN_ERR_NULL, "ring, ring_pos, slots, and x when there are tokens, are required");
+  if (!aligned(x, 16) || !aligned(ring, 16) || !aligned(ring_pos, 4) || !aligned(slots, 4) || !aligned(counts, 4) ||
+      !aligned(err_flag, 4))
+    return fail(GDN_ERR_ALIGN, "x, ring 16-byte aligned; ring_pos, slots, counts, err_flag 4-byte");
+  const size_t xbytes = static_cast<size_t>(total) * C * 2;
+  const size_t rbytes = static_cast<size_t>(n_slots) * (kConvK - 1) * C * 2;
+  if (overlap(x, xbytes, ring, rbytes)) return fail(GDN_ERR_ALIAS, "x overlaps the ring pool");
+  if (B > 0x7fffffff) return fail(GDN_ERR_SHAPE, "B too large");
+  conv_ring_append_kernel<<<static_cast<unsigned>(B), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(ring), ring_pos, slots, n_slots, counts,
+      cu_seqlens, cu_seqlens ? 0 : T, C, err_flag);
+  return cuda_status(cudaGetLastError(), "conv ring append launch");
 }
 
 extern "C" int gdn_conv_commit(const void* state_prev, const void* x, const int32_t* commit_n, void* state_out,

@@ -54,6 +54,12 @@ struct RecParams {
   float* ckpt;
   int B, T, Hk, Hv, Tsrc;
   unsigned flags;
+  // state pool mode: sequence b's state lives in slot slots[b] of a
+  // (n_slots, Hv, D, D) pool (state_in == state_out == the pool); pool_write
+  // says what the call leaves there (GDN_POOL_KEEP / _FINAL / _START)
+  const int32_t* slots;
+  int n_slots;
+  int pool_write;
 };
 
 __device__ __forceinline__ float4 ld_stream4(const float* p) {
@@ -108,7 +114,7 @@ __device__ __forceinline__ float softplus_f(float x) {
   return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x)));
 }
 
-template <bool BF16, int R>
+template <bool BF16, int R, bool POOL>
 __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
   constexpr int kRowsPerBlock = 4 * R;
   constexpr int kBlocksPerHead = kD / kRowsPerBlock;
@@ -121,8 +127,16 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
   const int kh = h / (p.Hv / p.Hk);
   const int col = lane * 4;
 
-  // Start state of this (sequence, head).
-  const float* src = p.state_in ? p.state_in + static_cast<size_t>(bh) * kD * kD : nullptr;
+  // Start state of this (sequence, head): the dense state, or its pool slot.
+  size_t sidx = static_cast<size_t>(bh);
+  bool slot_ok = true;
+  if constexpr (POOL) {
+    const int sl = p.slots[b];
+    slot_ok = sl >= 0 && sl < p.n_slots;
+    sidx = static_cast<size_t>(slot_ok ? sl : 0) * p.Hv + h;
+    if (!slot_ok && p.err_flag && threadIdx.x == 0) atomicExch(p.err_flag, 1);
+  }
+  const float* src = (p.state_in && slot_ok) ? p.state_in + sidx * kD * kD : nullptr;
   if (p.commit_n) {
     const int n = p.commit_n[b];
     if (n > 0 && n <= p.Tsrc) {
@@ -137,6 +151,15 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
   for (int r = 0; r < R; ++r) {
     s[r] = src ? ld_stream4(src + static_cast<size_t>(row0 + r) * kD + col)
                : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if constexpr (POOL) {
+    // a committed checkpoint (or a zero start) materialised in the slot; a
+    // start from the slot itself leaves it as it is
+    float* pool_row = p.state_out + (sidx * kD + row0) * kD + col;
+    if (p.pool_write == GDN_POOL_START && slot_ok && src != p.state_out + sidx * kD * kD) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) st_stream4(pool_row + static_cast<size_t>(r) * kD, s[r]);
+    }
   }
 
   const bool direct = (p.flags & GDN_F_GATES_DIRECT) != 0;
@@ -208,24 +231,24 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
     }
   }
 
-  if (p.state_out) {
-    float* dst = p.state_out + (static_cast<size_t>(bh) * kD + row0) * kD + col;
+  if (p.state_out && (!POOL || (slot_ok && p.pool_write == GDN_POOL_FINAL))) {
+    float* dst = p.state_out + (sidx * kD + row0) * kD + col;
 #pragma unroll
     for (int r = 0; r < R; ++r) st_stream4(dst + static_cast<size_t>(r) * kD, s[r]);
   }
 }
 
 
-template <bool BF16>
+template <bool BF16, bool POOL>
 cudaError_t launch_rows(const RecParams& p, int R, cudaStream_t st) {
   const long long bh = static_cast<long long>(p.B) * p.Hv;
   R = (R == 1 || R == 2 || R == 8) ? R : 4;
   const unsigned grid = static_cast<unsigned>(bh * (kD / (4 * R)));
   switch (R) {
-    case 1: recurrent_kernel<BF16, 1><<<grid, 128, 0, st>>>(p); break;
-    case 2: recurrent_kernel<BF16, 2><<<grid, 128, 0, st>>>(p); break;
-    case 8: recurrent_kernel<BF16, 8><<<grid, 128, 0, st>>>(p); break;
-    default: recurrent_kernel<BF16, 4><<<grid, 128, 0, st>>>(p); break;
+    case 1: recurrent_kernel<BF16, 1, POOL><<<grid, 128, 0, st>>>(p); break;
+    case 2: recurrent_kernel<BF16, 2, POOL><<<grid, 128, 0, st>>>(p); break;
+    case 8: recurrent_kernel<BF16, 8, POOL><<<grid, 128, 0, st>>>(p); break;
+    default: recurrent_kernel<BF16, 4, POOL><<<grid, 128, 0, st>>>(p); break;
   }
   return cudaGetLastError();
 }
@@ -256,7 +279,9 @@ int run_recurrent(const RecParams& p, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = (p.flags & GDN_F_QKV_F32) == 0;
   const int R = rows_per_warp(bh);
-  const cudaError_t e = bf16 ? launch_rows<true>(p, R, st) : launch_rows<false>(p, R, st);
+  cudaError_t e;
+  if (p.slots) e = bf16 ? launch_rows<true, true>(p, R, st) : launch_rows<false, true>(p, R, st);
+  else e = bf16 ? launch_rows<true, false>(p, R, st) : launch_rows<false, false>(p, R, st);
   return cuda_status(e, "gdn recurrent kernel launch");
 }
 
@@ -317,7 +342,7 @@ extern "C" int gdn_recurrent_fwd(const void* q, const void* k, const void* v, co
       overlap(o, obytes, ckpt, cbytes))
     return fail(GDN_ERR_ALIAS, "o overlaps a state or checkpoint buffer");
   RecParams p{q, k, v, a, b, A_log, dt_bias, state_in, nullptr, nullptr, nullptr,
-              state_out, o, T > 0 ? ckpt : nullptr, B, T, Hk, Hv, 0, flags};
+              state_out, o, T > 0 ? ckpt : nullptr, B, T, Hk, Hv, 0, flags, nullptr, 0, 0};
   return run_recurrent(p, stream);
 }
 
@@ -346,7 +371,41 @@ extern "C" int gdn_recurrent_fwd_from_ckpt(const void* q, const void* k, const v
       overlap(ckpt, cbytes, state_out, sbytes))
     return fail(GDN_ERR_ALIAS, "outputs overlap the committed checkpoints or state_prev");
   RecParams p{q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src, commit_n, err_flag,
-              state_out, o, T > 0 ? ckpt : nullptr, B, T, Hk, Hv, Tsrc, flags};
+              state_out, o, T > 0 ? ckpt : nullptr, B, T, Hk, Hv, Tsrc, flags, nullptr, 0, 0};
+  return run_recurrent(p, stream);
+}
+
+extern "C" int gdn_recurrent_fwd_pool(const void* q, const void* k, const void* v, const float* a,
+                                      const float* b, const float* A_log, const float* dt_bias, float* pool,
+                                      const int32_t* slots, int n_slots, const float* ckpt_src,
+                                      const int32_t* commit_n, int Tsrc, int pool_write, void* o, float* ckpt,
+                                      int32_t* err_flag, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                                      unsigned flags, void* stream) {
+  clear_error();
+  int rc = check_common(q, k, v, a, b, A_log, dt_bias, o, B, T, Hk, Hv, Dk, Dv, flags);
+  if (rc != GDN_OK) return rc;
+  if (B == 0) return GDN_OK;
+  if (!pool || !slots) return fail(GDN_ERR_NULL, "pool and slots are required");
+  if (n_slots <= 0 || static_cast<long long>(n_slots) * Hv * kD >= (1LL << 31))
+    return fail(GDN_ERR_SHAPE, "n_slots=%d out of range", n_slots);
+  if (pool_write != GDN_POOL_KEEP && pool_write != GDN_POOL_FINAL && pool_write != GDN_POOL_START)
+    return fail(GDN_ERR_FLAGS, "pool_write=%d is not GDN_POOL_KEEP, _FINAL or _START", pool_write);
+  if ((ckpt_src == nullptr) != (commit_n == nullptr))
+    return fail(GDN_ERR_NULL, "ckpt_src and commit_n go together");
+  if (commit_n && Tsrc <= 0) return fail(GDN_ERR_SHAPE, "Tsrc=%d must be positive", Tsrc);
+  if (!aligned(pool, 16) || !aligned(ckpt_src, 16) || !aligned(ckpt, 16) || !aligned(slots, 4) ||
+      !aligned(commit_n, 4) || !aligned(err_flag, 4))
+    return fail(GDN_ERR_ALIGN, "pool, ckpt_src, ckpt 16-byte aligned; slots, commit_n, err_flag 4-byte");
+  const size_t sbytes = static_cast<size_t>(B) * Hv * kD * kD * sizeof(float);
+  const size_t pbytes = static_cast<size_t>(n_slots) * Hv * kD * kD * sizeof(float);
+  const size_t srcbytes = commit_n ? sbytes * static_cast<size_t>(Tsrc) : 0;
+  const size_t cbytes = sbytes * static_cast<size_t>(T);
+  const size_t obytes = static_cast<size_t>(B) * T * Hv * kD * ((flags & GDN_F_O_BF16) ? 2 : 4);
+  if (overlap(pool, pbytes, ckpt_src, srcbytes) || overlap(pool, pbytes, ckpt, cbytes) ||
+      overlap(pool, pbytes, o, obytes) || overlap(ckpt, cbytes, ckpt_src, srcbytes) || overlap(o, obytes, ckpt, cbytes))
+    return fail(GDN_ERR_ALIAS, "pool, ckpt_src, ckpt and o must not overlap");
+  RecParams p{q, k, v, a, b, A_log, dt_bias, pool, ckpt_src, commit_n, err_flag,
+              pool, o, T > 0 ? ckpt : nullptr, B, T, Hk, Hv, commit_n ? Tsrc : 0, flags, slots, n_slots, pool_write};
   return run_recurrent(p, stream);
 }
 

@@ -50,6 +50,7 @@ SIGNATURES = {
     "gdn_take_device_error": [_vp, _vp],
     "gdn_recurrent_fwd": [_vp] * 11 + [_i] * 6 + [_u, _vp],
     "gdn_recurrent_fwd_from_ckpt": [_vp] * 10 + [_i] + [_vp] * 4 + [_i] * 6 + [_u, _vp],
+    "gdn_recurrent_fwd_pool": [_vp] * 9 + [_i] + [_vp] * 2 + [_i, _i] + [_vp] * 3 + [_i] * 6 + [_u, _vp],
     "gdn_delta_run": [_vp] * 9 + [_i] * 5 + [_vp],
     "gdn_tc05_selftest": [_vp] * 3 + [_i] * 3 + [_vp, _vp],
     "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
@@ -71,6 +72,8 @@ SIGNATURES = {
     "gdn_chunked_fwd_ws": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6
                           + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_conv_commit": [_vp] * 5 + [_i] * 4 + [_vp],
+    "gdn_conv1d_fwd_pool": [_vp] * 5 + [_i] + [_vp] * 2 + [_i] * 4 + [_u, _vp, _vp],
+    "gdn_conv_ring_append": [_vp] * 4 + [_i] + [_vp] * 2 + [_i] * 4 + [_vp, _vp],
     "gdn_gated_rmsnorm_fwd": [_vp] * 4 + [ctypes.c_longlong, _i, ctypes.c_float, _u, _vp],
 }
 
@@ -198,6 +201,64 @@ def recurrent_fwd_from_ckpt(q, k, v, a, b, A_log, dt_bias, state_prev, ckpt_src,
                                             ptr(state_out), ptr(o), ptr(ckpt), ptr(err_flag),
                                             B, T, Hk, Hv, Dk, D, flags, stream_ptr(dev)))
     return o, state_out, ckpt
+
+
+POOL_KEEP, POOL_FINAL, POOL_START = 0, 1, 2
+
+
+def recurrent_fwd_pool(q, k, v, a, b, A_log, dt_bias, pool, slots, pool_write=POOL_FINAL, ckpt_src=None,
+                       commit_n=None, o=None, ckpt=None, err_flag=None, *, l2norm=False, o_dtype=torch.float32):
+    """Decode / verify step over a state pool (``gdn_recurrent_fwd_pool``):
+    sequence b uses slot ``slots[b]`` of ``pool`` (n_slots, Hv, 128, 128)
+    fp32; start from the slot or (with ckpt_src, commit_n) a committed
+    checkpoint; ``pool_write`` POOL_FINAL / POOL_START / POOL_KEEP.
+    Returns (o, ckpt)."""
+    B, T, Hk, Dk = q.shape
+    Hv = v.shape[2]
+    flags = (F_QKV_F32 if q.dtype == torch.float32 else 0) | (F_QK_L2NORM if l2norm else 0)
+    if o_dtype == torch.bfloat16:
+        flags |= F_O_BF16
+    if slots.dtype != torch.int32 or (commit_n is not None and commit_n.dtype != torch.int32):
+        raise ValueError("slots and commit_n must be int32")
+    dev = _dev(q, k, v, a, b, A_log, dt_bias, pool, slots, ckpt_src, commit_n, o, ckpt, err_flag)
+    if o is None:
+        o = torch.empty((B, T, Hv, D), dtype=o_dtype, device=dev)
+    Tsrc = ckpt_src.shape[2] if ckpt_src is not None else 0
+    check(lib().gdn_recurrent_fwd_pool(ptr(q), ptr(k), ptr(v), ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
+                                       ptr(pool), ptr(slots), pool.shape[0], ptr(ckpt_src), ptr(commit_n), Tsrc,
+                                       pool_write, ptr(o), ptr(ckpt), ptr(err_flag),
+                                       B, T, Hk, Hv, Dk, D, flags, stream_ptr(dev)))
+    return o, ckpt
+
+
+def conv1d_fwd_pool(x, w, ring, ring_pos, slots, y=None, cu_seqlens=None, err_flag=None, *, bf16_ops=False,
+                    silu=True):
+    """gdn_conv1d_fwd with each sequence's window read from its slot of a
+    ring pool (ring (n_slots, 3, C) bf16, ring_pos (n_slots,) int32).  Returns y."""
+    if cu_seqlens is not None:
+        T, C = x.shape
+        B = cu_seqlens.numel() - 1
+    else:
+        B, T, C = x.shape
+    dev = _dev(x, w, ring, ring_pos, slots, y, cu_seqlens, err_flag)
+    if y is None:
+        y = torch.empty_like(x)
+    flags = (F_CONV_BF16_OPS if bf16_ops else 0) | (0 if silu else F_CONV_NO_SILU)
+    check(lib().gdn_conv1d_fwd_pool(ptr(x), ptr(w), ptr(ring), ptr(ring_pos), ptr(slots), ring.shape[0], ptr(y),
+                                    ptr(cu_seqlens), B, T, C, w.shape[1], flags, ptr(err_flag), stream_ptr(dev)))
+    return y
+
+
+def conv_ring_append(x, ring, ring_pos, slots, counts=None, cu_seqlens=None, err_flag=None):
+    """Move the first counts[b] (default: all) tokens of each sequence into its ring slot."""
+    if cu_seqlens is not None:
+        T, C = x.shape
+        B = cu_seqlens.numel() - 1
+    else:
+        B, T, C = x.shape
+    dev = _dev(x, ring, ring_pos, slots, counts, cu_seqlens, err_flag)
+    check(lib().gdn_conv_ring_append(ptr(x), ptr(ring), ptr(ring_pos), ptr(slots), ring.shape[0], ptr(counts),
+                                     ptr(cu_seqlens), B, T, C, 4, ptr(err_flag), stream_ptr(dev)))
 
 
 def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=False, b_mn=False, d_col=0):
