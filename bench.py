@@ -214,6 +214,83 @@ def time_graph(fn, steps, warmup, device, world):
     return max_over_ranks(ms, world, device)
 
 
+def run_pool_decode(args, lib, X, Bg, device, Lp=8):
+    """Decode over a state pool (gdn_recurrent_fwd_pool): Bg sequences in
+    seeded random slots of a pool of 2*Bg, Lp layers, against the dense
+    in-place launch on the same inputs (both CUDA-graph replays, states far
+    above L2); and one layer's conv step through the ring (gdn_conv1d_fwd_pool
+    + gdn_conv_ring_append, one row written per sequence) against the dense
+    conv with a carried (B, 3, C) window."""
+    import gdn_b200 as G
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    Lp = min(Lp, X.L)
+    n_slots = 2 * Bg
+    g = torch.Generator(device=device)
+    g.manual_seed(4242)
+    pools = [torch.randn((n_slots, X.hv, D, D), generator=g, device=device) * 0.05 for _ in range(Lp)]
+    slots = torch.randperm(n_slots, generator=g, device=device)[:Bg].to(torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def step_pool():
+        h = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        for layer in range(Lp):
+            rc = lib.gdn_recurrent_fwd_pool(P(X.q[layer]), P(X.k[layer]), P(X.v[layer]), P(X.a[layer]),
+                                            P(X.b[layer]), P(X.A_log[layer]), P(X.dt_bias[layer]), P(pools[layer]),
+                                            P(slots), n_slots, None, None, 0, G.POOL_FINAL, P(X.o[layer]), None,
+                                            P(err), Bg, 1, X.hk, X.hv, D, D, G.F_O_BF16, h)
+            if rc:
+                raise RuntimeError(lib.gdn_last_error().decode())
+
+    def step_dense():
+        h = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        for layer in range(Lp):
+            launch_layer(lib, X, layer, Bg, h)
+
+    steps = max(args.steps, 10)
+    ms_pool = time_graph(step_pool, steps, args.warmup, device, 1) / steps
+    ms_dense = time_graph(step_dense, steps, args.warmup, device, 1) / steps
+    per_step = 2 * Bg * X.hv * STATE_BYTES * Lp
+    Cc = 2 * X.hk * D + X.hv * D
+    x = torch.randn((Bg, 1, Cc), generator=g, device=device).bfloat16()
+    w = (torch.randn((Cc, 4), generator=g, device=device) * 0.5).bfloat16()
+    y = torch.empty_like(x)
+    ring = torch.zeros((n_slots, 3, Cc), dtype=torch.bfloat16, device=device)
+    pos = torch.zeros(n_slots, dtype=torch.int32, device=device)
+    win = [torch.zeros((Bg, 3, Cc), dtype=torch.bfloat16, device=device) for _ in range(2)]
+
+    def conv_ring():
+        h = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        rc = lib.gdn_conv1d_fwd_pool(P(x), P(w), P(ring), P(pos), P(slots), n_slots, P(y), None, Bg, 1, Cc, 4, 0,
+                                     P(err), h)
+        rc = rc or lib.gdn_conv_ring_append(P(x), P(ring), P(pos), P(slots), n_slots, None, None, Bg, 1, Cc, 4,
+                                            P(err), h)
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+
+    def conv_dense():
+        h = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        rc = lib.gdn_conv1d_fwd(P(x), P(w), P(win[0]), P(win[1]), P(y), None, Bg, 1, Cc, 4, 0, h)
+        if rc:
+            raise RuntimeError(lib.gdn_last_error().decode())
+
+    csteps = 200
+    us_ring = time_graph(conv_ring, csteps, args.warmup, device, 1) / csteps * 1e3
+    us_dense = time_graph(conv_dense, csteps, args.warmup, device, 1) / csteps * 1e3
+    torch.cuda.synchronize(device)
+    if int(err.item()):
+        raise RuntimeError("pool decode recorded a slot error")
+    out = {"workload": f"{Lp} layers x B={Bg} decode, states in random slots of a {n_slots}-slot pool "
+                       f"({n_slots * X.hv * STATE_BYTES * Lp / 1e9:.1f} GB)",
+           "recurrent_pool_gbs": round(per_step / (ms_pool * 1e-3) / 1e9, 1),
+           "recurrent_dense_gbs": round(per_step / (ms_dense * 1e-3) / 1e9, 1),
+           "conv_ring_us": round(us_ring, 2), "conv_dense_us": round(us_dense, 2),
+           "conv_note": f"one layer's conv step, B={Bg}, C={Cc}: ring (conv + one-row append) vs dense "
+                        "(conv + 3-row window copy)"}
+    del pools, ring, win
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, world, rank, local):
     import gdn_b200 as G
     import gdn_shard
@@ -306,6 +383,11 @@ def run_ours(args, world, rank, local):
             msb = time_graph(lambda: step(Bs), max(args.steps, 20), args.warmup, device, world)
             sweep[str(Bs)] = round(X.state_bytes(Bs) / (msb / max(args.steps, 20) * 1e-3) / 1e9, 1)
 
+    # --- the same decode over a serving-batch state pool (scattered slots) and the conv ring
+    pool = None
+    if world == 1 and not args.no_pool:
+        pool = run_pool_decode(args, lib, X, Bg, device)
+
     # --- end to end through the C ABI with host buffers (pipelined per layer)
     e2e = None
     if not args.no_e2e:
@@ -340,7 +422,7 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
                    "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
-        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill,
+        "sweep_gbs_by_batch": sweep, "pool_decode": pool, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill,
     }
     return line
 
@@ -881,6 +963,7 @@ def main():
     ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true", help="skip the config-2 verify/accept/rollback chain")
+    ap.add_argument("--no-pool", action="store_true", help="skip the state-pool / conv-ring decode comparison")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
     ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather"],
@@ -894,7 +977,7 @@ def main():
     args = ap.parse_args()
     if args.small:
         args.batch, args.layers, args.sweep = 64, 2, ""
-        args.no_e2e = args.no_cpu_baseline = args.no_prefill = args.no_verify = True
+        args.no_e2e = args.no_cpu_baseline = args.no_prefill = args.no_verify = args.no_pool = True
     args.warmup = max(args.warmup, 0)
 
     world, rank, local = dist_env()

@@ -23,6 +23,7 @@ constexpr int kConvVec = 8;          // channels per thread (one 16-byte bf16 ve
 constexpr int kConvThreads = 128;
 constexpr int kConvRun = 64;         // tokens per thread
 constexpr int kConvBatch = 8;        // rows loaded ahead of use (bytes in flight per thread)
+constexpr int kConvShortT = 16;      // uniform batches of at most this many tokens per sequence: one thread per token
 
 struct alignas(16) Bf16x8 {
   __nv_bfloat162 h[4];
@@ -77,6 +78,116 @@ struct ConvParams {
   int32_t* err;
 };
 
+// One output vector of 8 channels: the K taps over [window; x] and the SiLU.
+template <bool BF16_OPS>
+__device__ __forceinline__ Bf16x8 conv_taps(const float (&win)[kConvK - 1][kConvVec], const float (&xv)[kConvVec],
+                                           const float (&w)[kConvK][kConvVec], bool silu) {
+  float out[kConvVec];
+#pragma unroll
+  for (int e = 0; e < kConvVec; ++e) {
+    float acc;
+    if constexpr (BF16_OPS) {   // MLX per-op bf16: each product and each partial sum rounded
+      acc = bf16r(win[0][e] * w[0][e]);
+      acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
+      acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
+      acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
+      if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
+    } else {          // fp32 accumulation; the bf16 output rounding dwarfs the fast-exp error
+      acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
+      if (silu) acc = __fdividef(acc, 1.f + __expf(-acc));
+    }
+    out[e] = acc;
+  }
+  return pack8(out);
+}
+
+// The 8 channels x K taps of w (C, K) starting at channel c0 (32 contiguous bf16).
+__device__ __forceinline__ void load_taps(const __nv_bfloat16* wt, int c0, float (&w)[kConvK][kConvVec]) {
+  const Bf16x8* wp = reinterpret_cast<const Bf16x8*>(wt + static_cast<size_t>(c0) * kConvK);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float f[8];
+    unpack8(wp[q], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int flat = q * 8 + e;                 // = channel_offset * K + tap
+      w[flat % kConvK][flat / kConvK] = f[e];
+    }
+  }
+}
+
+// Row srow (0 = oldest) of sequence seq's carried window at channel c0: the
+// dense (B, K-1, C) state, or its pool slot's ring; null for a zero row (no
+// state, or a bad slot, which is reported).
+__device__ __forceinline__ const __nv_bfloat16* window_row(const ConvParams& p, int seq, int srow, int c0) {
+  if (!p.state_in) return nullptr;
+  if (!p.slots) return p.state_in + (static_cast<long long>(seq) * (kConvK - 1) + srow) * p.C + c0;
+  const int sl = p.slots[seq];
+  if (sl < 0 || sl >= p.n_slots) {
+    if (p.err) atomicExch(p.err, 1);
+    return nullptr;
+  }
+  int hd = p.ring_pos[sl] % (kConvK - 1);
+  if (hd < 0) hd += kConvK - 1;
+  return p.state_in + (static_cast<long long>(sl) * (kConvK - 1) + (hd + srow) % (kConvK - 1)) * p.C + c0;
+}
+
+// Short uniform sequences (decode T = 1, verify T = k+1): one thread per
+// (token, 8 channels), so a batch of single tokens spreads over the whole GPU
+// instead of walking 64 sequences per thread.  The thread of a sequence's
+// last token also writes the carried window (dense state_out).
+template <bool BF16_OPS>
+__global__ void __launch_bounds__(kConvThreads) conv1d_tok_kernel(const ConvParams p, int nvb) {
+  const long long tok = blockIdx.x / nvb;
+  const int c0 = ((blockIdx.x - static_cast<int>(tok) * nvb) * kConvThreads + threadIdx.x) * kConvVec;
+  if (c0 >= p.C || tok >= p.total) return;
+  const int seq = static_cast<int>(tok / p.T);
+  const int t = static_cast<int>(tok - static_cast<long long>(seq) * p.T);
+  const bool silu = !(p.flags & GDN_F_CONV_NO_SILU);
+  float w[kConvK][kConvVec];
+  load_taps(p.w, c0, w);
+  Bf16x8 raw[kConvK - 1], xr;
+  bool have[kConvK - 1];
+#pragma unroll
+  for (int j = 0; j < kConvK - 1; ++j) {        // window rows t-3 .. t-1 of [state; x_seq]
+    const int pos = t - (kConvK - 1) + j;
+    const __nv_bfloat16* src = pos >= 0 ? p.x + (tok - t + pos) * p.C + c0
+                                        : window_row(p, seq, (kConvK - 1) + pos, c0);
+    have[j] = src != nullptr;
+    if (src) raw[j] = *reinterpret_cast<const Bf16x8*>(src);
+  }
+  xr = *reinterpret_cast<const Bf16x8*>(p.x + tok * p.C + c0);
+  float win[kConvK - 1][kConvVec], xv[kConvVec];
+#pragma unroll
+  for (int j = 0; j < kConvK - 1; ++j) {
+    if (have[j]) {
+      unpack8(raw[j], win[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
+    }
+  }
+  unpack8(xr, xv);
+  *reinterpret_cast<Bf16x8*>(p.y + tok * p.C + c0) = conv_taps<BF16_OPS>(win, xv, w, silu);
+  if (p.state_out && t == p.T - 1) {
+    // the carried window: rows T .. T+K-2 of [state (K-1 rows); x_seq (T rows)]
+#pragma unroll
+    for (int r = 0; r < kConvK - 1; ++r) {
+      const int row = p.T + r;
+      Bf16x8 v;
+      if (row >= kConvK - 1) {
+        v = *reinterpret_cast<const Bf16x8*>(p.x + (tok - t + (row - (kConvK - 1))) * p.C + c0);
+      } else if (const __nv_bfloat16* sp = window_row(p, seq, row, c0)) {
+        v = *reinterpret_cast<const Bf16x8*>(sp);
+      } else {
+        float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        v = pack8(z);
+      }
+      *reinterpret_cast<Bf16x8*>(p.state_out + (static_cast<long long>(seq) * (kConvK - 1) + r) * p.C + c0) = v;
+    }
+  }
+}
+
 // One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
 // the 3-row causal window in registers, so every x element is read once
 // (plus a 3-row halo at the start of the run); rows are fetched 8 at a time
@@ -96,20 +207,7 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
   constexpr bool bf16_ops = BF16_OPS;
 
   float w[kConvK][kConvVec];
-  {
-    // w is (C, K): the 8 channels x 4 taps are 32 contiguous bf16
-    const Bf16x8* wp = reinterpret_cast<const Bf16x8*>(p.w + static_cast<size_t>(c0) * kConvK);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float f[8];
-      unpack8(wp[q], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int flat = q * 8 + e;                 // = channel_offset * K + tap
-        w[flat % kConvK][flat / kConvK] = f[e];
-      }
-    }
-  }
+  load_taps(p.w, c0, w);
 
   // token range of sequence `seq`: packed offsets, or seq*T .. seq*T+T
   auto seq_begin = [&](int sq) -> long long { return p.cu ? p.cu[sq] : static_cast<long long>(sq) * p.T; };
@@ -128,20 +226,7 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
       if (pos >= 0 && row >= 0 && row < p.total) {
         unpack8(*reinterpret_cast<const Bf16x8*>(p.x + row * p.C + c0), win[j]);
       } else if (p.state_in && pos < 0 && pos >= -(kConvK - 1)) {
-        const long long srow = (kConvK - 1) + pos;               // 0 .. K-2, oldest first
-        const __nv_bfloat16* sp = nullptr;
-        if (p.slots) {
-          const int sl = p.slots[seq];
-          if (sl >= 0 && sl < p.n_slots) {
-            int hd = p.ring_pos[sl] % (kConvK - 1);
-            if (hd < 0) hd += kConvK - 1;
-            sp = p.state_in + (static_cast<long long>(sl) * (kConvK - 1) + (hd + srow) % (kConvK - 1)) * p.C + c0;
-          } else if (p.err) {
-            atomicExch(p.err, 1);
-          }
-        } else {
-          sp = p.state_in + (static_cast<long long>(seq) * (kConvK - 1) + srow) * p.C + c0;
-        }
+        const __nv_bfloat16* sp = window_row(p, seq, static_cast<int>((kConvK - 1) + pos), c0);   // oldest first
         if (sp) {
           unpack8(*reinterpret_cast<const Bf16x8*>(sp), win[j]);
         } else {
@@ -179,23 +264,7 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
       }
       float xv[kConvVec];
       unpack8(xr[u], xv);
-      float out[kConvVec];
-#pragma unroll
-      for (int e = 0; e < kConvVec; ++e) {
-        float acc;
-        if constexpr (bf16_ops) {   // MLX per-op bf16: each product and each partial sum rounded
-          acc = bf16r(win[0][e] * w[0][e]);
-          acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
-          acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
-          acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
-          if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
-        } else {          // fp32 accumulation; the bf16 output rounding dwarfs the fast-exp error
-          acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
-          if (silu) acc = __fdividef(acc, 1.f + __expf(-acc));
-        }
-        out[e] = acc;
-      }
-      *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = pack8(out);
+      *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = conv_taps<bf16_ops>(win, xv, w, silu);
 #pragma unroll
       for (int e = 0; e < kConvVec; ++e) {
         win[0][e] = win[1][e];
@@ -381,7 +450,15 @@ int run_conv(const ConvParams& p, void* stream) {
   const long long total = p.total;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned gx = static_cast<unsigned>((C / kConvVec + kConvThreads - 1) / kConvThreads);
-  if (total > 0) {
+  if (total > 0 && !p.cu && p.T <= kConvShortT) {
+    const int nvb = static_cast<int>((C / kConvVec + kConvThreads - 1) / kConvThreads);
+    const long long blocks = total * nvb;
+    if (blocks > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
+    if (p.flags & GDN_F_CONV_BF16_OPS) conv1d_tok_kernel<true><<<static_cast<unsigned>(blocks), kConvThreads, 0, st>>>(p, nvb);
+    else conv1d_tok_kernel<false><<<static_cast<unsigned>(blocks), kConvThreads, 0, st>>>(p, nvb);
+    int rc = cuda_status(cudaGetLastError(), "conv1d launch");
+    if (rc != GDN_OK) return rc;
+  } else if (total > 0) {
     const long long gy = (total + kConvRun - 1) / kConvRun;
     if (gy > 65535LL * 1024) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
     // grid.y is limited to 65535: fold extra runs into grid.z is not needed below 2M tokens

@@ -114,8 +114,16 @@ __device__ __forceinline__ float softplus_f(float x) {
   return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x)));
 }
 
-template <bool BF16, int R, bool POOL>
-__global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
+// PM: 0 dense states; 1 pool, written back after the last position when
+// pool_write is GDN_POOL_FINAL; 2 pool, the start state written back
+// (GDN_POOL_START).  The start-state store is its own instantiation so that
+// the other modes carry no store between the state loads and the token loads.
+// 8 resident 128-thread blocks per SM (64 registers, no spills at R = 8):
+// the loads in flight per SM, not the instruction count, set the achieved
+// bandwidth -- 6 blocks at the compiler's own 80 registers streamed ~7% less.
+template <bool BF16, int R, int PM>
+__global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
+  constexpr bool POOL = PM != 0;
   constexpr int kRowsPerBlock = 4 * R;
   constexpr int kBlocksPerHead = kD / kRowsPerBlock;
   const int lane = threadIdx.x & 31;
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
   size_t sidx = static_cast<size_t>(bh);
   bool slot_ok = true;
   if constexpr (POOL) {
-    const int sl = p.slots[b];
+    const int sl = __ldg(p.slots + b);
     slot_ok = sl >= 0 && sl < p.n_slots;
     sidx = static_cast<size_t>(slot_ok ? sl : 0) * p.Hv + h;
     if (!slot_ok && p.err_flag && threadIdx.x == 0) atomicExch(p.err_flag, 1);
@@ -152,11 +160,11 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
     s[r] = src ? ld_stream4(src + static_cast<size_t>(row0 + r) * kD + col)
                : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if constexpr (POOL) {
+  if constexpr (PM == 2) {
     // a committed checkpoint (or a zero start) materialised in the slot; a
     // start from the slot itself leaves it as it is
     float* pool_row = p.state_out + (sidx * kD + row0) * kD + col;
-    if (p.pool_write == GDN_POOL_START && slot_ok && src != p.state_out + sidx * kD * kD) {
+    if (slot_ok && src != p.state_out + sidx * kD * kD) {
 #pragma unroll
       for (int r = 0; r < R; ++r) st_stream4(pool_row + static_cast<size_t>(r) * kD, s[r]);
     }
@@ -231,7 +239,7 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
     }
   }
 
-  if (p.state_out && (!POOL || (slot_ok && p.pool_write == GDN_POOL_FINAL))) {
+  if (p.state_out && (PM == 0 || (PM == 1 && slot_ok && p.pool_write == GDN_POOL_FINAL))) {
     float* dst = p.state_out + (sidx * kD + row0) * kD + col;
 #pragma unroll
     for (int r = 0; r < R; ++r) st_stream4(dst + static_cast<size_t>(r) * kD, s[r]);
@@ -239,18 +247,23 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const RecParams p) {
 }
 
 
-template <bool BF16, bool POOL>
+template <bool BF16, int PM>
 cudaError_t launch_rows(const RecParams& p, int R, cudaStream_t st) {
   const long long bh = static_cast<long long>(p.B) * p.Hv;
   R = (R == 1 || R == 2 || R == 8) ? R : 4;
   const unsigned grid = static_cast<unsigned>(bh * (kD / (4 * R)));
   switch (R) {
-    case 1: recurrent_kernel<BF16, 1, POOL><<<grid, 128, 0, st>>>(p); break;
-    case 2: recurrent_kernel<BF16, 2, POOL><<<grid, 128, 0, st>>>(p); break;
-    case 8: recurrent_kernel<BF16, 8, POOL><<<grid, 128, 0, st>>>(p); break;
-    default: recurrent_kernel<BF16, 4, POOL><<<grid, 128, 0, st>>>(p); break;
+    case 1: recurrent_kernel<BF16, 1, PM><<<grid, 128, 0, st>>>(p); break;
+    case 2: recurrent_kernel<BF16, 2, PM><<<grid, 128, 0, st>>>(p); break;
+    case 8: recurrent_kernel<BF16, 8, PM><<<grid, 128, 0, st>>>(p); break;
+    default: recurrent_kernel<BF16, 4, PM><<<grid, 128, 0, st>>>(p); break;
   }
   return cudaGetLastError();
+}
+
+template <int PM>
+cudaError_t launch_mode(const RecParams& p, bool bf16, int R, cudaStream_t st) {
+  return bf16 ? launch_rows<true, PM>(p, R, st) : launch_rows<false, PM>(p, R, st);
 }
 
 // Rows per warp.  Bytes in flight per SM set the achieved HBM bandwidth:
@@ -279,9 +292,9 @@ int run_recurrent(const RecParams& p, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = (p.flags & GDN_F_QKV_F32) == 0;
   const int R = rows_per_warp(bh);
-  cudaError_t e;
-  if (p.slots) e = bf16 ? launch_rows<true, true>(p, R, st) : launch_rows<false, true>(p, R, st);
-  else e = bf16 ? launch_rows<true, false>(p, R, st) : launch_rows<false, false>(p, R, st);
+  const cudaError_t e = !p.slots ? launch_mode<0>(p, bf16, R, st)
+                        : p.pool_write == GDN_POOL_START ? launch_mode<2>(p, bf16, R, st)
+                                                         : launch_mode<1>(p, bf16, R, st);
   return cuda_status(e, "gdn recurrent kernel launch");
 }
 
