@@ -239,7 +239,8 @@ int gdn_chunked_fwd_ws(const void* q, const void* k, const void* v,
  *         = bf16( o[t,h,d] * rsqrt(mean_d o[t,h,:]^2 + eps) * gamma[d] * silu(z[t,h,d]) )
  * instead of o (the reference's norm(o, z), cpp/src/model.cpp:350-354 and
  * :625-627, python/qwen35.py:159-180).  z: bf16, element (t, h, d) at
- * z[t*z_stride + h*128 + d]; gamma (128) fp32.  out_stride / out_head0 place
+ * z[t*z_stride + h*128 + d], 16-byte aligned with z_stride a multiple of 8
+ * (its rows are bulk-copied); gamma (128) fp32.  out_stride / out_head0 place
  * this call's Hv heads inside a wider row (e.g. the all-heads output of a
  * head-sharded layer); out 16-byte aligned, out_stride a multiple of 8.
  * Flags: GDN_F_QK_L2NORM only.  Other arguments and the workspace as

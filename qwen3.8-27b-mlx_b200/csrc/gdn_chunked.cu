@@ -131,8 +131,13 @@ constexpr uint32_t kScanG2 = kRecM;
 constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
 constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
 constexpr uint32_t kScanNorm = kScanBar + 64;       // fused norm: partial sums of squares, 4 x 64 floats
-constexpr uint32_t kScanOut = kScanNorm + 4 * kC * 4;   // fused norm: the chunk's bf16 output rows, 64 x 128
-constexpr uint32_t kScanSmem = kScanOut + kC * kD * 2;
+constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
+// fused norm: z rows of three chunks (chunk ch in buffer ch % 3), 64 x 128
+// bf16 each; a chunk's normed output rows overwrite its z rows in place
+constexpr uint32_t kScanZ = kScanSmem;
+constexpr uint32_t kZBuf = kC * kD * 2;
+constexpr uint32_t kScanSmemNorm = kScanZ + 3 * kZBuf;
+static_assert(kScanSmemNorm <= 232448, "scan with the fused norm: shared memory per CTA");
 
 __host__ __device__ constexpr size_t records_offset(int B) {
   return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
@@ -1102,17 +1107,26 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   };
   float* s_part = reinterpret_cast<float*>(sm + kScanNorm);   // [lane quarter][token] sums of y^2
   const float gam = NORM ? __ldg(p.gamma + c.row) : 0.f;
-  // fused norm: z of a worker's 16 tokens of a chunk, loaded a chunk before its
-  // use and left untouched until then (so the loads never stall the chunk)
-  unsigned short z_next[16];
-  uint32_t z_prev[8];                             // packed pairs, filled at the end of the chunk
+  // fused norm: the z rows of chunk ch (256 bytes per token) are copied into
+  // buffer ch % 3 by cp.async from the column group that normalises those
+  // tokens (16 tokens, two 16-byte pieces per thread), two chunks ahead of
+  // use; the load path keeps them off the bulk-copy engine that streams the
+  // records.  One commit group per chunk and thread.
   auto load_z = [&](int ch) {
+    if (mw) return;
     const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
-    const int nv = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC) - cg * 16;
-    const unsigned short* zp = reinterpret_cast<const unsigned short*>(p.z) + (t0 + cg * 16) * p.z_stride +
-                               c.h * kD + c.row;
+    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+    unsigned char* zb = sm + kScanZ + (ch % 3) * kZBuf;
+    const int tq = c.quarter * 32 + c.lane;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) z_next[i] = i < nv ? __ldg(zp + i * p.z_stride) : 0;
+    for (int k = 0; k < 2; ++k) {
+      const int piece = tq + k * 128;
+      const int tok = cg * 16 + (piece >> 4);
+      const int seg = (piece & 15) * 8;
+      if (tok < nvalid)
+        ptx::cp_async16(zb + (tok * kD + seg) * 2, p.z + (t0 + tok) * p.z_stride + c.h * kD + seg);
+    }
+    ptx::cp_async_commit();
   };
   // o rows of chunk ch from y^T: a worker's dv = row, tokens cg*16 + part*8 .. +7
   auto epi_o = [&](int ch, int part) {
@@ -1123,12 +1137,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     const int nv = nvalid - tok;
     float y[8];
     if constexpr (NORM) {
-      float zz[8];
-#pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        const uint32_t w = part ? z_prev[4 + i / 2] : z_prev[i / 2];
-        zz[i] = __uint_as_float(w << 16);
-        zz[i + 1] = __uint_as_float(w & 0xffff0000u);
+      __nv_bfloat16* zt = reinterpret_cast<__nv_bfloat16*>(sm + kScanZ + (ch % 3) * kZBuf);
+      if (part == 0) {         // this thread's copies of chunk ch; the barrier below publishes the group's
+        const int newer = n_chunks - 1 - ch;       // chunks whose z groups were committed after this one's
+        if (newer >= 2) ptx::cp_async_wait<2>();
+        else if (newer == 1) ptx::cp_async_wait<1>();
+        else ptx::cp_async_wait<0>();
       }
       tc::tmem_ld8(c.tb + col_y + c.my + tok, y);
       tc::tmem_ld_wait();
@@ -1148,14 +1162,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
       s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
       if ((c.lane & 3) == 0) s_part[c.quarter * kC + tok + (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0)] = s1v;
       asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");   // the 4 warps of this column group
-      // normalised rows into the shared tile, then 16-byte pieces of the 8 rows to every destination
-      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(sm + kScanOut);
+      // normalised rows over the z rows they gate (same thread, same element),
+      // then 16-byte pieces of the 8 rows to every destination
+      __nv_bfloat16* tile = zt;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float ss = s_part[tok + i] + s_part[kC + tok + i] + s_part[2 * kC + tok + i] + s_part[3 * kC + tok + i];
         const float r = rsqrtf(ss / static_cast<float>(kD) + p.eps);
-        const float sg = __fdividef(1.f, 1.f + __expf(-zz[i]));
-        tile[(tok + i) * kD + c.row] = __float2bfloat16_rn((y[i] * r * gam) * (zz[i] * sg));
+        const float zz = __bfloat162float(zt[(tok + i) * kD + c.row]);
+        const float sg = __fdividef(1.f, 1.f + __expf(-zz));
+        tile[(tok + i) * kD + c.row] = __float2bfloat16_rn((y[i] * r * gam) * (zz * sg));
       }
       asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");
       const int tt = c.quarter * 32 + c.lane;          // 128 threads: 8 rows x 16 pieces of 16 bytes
@@ -1195,6 +1211,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     load(1, 0);
     load(2, 0);
     load(3, 0);
+    if (NORM) {
+      load_z(0);
+      if (n_chunks > 1) load_z(1);
+    }
     if (!mw) {
       r_pass(true, 1.f);                  // tf32(R_0)
       tc::tmem_st_wait();
@@ -1203,7 +1223,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     __syncthreads();
   }
   for (int ch = 0; ch < n_chunks && !failed; ++ch) {
-    if (NORM && !mw) load_z(ch);
     const bool odd = ch & 1;
     const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
     const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
@@ -1246,6 +1265,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     tc::fence_before_sync();
     if (!mma_done(true)) { failed = true; break; }
     GDN_TICK(26);
+    if (NORM && ch + 2 < n_chunks) load_z(ch + 2);   // its buffer's chunk ch - 1 is normalised by now
     if (ch + 1 < n_chunks) {
       load(2, ch + 1);
       if (!mw) {
@@ -1256,11 +1276,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     tc::fence_before_sync();
     __syncthreads();
     GDN_TICK(27);
-    if (NORM) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        z_prev[i] = static_cast<uint32_t>(z_next[2 * i]) | (static_cast<uint32_t>(z_next[2 * i + 1]) << 16);
-    }
   }
   if (!failed && n_chunks > 0 && !mw) {
     epi_o(n_chunks - 1, 0);
@@ -1277,6 +1292,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   } else if (!mw) {
     state_store(p.carry, c, bh, cDR, cg * 32, 32);
   }
+  if (NORM) ptx::cp_async_wait<0>();               // no z copy may land after the CTA exits
   if (NORM && p.n_dst > 1) __threadfence_system();  // peer stores performed before the call's signal
   tc::fence_before_sync();
   __syncthreads();
@@ -1412,7 +1428,7 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
   static bool attr_scan_norm[64] = {false};
   const void* scan = p.z ? reinterpret_cast<const void*>(chunk_scan_kernel<true>)
                          : reinterpret_cast<const void*>(chunk_scan_kernel<false>);
-  rc = set_smem_attr(scan, kScanSmem, p.z ? attr_scan_norm : attr_scan);
+  rc = set_smem_attr(scan, p.z ? kScanSmemNorm : kScanSmem, p.z ? attr_scan_norm : attr_scan);
   if (rc != GDN_OK) return rc;
   const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
   for (int w = 0; w < pl.n_windows; ++w) {
@@ -1434,7 +1450,7 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
       rc = cuda_status(cudaGetLastError(), "chunk prep launch");
       if (rc != GDN_OK) return rc;
     }
-    if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
+    if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmemNorm, st>>>(p);
     else chunk_scan_kernel<false><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "chunk scan launch");
     if (rc != GDN_OK) return rc;
@@ -1524,7 +1540,8 @@ int run_norm(const void* q, const void* k, const void* v, long long q_stride, lo
   if (out_stride % 8) return fail(GDN_ERR_ALIGN, "out_stride must be a multiple of 8 elements (16 bytes)");
   for (int d = 0; d < n_dst; ++d)
     if (!dst[d] || !aligned(dst[d], 16)) return fail(GDN_ERR_ALIGN, "output %d is null or not 16-byte aligned", d);
-  if (!aligned(z, 2) || !aligned(gamma, 4) || !(eps >= 0.f)) return fail(GDN_ERR_ALIGN, "z, gamma misaligned or eps < 0");
+  if (!aligned(z, 16) || z_stride % 8 || !aligned(gamma, 4) || !(eps >= 0.f))
+    return fail(GDN_ERR_ALIGN, "z 16-byte aligned with z_stride a multiple of 8, gamma 4-byte aligned, eps >= 0");
   if (!workspace) return fail(GDN_ERR_NULL, "workspace is required (%zu bytes for one window)",
                               workspace_bytes(B, T, Hv, cu_seqlens != nullptr));
   if (!aligned(workspace, 256)) return fail(GDN_ERR_ALIGN, "workspace must be 256-byte aligned");

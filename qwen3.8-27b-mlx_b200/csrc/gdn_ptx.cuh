@@ -57,6 +57,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// ---- per-thread asynchronous copies (the load path, not the TMA engine) -------
+
+// 16 bytes global -> shared, L2 only; both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// this thread's copies done except for its N most recent groups
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---- bulk copies through the TMA engine (no tensor map, this CTA only) -------
 
 // global -> shared, completion counted in bytes on `bar`.  16-byte aligned
