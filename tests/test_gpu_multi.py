@@ -22,7 +22,8 @@ def free_port():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_norm_gather_over_nvlink_matches_single_gpu():
-    n = 2 if torch.cuda.device_count() < 4 else 4
+    cnt = torch.cuda.device_count()
+    n = 8 if cnt >= 8 else (4 if cnt >= 4 else 2)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
            os.path.join(HERE, "mgpu", "norm_gather_check.py")]
