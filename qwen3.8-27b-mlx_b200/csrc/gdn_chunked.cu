@@ -132,6 +132,12 @@ constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), op
 constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
 constexpr uint32_t kScanNorm = kScanBar + 64;       // fused norm: partial sums of squares, 4 x 64 floats
 constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
+// fused norm: mbarriers "y of a chunk parity is in TMEM" (arrived by the MMA
+// commit) and "... has been read" (one arrival per norm warp), then the
+// failure flag the norm warps poll; the first 256 bytes of kScanNorm hold
+// the norm warps' per-token partial sums
+constexpr uint32_t kScanYBar = kScanNorm + 768;
+constexpr uint32_t kScanFail = kScanNorm + 800;
 // fused norm: z rows of three chunks (chunk ch in buffer ch % 3), 64 x 128
 // bf16 each; a chunk's normed output rows overwrite its z rows in place
 constexpr uint32_t kScanZ = kScanSmem;
@@ -997,9 +1003,10 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
 // its lane 0 issues both, so that its issue stalls never delay the workers.
 constexpr int kScanWorkers = 512;
 constexpr int kScanThreads = kScanWorkers + 32;
+constexpr int kScanThreadsNorm = kScanThreads + 256;   // + 8 norm warps: two groups of the 4 TMEM lane quarters
 
 template <bool NORM>
-__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const ChunkParams p) {
+__global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chunk_scan_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const float4* sU0 = reinterpret_cast<const float4*>(sm + kRecU);
   const float* sSc = reinterpret_cast<const float*>(sm + kRecSc);
@@ -1012,7 +1019,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   ctx_init(c, p, bh - b * p.Hv);
   c.bar = bars;
   const bool mw = c.warp == kScanWorkers / 32;     // the MMA / copy warp
+  const bool worker = c.warp < kScanWorkers / 32;
+  const bool nw = NORM && c.warp > kScanWorkers / 32;   // a norm warp
   const bool issuer = mw && c.lane == 0;
+  uint64_t* ybar = reinterpret_cast<uint64_t*>(sm + kScanYBar);   // [0..1] y ready, [2..3] y read, by parity
+  volatile int* s_fail = reinterpret_cast<volatile int*>(sm + kScanFail);
+  // barriers of the chain (workers + copy warp); the norm warps keep their own
+  auto chain_sync = [&]() { asm volatile("bar.sync 7, %0;" ::"n"(kScanThreads) : "memory"); };
+  auto chain_or = [&](bool pred) -> bool {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 7, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "n"(kScanThreads)
+        : "memory");
+    return r != 0;
+  };
   const int cg = (c.warp >> 2) & 3;                // column group of a worker
   long long s0, s1;
   seq_range(p, b, s0, s1);
@@ -1026,8 +1049,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   // product, the second [y | R] or [R | y] in one N = 192 product; odd chunks
   // mirror the order of the stacked B operands in shared memory to match.
   constexpr uint32_t cR = 0, cDR = 256;
+  if (NORM && c.tid == 0) {
+    ptx::mbar_init(ybar + 0, 1);
+    ptx::mbar_init(ybar + 1, 1);
+    ptx::mbar_init(ybar + 2, 8);
+    ptx::mbar_init(ybar + 3, 8);
+    *s_fail = 0;
+  }
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kScanBar + 32), bars, 4, kTmemCols);
-  if (!mw) state_load(p.win_c0 == 0 ? p.state_in : p.carry, c, bh, cDR, cg * 32, 32);
+  if (worker) state_load(p.win_c0 == 0 ? p.state_in : p.carry, c, bh, cDR, cg * 32, 32);
   const uint32_t lane_cols = c.tb + c.my + cg * 32;   // a worker's 32 columns of R / R fp32
 
   // record groups issued and waited for, counted by the copy warp only
@@ -1071,9 +1101,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   // MMA completion: the copy warp polls, the CTA agrees (false if it gave up)
   auto mma_done = [&](bool ok_in) -> bool {
     bool ok = ok_in;
-    if (mw) ok = ptx::mbar_wait(c.bar, c.phase) && ok;
+    if (mw) ok = ok && ptx::mbar_wait(c.bar, c.phase);
     c.phase ^= 1u;
-    const bool all = !__syncthreads_or(!ok);
+    const bool all = !chain_or(!ok);
     tc::fence_after_sync();
     return all;
   };
@@ -1105,30 +1135,132 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     }
     ptx::fence_proxy_async_smem();
   };
-  float* s_part = reinterpret_cast<float*>(sm + kScanNorm);   // [lane quarter][token] sums of y^2
-  const float gam = NORM ? __ldg(p.gamma + c.row) : 0.f;
-  // fused norm: the z rows of chunk ch (256 bytes per token) are copied into
-  // buffer ch % 3 by cp.async from the column group that normalises those
-  // tokens (16 tokens, two 16-byte pieces per thread), two chunks ahead of
-  // use; the load path keeps them off the bulk-copy engine that streams the
-  // records.  One commit group per chunk and thread.
-  auto load_z = [&](int ch) {
-    if (mw) return;
-    const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
-    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-    unsigned char* zb = sm + kScanZ + (ch % 3) * kZBuf;
-    const int tq = c.quarter * 32 + c.lane;
+  // ---- fused norm: the 8 norm warps (warp % 4 = TMEM lane quarter q, dv =
+  // 32 q + lane; group g of 4 warps takes tokens 32 g .. 32 g + 31) normalise
+  // chunk ch from its y in TMEM while the chain runs chunk ch + 1, and store
+  // the bf16 rows to every destination.  z rows
+  // (256 bytes per token) come by cp.async three chunks ahead into buffer
+  // ch % 3, which the normed rows then overwrite in place to be stored as
+  // 16-byte pieces.  Handshakes: ybar[ch & 1] (the MMA commit after the
+  // second batch of chunk ch) says y is complete; ybar[2 + (ch & 1)] (one
+  // arrival per norm warp) says it has been read, before the first batch of
+  // chunk ch + 2 overwrites those columns.
+  auto norm_chunks = [&]() {
+    const int grp = (c.tid - kScanThreads) >> 7;     // token half of the chunk
+    const int nt = (c.tid - kScanThreads) & 127;     // thread of the group
+    const int bar_id = 5 + grp;
+    const float gam = __ldg(p.gamma + c.row);
+    float4* s_tok = reinterpret_cast<float4*>(sm + kScanNorm + grp * 256);   // [token of the round] sums by quarter
+    auto nbar = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory"); };
+    auto load_z = [&](int ch) {
+      const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
+      const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+      unsigned char* zb = sm + kScanZ + (ch % 3) * kZBuf;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int piece = tq + k * 128;
-      const int tok = cg * 16 + (piece >> 4);
-      const int seg = (piece & 15) * 8;
-      if (tok < nvalid)
-        ptx::cp_async16(zb + (tok * kD + seg) * 2, p.z + (t0 + tok) * p.z_stride + c.h * kD + seg);
+      for (int k = 0; k < 4; ++k) {
+        const int piece = nt + k * 128;
+        const int tok = grp * 32 + (piece >> 4);
+        const int seg = (piece & 15) * 8;
+        if (tok < nvalid)
+          ptx::cp_async16(zb + (tok * kD + seg) * 2, p.z + (t0 + tok) * p.z_stride + c.h * kD + seg);
+      }
+      ptx::cp_async_commit();
+    };
+    // a bounded wait that also gives up once the chain has failed
+    auto wait_or_fail = [&](uint64_t* bar, uint32_t parity) -> bool {
+      for (uint32_t i = 0; i < ptx::kSpinLimit; ++i) {
+        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if (*s_fail) return false;
+      }
+      return false;
+    };
+    for (int ch = 0; ch < 3 && ch < n_chunks; ++ch) load_z(ch);
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      // every norm thread takes the same branch: a thread that gave up makes all stop
+      uint32_t any_fail;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+          "bar.red.or.pred p, %2, 128, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(any_fail)
+          : "r"(static_cast<uint32_t>(!wait_or_fail(&ybar[ch & 1], (ch >> 1) & 1))), "r"(bar_id)
+          : "memory");
+      if (any_fail) {
+        if (nt == 0) atomicExch(p.err, 1);
+        break;
+      }
+      tc::fence_after_sync();
+      const int newer = n_chunks - 1 - ch;           // z groups committed after this chunk's
+      if (newer >= 2) ptx::cp_async_wait<2>();
+      else if (newer == 1) ptx::cp_async_wait<1>();
+      else ptx::cp_async_wait<0>();
+      nbar();                                        // every norm thread's z pieces of the chunk have landed
+      const uint32_t col_y = (ch & 1) ? 384 : 192;
+      const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
+      const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
+      __nv_bfloat16* zt = reinterpret_cast<__nv_bfloat16*>(sm + kScanZ + (ch % 3) * kZBuf);
+      for (int r = 0; r < 2; ++r) {                  // 16 tokens per round
+        const int tb = grp * 32 + r * 16;            // first token of the round
+        float y[16];
+        tc::tmem_ld16(c.tb + col_y + c.my + tb, y);
+        tc::tmem_ld_wait();
+        if (r == 1) {                                // this warp's y of the chunk is read: release its columns
+          tc::fence_before_sync();
+          __syncwarp();
+          if (c.lane == 0) ptx::mbar_arrive(&ybar[2 + (ch & 1)]);
+        }
+        // sums of y^2 over this warp's 32 dv for the 16 tokens: halve the
+        // token set per exchange (8 + 4 + 2 + 1 shuffles), then one more; the
+        // pair of lanes 2t, 2t + 1 ends with token t
+        float s8[8], s4[4], s2[2], s1v;
+        const bool b16 = c.lane & 16, b8 = c.lane & 8, b4 = c.lane & 4, b2 = c.lane & 2;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float lo = y[i] * y[i], hi = y[i + 8] * y[i + 8];
+          s8[i] = (b16 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b16 ? lo : hi, 16);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s4[i] = (b8 ? s8[i + 4] : s8[i]) + __shfl_xor_sync(0xffffffffu, b8 ? s8[i] : s8[i + 4], 8);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) s2[i] = (b4 ? s4[i + 2] : s4[i]) + __shfl_xor_sync(0xffffffffu, b4 ? s4[i] : s4[i + 2], 4);
+        s1v = (b2 ? s2[1] : s2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s2[0] : s2[1], 2);
+        s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
+        if ((c.lane & 1) == 0) reinterpret_cast<float*>(s_tok)[(c.lane >> 1) * 4 + c.quarter] = s1v;
+        nbar();
+        const float4 pp = s_tok[c.lane & 15];
+        const float rr = rsqrtf((pp.x + pp.y + pp.z + pp.w) / static_cast<float>(kD) + p.eps);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {               // normed rows over the z they gate (same element)
+          const float ri = __shfl_sync(0xffffffffu, rr, i);
+          __nv_bfloat16* e = zt + (tb + i) * kD + c.row;
+          const float zz = __bfloat162float(*e);
+          const float sg = __fdividef(1.f, 1.f + __expf(-zz));
+          *e = __float2bfloat16_rn((y[i] * ri * gam) * (zz * sg));
+        }
+        nbar();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {                // 16 rows x 16 pieces of 16 bytes
+          const int piece = nt + k * 128;
+          const int tok = tb + (piece >> 4);
+          const int seg = (piece & 15) * 8;
+          if (tok < nvalid) {
+            const uint4 v = *reinterpret_cast<const uint4*>(zt + tok * kD + seg);
+            const long long off = (t0 + tok) * p.out_stride + static_cast<long long>(p.out_head0 + c.h) * kD + seg;
+            if (off + 8 <= p.out_elems) {
+#pragma unroll
+              for (int d = 0; d < 8; ++d)
+                if (d < p.n_dst) *reinterpret_cast<uint4*>(p.dst[d] + off) = v;
+            } else {
+              atomicExch(p.err, 1);
+            }
+          }
+        }
+      }
+      nbar();                                        // buffer ch % 3 fully stored: refill it
+      if (ch + 3 < n_chunks) load_z(ch + 3);
     }
-    ptx::cp_async_commit();
+    ptx::cp_async_wait<0>();                         // no z copy may land after the CTA exits
   };
-  // o rows of chunk ch from y^T: a worker's dv = row, tokens cg*16 + part*8 .. +7
+  // o rows of chunk ch from y^T (plain scan): a worker's dv = row, tokens cg*16 + part*8 .. +7
   auto epi_o = [&](int ch, int part) {
     const uint32_t col_y = (ch & 1) ? 384 : 192;
     const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
@@ -1136,59 +1268,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
     const int tok = cg * 16 + part * 8;
     const int nv = nvalid - tok;
     float y[8];
-    if constexpr (NORM) {
-      __nv_bfloat16* zt = reinterpret_cast<__nv_bfloat16*>(sm + kScanZ + (ch % 3) * kZBuf);
-      if (part == 0) {         // this thread's copies of chunk ch; the barrier below publishes the group's
-        const int newer = n_chunks - 1 - ch;       // chunks whose z groups were committed after this one's
-        if (newer >= 2) ptx::cp_async_wait<2>();
-        else if (newer == 1) ptx::cp_async_wait<1>();
-        else ptx::cp_async_wait<0>();
-      }
-      tc::tmem_ld8(c.tb + col_y + c.my + tok, y);
-      tc::tmem_ld_wait();
-      // sum of y^2 over this warp's 32 rows for each of the 8 tokens: halve the
-      // token set per exchange (4 + 2 + 1 shuffles), then finish with 2
-      float s4[4], s2[2], s1v;
-      const bool b4 = c.lane & 16, b3 = c.lane & 8, b2 = c.lane & 4;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float lo = y[i] * y[i], hi = y[i + 4] * y[i + 4];
-        s4[i] = (b4 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b4 ? lo : hi, 16);
-      }
-#pragma unroll
-      for (int i = 0; i < 2; ++i) s2[i] = (b3 ? s4[i + 2] : s4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? s4[i] : s4[i + 2], 8);
-      s1v = (b2 ? s2[1] : s2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s2[0] : s2[1], 4);
-      s1v += __shfl_xor_sync(0xffffffffu, s1v, 2);
-      s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
-      if ((c.lane & 3) == 0) s_part[c.quarter * kC + tok + (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0)] = s1v;
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");   // the 4 warps of this column group
-      // normalised rows over the z rows they gate (same thread, same element),
-      // then 16-byte pieces of the 8 rows to every destination
-      __nv_bfloat16* tile = zt;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float ss = s_part[tok + i] + s_part[kC + tok + i] + s_part[2 * kC + tok + i] + s_part[3 * kC + tok + i];
-        const float r = rsqrtf(ss / static_cast<float>(kD) + p.eps);
-        const float zz = __bfloat162float(zt[(tok + i) * kD + c.row]);
-        const float sg = __fdividef(1.f, 1.f + __expf(-zz));
-        tile[(tok + i) * kD + c.row] = __float2bfloat16_rn((y[i] * r * gam) * (zz * sg));
-      }
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + cg), "r"(128) : "memory");
-      const int tt = c.quarter * 32 + c.lane;          // 128 threads: 8 rows x 16 pieces of 16 bytes
-      const int ti = tt >> 4, seg = (tt & 15) * 8;
-      if (ti < nv) {
-        const uint4 piece = *reinterpret_cast<const uint4*>(tile + (tok + ti) * kD + seg);
-        const long long off = (t0 + tok + ti) * p.out_stride + static_cast<long long>(p.out_head0 + c.h) * kD + seg;
-        if (off + 8 <= p.out_elems) {
-#pragma unroll
-          for (int d = 0; d < 8; ++d)
-            if (d < p.n_dst) *reinterpret_cast<uint4*>(p.dst[d] + off) = piece;
-        } else if (c.lane == 0) {
-          atomicExch(p.err, 1);
-        }
-      }
-      return;
-    }
     tc::tmem_ld8(c.tb + col_y + c.my + tok, y);
     tc::tmem_ld_wait();
     const size_t orow = static_cast<size_t>(p.Hv) * kD;
@@ -1207,92 +1286,100 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const Chunk
   };
 
   bool failed = false;
-  if (n_chunks > 0) {
-    load(1, 0);
-    load(2, 0);
-    load(3, 0);
-    if (NORM) {
-      load_z(0);
-      if (n_chunks > 1) load_z(1);
-    }
-    if (!mw) {
-      r_pass(true, 1.f);                  // tf32(R_0)
-      tc::tmem_st_wait();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-  }
-  for (int ch = 0; ch < n_chunks && !failed; ++ch) {
-    const bool odd = ch & 1;
-    const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
-    const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
-    const uint32_t col_u = odd ? 448 : 128;
-    // -W | Qs and U0^T | g_last of this chunk in shared memory
-    bool ok = wait_group(1, ch);
-    ok = wait_group(3, ch) && ok;
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    tc::fence_after_sync();
-    GDN_TICK(29);
-    if (issuer) {              // first batch: [U | y] = R [-W; Qs]^T (U0^T is added in the epilogue)
-      const uint32_t id = tc::instr_desc(tc::kTF32, 128, 2 * kC);
-      for (int j = 0; j < kD / 8; ++j)
-        tc::mma_ts_tf32(c.tb + col_b1, c.tb + cR + j * 8, desc(sm + kScanG1, j * 256, kSbo128), id, j > 0);
-      tc::mma_commit(c.bar);
-    } else if (!mw) {          // under it: R *= g_last(ch) for the update, half of the previous o
-      r_pass(false, sSc[0]);
-      if (ch > 0) epi_o(ch - 1, 0);
-      tc::tmem_st_wait();
-    }
-    tc::fence_before_sync();
-    if (!mma_done(true)) { failed = true; break; }
-    GDN_TICK(24);
-    if (ch + 1 < n_chunks) load(1, ch + 1);
-    if (!mw) epi_u(col_u);
-    ok = wait_group(2, ch);
-    tc::fence_before_sync();
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    tc::fence_after_sync();
-    GDN_TICK(25);
-    if (issuer) {              // second batch: [y | R] += U^T [M; K-hat^T]^T
-      const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC + kD);
-      for (int j = 0; j < kC / 8; ++j)
-        tc::mma_ss<tc::kTF32>(c.tb + col_b2, desc(sU, j * 256, kSbo64), desc(sm + kScanG2, j * 256, kSbo64), id, 1);
-      tc::mma_commit(c.bar);
-    } else if (!mw && ch > 0) {
-      epi_o(ch - 1, 1);        // under it: the other half of the previous o
-    }
-    if (ch + 1 < n_chunks) load(3, ch + 1);
-    tc::fence_before_sync();
-    if (!mma_done(true)) { failed = true; break; }
-    GDN_TICK(26);
-    if (NORM && ch + 2 < n_chunks) load_z(ch + 2);   // its buffer's chunk ch - 1 is normalised by now
-    if (ch + 1 < n_chunks) {
-      load(2, ch + 1);
-      if (!mw) {
-        r_pass(true, 1.f);                // tf32(R_{ch+1}) for the next first batch
+  if (nw) {
+    if (n_chunks > 0) norm_chunks();
+  } else {
+    if (n_chunks > 0) {
+      load(1, 0);
+      load(2, 0);
+      load(3, 0);
+      if (worker) {
+        r_pass(true, 1.f);                  // tf32(R_0)
         tc::tmem_st_wait();
       }
+      tc::fence_before_sync();
+      chain_sync();
     }
-    tc::fence_before_sync();
-    __syncthreads();
-    GDN_TICK(27);
-  }
-  if (!failed && n_chunks > 0 && !mw) {
-    epi_o(n_chunks - 1, 0);
-    epi_o(n_chunks - 1, 1);
-  }
-  if (failed) {
-    // bounded waits for the MMA and the bulk copies still in flight
-    if (c.tid == 0) atomicExch(p.err, 1);
-    if (mw) {
-      ptx::mbar_wait(c.bar, c.phase ^ 1u);
-      for (int g = 1; g <= 3; ++g)
-        if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
+    for (int ch = 0; ch < n_chunks && !failed; ++ch) {
+      const bool odd = ch & 1;
+      const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
+      const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
+      const uint32_t col_u = odd ? 448 : 128;
+      // -W | Qs and U0^T | g_last of this chunk in shared memory
+      bool ok = wait_group(1, ch);
+      ok = wait_group(3, ch) && ok;
+      if (chain_or(!ok)) { failed = true; break; }
+      tc::fence_after_sync();
+      GDN_TICK(29);
+      bool yok = true;
+      if (issuer) {              // first batch: [U | y] = R [-W; Qs]^T (U0^T is added in the epilogue)
+        // the norm warps have read y of chunk ch - 2, whose columns this batch overwrites
+        if (NORM && ch >= 2) yok = ptx::mbar_wait(&ybar[2 + (ch & 1)], ((ch >> 1) - 1) & 1);
+        if (yok) {
+          tc::fence_after_sync();
+          const uint32_t id = tc::instr_desc(tc::kTF32, 128, 2 * kC);
+          for (int j = 0; j < kD / 8; ++j)
+            tc::mma_ts_tf32(c.tb + col_b1, c.tb + cR + j * 8, desc(sm + kScanG1, j * 256, kSbo128), id, j > 0);
+          tc::mma_commit(c.bar);
+        }
+      } else if (worker) {       // under it: R *= g_last(ch) for the update, half of the previous o
+        r_pass(false, sSc[0]);
+        if (!NORM && ch > 0) epi_o(ch - 1, 0);
+        tc::tmem_st_wait();
+      }
+      tc::fence_before_sync();
+      if (!mma_done(yok)) { failed = true; break; }
+      GDN_TICK(24);
+      if (ch + 1 < n_chunks) load(1, ch + 1);
+      if (worker) epi_u(col_u);
+      ok = wait_group(2, ch);
+      tc::fence_before_sync();
+      if (chain_or(!ok)) { failed = true; break; }
+      tc::fence_after_sync();
+      GDN_TICK(25);
+      if (issuer) {              // second batch: [y | R] += U^T [M; K-hat^T]^T
+        const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC + kD);
+        for (int j = 0; j < kC / 8; ++j)
+          tc::mma_ss<tc::kTF32>(c.tb + col_b2, desc(sU, j * 256, kSbo64), desc(sm + kScanG2, j * 256, kSbo64), id, 1);
+        tc::mma_commit(c.bar);
+        if (NORM) tc::mma_commit(&ybar[ch & 1]);   // y of chunk ch complete: the norm warps take it
+      } else if (worker && !NORM && ch > 0) {
+        epi_o(ch - 1, 1);        // under it: the other half of the previous o
+      }
+      if (ch + 1 < n_chunks) load(3, ch + 1);
+      tc::fence_before_sync();
+      if (!mma_done(true)) { failed = true; break; }
+      GDN_TICK(26);
+      if (ch + 1 < n_chunks) {
+        load(2, ch + 1);
+        if (worker) {
+          r_pass(true, 1.f);                // tf32(R_{ch+1}) for the next first batch
+          tc::tmem_st_wait();
+        }
+      }
+      tc::fence_before_sync();
+      chain_sync();
+      GDN_TICK(27);
     }
-  } else if (!mw) {
-    state_store(p.carry, c, bh, cDR, cg * 32, 32);
+    if (!NORM && !failed && n_chunks > 0 && worker) {
+      epi_o(n_chunks - 1, 0);
+      epi_o(n_chunks - 1, 1);
+    }
+    if (failed) {
+      // bounded waits for the MMA and the bulk copies still in flight; the norm warps stop
+      if (c.tid == 0) {
+        atomicExch(p.err, 1);
+        if (NORM) *s_fail = 1;
+      }
+      if (mw) {
+        ptx::mbar_wait(c.bar, c.phase ^ 1u);
+        for (int g = 1; g <= 3; ++g)
+          if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
+      }
+    } else if (worker) {
+      state_store(p.carry, c, bh, cDR, cg * 32, 32);
+    }
   }
-  if (NORM) ptx::cp_async_wait<0>();               // no z copy may land after the CTA exits
   if (NORM && p.n_dst > 1) __threadfence_system();  // peer stores performed before the call's signal
   tc::fence_before_sync();
   __syncthreads();
@@ -1450,7 +1537,7 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
       rc = cuda_status(cudaGetLastError(), "chunk prep launch");
       if (rc != GDN_OK) return rc;
     }
-    if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmemNorm, st>>>(p);
+    if (p.z) chunk_scan_kernel<true><<<static_cast<unsigned>(p.B * p.Hv), kScanThreadsNorm, kScanSmemNorm, st>>>(p);
     else chunk_scan_kernel<false><<<static_cast<unsigned>(p.B * p.Hv), kScanThreads, kScanSmem, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "chunk scan launch");
     if (rc != GDN_OK) return rc;
