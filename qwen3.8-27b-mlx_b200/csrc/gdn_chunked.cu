@@ -84,30 +84,30 @@ constexpr uint32_t kOffBar = kOffSc + 10 * kC * 4;  // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
 
 // shared memory map of the prep kernel: regions are reused as the phases go,
-// so that two CTAs fit on an SM
-constexpr uint32_t kPKQ = 0;                        // [K; Q] rows 128 x 128, until (a) and its epilogue
-constexpr uint32_t kPA = 0;                         // A^T, plain, over the K rows once (a) has run
+// so that three CTAs fit on an SM
+constexpr uint32_t kPKQ = 0;                        // [K; Q] rows 128 x 128 bf16 (32 KiB), until (a) and Q-tilde
+constexpr uint32_t kSboKQ = (kD * 2 / 16) * 128;    // 8-row group stride of 128-wide bf16 rows
+constexpr uint32_t kPA = 0;                         // A^T, plain, row stride 68, once Q-tilde is written
 constexpr uint32_t kPY = kPA + kC * kPadA * 4;      // solve temporaries
-constexpr uint32_t kPX = 32768;                     // X, plain, over the Q rows once they are read
-constexpr uint32_t kPKt = 0;                        // K^T diag(beta g r_k) 128 x 64, after the solve
-constexpr uint32_t kPVt = 32768;                    // V^T diag(beta) 128 x 64, after the solve
-constexpr uint32_t kPTi = 65536;                    // T^-1 64 x 64
+constexpr uint32_t kPX = kPY + 3 * 256 * 4;         // X, plain
+constexpr uint32_t kPOp = 0;                        // V^T diag(beta), then K^T diag(beta g r_k): 128 x 64, after the solve
+constexpr uint32_t kPTi = 37888;                    // T^-1 64 x 64
 constexpr int kPrepHeads = 4;                       // value heads per prep CTA at most (one key head's)
 constexpr uint32_t kPSc = kPTi + kC * kC * 4;       // per-token scalars, 10 x 64 per value head
 constexpr uint32_t kPBar = kPSc + kPrepHeads * 10 * kC * 4;   // mbarrier, TMEM base, slot broadcast
 constexpr uint32_t kPrepSmem = kPBar + 64;
-static_assert(kPY + 3 * 256 * 4 <= kPX, "prep: solve temporaries overlap X");
 static_assert(kPX + kC * kPad * 4 <= kPTi, "prep: X overlaps T^-1");
-static_assert(2 * (kPrepSmem + 1024) <= 233472, "prep: two CTAs per SM");
+static_assert(kD * kC * 4 <= kPTi, "prep: the column operand overlaps T^-1");
+static_assert(3 * (kPrepSmem + 1024) <= 233472, "prep: three CTAs per SM");
 
 constexpr uint32_t kTmemCols = 512;
 // fused: [0,128) R (tf32), [128,256) R (fp32 master, state-update
 // accumulator), [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
 // [384,448) U^T; [448,512) y^T
 constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 384, kColY = 448;
-// prep: [0,64) G|P, [64,128) U0^T, [128,192) W^T
-constexpr uint32_t kPrepTmemCols = 256;
-constexpr uint32_t kPColGP = 0, kPColU = 64, kPColWt = 128;
+// prep: [0,64) G|P, [64,128) U0^T, then W^T
+constexpr uint32_t kPrepTmemCols = 128;
+constexpr uint32_t kPColGP = 0, kPColUW = 64;
 
 // One workspace record per (chunk, value head): the prep kernel's outputs as
 // tensor-core operands (K-major, no swizzle) in three groups that the scan
@@ -287,8 +287,8 @@ __device__ __forceinline__ void ctx_fused_layout(Ctx& c, unsigned char* sm) {
 // Shared-memory pointers of the prep kernel's layout (M and W go to the record).
 __device__ __forceinline__ void ctx_prep_layout(Ctx& c, unsigned char* sm) {
   c.sKQ = sm + kPKQ;
-  c.sKt = sm + kPKt;
-  c.sVt = sm + kPVt;
+  c.sKt = sm + kPOp;
+  c.sVt = sm + kPOp;
   c.sTi = sm + kPTi;
   c.sM = nullptr;
   c.sW = nullptr;
@@ -529,23 +529,6 @@ __device__ __forceinline__ void phase_epi_a(Ctx& c, uint32_t col, unsigned char*
     }
   }
   __syncthreads();
-}
-
-// diag(g r_q) Q rows of [K; Q] into q_dst with the decay g of scalar block
-// s_g (all 256 threads: thread -> token i, 32-dim quarter).  No barrier.
-__device__ __forceinline__ void phase_qtilde(const Ctx& c, const float* s_g, unsigned char* q_dst) {
-  const int i = c.tid >> 2;
-  const int c0 = (c.tid & 3) * 32;
-  const float sq = s_g[i] * c.s_rq[i];
-#pragma unroll
-  for (int cc = c0; cc < c0 + 32; cc += 4) {
-    float4 v = *reinterpret_cast<const float4*>(at(c.sKQ, kC + i, cc, kSbo128));
-    v.x = tc::to_tf32(v.x * sq);
-    v.y = tc::to_tf32(v.y * sq);
-    v.z = tc::to_tf32(v.z * sq);
-    v.w = tc::to_tf32(v.w * sq);
-    *reinterpret_cast<float4*>(at(q_dst, i, cc, kSbo128)) = v;
-  }
 }
 
 // T^-1 = (I + A)^-1 by forward substitution on all 64 columns at once:
@@ -881,42 +864,157 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
   if (threadIdx.x == 0) prefix[B] = carry;
 }
 
-// (b) U0^T = V^T diag(beta) T^-T and (c) W^T = K^T diag(beta g r_k) T^-T, both
+// Rows of K and Q (thread -> token i, 32-dim quarter) copied as bf16 into the
+// K-major operand [K; Q] of a kind::f16 product (the raw bf16 values are the
+// exact operands; the l2 norms are applied later as per-token scalars), and
+// their norms.  Ends with a barrier.
+__device__ __forceinline__ void prep_rows(const ChunkParams& p, Ctx& c, long long t0, long long s0, int nvalid) {
+  const int i = c.tid >> 2;
+  const int qd = c.tid & 3;
+  const bool valid = i < nvalid;
+  const long long tok = valid ? t0 + i : s0;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const __nv_bfloat16* src = (which ? p.q + tok * p.q_stride : p.k + tok * p.k_stride) + c.kh * kD + qd * 32;
+    uint4 v[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) v[m] = valid ? __ldg(reinterpret_cast<const uint4*>(src) + m) : make_uint4(0, 0, 0, 0);
+    float ss = 0.f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[m]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+      *reinterpret_cast<uint4*>(c.sKQ + tc::kmajor_offset(which * kC + i, qd * 32 + m * 8, 2, kSboKQ)) = v[m];
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    if (qd == 0) {
+      if (which) c.s_rq[i] = c.l2 ? rsqrtf(ss + 1e-6f) * c.qscale : 1.f;
+      else c.s_rk[i] = c.l2 ? rsqrtf(ss + 1e-6f) : 1.f;
+    }
+  }
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
+}
+
+// (a) [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127) at TMEM column 0, bf16 operands.
+__device__ __forceinline__ bool prep_mma_a(Ctx& c) {
+  if (c.tid == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC);
+    for (int j = 0; j < kD / 16; ++j)
+      tc::mma_ss<tc::kBF16>(c.tb + kPColGP, desc(c.sKQ, j * 256, kSboKQ), desc(c.sKQ, j * 256, kSboKQ), id, j > 0);
+    tc::mma_commit(c.bar);
+  }
+  return mma_wait(c);
+}
+
+// diag(g r_q) Q, tf32, into q_dst (record layout) from the bf16 Q rows, with
+// the decay g of scalar block s_g (thread -> token i, 32-dim quarter).  No barrier.
+__device__ __forceinline__ void prep_qtilde(const Ctx& c, const float* s_g, unsigned char* q_dst) {
+  const int i = c.tid >> 2;
+  const int c0 = (c.tid & 3) * 32;
+  const float sq = s_g[i] * c.s_rq[i];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(c.sKQ + tc::kmajor_offset(kC + i, c0 + m * 8, 2, kSboKQ));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      x[2 * e] = tc::to_tf32(f.x * sq);
+      x[2 * e + 1] = tc::to_tf32(f.y * sq);
+    }
+    *reinterpret_cast<float4*>(at(q_dst, i, c0 + m * 8, kSbo128)) = make_float4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<float4*>(at(q_dst, i, c0 + m * 8 + 4, kSbo128)) = make_float4(x[4], x[5], x[6], x[7]);
+  }
+}
+
+// Columns of V (is_k false) or K read from global two at a time (4-byte
+// loads), scaled per token by scale[], stored as rows of the transposed
+// operand (K-major, 64 tokens wide) at dst, and when dst2 is set scaled by
+// scale2[] into dst2 too.  All 256 threads: column pair tid & 63, token
+// quarter tid >> 6 (16 loads in flight per thread).
+__device__ __forceinline__ void prep_columns(const ChunkParams& p, const Ctx& c, long long t0, int nvalid, bool is_k,
+                                             const float* scale, unsigned char* dst, const float* scale2,
+                                             unsigned char* dst2) {
+  const int cc = 2 * (c.tid & 63);
+  const int tq = c.tid >> 6;
+  const long long stride = is_k ? p.k_stride : p.v_stride;
+  const __nv_bfloat16* src = (is_k ? p.k + c.kh * kD : p.v + c.h * kD) + cc + (t0 + tq * 16) * stride;
+  const int nv = nvalid - tq * 16;
+  __nv_bfloat162 raw[16];                   // all loads in flight before any use
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * stride) : __floats2bfloat162_rn(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    float x0[4], x1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float s = scale[tq * 16 + j + e];
+      const float2 f = __bfloat1622float2(raw[j + e]);
+      x0[e] = tc::to_tf32(f.x * s);
+      x1[e] = tc::to_tf32(f.y * s);
+    }
+    *reinterpret_cast<float4*>(at(dst, cc, tq * 16 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+    *reinterpret_cast<float4*>(at(dst, cc + 1, tq * 16 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+    if (dst2) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float s = scale2[tq * 16 + j + e];
+        const float2 f = __bfloat1622float2(raw[j + e]);
+        x0[e] = tc::to_tf32(f.x * s);
+        x1[e] = tc::to_tf32(f.y * s);
+      }
+      *reinterpret_cast<float4*>(at(dst2, cc, tq * 16 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+      *reinterpret_cast<float4*>(at(dst2, cc + 1, tq * 16 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+    }
+  }
+}
+
+// (b) U0^T = V^T diag(beta) T^-T, or (c) W^T = K^T diag(beta g r_k) T^-T:
 // M = 128 (Dv resp. Dk rows) x N = 64 tokens with T^-1 as the B operand.
-__device__ __forceinline__ bool phase_mma_bc_prep(Ctx& c) {
+__device__ __forceinline__ bool prep_mma_uw(Ctx& c) {
   if (c.tid == 0) {
     tc::fence_after_sync();
     const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
     for (int j = 0; j < kC / 8; ++j)
-      tc::mma_ss<tc::kTF32>(c.tb + kPColU, desc(c.sVt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
-    for (int j = 0; j < kC / 8; ++j)
-      tc::mma_ss<tc::kTF32>(c.tb + kPColWt, desc(c.sKt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
+      tc::mma_ss<tc::kTF32>(c.tb + kPColUW, desc(c.sVt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
     tc::mma_commit(c.bar);
   }
   return mma_wait(c);
 }
 
 // U0^T rows into the record by column quads (conflict-free reads for the scan
-// kernel's threads) and W^T columns, negated, into the record's K-major W
+// kernel's threads), or W^T columns, negated, into the record's K-major W
 // (token rows).
-__device__ __forceinline__ void phase_epi_prep(Ctx& c, unsigned char* rec) {
+__device__ __forceinline__ void prep_epi_uw(Ctx& c, unsigned char* rec, bool is_w) {
   float u[32];
-  tmem_ld<32>(c.tb + kPColU + c.my + c.half * 32, u);
-  float4* ud = reinterpret_cast<float4*>(rec + kRecU);
+  tmem_ld<32>(c.tb + kPColUW + c.my + c.half * 32, u);
+  if (!is_w) {
+    float4* ud = reinterpret_cast<float4*>(rec + kRecU);
 #pragma unroll
-  for (int e = 0; e < 32; e += 4)
-    ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
-  tmem_ld<32>(c.tb + kPColWt + c.my + c.half * 32, u);
+    for (int e = 0; e < 32; e += 4)
+      ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+  } else {
 #pragma unroll
-  for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = -tc::to_tf32(u[e]);
-  if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
+    for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = -tc::to_tf32(u[e]);
+    if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
+  }
 }
 
 // One CTA per (chunk, key head) handles the hpc value heads that share that
 // key head (hpc = Hv / Hk when it is at most kPrepHeads, else one): the K / Q
 // rows, their norms and [K; Q] K^T are formed once; gates, A, the solve, M,
-// the columns and U0 / W per value head.
-__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkParams p, int hpc) {
+// and per value head the V pass (U0) then the K pass (W, K-hat) through one
+// 32 KiB operand buffer and one accumulator, so that three CTAs fit on an SM.
+__global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkParams p, int hpc) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const long long slot = blockIdx.x;
   int* s_bc = reinterpret_cast<int*>(sm + kPBar + 16);
@@ -958,32 +1056,43 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const ChunkPara
   }
   GDN_TICK(16);
   head_scalars(0);
-  phase_rows(p, c, t0, s0, nvalid);            // shared K / Q rows and norms (ends with a barrier)
+  prep_rows(p, c, t0, s0, nvalid);             // shared K / Q rows and norms (ends with a barrier)
   GDN_TICK(17);
-  bool ok = phase_mma_a(c, kPColGP);           // G | P, shared, kept in TMEM for every head
+  bool ok = prep_mma_a(c);                     // G | P, shared, kept in TMEM for every head
   GDN_TICK(18);
   for (int j = 0; j < hpc && ok; ++j) {
     head_scalars(j);
     head_gates(j);
     unsigned char* rec = record(p, slot, c.h);
-    if (j == 0) {                              // Q rows are overwritten by the first solve: Qs for all heads now
-      for (int jj = 0; jj < hpc; ++jj) phase_qtilde(c, sc0 + jj * 10 * kC + 128, record(p, slot, h0 + jj) + kRecQ);
+    if (j == 0) {                              // the Q rows are overwritten by A: Q-tilde for all heads now
+      for (int jj = 0; jj < hpc; ++jj) prep_qtilde(c, sc0 + jj * 10 * kC + 128, record(p, slot, h0 + jj) + kRecQ);
+      __syncthreads();
     }
-    phase_epi_a(c, kPColGP, rec + kRecM, nullptr);     // A over the K rows; M to the record
+    phase_epi_a(c, kPColGP, rec + kRecM, nullptr);     // A over the rows; M to the record
     GDN_TICK(19);
-    phase_solve(c);                                    // X over the Q rows
+    phase_solve(c);                                    // X, then T^-1
     GDN_TICK(20);
-    phase_cols(p, c, t0, nvalid, rec + kRecKh);        // K^T, V^T over A and X; K-hat^T to the record
-    tc::fence_before_sync();
+    if (c.tid < kC) {
+      c.s_kw[c.tid] = c.s_beta[c.tid] * c.s_g[c.tid] * c.s_rk[c.tid];
+      c.s_kh[c.tid] = c.s_ratio[c.tid] * c.s_rk[c.tid];
+    }
     __syncthreads();
-    GDN_TICK(21);
-    ok = phase_mma_bc_prep(c);
-    GDN_TICK(22);
-    if (ok) {
-      phase_epi_prep(c, rec);
+    for (int pass = 0; pass < 2 && ok; ++pass) {       // V: U0^T; then K: W^T (and K-hat^T to the record)
+      const bool is_k = pass == 1;
+      prep_columns(p, c, t0, nvalid, is_k, is_k ? c.s_kw : c.s_beta, c.sVt, is_k ? c.s_kh : nullptr,
+                   is_k ? rec + kRecKh : nullptr);
+      ptx::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncthreads();
-      GDN_TICK(23);
+      GDN_TICK(21);
+      ok = prep_mma_uw(c);
+      GDN_TICK(22);
+      if (ok) {
+        prep_epi_uw(c, rec, is_k);
+        tc::fence_before_sync();
+        __syncthreads();
+        GDN_TICK(23);
+      }
     }
   }
   if (!ok) {

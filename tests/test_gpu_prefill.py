@@ -213,9 +213,11 @@ def test_chunked_varlen_packed(split):
 
 @pytest.mark.parametrize("lens", [[300], [130, 130, 130], [100, 0, 257, 64, 3, 1, 640]])
 def test_split_schedule_matches_fused(lens):
-    """The split schedule forms the same tf32 operands as the fused kernel (W
-    as W^T = K^T diag(beta g r_k) T^-T, the other products unchanged), so the
-    two agree far inside the oracle bound (1e-5 relative L2); a second call on
+    """The split schedule forms the same products as the fused kernel (W as
+    W^T = K^T diag(beta g r_k) T^-T; [K; Q] K^T from the raw bf16 rows with
+    bf16 operands where the fused kernel uses tf32 -- the same exact products,
+    summed in another order inside the tensor core), so the two agree far
+    inside the oracle bound of 2e-3 (1e-4 relative L2 here); a second call on
     the same reused, unzeroed workspace gives the same bits as the first."""
     rng = np.random.default_rng(60 + len(lens))
     total = sum(lens)
@@ -230,8 +232,8 @@ def test_split_schedule_matches_fused(lens):
     ws = torch.full((need,), 0xAB, dtype=torch.uint8, device="cuda")
     o_1, S_1 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
     o_2, S_2 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
-    assert O.rel_l2(host(o_1), host(o_f)) < 1e-5, O.rel_l2(host(o_1), host(o_f))
-    assert O.rel_l2(host(S_1), host(S_f)) < 1e-5, O.rel_l2(host(S_1), host(S_f))
+    assert O.rel_l2(host(o_1), host(o_f)) < 1e-4, O.rel_l2(host(o_1), host(o_f))
+    assert O.rel_l2(host(S_1), host(S_f)) < 1e-4, O.rel_l2(host(S_1), host(S_f))
     assert torch.equal(o_1, o_2) and torch.equal(S_1, S_2)
     assert G.take_device_error() == 0
 
