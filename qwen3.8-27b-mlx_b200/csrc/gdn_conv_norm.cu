@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include "gdn_internal.h"
+#include "gdn_ptx.cuh"
 
 namespace gdn {
 namespace {
@@ -190,10 +191,11 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_tok_kernel(const ConvPara
 
 // One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
 // the 3-row causal window in registers, so every x element is read once
-// (plus a 3-row halo at the start of the run); rows are fetched 8 at a time
-// ahead of use so that each thread keeps 128 bytes of loads in flight.
+// (plus a 3-row halo at the start of the run); rows stream in 8 at a time
+// through a cp.async double buffer (32 KiB per block, 80 registers, six
+// blocks per SM), so the next 8 rows are in flight while these are computed.
 template <bool BF16_OPS>
-__global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParams p) {
+__global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParams p) {
   const long long t_begin = static_cast<long long>(blockIdx.y) * kConvRun;
   if (t_begin >= p.total) return;
   // one binary search of cu_seqlens per block, shared through shared memory
@@ -241,12 +243,26 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
   };
   load_window(t_begin);
 
-  for (long long tb = t_begin; tb < t_end; tb += kConvBatch) {
-    // issue the batch's row loads before any of them is used
-    Bf16x8 xr[kConvBatch];
+  // x rows of a batch go through a per-thread double buffer in shared memory
+  // by cp.async: batch k + 1 streams in while batch k is computed, and the
+  // rows hold no registers while in flight.  Each thread reads only its own
+  // slots, so no barrier is needed.
+  __shared__ Bf16x8 stage[2][kConvBatch][kConvThreads];
+  auto issue = [&](long long tb, int sbuf) {
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u)
-      if (tb + u < t_end) xr[u] = *reinterpret_cast<const Bf16x8*>(p.x + (tb + u) * p.C + c0);
+      if (tb + u < t_end) ptx::cp_async16(&stage[sbuf][u][threadIdx.x], p.x + (tb + u) * p.C + c0);
+    ptx::cp_async_commit();
+  };
+  issue(t_begin, 0);
+  int sbuf = 0;
+  for (long long tb = t_begin; tb < t_end; tb += kConvBatch, sbuf ^= 1) {
+    if (tb + kConvBatch < t_end) {
+      issue(tb + kConvBatch, sbuf ^ 1);
+      ptx::cp_async_wait<1>();
+    } else {
+      ptx::cp_async_wait<0>();
+    }
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u) {
       const long long t = tb + u;
@@ -263,7 +279,7 @@ __global__ void __launch_bounds__(kConvThreads, 4) conv1d_kernel(const ConvParam
         load_window(t);
       }
       float xv[kConvVec];
-      unpack8(xr[u], xv);
+      unpack8(stage[sbuf][u][threadIdx.x], xv);
       *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = conv_taps<bf16_ops>(win, xv, w, silu);
 #pragma unroll
       for (int e = 0; e < kConvVec; ++e) {
