@@ -1,0 +1,167 @@
+"""One Gated DeltaNet layer around the GDN kernels: the host-side mirror of
+GatedDeltaNet::operator() (cpp/src/model.cpp:582-641; python/qwen35.py:
+575-640) for prefill, on this GPU's K-head shard.
+
+    qkv = in_proj_qkv(x)            bf16 GEMM (cuBLAS through torch.matmul)
+    z   = in_proj_z(x)              bf16 GEMM
+    a, b = in_proj_a(x), in_proj_b(x) -> fp32
+    y   = silu(conv1d(qkv))         gdn_conv1d_fwd
+    out = norm(chunked(q, k, v, a, b), z)
+                                    gdn_chunked_norm_fwd_ws, or on several ranks
+                                    gdn_chunked_norm_gather_ws + gdn_gather_wait
+                                    (every rank ends with all heads)
+    y   = out_proj(out)             bf16 GEMM on this rank's token slice
+
+The projections are plain library GEMMs.  With the heads sharded, in_proj
+needs no exchange (x is replicated and each rank produces its own channels);
+after the fused gather every rank holds all heads of every token, so each
+computes out_proj for 1/N of the tokens -- the result of a row-parallel
+out_proj followed by a reduce-scatter, with no further communication.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+import gdn_b200 as G
+import gdn_shard
+
+D = 128
+
+
+class GDNLayer:
+    """Weights of one layer for one rank: W_qkv (C_shard, hidden) rows of the
+    shard's conv channels [q | k | v], W_z (hv*128, hidden), W_a, W_b (hv,
+    hidden), conv_w (C_shard, 4), A_log / dt_bias (hv,), gamma (128,) fp32 and
+    the full W_out (hidden, Hv*128).  All bf16 unless noted, on one device."""
+
+    def __init__(self, W_qkv, W_z, W_a, W_b, conv_w, A_log, dt_bias, gamma, W_out, Hk: int, Hv: int,
+                 rank: int = 0, world: int = 1, eps: float = 1e-6):
+        self.shard = gdn_shard.head_shard(rank, world, Hk, Hv)
+        self.rank, self.world = rank, world
+        self.Hk, self.Hv = Hk, Hv
+        self.W_qkv, self.W_z, self.W_a, self.W_b = W_qkv, W_z, W_a, W_b
+        self.conv_w, self.A_log, self.dt_bias, self.gamma, self.W_out = conv_w, A_log, dt_bias, gamma, W_out
+        self.eps = eps
+        self.hk, self.hv = self.shard.hk, self.shard.hv
+        self.C = 2 * self.hk * D + self.hv * D
+        if W_qkv.shape[0] != self.C or W_z.shape[0] != self.hv * D or conv_w.shape[0] != self.C:
+            raise ValueError("weights do not match the head shard")
+        self._ws: Optional[torch.Tensor] = None
+        self._gathers = None
+        self._g_i = 0
+
+    def token_slice(self, tokens: int):
+        """The rows of the layer output this rank computes."""
+        per = (tokens + self.world - 1) // self.world
+        lo = min(self.rank * per, tokens)
+        return lo, min(lo + per, tokens)
+
+    def _workspace(self, B, T, packed, device):
+        need = G.chunked_workspace_bytes(B, T, self.hv, packed)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+        return self._ws
+
+    def projections(self, x):
+        """in_proj_qkv, in_proj_z, in_proj_a, in_proj_b of x (tokens, hidden) bf16."""
+        qkv = x @ self.W_qkv.t()
+        z = x @ self.W_z.t()
+        a = (x @ self.W_a.t()).float()
+        b = (x @ self.W_b.t()).float()
+        return qkv, z, a, b
+
+    def core(self, qkv, z, a, b, cu_seqlens=None, B: int = 1, state_out=None):
+        """conv -> chunked recurrence with the gated norm (and, on several
+        ranks, the head all-gather fused into it).  Returns (tokens, Hv, 128) bf16."""
+        tokens = qkv.shape[0]
+        dev = qkv.device
+        packed = cu_seqlens is not None
+        T = tokens if packed else tokens // B
+        y, _ = G.conv1d_fwd(qkv if packed else qkv.view(B, T, qkv.shape[1]), self.conv_w, cu_seqlens=cu_seqlens)
+        hk, hv, C = self.hk, self.hv, self.C
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        base = y.data_ptr()
+        q = ctypes.c_void_p(base)
+        k = ctypes.c_void_p(base + hk * D * 2)
+        v = ctypes.c_void_p(base + 2 * hk * D * 2)
+        ws = self._workspace(B, T, packed, dev)
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        lib = G.lib()
+        zc = z.contiguous()
+        cu = P(cu_seqlens) if packed else None
+        if self.world == 1:
+            out = torch.empty((tokens, self.Hv, D), dtype=torch.bfloat16, device=dev)
+            G.check(lib.gdn_chunked_norm_fwd_ws(q, k, v, C, C, C, P(a), P(b), P(self.A_log), P(self.dt_bias), None,
+                                                P(state_out) if state_out is not None else None, P(zc), hv * D,
+                                                P(self.gamma), ctypes.c_float(self.eps), P(out), self.Hv * D, 0,
+                                                cu, B, T, hk, hv, D, D, G.F_QK_L2NORM, P(ws), ws.numel(), st))
+            return out
+        if self._gathers is None or self._gathers[0].out.shape[0] != tokens:
+            self._gathers = [gdn_shard.PeerGather(tokens, self.Hv, dev) for _ in range(2)]
+        pg = self._gathers[self._g_i]
+        self._g_i ^= 1
+        pg.run(lib, q, k, v, C, C, C, P(a), P(b), P(self.A_log), P(self.dt_bias), None,
+               P(state_out) if state_out is not None else None, P(zc), hv * D, P(self.gamma), self.eps,
+               self.shard.v0, cu, B, T, hk, hv, G.F_QK_L2NORM, P(ws), ws.numel(), st)
+        pg.wait(lib, st)
+        return pg.out
+
+    def forward_prefill(self, x, cu_seqlens=None, B: int = 1, state_out=None):
+        """The layer on x (tokens, hidden) bf16: returns (y rows of this
+        rank's token slice (rows, hidden) bf16, (lo, hi))."""
+        qkv, z, a, b = self.projections(x)
+        out = self.core(qkv, z, a, b, cu_seqlens, B, state_out)
+        lo, hi = self.token_slice(x.shape[0])
+        y = out[lo:hi].reshape(hi - lo, self.Hv * D) @ self.W_out.t()
+        return y, (lo, hi)
+
+    def gather_errors(self) -> int:
+        return sum(int(pg.err.item()) for pg in self._gathers) if self._gathers else 0
+
+    def close(self):
+        """Release the peer mappings (collective on several ranks)."""
+        if self._gathers:
+            for pg in self._gathers:
+                pg.close()
+            self._gathers = None
+
+
+def shard_weights(full: dict, rank: int, world: int, Hk: int, Hv: int) -> dict:
+    """This rank's rows of a layer's full weights (dict with W_qkv, W_z, W_a,
+    W_b, conv_w, A_log, dt_bias, gamma, W_out): its conv channels, its value
+    heads; gamma and W_out whole."""
+    sh = gdn_shard.head_shard(rank, world, Hk, Hv)
+    idx = torch.tensor(gdn_shard.channel_index(sh, Hk), device=full["W_qkv"].device)
+    vrows = slice(sh.v0 * D, sh.v1 * D)
+    return {"W_qkv": full["W_qkv"][idx].contiguous(), "W_z": full["W_z"][vrows].contiguous(),
+            "W_a": full["W_a"][sh.v0:sh.v1].contiguous(), "W_b": full["W_b"][sh.v0:sh.v1].contiguous(),
+            "conv_w": full["conv_w"][idx].contiguous(), "A_log": full["A_log"][sh.v0:sh.v1].contiguous(),
+            "dt_bias": full["dt_bias"][sh.v0:sh.v1].contiguous(), "gamma": full["gamma"], "W_out": full["W_out"]}
+
+
+def random_weights(hidden: int, Hk: int, Hv: int, device, seed: int = 0) -> dict:
+    """Seeded full weights of one layer with the reference's shapes
+    (cpp/src/model.cpp:157-177): bf16 projections scaled 1/sqrt(fan-in),
+    conv N(0, 0.5), A_log U(0, ln 16), dt_bias U(0, 1), gamma N(1, 0.1)."""
+    import math
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    C = 2 * Hk * D + Hv * D
+
+    def lin(o, i):
+        return (torch.randn((o, i), generator=g, device=device) / math.sqrt(i)).bfloat16()
+    return {"W_qkv": lin(C, hidden), "W_z": lin(Hv * D, hidden), "W_a": lin(Hv, hidden), "W_b": lin(Hv, hidden),
+            "conv_w": (torch.randn((C, 4), generator=g, device=device) * 0.5).bfloat16(),
+            "A_log": torch.rand((Hv,), generator=g, device=device) * math.log(16.0),
+            "dt_bias": torch.rand((Hv,), generator=g, device=device),
+            "gamma": 1 + 0.1 * torch.randn((D,), generator=g, device=device),
+            "W_out": lin(hidden, Hv * D)}
+
+
+def layer_from(weights: dict, Hk: int, Hv: int, rank: int = 0, world: int = 1) -> GDNLayer:
+    w = shard_weights(weights, rank, world, Hk, Hv) if world > 1 else weights
+    return GDNLayer(w["W_qkv"], w["W_z"], w["W_a"], w["W_b"], w["conv_w"], w["A_log"], w["dt_bias"], w["gamma"],
+                    w["W_out"], Hk, Hv, rank, world)
