@@ -408,6 +408,9 @@ def run_ours(args, world, rank, local):
         prefill = run_prefill(args, lib, device, world)
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
+    layer = None
+    if not args.no_prefill and not args.no_layer:
+        layer = run_layer(args, device, world)
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -422,7 +425,7 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
                    "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
-        "sweep_gbs_by_batch": sweep, "pool_decode": pool, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill,
+        "sweep_gbs_by_batch": sweep, "pool_decode": pool, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill, "layer": layer,
     }
     return line
 
@@ -853,6 +856,81 @@ def run_prefill(args, lib, device, world):
     return res
 
 
+HIDDEN = 5120                      # hidden_size (python/qwen35.py:75)
+LAYER_FLOP_PER_TOKEN = 2 * HIDDEN * (2 * HK * D + 2 * HV * D + 2 * HV) + 2 * HV * D * HIDDEN   # in_proj + out_proj
+
+
+def run_layer(args, device, world):
+    """A whole GDN layer (gdn_layer.GDNLayer) on configs 3 and 4: in_proj
+    GEMMs (cuBLAS) -> conv -> chunked recurrence with the norm (and, for N > 1,
+    the head all-gather fused into it) -> out_proj on this rank's token slice
+    (cuBLAS).  tokens/s counts every token once per max-over-ranks second;
+    per-part ms and the GEMMs' TFLOP/s come from CUDA events on each rank."""
+    import gdn_layer
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    w = gdn_layer.random_weights(HIDDEN, HK, HV, device, seed=31)
+    layer = gdn_layer.layer_from(w, HK, HV, rank, world)
+    res = {}
+    cases = [("config3", [args.prefill_T])]
+    if not args.no_config4:
+        cases.append(("config4", config4_lengths()))
+    st = torch.cuda.current_stream(device)
+    for name, lens in cases:
+        tokens = sum(lens)
+        packed = len(set(lens)) > 1
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=device) if packed else None
+        g = torch.Generator(device=device)
+        g.manual_seed(77)
+        x = torch.randn((tokens, HIDDEN), generator=g, device=device).bfloat16()
+        B = len(lens)
+        steps = max(2, args.steps // 10) if name == "config4" else max(3, args.steps // 5)
+        for _ in range(max(args.warmup, 1)):
+            layer.forward_prefill(x, cu_seqlens=cu, B=B)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device) as clk:
+            e0.record(st)
+            for _ in range(steps):
+                y, (lo, hi) = layer.forward_prefill(x, cu_seqlens=cu, B=B)
+            e1.record(st)
+            torch.cuda.synchronize(device)
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+        if max_over_ranks(float(layer.gather_errors()), world, device):
+            raise RuntimeError("layer gather wait timed out")
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(st)
+        qkv, z, a, b = layer.projections(x)
+        ev[1].record(st)
+        out = layer.core(qkv, z, a, b, cu_seqlens=cu, B=B)
+        ev[2].record(st)
+        y = out[lo:hi].reshape(hi - lo, HV * D) @ layer.W_out.t()
+        ev[3].record(st)
+        torch.cuda.synchronize(device)
+        parts = {"in_proj": ev[0].elapsed_time(ev[1]), "gdn_core": ev[1].elapsed_time(ev[2]),
+                 "out_proj": ev[2].elapsed_time(ev[3])}
+        in_flop = 2 * tokens * HIDDEN * (layer.C + layer.hv * D + 2 * layer.hv)
+        out_flop = 2 * (hi - lo) * HV * D * HIDDEN
+        res[name] = {
+            "workload": (f"{name}: {B} seq, {tokens} tokens, hidden {HIDDEN}: in_proj_qkv/z/a/b (cuBLAS bf16) -> "
+                         f"conv -> chunked + gated norm" + (" + NVLink head gather" if world > 1 else "")
+                         + " -> out_proj on the rank's token slice (cuBLAS bf16)"),
+            "tokens_per_s": round(tokens / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+            "part_ms": {k: round(v, 4) for k, v in parts.items()},
+            "gemm_tflops": {"in_proj": round(in_flop / (parts["in_proj"] * 1e-3) / 1e12, 1),
+                            "out_proj": round(out_flop / (parts["out_proj"] * 1e-3) / 1e12, 1)},
+            "flop_per_token_projections": LAYER_FLOP_PER_TOKEN, "clocks": clk.summary(),
+            "note": "the GEMMs hold the GPU at its power cap, so the latency-bound recurrence kernels run at the "
+                    "capped SM clock here (compare prefill.kernel_ms)"}
+        del x, qkv, z, a, b, out, y
+        torch.cuda.empty_cache()
+    layer.close()
+    del layer, w
+    torch.cuda.empty_cache()
+    return res
+
+
 def cpu_prefill_baseline(T=512, seconds=10.0):
     """The reference's prefill CPU path (chunked_delta, numpy oracle with BLAS
     threads) plus conv and gated norm on a bounded sample; tokens/s."""
@@ -964,6 +1042,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true", help="skip the config-2 verify/accept/rollback chain")
     ap.add_argument("--no-pool", action="store_true", help="skip the state-pool / conv-ring decode comparison")
+    ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer prefill (projections included)")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
     ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather"],
@@ -977,7 +1056,7 @@ def main():
     args = ap.parse_args()
     if args.small:
         args.batch, args.layers, args.sweep = 64, 2, ""
-        args.no_e2e = args.no_cpu_baseline = args.no_prefill = args.no_verify = args.no_pool = True
+        args.no_e2e = args.no_cpu_baseline = args.no_prefill = args.no_verify = args.no_pool = args.no_layer = True
     args.warmup = max(args.warmup, 0)
 
     world, rank, local = dist_env()
@@ -996,6 +1075,8 @@ def main():
             device = torch.device("cuda", local)
             torch.cuda.set_device(device)
             line = {"prefill": run_prefill(args, G.lib(), device, world)}
+            if not args.no_layer:
+                line["layer"] = run_layer(args, device, world)
             if rank == 0:
                 print(json.dumps(line), flush=True)
             return 0
