@@ -409,8 +409,10 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0 and not args.no_cpu_baseline:
             prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
     layer = None
-    if not args.no_prefill and not args.no_layer:
-        layer = run_layer(args, device, world)
+    if not args.no_layer:
+        layer = {"decode": run_layer_decode(args, device, world)}
+        if not args.no_prefill:
+            layer.update(run_layer(args, device, world))
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -929,6 +931,63 @@ def run_layer(args, device, world):
     del layer, w
     torch.cuda.empty_cache()
     return res
+
+
+def run_layer_decode(args, device, world, Lp=8):
+    """Decode steps through whole layers (gdn_layer.GDNLayer.forward_decode):
+    B = args.batch sequences per step in seeded random slots of per-layer
+    state pools (2B slots) and conv rings, Lp layers sharing one weight set
+    (232 MB per layer of projection weights, re-read every layer), replayed
+    from a CUDA graph at N = 1 (eager with the NCCL head all-gather at N > 1).
+    tokens/s are for a 48-layer stack: B / (48 x the per-layer time)."""
+    import gdn_layer
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    w = gdn_layer.random_weights(HIDDEN, HK, HV, device, seed=41)
+    layer = gdn_layer.layer_from(w, HK, HV, rank, world)
+    B = args.batch
+    n_slots = 2 * B
+    g = torch.Generator(device=device)
+    g.manual_seed(43)
+    pools = [torch.randn((n_slots, layer.hv, D, D), generator=g, device=device) * 0.05 for _ in range(Lp)]
+    rings = [torch.zeros((n_slots, 3, layer.C), dtype=torch.bfloat16, device=device) for _ in range(Lp)]
+    poss = [torch.zeros(n_slots, dtype=torch.int32, device=device) for _ in range(Lp)]
+    slots = torch.randperm(n_slots, generator=g, device=device)[:B].to(torch.int32)
+    xs = [torch.randn((B, HIDDEN), generator=g, device=device).bfloat16() for _ in range(Lp)]
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def step():
+        for i in range(Lp):
+            layer.forward_decode(xs[i], pools[i], slots, rings[i], poss[i], err_flag=err)
+
+    steps = max(args.steps, 10)
+    if world == 1:
+        ms = time_graph(step, steps, max(args.warmup, 3), device, world) / steps
+    else:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    torch.cuda.synchronize(device)
+    if int(err.item()):
+        raise RuntimeError("decode layer recorded a slot error")
+    per_layer = ms / Lp
+    out = {"workload": f"{Lp} whole layers x B={B} decode (hidden {HIDDEN}; in_proj / out_proj cuBLAS bf16, conv ring, "
+                       f"state pool in random slots of {n_slots}, gated norm"
+                       + (", NCCL head all-gather, token-sliced out_proj" if world > 1 else "") + ")",
+           "ms_per_layer": round(per_layer, 4), "tokens_per_s_48_layers": round(B / (48 * per_layer * 1e-3), 1),
+           "timing": "CUDA graph replay" if world == 1 else "eager"}
+    layer.close()
+    del layer, w, pools, rings, xs
+    torch.cuda.empty_cache()
+    return out
 
 
 def cpu_prefill_baseline(T=512, seconds=10.0):

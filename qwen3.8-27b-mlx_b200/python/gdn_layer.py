@@ -1,6 +1,7 @@
 """One Gated DeltaNet layer around the GDN kernels: the host-side mirror of
 GatedDeltaNet::operator() (cpp/src/model.cpp:582-641; python/qwen35.py:
-575-640) for prefill, on this GPU's K-head shard.
+575-640) for prefill and for a decode step over a serving batch's state pool,
+on this GPU's K-head shard.  Prefill:
 
     qkv = in_proj_qkv(x)            bf16 GEMM (cuBLAS through torch.matmul)
     z   = in_proj_z(x)              bf16 GEMM
@@ -117,6 +118,36 @@ class GDNLayer:
         lo, hi = self.token_slice(x.shape[0])
         y = out[lo:hi].reshape(hi - lo, self.Hv * D) @ self.W_out.t()
         return y, (lo, hi)
+
+    def forward_decode(self, x, pool, slots, ring, ring_pos, err_flag=None):
+        """One decode step of B sequences (x (B, hidden) bf16, one token each)
+        whose states live in slots of a pool (pool (n_slots, hv, 128, 128)
+        fp32, slots (B,) int32) and whose conv windows are rings (ring
+        (n_slots, 3, C_shard) bf16, ring_pos (n_slots,) int32): in_proj ->
+        conv over the ring (+ its one-row append) -> the recurrence on the
+        pool, written back -> gated norm -> out_proj.  On several ranks the
+        normed heads (6144 x 2 bytes per token) are all-gathered by NCCL and
+        each rank projects its token slice.  Returns (y rows, (lo, hi))."""
+        B = x.shape[0]
+        hk, hv = self.hk, self.hv
+        qkv, z, a, b = self.projections(x)
+        qkv3 = qkv.view(B, 1, self.C)
+        y = G.conv1d_fwd_pool(qkv3, self.conv_w, ring, ring_pos, slots, err_flag=err_flag)
+        G.conv_ring_append(qkv3, ring, ring_pos, slots, err_flag=err_flag)
+        # the decode kernel reads (B, T, heads, 128) rows: contiguous copies of the conv output's q | k | v
+        q = y[..., :hk * D].reshape(B, 1, hk, D).contiguous()
+        k = y[..., hk * D:2 * hk * D].reshape(B, 1, hk, D).contiguous()
+        v = y[..., 2 * hk * D:].reshape(B, 1, hv, D).contiguous()
+        o, _ = G.recurrent_fwd_pool(q, k, v, a.view(B, 1, hv), b.view(B, 1, hv), self.A_log, self.dt_bias, pool,
+                                    slots, G.POOL_FINAL, err_flag=err_flag, l2norm=True)
+        normed = G.gated_rmsnorm_fwd(o.view(B * hv, D), z.view(B * hv, D), self.gamma, eps=self.eps).view(B, hv * D)
+        if self.world > 1:
+            import torch.distributed as dist
+            parts = torch.empty((self.world, B, hv * D), dtype=normed.dtype, device=normed.device)
+            dist.all_gather_into_tensor(parts, normed)
+            normed = parts.permute(1, 0, 2).reshape(B, self.Hv * D)
+        lo, hi = self.token_slice(B)
+        return normed[lo:hi] @ self.W_out.t(), (lo, hi)
 
     def gather_errors(self) -> int:
         return sum(int(pg.err.item()) for pg in self._gathers) if self._gathers else 0
