@@ -935,7 +935,7 @@ def run_layer(args, device, world):
 
 def run_layer_decode(args, device, world, Lp=8):
     """Decode steps through whole layers (gdn_layer.GDNLayer.forward_decode):
-    B = args.batch sequences per step in seeded random slots of per-layer
+    B = args.batch x N sequences per step in seeded random slots of per-layer
     state pools (2B slots) and conv rings, Lp layers sharing one weight set
     (232 MB per layer of projection weights, re-read every layer), replayed
     from a CUDA graph at N = 1 (eager with the NCCL head all-gather at N > 1).
@@ -944,7 +944,7 @@ def run_layer_decode(args, device, world, Lp=8):
     rank = torch.distributed.get_rank() if world > 1 else 0
     w = gdn_layer.random_weights(HIDDEN, HK, HV, device, seed=41)
     layer = gdn_layer.layer_from(w, HK, HV, rank, world)
-    B = args.batch
+    B = args.batch * world                  # per-GPU work fixed: each rank runs every sequence on 1/N of the heads
     n_slots = 2 * B
     g = torch.Generator(device=device)
     g.manual_seed(43)
