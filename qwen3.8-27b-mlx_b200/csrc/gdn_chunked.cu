@@ -44,7 +44,7 @@
 namespace gdn {
 
 #ifdef GDN_CHUNK_TIMING
-__device__ long long g_chunk_timing[32];   // [0,13) fused, [16,24) prep, [24,29) scan
+__device__ long long g_chunk_timing[32];   // [0,13) fused, [16,24) and 30 prep, [24,29) scan
 #define GDN_TICK(slot)                                                          \
   do {                                                                          \
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {               \
@@ -1067,6 +1067,7 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
     if (j == 0) {                              // the Q rows are overwritten by A: Q-tilde for all heads now
       for (int jj = 0; jj < hpc; ++jj) prep_qtilde(c, sc0 + jj * 10 * kC + 128, record(p, slot, h0 + jj) + kRecQ);
       __syncthreads();
+      GDN_TICK(30);
     }
     phase_epi_a(c, kPColGP, rec + kRecM, nullptr);     // A over the rows; M to the record
     GDN_TICK(19);
