@@ -135,5 +135,41 @@ inline Result run_gated(const DeviceArray& q, const DeviceArray& k, const Device
   return r;
 }
 
+// The states of a serving batch in slots of a pool (gdn_recurrent_fwd_pool):
+// the layout of DeltaCache::state across a batch (cpp/src/model.hpp:211-227),
+// where admitting or retiring a sequence only rewrites the slot indices.
+class StatePool {
+ public:
+  StatePool(int n_slots, int Hv, int D = 128)
+      : pool_({n_slots, Hv, D, D}, DType::F32), n_slots_(n_slots), Hv_(Hv) {}
+  DeviceArray& states() { return pool_; }
+  int n_slots() const { return n_slots_; }
+
+  // One decode / verify step of the sequences in `slots` (B int32 on the
+  // device): the north-star inputs of run_gated; the new states are written
+  // back to the slots (GDN_POOL_FINAL), or left alone with per-position
+  // checkpoints returned (record mode, GDN_POOL_KEEP).
+  Result step(const DeviceArray& q, const DeviceArray& k, const DeviceArray& v, const DeviceArray& a,
+              const DeviceArray& b, const DeviceArray& A_log, const DeviceArray& dt_bias, const DeviceArray& slots,
+              bool record = false, bool l2norm = false, cudaStream_t stream = nullptr) {
+    const int B = static_cast<int>(q.shape(0)), L = static_cast<int>(q.shape(1)), Hk = static_cast<int>(q.shape(2)),
+              Dk = static_cast<int>(q.shape(3)), Hv = static_cast<int>(v.shape(2)), Dv = static_cast<int>(v.shape(3));
+    if (Hv != Hv_) throw std::runtime_error("gdn: value heads do not match the pool");
+    unsigned flags = (q.dtype() == DType::F32 ? GDN_F_QKV_F32 : 0u) | (l2norm ? GDN_F_QK_L2NORM : 0u);
+    Result r{DeviceArray({B, L, Hv, Dv}, DType::F32), {}, {}};
+    if (record) r.states = DeviceArray({B, Hv, L, Dv, Dk}, DType::F32);
+    check_gdn(gdn_recurrent_fwd_pool(q.data(), k.data(), v.data(), a.as<float>(), b.as<float>(), A_log.as<float>(),
+                                     dt_bias.as<float>(), pool_.as<float>(), slots.as<int32_t>(), n_slots_, nullptr,
+                                     nullptr, 0, record ? GDN_POOL_KEEP : GDN_POOL_FINAL, r.o.data(),
+                                     record ? r.states.as<float>() : nullptr, nullptr, B, L, Hk, Hv, Dk, Dv, flags,
+                                     stream));
+    return r;
+  }
+
+ private:
+  DeviceArray pool_;
+  int n_slots_, Hv_;
+};
+
 }  // namespace delta
 }  // namespace gdn

@@ -5,6 +5,7 @@
 // s_out and every collected state (the reference's bound is 2e-5).
 // Built and run by tests/test_gpu_cpp.py; prints one "[ok]"/"[FAIL]" line
 // per check and exits non-zero on any failure.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <random>
@@ -88,6 +89,47 @@ int main() {
     std::snprintf(buf, sizeof(buf), "B=%d L=%3d H=%2d  out %.2e  state %.2e  collect (%d states) %.2e", c.B, c.L,
                   c.H, eo, es, c.L, ec);
     check(eo < 1e-5f && es < 1e-5f && ec < 1e-5f, buf);
+  }
+  // a state pool: one step of 3 sequences in slots {5, 0, 3} of 7 equals the dense step on those
+  // states, bit for bit, and leaves the other slots untouched
+  {
+    using gdn::DeviceArray;
+    using gdn::DType;
+    const int B = 3, L = 1, Hk = 16, Hv = 48, n_slots = 7;
+    const int slot_of[B] = {5, 0, 3};
+    const size_t per = size_t(Hv) * D * D;
+    std::vector<float> q(size_t(B) * L * Hk * D), k(q.size()), v(size_t(B) * L * Hv * D), a(size_t(B) * L * Hv),
+        b(a.size()), A_log(Hv), dt(Hv), pool(per * n_slots), dense(per * B);
+    for (auto& x : q) x = N01(rng);
+    for (auto& x : k) x = N01(rng);
+    for (auto& x : v) x = N01(rng);
+    for (auto& x : a) x = N01(rng);
+    for (auto& x : b) x = N01(rng);
+    for (auto& x : A_log) x = 2.7f * Ubt(rng);
+    for (auto& x : dt) x = Ubt(rng);
+    for (auto& x : pool) x = 0.05f * N01(rng);
+    for (int i = 0; i < B; ++i)
+      std::copy(pool.begin() + per * slot_of[i], pool.begin() + per * (slot_of[i] + 1), dense.begin() + per * i);
+    DeviceArray dq({B, L, Hk, D}, DType::F32), dk({B, L, Hk, D}, DType::F32), dv({B, L, Hv, D}, DType::F32),
+        da({B, L, Hv}, DType::F32), db({B, L, Hv}, DType::F32), dA({Hv}, DType::F32), ddt({Hv}, DType::F32),
+        dS({B, Hv, D, D}, DType::F32), dslots({B}, DType::I32);
+    dq.upload(q.data()); dk.upload(k.data()); dv.upload(v.data()); da.upload(a.data()); db.upload(b.data());
+    dA.upload(A_log.data()); ddt.upload(dt.data()); dS.upload(dense.data()); dslots.upload(slot_of);
+    gdn::delta::StatePool sp(n_slots, Hv);
+    sp.states().upload(pool.data());
+    gdn::delta::Result want = gdn::delta::run_gated(dq, dk, dv, da, db, dA, ddt, &dS, false, true);
+    gdn::delta::Result got = sp.step(dq, dk, dv, da, db, dA, ddt, dslots, false, true);
+    std::vector<float> o1(size_t(B) * L * Hv * D), o2(o1.size()), S1(per * B), P2(pool.size());
+    want.o.download(o1.data());
+    want.s_out.download(S1.data());
+    got.o.download(o2.data());
+    sp.states().download(P2.data());
+    bool same = o1 == o2;
+    for (int i = 0; i < B; ++i)
+      same = same && std::equal(S1.begin() + per * i, S1.begin() + per * (i + 1), P2.begin() + per * slot_of[i]);
+    for (int s2 : {1, 2, 4, 6})
+      same = same && std::equal(pool.begin() + per * s2, pool.begin() + per * (s2 + 1), P2.begin() + per * s2);
+    check(same, "state pool step == dense step on the slots (bit for bit), other slots untouched");
   }
   // a rejected call throws with the library's message, like the reference's MLX errors
   bool threw = false;
