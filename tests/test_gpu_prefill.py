@@ -471,3 +471,52 @@ def test_chunked_head_ratios(Hk, Hv, split):
     ro, rS = oracle_chunked(inp)
     assert O.rel_l2(host(o), ro) < PREFILL_TOL
     assert O.rel_l2(host(S), rS) < PREFILL_TOL
+
+
+@pytest.mark.parametrize("lens", [[300, 300], [100, 0, 257, 64, 3, 1, 640]])
+def test_chunked_norm_in_windows_matches_one_pass(lens):
+    """gdn_chunked_norm_fwd_ws with a workspace of w = 1, 2, 3 chunks per
+    sequence (the norm warps take the window's chunk offsets for z and the
+    output rows): the normed output and the final state bit-identical to one
+    pass."""
+    import ctypes
+    rng = np.random.default_rng(90 + len(lens))
+    Hk, Hv = 2, 6
+    total = sum(lens)
+    packed = len(set(lens)) > 1
+    inp = chunk_inputs(rng, 1, total, Hk, Hv)
+    z, gamma = norm_inputs(rng, (total, Hv, 128))
+    S0 = dev(rng.standard_normal((len(lens), Hv, 128, 128), dtype=np.float32) * np.float32(0.05))
+    if packed:
+        cu = dev(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), torch.int32)
+        B, T = len(lens), total
+        t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0])  # noqa: E731
+        zz = dev(z, torch.bfloat16)
+    else:
+        cu = None
+        B, T = len(lens), lens[0]
+        t = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]), torch.bfloat16)  # noqa: E731
+        g = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]))  # noqa: E731
+        zz = dev(z.reshape(B, T, Hv, 128), torch.bfloat16)
+    q, k, v, a, b = t("q"), t("k"), t("v"), g("a"), g("b")
+    A_log, dtb, gam = dev(inp["A_log"]), dev(inp["dt_bias"]), dev(gamma)
+    out_ref, S_ref = G.chunked_norm_fwd(q, k, v, a, b, A_log, dtb, zz, gam, state_in=S0, cu_seqlens=cu)
+    L = G.lib()
+    rec = L.gdn_chunked_workspace_bytes(1, 64, 1, 0) - L.gdn_chunked_workspace_bytes(1, 0, 1, 0)
+    base = G.chunked_workspace_min_bytes(B, Hv, True)
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    for w in (1, 2, 3):
+        size = base + (w - 1) * B * Hv * rec
+        ws = torch.empty(size, dtype=torch.uint8, device="cuda")
+        out = torch.empty_like(out_ref)
+        S = torch.empty_like(S_ref)
+        rc = L.gdn_chunked_norm_fwd_ws(P(q), P(k), P(v), q.stride(-3), k.stride(-3), v.stride(-3), P(a), P(b),
+                                       P(A_log), P(dtb), P(S0), P(S), P(zz), Hv * 128, P(gam), ctypes.c_float(1e-6),
+                                       P(out), Hv * 128, 0, P(cu), B, T, Hk, Hv, 128, 128, G.F_QK_L2NORM, P(ws),
+                                       ctypes.c_size_t(size), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == G.GDN_OK, L.gdn_last_error().decode()
+        torch.cuda.synchronize()
+        assert torch.equal(out, out_ref), w
+        assert torch.equal(S, S_ref), w
+    assert G.take_device_error() == 0
