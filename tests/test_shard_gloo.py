@@ -98,3 +98,33 @@ def test_sharded_layer_equals_unsharded(world):
     assert np.array_equal(out, ref)
     assert np.array_equal(states, cache.state)
     assert tmax == float(world)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_layer_weight_shards_and_token_slices(world):
+    """gdn_layer's host logic on CPU tensors: the ranks' weight rows put back
+    together are the full weights (conv channels in [q | k | v] order, value
+    heads in order), W_out and gamma are whole on every rank, and the token
+    slices of out_proj cover every token exactly once."""
+    import gdn_layer
+    Hk, Hv, hidden = 16, 48, 64
+    w = gdn_layer.random_weights(hidden, Hk, Hv, torch.device("cpu"), seed=3)
+    parts = [gdn_layer.shard_weights(w, r, world, Hk, Hv) for r in range(world)]
+    idx = [S.channel_index(S.head_shard(r, world, Hk, Hv), Hk) for r in range(world)]
+    qkv = torch.empty_like(w["W_qkv"])
+    conv = torch.empty_like(w["conv_w"])
+    for p, ix in zip(parts, idx):
+        qkv[ix] = p["W_qkv"]
+        conv[ix] = p["conv_w"]
+    assert torch.equal(qkv, w["W_qkv"]) and torch.equal(conv, w["conv_w"])
+    for name in ("W_z", "W_a", "W_b", "A_log", "dt_bias"):
+        assert torch.equal(torch.cat([p[name] for p in parts]), w[name]), name
+    assert all(torch.equal(p["W_out"], w["W_out"]) and torch.equal(p["gamma"], w["gamma"]) for p in parts)
+    for tokens in (0, 1, 7, 4096, 427463):
+        layers = [gdn_layer.GDNLayer(p["W_qkv"], p["W_z"], p["W_a"], p["W_b"], p["conv_w"], p["A_log"], p["dt_bias"],
+                                     p["gamma"], p["W_out"], Hk, Hv, r, world) for r, p in enumerate(parts)]
+        cover = []
+        for L in layers:
+            lo, hi = L.token_slice(tokens)
+            cover.extend(range(lo, hi))
+        assert cover == list(range(tokens)), tokens
