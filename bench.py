@@ -171,9 +171,11 @@ class DecodeLayers:
         return 2 * (B or self.B) * self.hv * STATE_BYTES * self.L
 
 
-def launch_layer(lib, X, layer, B, stream_handle, q=None, k=None, v=None, a=None, b=None, o=None):
+def launch_layer(lib, X, layer, B, stream_handle, q=None, k=None, v=None, a=None, b=None, o=None, overlap=False):
     """One gdn_recurrent_fwd launch over the first B sequences of one layer
-    (in-place state update, bf16 output)."""
+    (in-place state update, bf16 output); overlap: GDN_F_OVERLAP_PREV -- the
+    previous kernel in the stream is another layer's, so this launch may
+    overlap its tail."""
     import gdn_b200 as G
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     S = X.S[layer]
@@ -181,7 +183,8 @@ def launch_layer(lib, X, layer, B, stream_handle, q=None, k=None, v=None, a=None
                                P(v if v is not None else X.v[layer]), P(a if a is not None else X.a[layer]),
                                P(b if b is not None else X.b[layer]), P(X.A_log[layer]), P(X.dt_bias[layer]),
                                P(S), P(S), P(o if o is not None else X.o[layer]), None,
-                               B, 1, X.hk, X.hv, D, D, G.F_O_BF16, stream_handle)
+                               B, 1, X.hk, X.hv, D, D, G.F_O_BF16 | (G.F_OVERLAP_PREV if overlap else 0),
+                               stream_handle)
     if rc != 0:
         raise RuntimeError(f"gdn_recurrent_fwd failed: {rc} {lib.gdn_last_error().decode()}")
 
@@ -317,7 +320,7 @@ def run_ours(args, world, rank, local):
         st = torch.cuda.current_stream(device)
         h = ctypes.c_void_p(st.cuda_stream)
         for layer in range(L):
-            launch_layer(lib, X, layer, Bsub, h)
+            launch_layer(lib, X, layer, Bsub, h, overlap=True)   # consecutive launches are different layers
             if world > 1:
                 comm.wait_stream(st)
                 with torch.cuda.stream(comm):

@@ -53,6 +53,14 @@ extern "C" {
 #define GDN_F_GATES_DIRECT  0x4u  /* a holds alpha and b holds beta; A_log, dt_bias unused */
 #define GDN_F_QK_L2NORM     0x8u  /* l2-normalise q, k per head (eps 1e-6 inside the
                                      rsqrt) and scale q by Dk^-1/2 inside the kernel */
+#define GDN_F_OVERLAP_PREV  0x10u /* gdn_recurrent_fwd only: launch as a programmatic
+                                     dependent of the previous kernel in the stream, so
+                                     the launch and the state loads overlap its tail;
+                                     every other input is read after it has completed.
+                                     The caller guarantees that the previous kernel does
+                                     not write this call's state_in (e.g. consecutive
+                                     layers of a decode step).  Pays off at small batch
+                                     (launch-latency bound), neutral at large batch. */
 
 /* ---- flags of the front-end / back-end kernels --------------------------- */
 #define GDN_F_CONV_BF16_OPS 0x100u  /* conv: MLX's per-op bf16 arithmetic (each product and

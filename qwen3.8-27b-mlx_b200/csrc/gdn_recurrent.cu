@@ -134,6 +134,9 @@ __global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
   const int h = bh - b * p.Hv;
   const int kh = h / (p.Hv / p.Hk);
   const int col = lane * 4;
+  // the next kernel in the stream may begin launching (a programmatic
+  // dependent waits for this grid's completion before reading its inputs)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // Start state of this (sequence, head): the dense state, or its pool slot.
   size_t sidx = static_cast<size_t>(bh);
@@ -169,6 +172,10 @@ __global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
       for (int r = 0; r < R; ++r) st_stream4(pool_row + static_cast<size_t>(r) * kD, s[r]);
     }
   }
+  // launched with GDN_F_OVERLAP_PREV: the state rows above are in flight while
+  // the previous grid finishes; the token inputs are read only after it has
+  // completed (a no-op for an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const bool direct = (p.flags & GDN_F_GATES_DIRECT) != 0;
   const bool l2 = (p.flags & GDN_F_QK_L2NORM) != 0;
@@ -247,18 +254,36 @@ __global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
 }
 
 
+template <bool BF16, int R, int PM>
+cudaError_t launch_one(const RecParams& p, unsigned grid, cudaStream_t st) {
+  if (!(p.flags & GDN_F_OVERLAP_PREV)) {
+    recurrent_kernel<BF16, R, PM><<<grid, 128, 0, st>>>(p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, recurrent_kernel<BF16, R, PM>, p);
+}
+
 template <bool BF16, int PM>
 cudaError_t launch_rows(const RecParams& p, int R, cudaStream_t st) {
   const long long bh = static_cast<long long>(p.B) * p.Hv;
   R = (R == 1 || R == 2 || R == 8) ? R : 4;
   const unsigned grid = static_cast<unsigned>(bh * (kD / (4 * R)));
   switch (R) {
-    case 1: recurrent_kernel<BF16, 1, PM><<<grid, 128, 0, st>>>(p); break;
-    case 2: recurrent_kernel<BF16, 2, PM><<<grid, 128, 0, st>>>(p); break;
-    case 8: recurrent_kernel<BF16, 8, PM><<<grid, 128, 0, st>>>(p); break;
-    default: recurrent_kernel<BF16, 4, PM><<<grid, 128, 0, st>>>(p); break;
+    case 1: return launch_one<BF16, 1, PM>(p, grid, st);
+    case 2: return launch_one<BF16, 2, PM>(p, grid, st);
+    case 8: return launch_one<BF16, 8, PM>(p, grid, st);
+    default: return launch_one<BF16, 4, PM>(p, grid, st);
   }
-  return cudaGetLastError();
 }
 
 template <int PM>
@@ -298,7 +323,7 @@ int run_recurrent(const RecParams& p, void* stream) {
   return cuda_status(e, "gdn recurrent kernel launch");
 }
 
-constexpr unsigned kKnownFlags = GDN_F_QKV_F32 | GDN_F_O_BF16 | GDN_F_GATES_DIRECT | GDN_F_QK_L2NORM;
+constexpr unsigned kKnownFlags = GDN_F_QKV_F32 | GDN_F_O_BF16 | GDN_F_GATES_DIRECT | GDN_F_QK_L2NORM | GDN_F_OVERLAP_PREV;
 
 // Checks shared by both recurrent entry points.
 int check_common(const void* q, const void* k, const void* v, const float* a, const float* b,
@@ -370,6 +395,8 @@ extern "C" int gdn_recurrent_fwd_from_ckpt(const void* q, const void* k, const v
   int rc = check_common(q, k, v, a, b, A_log, dt_bias, o, B, T, Hk, Hv, Dk, Dv, flags);
   if (rc != GDN_OK) return rc;
   if (B == 0) return GDN_OK;
+  if (flags & GDN_F_OVERLAP_PREV)
+    return fail(GDN_ERR_FLAGS, "GDN_F_OVERLAP_PREV: commit_n may come from the previous kernel");
   if (!ckpt_src || !commit_n) return fail(GDN_ERR_NULL, "ckpt_src and commit_n are required");
   if (Tsrc <= 0) return fail(GDN_ERR_SHAPE, "Tsrc=%d must be positive", Tsrc);
   if (!state_out && !ckpt) return fail(GDN_ERR_NULL, "state_out and ckpt are both NULL");
@@ -398,6 +425,8 @@ extern "C" int gdn_recurrent_fwd_pool(const void* q, const void* k, const void* 
   int rc = check_common(q, k, v, a, b, A_log, dt_bias, o, B, T, Hk, Hv, Dk, Dv, flags);
   if (rc != GDN_OK) return rc;
   if (B == 0) return GDN_OK;
+  if (flags & GDN_F_OVERLAP_PREV)
+    return fail(GDN_ERR_FLAGS, "GDN_F_OVERLAP_PREV: slots and commit_n may come from the previous kernel");
   if (!pool || !slots) return fail(GDN_ERR_NULL, "pool and slots are required");
   if (n_slots <= 0 || static_cast<long long>(n_slots) * Hv * kD >= (1LL << 31))
     return fail(GDN_ERR_SHAPE, "n_slots=%d out of range", n_slots);

@@ -32,6 +32,7 @@ F_QKV_F32 = 0x1
 F_O_BF16 = 0x2
 F_GATES_DIRECT = 0x4
 F_QK_L2NORM = 0x8
+F_OVERLAP_PREV = 0x10
 F_CONV_BF16_OPS = 0x100
 F_CONV_NO_SILU = 0x200
 F_NORM_IN_BF16 = 0x400
@@ -145,7 +146,7 @@ def _dev(*ts):
 
 def recurrent_fwd(q, k, v, a, b, A_log=None, dt_bias=None, state_in=None, state_out=None,
                   o=None, ckpt=None, *, gates_direct=False, l2norm=False,
-                  o_dtype=torch.float32):
+                  o_dtype=torch.float32, overlap_prev=False):
     """One decode / verify step through ``gdn_recurrent_fwd``.
 
     q, k (B,T,Hk,128) and v (B,T,Hv,128), all bf16 or all fp32; a, b (B,T,Hv)
@@ -167,6 +168,8 @@ def recurrent_fwd(q, k, v, a, b, A_log=None, dt_bias=None, state_in=None, state_
         flags |= F_QK_L2NORM
     if o_dtype == torch.bfloat16:
         flags |= F_O_BF16
+    if overlap_prev:
+        flags |= F_OVERLAP_PREV
     dev = _dev(q, k, v, a, b, A_log, dt_bias, state_in, state_out, o, ckpt)
     if o is None:
         o = torch.empty((B, T, Hv, v.shape[-1]), dtype=o_dtype, device=dev)

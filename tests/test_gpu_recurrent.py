@@ -222,3 +222,32 @@ def test_bulk_copy_path_rollback_in_place_and_zero_state():
 
 def test_no_device_errors_recorded():
     assert G.take_device_error() == 0
+
+
+def test_overlap_prev_flag_gives_the_same_bits_and_is_refused_elsewhere():
+    """GDN_F_OVERLAP_PREV (launch as a programmatic dependent of the previous
+    kernel) over a chain of three layers with their own states: the same o
+    and states as ordinary launches; the from-checkpoint and pool entries,
+    whose commit_n / slots may come from the previous kernel, refuse it."""
+    rng = np.random.default_rng(44)
+    B = 5
+    layers = [O.synth_decode_inputs(rng, B, 1) for _ in range(3)]
+    res = {}
+    for ov in (False, True):
+        outs = []
+        for inp in layers:
+            o, S, _ = G.recurrent_fwd(*device_inputs(inp), state_in=dev(inp["S0"]), overlap_prev=ov)
+            outs.append((o, S))
+        torch.cuda.synchronize()
+        res[ov] = outs
+    for (o1, S1), (o2, S2) in zip(res[False], res[True]):
+        assert torch.equal(o1, o2) and torch.equal(S1, S2)
+    inp = layers[0]
+    ck = torch.zeros((B, 48, 1, 128, 128), device="cuda")
+    n = torch.zeros(B, dtype=torch.int32, device="cuda")
+    with pytest.raises(G.GdnError) as e:
+        G.check(G.lib().gdn_recurrent_fwd_from_ckpt(*[G.ptr(t) for t in device_inputs(inp)], G.ptr(dev(inp["S0"])),
+                                                    G.ptr(ck), G.ptr(n), 1, G.ptr(dev(inp["S0"])),
+                                                    G.ptr(torch.empty((B, 1, 48, 128), device="cuda")), None, None,
+                                                    B, 1, 16, 48, 128, 128, G.F_OVERLAP_PREV, None))
+    assert e.value.code == G.GDN_ERR_FLAGS
