@@ -387,9 +387,22 @@ def run_ours(args, world, rank, local):
             sweep[str(Bs)] = round(X.state_bytes(Bs) / (msb / max(args.steps, 20) * 1e-3) / 1e9, 1)
 
     # --- the same decode over a serving-batch state pool (scattered slots) and the conv ring
+    def guarded(name, fn):
+        """An optional section: its exception becomes an "error" entry of the
+        line (and a traceback on stderr) instead of costing the headline.  Its
+        failures are the same on every rank (the collective checks raise on all
+        ranks together), so the ranks stay in step."""
+        try:
+            return fn()
+        except Exception as e:  # noqa: BLE001
+            import traceback
+            traceback.print_exc(file=sys.stderr)
+            torch.cuda.empty_cache()
+            return {"error": f"{name}: {type(e).__name__}: {e}"}
+
     pool = None
     if world == 1 and not args.no_pool:
-        pool = run_pool_decode(args, lib, X, Bg, device)
+        pool = guarded("pool_decode", lambda: run_pool_decode(args, lib, X, Bg, device))
 
     # --- end to end through the C ABI with host buffers (pipelined per layer)
     e2e = None
@@ -402,20 +415,20 @@ def run_ours(args, world, rank, local):
 
     verify = None
     if not args.no_verify:
-        verify = run_verify_chain(args, lib, device, world, hk, hv, hbm_peak)
+        verify = guarded("verify_chain", lambda: run_verify_chain(args, lib, device, world, hk, hv, hbm_peak))
 
     prefill = None
     if not args.no_prefill:
         del X
         torch.cuda.empty_cache()
-        prefill = run_prefill(args, lib, device, world)
-        if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        prefill = guarded("prefill", lambda: run_prefill(args, lib, device, world))
+        if world == 1 and rank == 0 and not args.no_cpu_baseline and "config3" in prefill:
             prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
     layer = None
     if not args.no_layer:
-        layer = {"decode": run_layer_decode(args, device, world)}
+        layer = {"decode": guarded("layer.decode", lambda: run_layer_decode(args, device, world))}
         if not args.no_prefill:
-            layer.update(run_layer(args, device, world))
+            layer.update(guarded("layer", lambda: run_layer(args, device, world)))
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
