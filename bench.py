@@ -441,7 +441,9 @@ def run_ours(args, world, rank, local):
                    "parallelism": "single" if world == 1 else f"kheads{world}+allgather",
                    "heads_per_gpu": {"k": hk, "v": hv},
                    "l2": f"inputs larger than L2 (state {bytes_step_rank / 2 / 1e9:.1f} GB per GPU)",
-                   "timing": "CUDA graph replay of the 48 launches" if world == 1 else "eager + NCCL all-gather"},
+                   "timing": ("CUDA graph replay of the 48 launches, each a programmatic dependent of the previous "
+                              "layer's (GDN_F_OVERLAP_PREV)") if world == 1 else
+                             "eager + NCCL all-gather, launches with GDN_F_OVERLAP_PREV"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
         "sweep_gbs_by_batch": sweep, "pool_decode": pool, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill, "layer": layer,
     }
