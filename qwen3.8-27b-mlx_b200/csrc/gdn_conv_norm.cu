@@ -23,7 +23,8 @@ constexpr int kConvK = 4;            // linear_conv_kernel_dim (python/qwen35.py
 constexpr int kConvVec = 8;          // channels per thread (one 16-byte bf16 vector)
 constexpr int kConvThreads = 128;
 constexpr int kConvRun = 64;         // tokens per thread
-constexpr int kConvBatch = 8;        // rows loaded ahead of use (bytes in flight per thread)
+constexpr int kConvBatch = 4;        // rows per cp.async group
+constexpr int kConvStages = 4;       // groups per thread in the shared-memory ring (stages x batch = 16 rows, 256 bytes)
 constexpr int kConvShortT = 16;      // uniform batches of at most this many tokens per sequence: one thread per token
 
 struct alignas(16) Bf16x8 {
@@ -191,9 +192,10 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_tok_kernel(const ConvPara
 
 // One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
 // the 3-row causal window in registers, so every x element is read once
-// (plus a 3-row halo at the start of the run); rows stream in 8 at a time
-// through a cp.async double buffer (32 KiB per block, 80 registers, six
-// blocks per SM), so the next 8 rows are in flight while these are computed.
+// (plus a 3-row halo at the start of the run); rows stream in through a
+// per-thread ring of cp.async groups in shared memory (4 groups of 4 rows,
+// 32 KiB per block, 80 registers, six blocks per SM), so 12 rows are in
+// flight while 4 are computed.
 template <bool BF16_OPS>
 __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParams p) {
   const long long t_begin = static_cast<long long>(blockIdx.y) * kConvRun;
@@ -243,26 +245,28 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
   };
   load_window(t_begin);
 
-  // x rows of a batch go through a per-thread double buffer in shared memory
-  // by cp.async: batch k + 1 streams in while batch k is computed, and the
-  // rows hold no registers while in flight.  Each thread reads only its own
-  // slots, so no barrier is needed.
-  __shared__ Bf16x8 stage[2][kConvBatch][kConvThreads];
+  // x rows go through a per-thread ring of kConvStages groups in shared
+  // memory by cp.async: batches k + 1 .. k + kConvStages - 1 stream in while
+  // batch k is computed, and the rows hold no registers while in flight.
+  // Each thread reads only its own slots, so no barrier is needed.
+  __shared__ Bf16x8 stage[kConvStages][kConvBatch][kConvThreads];
   auto issue = [&](long long tb, int sbuf) {
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u)
       if (tb + u < t_end) ptx::cp_async16(&stage[sbuf][u][threadIdx.x], p.x + (tb + u) * p.C + c0);
     ptx::cp_async_commit();
   };
-  issue(t_begin, 0);
+#pragma unroll
+  for (int g = 0; g < kConvStages - 1; ++g) {            // one commit group per stage, empty past the run
+    if (t_begin + g * kConvBatch < t_end) issue(t_begin + g * kConvBatch, g);
+    else ptx::cp_async_commit();
+  }
   int sbuf = 0;
-  for (long long tb = t_begin; tb < t_end; tb += kConvBatch, sbuf ^= 1) {
-    if (tb + kConvBatch < t_end) {
-      issue(tb + kConvBatch, sbuf ^ 1);
-      ptx::cp_async_wait<1>();
-    } else {
-      ptx::cp_async_wait<0>();
-    }
+  for (long long tb = t_begin; tb < t_end; tb += kConvBatch, sbuf = (sbuf + 1) % kConvStages) {
+    const long long nxt = tb + (kConvStages - 1) * kConvBatch;  // into the stage read in the previous batch
+    if (nxt < t_end) issue(nxt, (sbuf + kConvStages - 1) % kConvStages);
+    else ptx::cp_async_commit();
+    ptx::cp_async_wait<kConvStages - 1>();                // this batch's group has landed
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u) {
       const long long t = tb + u;
