@@ -292,19 +292,19 @@ cudaError_t launch_mode(const RecParams& p, bool bf16, int R, cudaStream_t st) {
 }
 
 // Rows per warp.  Bytes in flight per SM set the achieved HBM bandwidth:
-// with R rows a warp has R x 512 B of loads outstanding, so the largest R
-// that still fills the GPU with about one full wave of blocks wins.  Measured
-// on B200, one layer at B = 256 (in-place update, bf16 q/k/v/o): R = 1, 2, 4,
-// 8 -> 2.5, 4.2, 5.5, 6.2 TB/s.  Small batches fall back to fewer rows so that
-// every SM still gets warps.
+// with R rows a warp has R x 512 B of loads outstanding.  Measured on B200,
+// one layer at B = 256 (in-place update, bf16 q/k/v/o): R = 1, 2, 4, 8 ->
+// 2.5, 4.2, 5.5, 6.2 TB/s.  Small batches take fewer rows only down to about
+// 2.5 blocks per SM: a 48-layer step at B = 1, 2, 3 took 150, 204, 239 us this
+// way against 202, 220, 267 us when a full wave of blocks was kept.
 int rows_per_warp(long long bh) {
 #ifdef GDN_REC_ROWS
   (void)bh;
   return GDN_REC_ROWS;
 #else
-  const long long one_wave = 148LL * 8;        // SMs x resident 128-thread blocks
+  const long long min_blocks = 148LL * 5 / 2;   // at B = 1 (48 heads): R = 4, 384 blocks
   for (int R = 8; R > 1; R >>= 1)
-    if (bh * (kD / (4 * R)) >= one_wave) return R;
+    if (bh * (kD / (4 * R)) >= min_blocks) return R;
   return 1;
 #endif
 }
