@@ -61,6 +61,31 @@ def test_spec_verify_matches_oracle(B, k, V):
             assert near_cdf_step(p[b], q[b], j, k, float(us[b])) and abs(int(tok[b]) - v) <= 1, (b, tok[b], v)
 
 
+@pytest.mark.parametrize("V", [65536 + 333, 151936])
+def test_cluster_path_ragged_and_empty_residual(V):
+    """Vocabularies of 64K entries and more take the 8-CTA cluster kernel.
+    V = 65869 leaves the last CTA of the cluster 2 of 65 blocks.  Half the
+    sequences have p = 0.5 q on the rejected row (an empty residual, so the
+    cluster re-sums p itself); every draft there is rejected by u > 0.5."""
+    B, k = 6, 2
+    rng = np.random.default_rng(V)
+    p, q, draft, ua, us = spec_case(rng, B, k, V)
+    for b in range(0, B, 2):
+        p[b, 0] = 0.5 * q[b, 0]
+        ua[b, 0] = 0.75
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    acc, commit, tok = G.spec_verify(dev(p), dev(q), dev(draft, torch.int32), dev(ua), dev(us), err_flag=err)
+    acc, commit, tok = acc.cpu().numpy(), commit.cpu().numpy(), tok.cpu().numpy()
+    assert int(err.item()) == 0
+    for b in range(B):
+        j, n, v = O.spec_verify(p[b], q[b], draft[b], ua[b], us[b])
+        if b % 2 == 0:
+            assert j == 0
+        assert (acc[b], commit[b]) == (j, n), b
+        if tok[b] != v:
+            assert near_cdf_step(p[b], q[b], j, k, float(us[b])) and abs(int(tok[b]) - v) <= 1, (b, tok[b], v)
+
+
 def test_out_of_range_draft_is_rejected_and_flagged():
     rng = np.random.default_rng(3)
     p, q, draft, ua, us = spec_case(rng, 4, 3, 50)
