@@ -106,3 +106,64 @@ def test_gates_direct_needs_no_gate_parameters():
 def test_valid_call_without_gpu_reports_cuda_error_not_a_cpu_fallback():
     assert rec() == G.GDN_ERR_CUDA
     assert "gdn recurrent kernel launch" in G.lib().gdn_last_error().decode()
+
+
+def spec(**kw):
+    args = dict(p=FAKE, q=FAKE + (1 << 32), draft=FAKE + (2 << 32), u_accept=FAKE + (3 << 32),
+                u_sample=FAKE + (4 << 32), B=2, k=3, V=1000, accept_len=FAKE + (5 << 32),
+                commit_n=FAKE + (6 << 32), token=FAKE + (7 << 32), err=FAKE + (8 << 32))
+    args.update(kw)
+    p = lambda x: None if x is None else ctypes.c_void_p(x)  # noqa: E731
+    return G.lib().gdn_spec_verify(p(args["p"]), p(args["q"]), p(args["draft"]), p(args["u_accept"]),
+                                   p(args["u_sample"]), args["B"], args["k"], args["V"], p(args["accept_len"]),
+                                   p(args["commit_n"]), p(args["token"]), p(args["err"]), None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(k=0), G.GDN_ERR_SHAPE),
+    (dict(k=33), G.GDN_ERR_SHAPE),
+    (dict(V=0), G.GDN_ERR_SHAPE),
+    (dict(V=4096 * 1024 + 1), G.GDN_ERR_SHAPE),
+    (dict(B=-1), G.GDN_ERR_SHAPE),
+    (dict(p=None), G.GDN_ERR_NULL),
+    (dict(token=None), G.GDN_ERR_NULL),
+    (dict(err=None), G.GDN_ERR_NULL),
+    (dict(q=FAKE + (1 << 32) + 2), G.GDN_ERR_ALIGN),
+    (dict(draft=FAKE + (2 << 32) + 1), G.GDN_ERR_ALIGN),
+])
+def test_spec_verify_bad_arguments_are_rejected(kw, code):
+    assert spec(**kw) == code
+    assert G.lib().gdn_last_error().decode() != ""
+
+
+def test_spec_verify_batch_zero_is_a_no_op():
+    assert spec(B=0) == G.GDN_OK
+    assert G.lib().gdn_last_error().decode() == ""
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path only")
+@pytest.mark.parametrize("V,what", [(1000, "spec verify launch"), (151936, "spec verify (cluster) launch")])
+def test_spec_verify_without_gpu_reports_cuda_error_on_either_launch_path(V, what):
+    """Below 64K vocabulary entries one CTA per sequence, from 64K on an
+    8-CTA cluster per sequence: both report the failed launch, neither falls
+    back to the CPU."""
+    assert spec(V=V) == G.GDN_ERR_CUDA
+    assert what in G.lib().gdn_last_error().decode()
+
+
+def test_overlap_flag_is_refused_outside_the_dense_decode_entry():
+    """GDN_F_OVERLAP_PREV (launch as a programmatic dependent of the previous
+    kernel) is accepted by gdn_recurrent_fwd only; the checkpoint and pool
+    entries refuse it before any CUDA call."""
+    lib = G.lib()
+    v = lambda x: ctypes.c_void_p(x)  # noqa: E731
+    inputs = [v(FAKE), v(FAKE + 4096), v(FAKE + 8192), v(FAKE + 12288), v(FAKE + 16384), v(FAKE + 20480),
+              v(FAKE + 24576)]
+    rc = lib.gdn_recurrent_fwd_from_ckpt(*inputs, v(FAKE + (1 << 32)), v(FAKE + (2 << 32)), v(FAKE + (3 << 32)), 4,
+                                         v(FAKE + (5 << 32)), v(FAKE + (6 << 32)), None, v(FAKE + (7 << 32)),
+                                         1, 1, 16, 48, 128, 128, G.F_OVERLAP_PREV, None)
+    assert rc == G.GDN_ERR_FLAGS
+    rc = lib.gdn_recurrent_fwd_pool(*inputs, v(FAKE + (1 << 32)), v(FAKE + (2 << 32)), 4, None, None, 0,
+                                    G.POOL_FINAL, v(FAKE + (3 << 32)), None, v(FAKE + (4 << 32)),
+                                    1, 1, 16, 48, 128, 128, G.F_OVERLAP_PREV, None)
+    assert rc == G.GDN_ERR_FLAGS
