@@ -411,7 +411,7 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(seconds=args.cpu_seconds)
+        cpu = cpu_baseline(seconds=args.cpu_seconds, B=Bg, L=args.ref_layers)
 
     verify = None
     if not args.no_verify:
@@ -423,13 +423,35 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         prefill = guarded("prefill", lambda: run_prefill(args, lib, device, world))
         if world == 1 and rank == 0 and not args.no_cpu_baseline and "config3" in prefill:
-            prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
+            prefill["config3"]["cpu_baseline"] = cpu_prefill_baseline(T=args.prefill_T, seconds=args.cpu_seconds)
     layer = None
     if not args.no_layer:
         layer = {"decode": guarded("layer.decode", lambda: run_layer_decode(args, device, world))}
         if not args.no_prefill:
             layer.update(guarded("layer", lambda: run_layer(args, device, world)))
 
+    # compact copies of the secondary results where a reader of the line looks
+    # first: the decode sweep next to the headline's roofline, and the prefill
+    # configs' throughput and tensor-roofline fractions (details in *_detail)
+    roofline["by_batch_gbs"] = sweep
+    roofline["by_batch_frac"] = {b: round(v / hbm_peak, 4) for b, v in sweep.items()}
+    prefill_summary = None
+    if isinstance(prefill, dict):
+        prefill_summary = {}
+        for name, r in prefill.items():
+            if not isinstance(r, dict) or "roofline" not in r:
+                prefill_summary[name] = r
+                continue
+            keep = {k: r[k] for k in ("schedule", "tokens_per_s", "tokens_per_s_per_layer", "ms_per_layer",
+                                      "tokens_per_s_without_gather") if k in r}
+            if "stack_48_layers" in r:
+                keep["tokens_per_s_48_layers"] = r["stack_48_layers"]["tokens_per_s"]
+                keep["ms_48_layers"] = r["stack_48_layers"]["ms"]
+            keep["chunked_ms"] = r["kernel_ms"].get("chunked")
+            keep["tensor_frac"] = r["roofline"]["frac"]
+            if "cpu_baseline" in r:
+                keep["cpu_tokens_per_s"] = r["cpu_baseline"]["value"]
+            prefill_summary[name] = keep
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -445,7 +467,8 @@ def run_ours(args, world, rank, local):
                               "layer's (GDN_F_OVERLAP_PREV)") if world == 1 else
                              "eager + NCCL all-gather, launches with GDN_F_OVERLAP_PREV"},
         "roofline": roofline, "clocks": clocks, "gpu_launches": args.steps * L,
-        "sweep_gbs_by_batch": sweep, "pool_decode": pool, "e2e": e2e, "cpu_baseline": cpu, "verify_chain": verify, "prefill": prefill, "layer": layer,
+        "sweep_gbs_by_batch": sweep, "e2e": e2e, "cpu_baseline": cpu, "prefill": prefill_summary,
+        "pool_decode": pool, "verify_chain": verify, "prefill_detail": prefill, "layer": layer,
     }
     return line
 
@@ -825,6 +848,29 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
     return ms, kms
 
 
+def time_stack(X, lib, device, world, n_layers, gathered=None):
+    """Max-over-ranks ms of n_layers layer steps back to back (one pass, after
+    the schedule's own warm-up): BASELINE config 4 is a stack of 48 GDN layers
+    (the same shapes in every layer, so one set of buffers serves them all)."""
+    st = torch.cuda.current_stream(device)
+    h = ctypes.c_void_p(st.cuda_stream)
+    fused_gather = X.schedule == "split_gather"
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n_layers):
+        X.step(lib, h)
+        if gathered is not None and not fused_gather:
+            torch.distributed.all_gather_into_tensor(gathered, X.out)
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    if fused_gather and max_over_ranks(float(X.gather_errors()), world, device):
+        raise RuntimeError("gdn_gather_wait timed out on a rank: peer gather incomplete")
+    return max_over_ranks(e0.elapsed_time(e1), world, device)
+
+
 def run_prefill(args, lib, device, world):
     """Configs 3 and 4 on this rank's K-head shard (16/N key, 48/N value heads);
     for N > 1 each layer ends with the NCCL all-gather of the bf16 outputs, or
@@ -854,9 +900,15 @@ def run_prefill(args, lib, device, world):
             X.use_schedule(sched)
             timed[sched] = time_prefill_layer(X, lib, device, world, steps, max(args.warmup, 1)
                                               if name == "config4" else max(args.warmup, 3), gathered)
-        X.close()
         best = min(timed, key=lambda k: timed[k][0])
         ms, kms = timed[best]
+        stack = None
+        if name == "config4" and args.stack_layers > 0:
+            X.use_schedule(best)
+            ms_stack = time_stack(X, lib, device, world, args.stack_layers, gathered)
+            stack = {"layers": args.stack_layers, "ms": round(ms_stack, 3),
+                     "tokens_per_s": round(X.N / (ms_stack * 1e-3), 1)}
+        X.close()
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
         kernel = {"fused": "chunked_kernel", "split": "chunk_prep_kernel + chunk_scan_kernel",
                   "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>",
@@ -869,7 +921,9 @@ def run_prefill(args, lib, device, world):
                          f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
                          + ((" -> all-gather fused into the scan (NVLink peer stores)" if best == "split_gather"
                              else " -> NCCL all-gather") if world > 1 else "")),
-            "tokens_per_s": round(X.N / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+            ("tokens_per_s" if name == "config3" else "tokens_per_s_per_layer"): round(X.N / (ms * 1e-3), 1),
+            "ms_per_layer": round(ms, 4),
+            **({"stack_48_layers": stack} if stack else {}),
             **({"tokens_per_s_without_gather": round(X.N / (kms["layer_without_gather"] * 1e-3), 1)}
                if "layer_without_gather" in kms else {}),
             "kernel_ms": {k: round(v, 4) for k, v in kms.items()},
@@ -1014,9 +1068,10 @@ def run_layer_decode(args, device, world, Lp=8):
     return out
 
 
-def cpu_prefill_baseline(T=512, seconds=10.0):
+def cpu_prefill_baseline(T=4096, seconds=10.0):
     """The reference's prefill CPU path (chunked_delta, numpy oracle with BLAS
-    threads) plus conv and gated norm on a bounded sample; tokens/s."""
+    threads) plus conv and gated norm, whole config-3 layers (at least one)
+    for about `seconds`; tokens/s."""
     import gdn_oracle as O
     rng = np.random.default_rng(7)
     C = 2 * HK * D + HV * D
@@ -1063,9 +1118,11 @@ def cpu_step(layers, threads):
                       S_out=x["S"], nthreads=threads)
 
 
-def cpu_baseline(seconds=10.0, B=1):
+def cpu_baseline(seconds=10.0, B=256, L=4):
+    """The C oracle on the headline decode workload's batch (B sequences, all
+    48 heads), L layers per step (a bounded sample of the 48), ~`seconds`."""
     threads = os.cpu_count() or 1
-    layers = cpu_sample(B)
+    layers = cpu_sample(B, L)
     cpu_step(layers, threads)
     n, t0 = 0, time.perf_counter()
     while True:
@@ -1076,16 +1133,20 @@ def cpu_baseline(seconds=10.0, B=1):
             break
     gbs = n * 2 * B * HV * STATE_BYTES * len(layers) / el / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} steps of 48 layers x B={B} decode, C restatement of delta::run_reference "
-                      f"(oracle/gdn_oracle.c, OpenMP over heads), {el:.1f} s"}
+            "sample": f"{n} steps of {L} of the 48 layers x B={B} decode, C restatement of "
+                      f"delta::run_reference (oracle/gdn_oracle.c, OpenMP over heads), {el:.1f} s"}
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the C restatement of delta::run_reference on the
+    host cores, at the headline workload's batch (args.batch x N sequences,
+    all 48 heads), each step args.ref_layers of the 48 layers."""
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    B = 1
-    layers = cpu_sample(B)
+    B = args.batch * world
+    Ls = args.ref_layers
+    layers = cpu_sample(B, Ls)
     for _ in range(args.warmup):
         cpu_step(layers, threads)
     t0 = time.perf_counter()
@@ -1094,14 +1155,16 @@ def run_reference(args, world, rank):
     el = time.perf_counter() - t0
     ms = el * 1e3 / args.steps
     gbs = 2 * B * HV * STATE_BYTES * len(layers) / (ms * 1e-3) / 1e9
-    sample = (f"each step: 48 layers x B={B} of the config-1 decode (a bounded sample of B=256), "
-              f"C restatement of delta::run_reference (oracle/gdn_oracle.c), {threads} threads")
+    sample = (f"each step: {Ls} of the 48 layers x B={B} of the config-1 decode (the layers are alike, so "
+              f"GB/s is that of the 48-layer step), C restatement of delta::run_reference "
+              f"(oracle/gdn_oracle.c), {threads} threads")
     return {"metric": METRIC, "impl": "reference", "value": round(gbs, 3), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; BASELINE config-0 distributions)",
-            "config": {"workload": "config1: 48 GDN layers, decode T=1 (CPU sample B=1)", "global_batch": B,
-                       "seq_len": 1, "layers": 48, "parallelism": "cpu"},
+            "config": {"workload": f"config1: 48 GDN layers, decode T=1, B={B} (CPU sample: {Ls} layers per step)",
+                       "global_batch": B, "seq_len": 1, "layers": 48, "layers_per_step_sampled": Ls,
+                       "parallelism": "cpu"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1119,6 +1182,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-layers", type=int, default=4,
+                    help="CPU baseline / reference arm: layers of the 48 run per step (bounded sample)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per launch from an ncu capture, reported as roofline.traffic")
     ap.add_argument("--small", action="store_true", help="ncu-sized case: B=64 (201 MB of state per layer, above L2), 2 layers, no extras")
@@ -1134,6 +1199,8 @@ def main():
     ap.add_argument("--no-peer-gather", action="store_true",
                     help="N > 1: leave out the schedule whose scan stores into every rank's output over NVLink")
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
+    ap.add_argument("--stack-layers", type=int, default=48,
+                    help="config 4: also time this many layer steps back to back (BASELINE's 48-layer stack; 0 = skip)")
     ap.add_argument("--prefill-ws-gb", type=float, default=0.0,
                     help="cap the split schedule's workspace (GB); smaller than one pass runs in windows")
     args = ap.parse_args()

@@ -59,8 +59,12 @@ extern "C" {
                                      every other input is read after it has completed.
                                      The caller guarantees that the previous kernel does
                                      not write this call's state_in (e.g. consecutive
-                                     layers of a decode step).  Pays off at small batch
-                                     (launch-latency bound), neutral at large batch. */
+                                     layers of a decode step).  Kernels further back are
+                                     complete before the state loads start (the kernel
+                                     lets its own dependents launch only after its wait),
+                                     so two layers used in turn are safe.  Pays off at
+                                     small batch (launch-latency bound), neutral at large
+                                     batch. */
 
 /* ---- flags of the front-end / back-end kernels --------------------------- */
 #define GDN_F_CONV_BF16_OPS 0x100u  /* conv: MLX's per-op bf16 arithmetic (each product and
@@ -315,9 +319,18 @@ int gdn_chunked_norm_gather_ws(const void* q, const void* k, const void* v,
  * gdn_gather_wait -- stream-ordered wait until every rank r < world has
  * signalled at least `expected` calls in flags[r] (this rank's counter array
  * of gdn_chunked_norm_gather_ws), with acquire semantics at system scope.
- * Bounded: after about 4 s it sets *err_flag and returns.
+ * Bounded: after about 4 s it sets *err_flag and the device error word
+ * (gdn_take_device_error) and returns.
  */
 int gdn_gather_wait(const uint32_t* flags, int world, unsigned expected, int32_t* err_flag, void* stream);
+
+/*
+ * gdn_gather_wait_timeout -- gdn_gather_wait with the caller's limit,
+ * 1 <= limit_ms <= 60000 milliseconds of %globaltimer polling.  No
+ * counterpart in the reference (it runs on one device).
+ */
+int gdn_gather_wait_timeout(const uint32_t* flags, int world, unsigned expected, unsigned limit_ms,
+                            int32_t* err_flag, void* stream);
 
 /*
  * gdn_ipc_export / gdn_ipc_open / gdn_ipc_close -- share a device buffer with
@@ -341,13 +354,22 @@ int gdn_ipc_close(void* base);
  * allocates no memory.  No counterpart in the reference; it serves callers
  * that cannot allocate device memory at call time.
  *   Arguments, flags and results as gdn_chunked_fwd.
- *   Limit: gdn_chunked_workspace_bytes(B, T, Hv, cu_seqlens != NULL) must not
- *   exceed GDN_CHUNKED_STATIC_SCRATCH_BYTES (about 450 (64-token chunk, value
- *   head) pairs, e.g. 576 tokens x 48 heads or 4800 tokens x 6 heads); larger
- *   calls return GDN_ERR_SHAPE and touch nothing.
+ *   Limit: a call whose records fit the scratch runs in one pass, a longer
+ *   one in windows of chunks (bit-identical results); only a call with
+ *   gdn_chunked_workspace_min_bytes(B, Hv, state_out != NULL) above
+ *   GDN_CHUNKED_STATIC_SCRATCH_BYTES (one record per sequence and value head
+ *   no longer fits, e.g. B x Hv above about 450) returns GDN_ERR_SHAPE and
+ *   touches nothing.
  *   The first call on each device looks up the scratch's address
  *   (cudaGetSymbolAddress, with that device current) and sets the kernels'
- *   shared-memory attributes; make that first call before any stream capture.
+ *   shared-memory attributes; make that first call before any stream capture,
+ *   and before an engine hands the device's free memory to its own pools:
+ *   the 64 MiB array belongs to the module that holds every chunked kernel,
+ *   so every process that uses any chunked entry point pays it on each
+ *   device, reserved when that module is loaded there (lazily, at its first
+ *   use, under CUDA's default lazy loading).  The address is cached per
+ *   device for the life of the process: do not use the library across a
+ *   cudaDeviceReset.
  *   Nothing in the scratch needs to start at zero.  There is one scratch per
  *   device: calls on the same device that overlap in time (different streams
  *   or host threads without ordering between them) race on it.
@@ -433,8 +455,12 @@ int gdn_gated_rmsnorm_fwd(const void* o, const void* z, const float* gamma, void
  * mode bit 0: operands rounded to bf16 (kind::f16) instead of tf32;
  * bit 1: A negated by the instruction descriptor; bit 2: A read from tensor
  * memory (tf32 only); bit 3: A laid out MN-major in shared memory; bit 4: B
- * laid out MN-major.  N, K multiples of 16 in [16, 128].  *status (device
- * int32) is set to 1 if the bounded wait for the MMA timed out.
+ * laid out MN-major; bit 7 (alone): issue no MMA and wait on the barrier
+ * with a poll budget of 4096, so that the bounded wait runs out (a test of
+ * the timeout path: *status and the device error word are set, D is not
+ * written, the kernel returns).  N, K multiples of 16 in [16, 128].
+ * *status (device int32) is set to 1 if the bounded wait for the MMA timed
+ * out, and so is the device error word (gdn_take_device_error).
  */
 int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                       int* status, void* stream);

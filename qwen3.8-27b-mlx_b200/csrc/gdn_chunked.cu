@@ -1776,9 +1776,10 @@ __global__ void gather_signal_kernel(FlagPtrs fp, int rank, int world) {
   }
 }
 
-// Wait until every rank has signalled `expected` calls (bounded: about 4 s of
-// polling, then *err = 1 and return).
-__global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t expected, int32_t* err) {
+// Wait until every rank has signalled `expected` calls (bounded: limit_ns of
+// polling by %globaltimer, then *err = 1, the device error word set, return).
+__global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t expected, int32_t* err,
+                                   unsigned long long limit_ns, int* dev_err) {
   const int r = threadIdx.x;
   if (r >= world) return;
   unsigned long long t0;
@@ -1789,8 +1790,9 @@ __global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t ex
     if (static_cast<int32_t>(v - expected) >= 0) return;
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > 4000000000ull) {
+    if (t - t0 > limit_ns) {
       atomicExch(err, 1);
+      atomicExch(dev_err, 1);
       return;
     }
     __nanosleep(200);
@@ -1845,13 +1847,23 @@ extern "C" int gdn_chunked_norm_gather_ws(const void* q, const void* k, const vo
   return cuda_status(cudaGetLastError(), "gather signal launch");
 }
 
-extern "C" int gdn_gather_wait(const uint32_t* flags, int world, unsigned expected, int32_t* err_flag, void* stream) {
+extern "C" int gdn_gather_wait_timeout(const uint32_t* flags, int world, unsigned expected, unsigned limit_ms,
+                                       int32_t* err_flag, void* stream) {
   clear_error();
   if (world < 1 || world > 8) return fail(GDN_ERR_SHAPE, "world %d: need 1 <= world <= 8", world);
+  if (limit_ms < 1 || limit_ms > 60000) return fail(GDN_ERR_RANGE, "limit_ms %u: need 1 .. 60000", limit_ms);
   if (!flags || !err_flag) return fail(GDN_ERR_NULL, "flags and err_flag are required");
   if (!aligned(flags, 4) || !aligned(err_flag, 4)) return fail(GDN_ERR_ALIGN, "flags, err_flag 4-byte aligned");
-  gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, expected, err_flag);
+  int* dev_err = nullptr;
+  int rc = device_error_ptr(&dev_err);
+  if (rc != GDN_OK) return rc;
+  gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      flags, world, expected, err_flag, static_cast<unsigned long long>(limit_ms) * 1000000ull, dev_err);
   return cuda_status(cudaGetLastError(), "gather wait launch");
+}
+
+extern "C" int gdn_gather_wait(const uint32_t* flags, int world, unsigned expected, int32_t* err_flag, void* stream) {
+  return gdn_gather_wait_timeout(flags, world, expected, 4000u, err_flag, stream);
 }
 
 // Scratch of gdn_chunked_fwd_static: a fixed device array, so that the call
@@ -1864,7 +1876,9 @@ namespace gdn {
 namespace {
 
 // Address of g_chunked_static_scratch on the current device, looked up once per
-// device (cudaGetSymbolAddress with that device current) and cached.
+// device (cudaGetSymbolAddress with that device current) and cached for the
+// life of the process: the library must not be used across a
+// cudaDeviceReset (the cached address would then be stale).
 int static_scratch_ptr(unsigned char** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};
@@ -1896,17 +1910,21 @@ extern "C" int gdn_chunked_fwd_static(const void* q, const void* k, const void* 
   int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, o,
                         cu_seqlens, B, T, Hk, Hv, Dk, Dv, flags);
   if (rc != GDN_OK || B == 0) return rc;
-  const size_t need = workspace_bytes(B, T, Hv, cu_seqlens != nullptr);
+  // the call runs in one pass when its records fit the scratch, else in
+  // windows of chunks (bit-identical); only a call whose smallest window
+  // (one chunk of every sequence, plus the carried state without state_out)
+  // does not fit is refused
+  const size_t need = workspace_min_bytes(B, Hv, state_out == nullptr);
   if (need > GDN_CHUNKED_STATIC_SCRATCH_BYTES)
     return fail(GDN_ERR_SHAPE,
-                "gdn_chunked_fwd_static: B=%d T=%d Hv=%d needs %zu bytes of scratch, more than the %llu of the "
-                "static scratch; split the call or use gdn_chunked_fwd_ws",
-                B, T, Hv, need, static_cast<unsigned long long>(GDN_CHUNKED_STATIC_SCRATCH_BYTES));
+                "gdn_chunked_fwd_static: B=%d Hv=%d needs at least %zu bytes of scratch, more than the %llu of the "
+                "static scratch; split the batch or use gdn_chunked_fwd_ws",
+                B, Hv, need, static_cast<unsigned long long>(GDN_CHUNKED_STATIC_SCRATCH_BYTES));
   if (Hv > 65535) return fail(GDN_ERR_SHAPE, "too many value heads for one launch");
   unsigned char* ws = nullptr;
   rc = static_scratch_ptr(&ws);
   if (rc != GDN_OK) return rc;
-  return run_split(p, T, ws, need, static_cast<cudaStream_t>(stream));
+  return run_split(p, T, ws, GDN_CHUNKED_STATIC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
 }
 
 #ifdef GDN_CHUNK_TIMING

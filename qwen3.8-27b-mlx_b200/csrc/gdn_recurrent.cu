@@ -134,10 +134,6 @@ __global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
   const int h = bh - b * p.Hv;
   const int kh = h / (p.Hv / p.Hk);
   const int col = lane * 4;
-  // the next kernel in the stream may begin launching (a programmatic
-  // dependent waits for this grid's completion before reading its inputs)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
   // Start state of this (sequence, head): the dense state, or its pool slot.
   size_t sidx = static_cast<size_t>(bh);
   bool slot_ok = true;
@@ -176,6 +172,13 @@ __global__ void __launch_bounds__(128, 8) recurrent_kernel(const RecParams p) {
   // the previous grid finishes; the token inputs are read only after it has
   // completed (a no-op for an ordinary launch)
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Only now may the next kernel in the stream begin launching.  Triggering
+  // after the wait means a dependent launch N + 1 starts only once every
+  // block of launch N has seen launch N - 1 complete, so dependents never
+  // chain further than one kernel: a launch's early state loads can overlap
+  // the previous kernel only, never one further back that might still be
+  // writing those states (two layers used in turn, A B A B, stay correct).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const bool direct = (p.flags & GDN_F_GATES_DIRECT) != 0;
   const bool l2 = (p.flags & GDN_F_QK_L2NORM) != 0;
@@ -309,8 +312,8 @@ int rows_per_warp(long long bh) {
 #endif
 }
 
-// Which kernel streams the state: the bulk-copy ring once there are enough
-// 32-row units for several per CTA slot, the register kernel for small batches.
+// Launch the decode / verify kernel over B x Hv (sequence, value head) pairs
+// with the rows per warp that rows_per_warp() picks for that count.
 int run_recurrent(const RecParams& p, void* stream) {
   if (p.B == 0) return GDN_OK;
   const long long bh = static_cast<long long>(p.B) * p.Hv;

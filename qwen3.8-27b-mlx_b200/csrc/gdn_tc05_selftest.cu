@@ -4,7 +4,10 @@
 // same shared-memory layout, descriptors and TMEM load/store helpers as the
 // prefill kernel.  Modes: tf32 or bf16 operands, A negated by the instruction
 // descriptor, A read from tensor memory instead of shared memory, MN-major
-// operands, D at a column offset of 64 and/or 128 (N up to 256).
+// operands, D at a column offset of 64 and/or 128 (N up to 256).  A last mode
+// issues no MMA at all and waits on the barrier with a small poll budget, so
+// that the bounded wait runs out: the kernel must then report the timeout
+// (status word and the library's device error word) and return cleanly.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -18,7 +21,7 @@ constexpr int kSelfTestCols = 512;   // TMEM columns: D from column 0, 64, 128 o
 
 __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                             float* __restrict__ D, int N, int K, int mode,
-                                                            int* __restrict__ status) {
+                                                            int* __restrict__ status, int* __restrict__ dev_err) {
   extern __shared__ __align__(128) unsigned char smem[];
   const bool bf = (mode & 1) != 0;
   const int E = bf ? 2 : 4;
@@ -77,7 +80,10 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
     tc::fence_after_sync();
   }
 
-  if (tid == 0) {
+  // timeout mode: nothing is committed to the barrier; a small poll budget
+  const bool no_mma = (mode & 128) != 0;
+  const uint32_t limit = no_mma ? (1u << 12) : ptx::kSpinLimit;
+  if (tid == 0 && !no_mma) {
     const uint32_t idesc = tc::instr_desc(bf ? tc::kBF16 : tc::kTF32, 128, N, (mode & 2) != 0, false, a_mn, b_mn);
     const int steps = static_cast<int>(kbytes / 32);
     const int kgroups = bf ? 2 : 1;                 // K groups of 8 per MMA
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
     }
     tc::mma_commit(bar);
   }
-  bool ok = ptx::mbar_wait(bar, 0);
+  bool ok = ptx::mbar_wait(bar, 0, limit);
   tc::fence_after_sync();
   if (__syncthreads_and(ok)) {
     for (int c = 0; c < N; c += 16) {
@@ -106,8 +112,11 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
       for (int i = 0; i < 16; ++i) D[static_cast<size_t>(tid) * N + c + i] = v[i];
     }
   } else {
-    if (tid == 0) *status = 1;
-    ok = ptx::mbar_wait(bar, 0);       // give the MMA another bounded chance to land
+    if (tid == 0) {
+      *status = 1;
+      atomicExch(dev_err, 1);
+    }
+    ok = ptx::mbar_wait(bar, 0, limit);   // give an MMA in flight another bounded chance to land
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -122,7 +131,8 @@ using namespace gdn;
 extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                                  int* status, void* stream) {
   clear_error();
-  if (mode & ~127) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~127);
+  if (mode & ~255) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~255);
+  if ((mode & 128) && (mode & 127)) return fail(GDN_ERR_FLAGS, "the timeout mode (bit 7) takes no other bit");
   if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
   if ((mode & 4) && (mode & 8)) return fail(GDN_ERR_FLAGS, "A from tensor memory has no MN-major form");
   // MN-major operands are exercised with bf16 only: on sm_100a with this
@@ -138,10 +148,13 @@ extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N
     return fail(GDN_ERR_ALIGN, "buffers must be 4-byte aligned");
   const int E = (mode & 1) ? 2 : 4;
   const size_t smem = static_cast<size_t>(128 + N) * K * E + 16;
-  int rc = cuda_status(cudaFuncSetAttribute(tc05_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  int* dev_err = nullptr;
+  int rc = device_error_ptr(&dev_err);
+  if (rc != GDN_OK) return rc;
+  rc = cuda_status(cudaFuncSetAttribute(tc05_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem)),
                        "tc05 self-test smem attribute");
   if (rc != GDN_OK) return rc;
-  tc05_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(A, B, D, N, K, mode, status);
+  tc05_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(A, B, D, N, K, mode, status, dev_err);
   return cuda_status(cudaGetLastError(), "tc05 self-test launch");
 }

@@ -63,6 +63,7 @@ SIGNATURES = {
                                   ctypes.c_float, _vp, _vp, _i, _i, ctypes.c_longlong, ctypes.c_longlong, _i, _vp]
                                   + [_i] * 6 + [_u, _vp, ctypes.c_size_t, _vp],
     "gdn_gather_wait": [_vp, _i, _u, _vp, _vp],
+    "gdn_gather_wait_timeout": [_vp, _i, _u, _u, _vp, _vp],
     "gdn_ipc_export": [_vp, _vp, _vp],
     "gdn_ipc_open": [_vp, ctypes.c_size_t, _vp, _vp],
     "gdn_ipc_close": [_vp],

@@ -4,10 +4,10 @@ stand-in for MLX (``mlx_stub/``; MLX itself is not installable here).
 
 Run once, in a container where the reference checkout exists:
 
-    python tests/golden/gen_golden.py [--ref /path/to/reference/python]
+    python tests/golden/gen_golden.py --ref /path/to/reference/python
 
-The reference path can also come from the GDN_REFERENCE_PY environment
-variable.  Outputs (``*.npz``) are committed; tests only read them and never
+The reference path can come from the GDN_REFERENCE_PY environment variable
+instead; one of the two is required.  Outputs (``*.npz``) are committed; tests only read them and never
 touch the reference tree.
 
 What is pinned (all functions are the reference's own, unmodified):
@@ -219,9 +219,12 @@ def gen_spec(mx, seed, name):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("GDN_REFERENCE_PY", "/root/reference/python"))
+    ap.add_argument("--ref", default=os.environ.get("GDN_REFERENCE_PY"),
+                    help="the reference checkout's python/ folder (or set GDN_REFERENCE_PY)")
     ap.add_argument("--only", choices=["spec"], default=None, help="regenerate one file set only")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref /path/to/reference/python or set GDN_REFERENCE_PY")
     mx, qwen35 = load_reference(args.ref)
     if args.only == "spec":
         gen_spec(mx, 1008, "spec_residual.npz")

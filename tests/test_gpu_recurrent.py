@@ -188,10 +188,10 @@ def test_large_batch_linearity_and_spot_check():
         assert O.rel_err(host(o1[bi:bi + 1]), ro) < TOL and O.rel_err(host(T1[bi:bi + 1]), rS) < TOL
 
 
-def test_bulk_copy_path_rollback_in_place_and_zero_state():
-    """A batch large enough for the bulk-copy (TMA engine) kernel: rollback by
-    index with an out-of-range entry, then an in-place step, then a zero start
-    state; all against the oracle, and no bounded wait may have timed out."""
+def test_rollback_in_place_and_zero_state_b24():
+    """B = 24, T = 2 (eight rows per warp): rollback by index with an
+    out-of-range entry, then an in-place step, then a zero start state; all
+    against the oracle, and no kernel may have set the device error word."""
     B, T = 24, 2
     rng = np.random.default_rng(14)
     ver = O.synth_decode_inputs(rng, B, T)
@@ -251,3 +251,49 @@ def test_overlap_prev_flag_gives_the_same_bits_and_is_refused_elsewhere():
                                                     G.ptr(torch.empty((B, 1, 48, 128), device="cuda")), None, None,
                                                     B, 1, 16, 48, 128, 128, G.F_OVERLAP_PREV, None))
     assert e.value.code == G.GDN_ERR_FLAGS
+
+
+def test_overlap_prev_two_layers_in_turn_from_a_graph_is_bit_identical():
+    """Two layers used in turn (A, B, A, B, ... for 20 steps) at B = 1, each
+    updating its own state in place, launched with GDN_F_OVERLAP_PREV and
+    replayed from a CUDA graph: launch N + 2 reads the state that launch N
+    wrote, so the o rows and final states must equal those of ordinary
+    launches bit for bit."""
+    rng = np.random.default_rng(45)
+    steps = 20
+    layers = [O.synth_decode_inputs(rng, 1, 1) for _ in range(2)]
+    ins = [device_inputs(inp) for inp in layers]
+
+    def run(overlap, graph):
+        states = [dev(inp["S0"]) for inp in layers]
+        outs = [torch.empty((1, 1, 48, 128), device="cuda") for _ in range(steps)]
+
+        def body():
+            for s in range(steps):
+                j = s % 2
+                G.recurrent_fwd(*ins[j], state_in=states[j], state_out=states[j], o=outs[s], overlap_prev=overlap)
+        if graph:
+            body()                                  # warm-up (module loading) outside the capture
+            torch.cuda.synchronize()
+            for j, inp in enumerate(layers):
+                states[j].copy_(dev(inp["S0"]))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                body()
+            for j, inp in enumerate(layers):
+                states[j].copy_(dev(inp["S0"]))
+            torch.cuda.synchronize()
+            g.replay()
+        else:
+            body()
+        torch.cuda.synchronize()
+        return outs, states
+
+    ref_o, ref_S = run(False, False)
+    got_o, got_S = run(True, True)
+    for s in range(steps):
+        assert torch.equal(ref_o[s], got_o[s]), s
+    for j in range(2):
+        assert torch.equal(ref_S[j], got_S[j]), j
+    assert not torch.equal(ref_S[0], dev(layers[0]["S0"]))    # the chain really moved the states
+    assert G.take_device_error() == 0

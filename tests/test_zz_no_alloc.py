@@ -1,13 +1,18 @@
 """gdn_chunked_fwd_static -- the chunked prefill on the library's fixed device
-scratch (no allocation in the call) -- through the C ABI, against the
-caller-workspace entry point gdn_chunked_fwd_ws on the same inputs.
+scratch, for callers that cannot allocate device memory when they call (an
+FFI binding with no device allocator, an engine that handed all free memory
+to its pools at start-up) -- through the C ABI, against the caller-workspace
+entry point gdn_chunked_fwd_ws on the same inputs.
 
-Two calls in a row with different shapes (a uniform batch with a start state
-and fp32 o, then packed sequences with bf16 o and zero start state), so the
-second call runs on scratch that still holds the first call's records.
-Tolerance: 2e-3 relative L2 on o and the final state, the prefill bound of
-the other chunked tests.  A call that needs more than the 64 MiB scratch is
-rejected with GDN_ERR_SHAPE and leaves its outputs untouched.
+Both entries run the same kernels on the same inputs, so the results must be
+bit-identical (torch.equal).  Two calls in a row with different shapes (a
+uniform batch with a start state and fp32 o, then packed sequences with bf16
+o and zero start state), so the second call runs on scratch that still holds
+the first call's records; the first is also checked against the CPU oracle
+directly (2e-3 relative L2, the prefill bound).  A call longer than the 64 MiB
+scratch holds runs in windows, again bit-identical to one pass on a caller
+workspace; a batch whose smallest window does not fit is rejected with
+GDN_ERR_SHAPE and leaves its outputs untouched.
 
 Collected last (file name) so that it also runs after every other test in the
 same process; it passes alone too.
@@ -86,6 +91,18 @@ def rel_l2(a, b):
     return O.rel_l2(a.float().cpu().numpy(), b.float().cpu().numpy())
 
 
+def oracle(X):
+    """O.chunked_delta per sequence (uniform batch) from the host copies."""
+    q = O.l2norm(X["q"].float().cpu().numpy().reshape(X["B"], X["T"], X["Hk"], D)) * np.float32(D ** -0.5)
+    k = O.l2norm(X["k"].float().cpu().numpy().reshape(X["B"], X["T"], X["Hk"], D))
+    v = X["v"].float().cpu().numpy().reshape(X["B"], X["T"], X["Hv"], D)
+    a = X["a"].cpu().numpy().reshape(X["B"], X["T"], X["Hv"])
+    b = X["b"].cpu().numpy().reshape(X["B"], X["T"], X["Hv"])
+    al, bt = O.gates(a, b, X["A_log"].cpu().numpy(), X["dt_bias"].cpu().numpy())
+    S0 = None if X["S0"] is None else X["S0"].cpu().numpy()
+    return O.chunked_delta(O.expand_heads(q, X["Hv"]), O.expand_heads(k, X["Hv"]), v, al, bt, S0)
+
+
 def test_static_scratch_matches_workspace_entry_on_two_calls_in_a_row():
     L = G.lib()
     X1 = make_inputs(70, [200, 200], Hk=2, Hv=6, packed=False, state=True)
@@ -101,19 +118,41 @@ def test_static_scratch_matches_workspace_entry_on_two_calls_in_a_row():
     assert rc1 == G.GDN_OK and rc2 == G.GDN_OK, L.gdn_last_error().decode()
     torch.cuda.synchronize()
     for (o, S), (ro, rS) in (((o1, S1), r1), ((o2, S2), r2)):
-        assert rel_l2(o, ro) < PREFILL_TOL, rel_l2(o, ro)
-        assert rel_l2(S, rS) < PREFILL_TOL, rel_l2(S, rS)
+        assert torch.equal(o, ro) and torch.equal(S, rS)
+    oo, oS = oracle(X1)
+    assert rel_l2(o1.view(2, 200, 6, D), torch.from_numpy(oo)) < PREFILL_TOL
+    assert rel_l2(S1, torch.from_numpy(oS)) < PREFILL_TOL
     assert G.take_device_error() == 0
 
 
-def test_static_scratch_rejects_a_call_beyond_its_size():
-    """768 (chunk, head) records (16 chunks x 48 heads, 109 MiB) exceed the
-    64 MiB scratch: GDN_ERR_SHAPE, outputs untouched.  The buffers have the
-    call's full size, so nothing could be out of bounds either way."""
+def test_static_scratch_runs_a_longer_call_in_windows():
+    """1,024 tokens x 48 value heads need 109 MiB of records in one pass; the
+    static entry runs them in windows of its 64 MiB, bit-identical to one pass
+    on a caller workspace (with and without state_out)."""
     L = G.lib()
-    X = make_inputs(72, [1024], Hk=16, Hv=48, packed=False, state=False)
+    X = make_inputs(73, [1024], Hk=16, Hv=48, packed=False, state=True)
     need = L.gdn_chunked_workspace_bytes(1, 1024, 48, 0)
     assert need > 64 << 20
+    ro, rS = reference(X, G.F_QK_L2NORM, torch.float32)
+    o, S = outputs(X, torch.float32)
+    rc = call(L.gdn_chunked_fwd_static, X, o, S, G.F_QK_L2NORM)
+    assert rc == G.GDN_OK, L.gdn_last_error().decode()
+    o2, _ = outputs(X, torch.float32)
+    rc = call(L.gdn_chunked_fwd_static, X, o2, None, G.F_QK_L2NORM)
+    assert rc == G.GDN_OK, L.gdn_last_error().decode()
+    torch.cuda.synchronize()
+    assert torch.equal(o, ro) and torch.equal(S, rS) and torch.equal(o2, ro)
+    assert G.take_device_error() == 0
+
+
+def test_static_scratch_rejects_a_batch_whose_smallest_window_does_not_fit():
+    """10 sequences x 48 value heads: one record each (480 records of 145 KiB)
+    already exceed the 64 MiB scratch: GDN_ERR_SHAPE, outputs untouched.  The
+    buffers have the call's full size, so nothing could be out of bounds
+    either way."""
+    L = G.lib()
+    X = make_inputs(72, [64] * 10, Hk=16, Hv=48, packed=False, state=False)
+    assert G.chunked_workspace_min_bytes(10, 48, True) > 64 << 20
     o, S = outputs(X, torch.float32)
     rc = call(L.gdn_chunked_fwd_static, X, o, S, G.F_QK_L2NORM)
     assert rc == G.GDN_ERR_SHAPE
