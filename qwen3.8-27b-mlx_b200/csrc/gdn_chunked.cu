@@ -44,10 +44,12 @@
 namespace gdn {
 
 #ifdef GDN_CHUNK_TIMING
-__device__ long long g_chunk_timing[32];   // [0,13) fused, [16,24) and 30 prep, [24,29) scan
+// phase cycles of one CTA in the middle of the grid (a steady-state wave, warm
+// instruction cache): [0,13) fused, [8,15), [16,24) and 31 prep, [24,29) scan
+__device__ long long g_chunk_timing[32];
 #define GDN_TICK(slot)                                                          \
   do {                                                                          \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {               \
+    if (blockIdx.x == gridDim.x / 2 && blockIdx.y == 0 && threadIdx.x == 0) {   \
       const long long now_ = clock64();                                         \
       g_chunk_timing[slot] += now_ - c.tick;                                    \
       c.tick = now_;                                                            \
@@ -83,21 +85,23 @@ constexpr uint32_t kOffSc = kOffY + 3 * 256 * 4;    // per-token scalars, 10 x 6
 constexpr uint32_t kOffBar = kOffSc + 10 * kC * 4;  // mbarrier, TMEM base
 constexpr uint32_t kSmemBytes = kOffBar + 64;
 
-// shared memory map of the prep kernel: regions are reused as the phases go,
-// so that three CTAs fit on an SM
-constexpr uint32_t kPKQ = 0;                        // [K; Q] rows 128 x 128 bf16 (32 KiB), until (a) and Q-tilde
-constexpr uint32_t kSboKQ = (kD * 2 / 16) * 128;    // 8-row group stride of 128-wide bf16 rows
-constexpr uint32_t kPA = 0;                         // A^T, plain, row stride 68, once Q-tilde is written
-constexpr uint32_t kPY = kPA + kC * kPadA * 4;      // solve temporaries
-constexpr uint32_t kPX = kPY + 3 * 256 * 4;         // X, plain
-constexpr uint32_t kPOp = 0;                        // V^T diag(beta), then K^T diag(beta g r_k): 128 x 64, after the solve
-constexpr uint32_t kPTi = 37888;                    // T^-1 64 x 64
-constexpr int kPrepHeads = 4;                       // value heads per prep CTA at most (one key head's)
-constexpr uint32_t kPSc = kPTi + kC * kC * 4;       // per-token scalars, 10 x 64 per value head
-constexpr uint32_t kPBar = kPSc + kPrepHeads * 10 * kC * 4;   // mbarrier, TMEM base, slot broadcast
-constexpr uint32_t kPrepSmem = kPBar + 64;
-static_assert(kPX + kC * kPad * 4 <= kPTi, "prep: X overlaps T^-1");
-static_assert(kD * kC * 4 <= kPTi, "prep: the column operand overlaps T^-1");
+// shared memory map of the prep kernel (one CTA per (chunk, value head),
+// three per SM).  Rows of K, Q and V arrive by cp.async in one layout,
+// element (t, d) at kmajor_offset(t, d, 2, 2048): read as an R x K operand it
+// is the K-major [K; Q] of G | P = [K; Q] K^T, read as an M x K operand with
+// M = d it is the MN-major K^T / V^T of W^T and U0^T, so no row is ever
+// transposed.  Regions are reused as the phases go.
+constexpr uint32_t kSboKQ = (kD * 2 / 16) * 128;    // 8-row group stride of 128-wide bf16 rows (2048)
+constexpr uint32_t kQK = 0;                         // K rows, bf16 (16 KiB)
+constexpr uint32_t kQQ = kQK + kC * kD * 2;         // Q rows (16 KiB); V rows once G | P and Q-tilde are done
+constexpr uint32_t kQA = kQQ + kC * kD * 2;         // A, row-major, row stride kPadA; then the U0 operand hi | lo
+constexpr uint32_t kQX = kQA + kC * kPadA * 4;      // X = T^-1, row-major, row stride kPadA; then the W operand hi | lo
+constexpr uint32_t kQY = kQX + kC * kPadA * 4;      // level products of the blocked solve, 3 x 16 x 16
+constexpr uint32_t kQSc = kQY + 3 * 256 * 4;        // per-token scalars, 10 x 64
+constexpr uint32_t kQBar = kQSc + 10 * kC * 4;      // mbarrier, TMEM base, (sequence, chunk) broadcast
+constexpr uint32_t kPrepSmem = kQBar + 64;
+constexpr uint32_t kSboOp = (kC * 2 / 16) * 128;    // 8-row group stride of the 64-token bf16 operands (1024)
+static_assert(2 * kC * kC * 2 <= kC * kPadA * 4, "prep: an operand pair fits the A / X region it replaces");
 static_assert(3 * (kPrepSmem + 1024) <= 233472, "prep: three CTAs per SM");
 
 constexpr uint32_t kTmemCols = 512;
@@ -105,9 +109,9 @@ constexpr uint32_t kTmemCols = 512;
 // accumulator), [256,320) G|P during (a); [256,384) W (lanes 0-63) during (c);
 // [384,448) U^T; [448,512) y^T
 constexpr uint32_t kColR = 0, kColDR = 128, kColGP = 256, kColW = 256, kColU = 384, kColY = 448;
-// prep: [0,64) G|P, [64,128) U0^T, then W^T
+// prep: [0,64) G|P, then W^T; [64,128) U0^T
 constexpr uint32_t kPrepTmemCols = 128;
-constexpr uint32_t kPColGP = 0, kPColUW = 64;
+constexpr uint32_t kPColGP = 0, kPColW = 0, kPColU = 64;
 
 // One workspace record per (chunk, value head): the prep kernel's outputs as
 // tensor-core operands (K-major, no swizzle) in three groups that the scan
@@ -282,21 +286,6 @@ __device__ __forceinline__ void ctx_fused_layout(Ctx& c, unsigned char* sm) {
   c.sY = reinterpret_cast<float*>(sm + kOffY);
   ctx_scalars(c, reinterpret_cast<float*>(sm + kOffSc));
   c.bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
-}
-
-// Shared-memory pointers of the prep kernel's layout (M and W go to the record).
-__device__ __forceinline__ void ctx_prep_layout(Ctx& c, unsigned char* sm) {
-  c.sKQ = sm + kPKQ;
-  c.sKt = sm + kPOp;
-  c.sVt = sm + kPOp;
-  c.sTi = sm + kPTi;
-  c.sM = nullptr;
-  c.sW = nullptr;
-  c.sX = reinterpret_cast<float*>(sm + kPX);
-  c.sA = reinterpret_cast<float*>(sm + kPA);
-  c.sY = reinterpret_cast<float*>(sm + kPY);
-  ctx_scalars(c, reinterpret_cast<float*>(sm + kPSc));
-  c.bar = reinterpret_cast<uint64_t*>(sm + kPBar);
 }
 
 // Thread geometry and per-head constants (pointers are set by a layout function).
@@ -864,160 +853,134 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
   if (threadIdx.x == 0) prefix[B] = carry;
 }
 
-// Rows of K and Q (thread -> token i, 32-dim quarter) copied as bf16 into the
-// K-major operand [K; Q] of a kind::f16 product (the raw bf16 values are the
-// exact operands; the l2 norms are applied later as per-token scalars), and
-// their norms.  Ends with a barrier.
-__device__ __forceinline__ void prep_rows(const ChunkParams& p, Ctx& c, long long t0, long long s0, int nvalid) {
-  const int i = c.tid >> 2;
-  const int qd = c.tid & 3;
-  const bool valid = i < nvalid;
-  const long long tok = valid ? t0 + i : s0;
+// 16-byte row pieces of one 64 x 128 bf16 matrix (rows at src + t * stride,
+// t < nvalid; zero rows after) into the prep layout at dst, by cp.async.  Warp
+// item it covers tokens 8 (it / 4) .. +7 and the 16-byte pieces 4 (it % 4) ..
+// +3 of each: a warp reads 8 rows x 64 bytes and writes 32 distinct bank
+// groups.
+__device__ __forceinline__ void prep_copy_rows(unsigned char* dst, const __nv_bfloat16* src, long long stride,
+                                               int nvalid, int warp, int lane) {
 #pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    const __nv_bfloat16* src = (which ? p.q + tok * p.q_stride : p.k + tok * p.k_stride) + c.kh * kD + qd * 32;
-    uint4 v[4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) v[m] = valid ? __ldg(reinterpret_cast<const uint4*>(src) + m) : make_uint4(0, 0, 0, 0);
-    float ss = 0.f;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[m]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h[e]);
-        ss += f.x * f.x + f.y * f.y;
-      }
-      *reinterpret_cast<uint4*>(c.sKQ + tc::kmajor_offset(which * kC + i, qd * 32 + m * 8, 2, kSboKQ)) = v[m];
-    }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    if (qd == 0) {
-      if (which) c.s_rq[i] = c.l2 ? rsqrtf(ss + 1e-6f) * c.qscale : 1.f;
-      else c.s_rk[i] = c.l2 ? rsqrtf(ss + 1e-6f) : 1.f;
-    }
+  for (int it = warp; it < 32; it += 8) {
+    const int t = (it >> 2) * 8 + (lane & 7);
+    const int kg = (it & 3) * 4 + (lane >> 3);
+    unsigned char* d = dst + tc::kmajor_offset(t, kg * 8, 2, kSboKQ);
+    if (t < nvalid) ptx::cp_async16(d, src + t * stride + kg * 8);
+    else *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
   }
-  ptx::fence_proxy_async_smem();
+}
+
+// (x0, x1) as bf16 pairs hi = bf16(x), lo = bf16(x - hi): hi + lo equals x to
+// about 2^-16 relative, so two kind::f16 products (hi, then lo) carry an fp32
+// operand more precisely than one tf32 product.
+__device__ __forceinline__ void split_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// 4 x 4 transpose across the lanes u = lane % 4 of each lane quad: lane u
+// holds M[u][0..3] on entry and M[0..3][u] on return.
+__device__ __forceinline__ void quad_transpose(float& v0, float& v1, float& v2, float& v3, int u) {
+  const bool o1 = u & 1, o2 = u & 2;
+  float s0 = __shfl_xor_sync(0xffffffffu, o1 ? v0 : v1, 1);
+  float s1 = __shfl_xor_sync(0xffffffffu, o1 ? v2 : v3, 1);
+  if (o1) { v0 = s0; v2 = s1; } else { v1 = s0; v3 = s1; }
+  s0 = __shfl_xor_sync(0xffffffffu, o2 ? v0 : v2, 2);
+  s1 = __shfl_xor_sync(0xffffffffu, o2 ? v1 : v3, 2);
+  if (o2) { v0 = s0; v1 = s1; } else { v2 = s0; v3 = s1; }
+}
+
+// One level of the blocked inverse X = (I + A)^-1 over 16 x 16 blocks: for
+// the 4 - lv output blocks (b + lv, b),
+//   Y = sum_{m < lv} A[b+lv][b+m] X[b+m][b],   X[b+lv][b] = -D[b+lv] Y
+// with D the (already stored) inverse diagonal blocks -- block forward
+// substitution, the same products as row-by-row substitution in another
+// order.  Thread (block b, 4 x 4 tile (ti, tj)) keeps its tile in registers
+// and reads 4 x 4 operand tiles as float4 rows; ends with a barrier.
+__device__ __forceinline__ void solve_level(int lv, const float* sA, float* sX, float* sY, int tid) {
+  const int nb = 4 - lv;
+  const bool act = tid < nb * 16;
+  const int b = tid >> 4, ti = (tid >> 2) & 3, tj = tid & 3;
+  const int rb = b + lv;
+  if (act) {
+    float y[4][4] = {};
+    for (int m = 0; m < lv; ++m) {
+      const int cb = b + m;
+      const float* arow = sA + (16 * rb + 4 * ti) * kPadA + 16 * cb;
+      const float* xrow = sX + (16 * cb) * kPadA + 16 * b + 4 * tj;
+#pragma unroll
+      for (int kk = 0; kk < 16; kk += 4) {
+        float4 a[4], x[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(arow + r * kPadA + kk);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const float4*>(xrow + (kk + u) * kPadA);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float av[4] = {a[r].x, a[r].y, a[r].z, a[r].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            y[r][0] += av[u] * x[u].x;
+            y[r][1] += av[u] * x[u].y;
+            y[r][2] += av[u] * x[u].z;
+            y[r][3] += av[u] * x[u].w;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      *reinterpret_cast<float4*>(sY + b * 256 + (4 * ti + r) * 16 + 4 * tj) = make_float4(y[r][0], y[r][1], y[r][2], y[r][3]);
+  }
+  __syncthreads();
+  if (act) {
+    float x[4][4] = {};
+    const float* drow = sX + (16 * rb + 4 * ti) * kPadA + 16 * rb;
+#pragma unroll
+    for (int mm = 0; mm < 16; mm += 4) {
+      float4 d[4], yv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) d[r] = *reinterpret_cast<const float4*>(drow + r * kPadA + mm);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) yv[u] = *reinterpret_cast<const float4*>(sY + b * 256 + (mm + u) * 16 + 4 * tj);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float dv[4] = {d[r].x, d[r].y, d[r].z, d[r].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          x[r][0] -= dv[u] * yv[u].x;
+          x[r][1] -= dv[u] * yv[u].y;
+          x[r][2] -= dv[u] * yv[u].z;
+          x[r][3] -= dv[u] * yv[u].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      *reinterpret_cast<float4*>(sX + (16 * rb + 4 * ti + r) * kPadA + 16 * b + 4 * tj) =
+          make_float4(x[r][0], x[r][1], x[r][2], x[r][3]);
+  }
   __syncthreads();
 }
 
-// (a) [K; Q] K^T -> G (lanes 0-63), P (lanes 64-127) at TMEM column 0, bf16 operands.
-__device__ __forceinline__ bool prep_mma_a(Ctx& c) {
-  if (c.tid == 0) {
-    tc::fence_after_sync();
-    const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC);
-    for (int j = 0; j < kD / 16; ++j)
-      tc::mma_ss<tc::kBF16>(c.tb + kPColGP, desc(c.sKQ, j * 256, kSboKQ), desc(c.sKQ, j * 256, kSboKQ), id, j > 0);
-    tc::mma_commit(c.bar);
-  }
-  return mma_wait(c);
-}
-
-// diag(g r_q) Q, tf32, into q_dst (record layout) from the bf16 Q rows, with
-// the decay g of scalar block s_g (thread -> token i, 32-dim quarter).  No barrier.
-__device__ __forceinline__ void prep_qtilde(const Ctx& c, const float* s_g, unsigned char* q_dst) {
-  const int i = c.tid >> 2;
-  const int c0 = (c.tid & 3) * 32;
-  const float sq = s_g[i] * c.s_rq[i];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(c.sKQ + tc::kmajor_offset(kC + i, c0 + m * 8, 2, kSboKQ));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    float x[8];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(h[e]);
-      x[2 * e] = tc::to_tf32(f.x * sq);
-      x[2 * e + 1] = tc::to_tf32(f.y * sq);
-    }
-    *reinterpret_cast<float4*>(at(q_dst, i, c0 + m * 8, kSbo128)) = make_float4(x[0], x[1], x[2], x[3]);
-    *reinterpret_cast<float4*>(at(q_dst, i, c0 + m * 8 + 4, kSbo128)) = make_float4(x[4], x[5], x[6], x[7]);
-  }
-}
-
-// Columns of V (is_k false) or K read from global two at a time (4-byte
-// loads), scaled per token by scale[], stored as rows of the transposed
-// operand (K-major, 64 tokens wide) at dst, and when dst2 is set scaled by
-// scale2[] into dst2 too.  All 256 threads: column pair tid & 63, token
-// quarter tid >> 6 (16 loads in flight per thread).
-__device__ __forceinline__ void prep_columns(const ChunkParams& p, const Ctx& c, long long t0, int nvalid, bool is_k,
-                                             const float* scale, unsigned char* dst, const float* scale2,
-                                             unsigned char* dst2) {
-  const int cc = 2 * (c.tid & 63);
-  const int tq = c.tid >> 6;
-  const long long stride = is_k ? p.k_stride : p.v_stride;
-  const __nv_bfloat16* src = (is_k ? p.k + c.kh * kD : p.v + c.h * kD) + cc + (t0 + tq * 16) * stride;
-  const int nv = nvalid - tq * 16;
-  __nv_bfloat162 raw[16];                   // all loads in flight before any use
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-    raw[j] = j < nv ? *reinterpret_cast<const __nv_bfloat162*>(src + j * stride) : __floats2bfloat162_rn(0.f, 0.f);
-#pragma unroll
-  for (int j = 0; j < 16; j += 4) {
-    float x0[4], x1[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float s = scale[tq * 16 + j + e];
-      const float2 f = __bfloat1622float2(raw[j + e]);
-      x0[e] = tc::to_tf32(f.x * s);
-      x1[e] = tc::to_tf32(f.y * s);
-    }
-    *reinterpret_cast<float4*>(at(dst, cc, tq * 16 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-    *reinterpret_cast<float4*>(at(dst, cc + 1, tq * 16 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
-    if (dst2) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float s = scale2[tq * 16 + j + e];
-        const float2 f = __bfloat1622float2(raw[j + e]);
-        x0[e] = tc::to_tf32(f.x * s);
-        x1[e] = tc::to_tf32(f.y * s);
-      }
-      *reinterpret_cast<float4*>(at(dst2, cc, tq * 16 + j, kSbo64)) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-      *reinterpret_cast<float4*>(at(dst2, cc + 1, tq * 16 + j, kSbo64)) = make_float4(x1[0], x1[1], x1[2], x1[3]);
-    }
-  }
-}
-
-// (b) U0^T = V^T diag(beta) T^-T, or (c) W^T = K^T diag(beta g r_k) T^-T:
-// M = 128 (Dv resp. Dk rows) x N = 64 tokens with T^-1 as the B operand.
-__device__ __forceinline__ bool prep_mma_uw(Ctx& c) {
-  if (c.tid == 0) {
-    tc::fence_after_sync();
-    const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
-    for (int j = 0; j < kC / 8; ++j)
-      tc::mma_ss<tc::kTF32>(c.tb + kPColUW, desc(c.sVt, j * 256, kSbo64), desc(c.sTi, j * 256, kSbo64), id, j > 0);
-    tc::mma_commit(c.bar);
-  }
-  return mma_wait(c);
-}
-
-// U0^T rows into the record by column quads (conflict-free reads for the scan
-// kernel's threads), or W^T columns, negated, into the record's K-major W
-// (token rows).
-__device__ __forceinline__ void prep_epi_uw(Ctx& c, unsigned char* rec, bool is_w) {
-  float u[32];
-  tmem_ld<32>(c.tb + kPColUW + c.my + c.half * 32, u);
-  if (!is_w) {
-    float4* ud = reinterpret_cast<float4*>(rec + kRecU);
-#pragma unroll
-    for (int e = 0; e < 32; e += 4)
-      ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
-  } else {
-#pragma unroll
-    for (int e = 0; e < 32; ++e) *at(rec + kRecW, c.half * 32 + e, c.row, kSbo128) = -tc::to_tf32(u[e]);
-    if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
-  }
-}
-
-// One CTA per (chunk, key head) handles the hpc value heads that share that
-// key head (hpc = Hv / Hk when it is at most kPrepHeads, else one): the K / Q
-// rows, their norms and [K; Q] K^T are formed once; gates, A, the solve, M,
-// and per value head the V pass (U0) then the K pass (W, K-hat) through one
-// 32 KiB operand buffer and one accumulator, so that three CTAs fit on an SM.
-__global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkParams p, int hpc) {
+// One CTA per (chunk, value head), value head fastest in the grid so that the
+// CTAs sharing a key head read its K / Q rows from L2.  Phases:
+//   rows of K, Q (cp.async) | gates -> norms, Q-tilde to the record ->
+//   G | P = [K; Q] K^T (kind::f16, exact bf16 operands) -> A (shared memory),
+//   M to the record; V rows (cp.async) -> T^-1 = (I + A)^-1 blocked: the 16 x 16
+//   diagonal blocks by substitution while the other warps write K-hat^T to the
+//   record, then three levels of block products -> the U0 / W right-hand
+//   operands diag(beta) T^-T and diag(beta g r_k) T^-T as bf16 hi + lo pairs
+//   (x = hi + lo to 2^-16 relative) -> U0^T = V^T B_U, W^T = K^T B_W
+//   (kind::f16, V^T and K^T MN-major straight from the rows) -> the record.
+__global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  const long long slot = blockIdx.x;
-  int* s_bc = reinterpret_cast<int*>(sm + kPBar + 16);
+  const long long unit = blockIdx.x;
+  const long long slot = unit / p.Hv;
+  int* s_bc = reinterpret_cast<int*>(sm + kQBar + 16);
   if (threadIdx.x == 0) {
     int b = 0, ch = 0;
     const bool used = slot_to_chunk(p, slot, b, ch);
@@ -1028,72 +991,293 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   const int b = s_bc[0];
   if (b < 0) return;
   const int ch = s_bc[1];
-  const int h0 = blockIdx.y * hpc;
   Ctx c;
-  ctx_init(c, p, h0);
-  ctx_prep_layout(c, sm);
-  float* sc0 = reinterpret_cast<float*>(sm + kPSc);
-  auto head_scalars = [&](int j) {             // scalar block of head j; the norms live in block 0
-    ctx_scalars(c, sc0 + j * 10 * kC);
-    c.s_rk = sc0 + 320;
-    c.s_rq = sc0 + 384;
-  };
-  auto head_gates = [&](int j) {               // per-head constants of value head h0 + j
-    c.h = h0 + j;
-    c.A_h = expf(__ldg(p.A_log + c.h));
-    c.dtb = __ldg(p.dt_bias + c.h);
-  };
+  ctx_init(c, p, static_cast<int>(unit - slot * p.Hv));
+  ctx_scalars(c, reinterpret_cast<float*>(sm + kQSc));
+  c.bar = reinterpret_cast<uint64_t*>(sm + kQBar);
+  unsigned char* sK = sm + kQK;
+  unsigned char* sQ = sm + kQQ;   // then V
+  float* sA = reinterpret_cast<float*>(sm + kQA);
+  float* sX = reinterpret_cast<float*>(sm + kQX);
+  float* sY = reinterpret_cast<float*>(sm + kQY);
   long long s0, s1;
   seq_range(p, b, s0, s1);
   const long long t0 = s0 + static_cast<long long>(ch) * kC;
   const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kPBar + 8), c.bar, 1, kPrepTmemCols);
+  unsigned char* rec = record(p, slot, c.h);
 
-  for (int j = 0; j < hpc; ++j) {              // gates of every value head first
-    head_scalars(j);
-    head_gates(j);
-    phase_gates(p, c, t0, nvalid);
-  }
+  prep_copy_rows(sK, p.k + t0 * p.k_stride + c.kh * kD, p.k_stride, nvalid, c.warp, c.lane);
+  prep_copy_rows(sQ, p.q + t0 * p.q_stride + c.kh * kD, p.q_stride, nvalid, c.warp, c.lane);
+  ptx::cp_async_commit();
+  tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kQBar + 8), c.bar, 1, kPrepTmemCols);
+  phase_gates(p, c, t0, nvalid);
+  ptx::cp_async_wait<0>();
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
   GDN_TICK(16);
-  head_scalars(0);
-  prep_rows(p, c, t0, s0, nvalid);             // shared K / Q rows and norms (ends with a barrier)
-  GDN_TICK(17);
-  bool ok = prep_mma_a(c);                     // G | P, shared, kept in TMEM for every head
-  GDN_TICK(18);
-  for (int j = 0; j < hpc && ok; ++j) {
-    head_scalars(j);
-    head_gates(j);
-    unsigned char* rec = record(p, slot, c.h);
-    if (j == 0) {                              // the Q rows are overwritten by A: Q-tilde for all heads now
-      for (int jj = 0; jj < hpc; ++jj) prep_qtilde(c, sc0 + jj * 10 * kC + 128, record(p, slot, h0 + jj) + kRecQ);
-      __syncthreads();
-      GDN_TICK(30);
+
+  // norms (thread: token i = 8 warp + lane % 8, 32-dim quarter qd = lane / 8,
+  // so that the 8 lanes of each 16-byte shared-memory wavefront read 8
+  // distinct rows), the per-token scales of the record's K-hat^T and of W's
+  // right-hand side, Q-tilde to the record
+  {
+    const int i = c.warp * 8 + (c.lane & 7), qd = c.lane >> 3;
+    uint4 kr[4], qr[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      kr[m] = *reinterpret_cast<const uint4*>(sK + tc::kmajor_offset(i, qd * 32 + m * 8, 2, kSboKQ));
+      qr[m] = *reinterpret_cast<const uint4*>(sQ + tc::kmajor_offset(i, qd * 32 + m * 8, 2, kSboKQ));
     }
-    phase_epi_a(c, kPColGP, rec + kRecM, nullptr);     // A over the rows; M to the record
-    GDN_TICK(19);
-    phase_solve(c);                                    // X, then T^-1
-    GDN_TICK(20);
-    if (c.tid < kC) {
-      c.s_kw[c.tid] = c.s_beta[c.tid] * c.s_g[c.tid] * c.s_rk[c.tid];
-      c.s_kh[c.tid] = c.s_ratio[c.tid] * c.s_rk[c.tid];
+    float sk = 0.f, sq = 0.f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const __nv_bfloat162* hk = reinterpret_cast<const __nv_bfloat162*>(&kr[m]);
+      const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&qr[m]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fk = __bfloat1622float2(hk[e]);
+        const float2 fq = __bfloat1622float2(hq[e]);
+        sk += fk.x * fk.x + fk.y * fk.y;
+        sq += fq.x * fq.x + fq.y * fq.y;
+      }
+    }
+    sk += __shfl_xor_sync(0xffffffffu, sk, 8);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 16);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 16);
+    const float rk = c.l2 ? rsqrtf(sk + 1e-6f) : 1.f;
+    const float rq = c.l2 ? rsqrtf(sq + 1e-6f) * c.qscale : 1.f;
+    if (qd == 0) {
+      c.s_rk[i] = rk;
+      c.s_rq[i] = rq;
+      c.s_kw[i] = c.s_beta[i] * c.s_g[i] * rk;
+      c.s_kh[i] = c.s_ratio[i] * rk;
+    }
+    const float s = c.s_g[i] * rq;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&qr[m]);
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(hq[e]);
+        x[2 * e] = tc::to_tf32(f.x * s);
+        x[2 * e + 1] = tc::to_tf32(f.y * s);
+      }
+      *reinterpret_cast<float4*>(at(rec + kRecQ, i, qd * 32 + m * 8, kSbo128)) = make_float4(x[0], x[1], x[2], x[3]);
+      *reinterpret_cast<float4*>(at(rec + kRecQ, i, qd * 32 + m * 8 + 4, kSbo128)) =
+          make_float4(x[4], x[5], x[6], x[7]);
+    }
+  }
+  __syncthreads();
+  GDN_TICK(17);
+
+  // (a) G | P = [K; Q] K^T at TMEM columns [0, 64)
+  if (c.tid == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC);
+    for (int j = 0; j < kD / 16; ++j)
+      tc::mma_ss<tc::kBF16>(c.tb + kPColGP, desc(sK, j * 256, kSboKQ), desc(sK, j * 256, kSboKQ), id, j > 0);
+    tc::mma_commit(c.bar);
+  }
+  bool ok = mma_wait(c);
+  GDN_TICK(18);
+  // the Q rows are no longer read: V rows into their place, landing during the solve
+  prep_copy_rows(sQ, p.v + t0 * p.v_stride + c.h * kD, p.v_stride, nvalid, c.warp, c.lane);
+  ptx::cp_async_commit();
+  GDN_TICK(8);
+  if (ok) {
+    // A (lanes 0-63, row-major) and M (lanes 64-127, to the record)
+    float gp[32];
+    tmem_ld<32>(c.tb + kPColGP + c.my + c.half * 32, gp);
+    GDN_TICK(9);
+    if (c.quarter < 2) {
+      const int i = c.row;
+      const float fi = c.s_beta[i] * c.s_rk[i];
+      const float gi = c.s_gam[i];
+      float* arow = sA + i * kPadA + c.half * 32;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
+        const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
+        const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
+        float a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = c.half * 32 + e + u;
+          a[u] = (j < i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+        }
+        *reinterpret_cast<float4*>(arow + e) = make_float4(a[0], a[1], a[2], a[3]);
+      }
+    } else {
+      const int i = c.row - kC;
+      const float fi = c.s_rq[i];
+      const float gi = c.s_gam[i];
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
+        const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
+        const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
+        float m[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = c.half * 32 + e + u;
+          m[u] = (j <= i) ? tc::to_tf32(fi * rk[u] * __expf(gi - gm[u]) * gp[e + u]) : 0.f;
+        }
+        *reinterpret_cast<float4*>(at(rec + kRecM, i, c.half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  GDN_TICK(19);
+
+  if (ok) {
+    // diagonal blocks D_bb = (I + A_bb)^-1 (warps 0-1: block bb, column cc) ...
+    if (c.tid < 64) {
+      const int bb = c.tid >> 4, cc = c.tid & 15;
+      const float* ab = sA + (16 * bb) * kPadA + 16 * bb;
+      float x[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) x[r] = (r == cc) ? 1.f : 0.f;
+#pragma unroll
+      for (int r = 0; r < 15; ++r) {
+        const float xr = x[r];
+#pragma unroll
+        for (int i = r + 1; i < 16; ++i) x[i] -= ab[i * kPadA + r] * xr;
+      }
+      float* xb = sX + (16 * bb) * kPadA + 16 * bb + cc;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) xb[r * kPadA] = x[r];
+    } else {
+      // ... while warps 2-7 write K-hat^T = K^T diag(e^{Gam_last-Gam} r_k) to the
+      // record.  Job J: the 8 x 8 core matrices (token groups 4 (J / 16) .. +3,
+      // k group J % 16) of the K rows, transposed by ldmatrix: lane L holds
+      // k = 8 kg + L / 4 at tokens 2 (L % 4), +1 of each; lanes L, L ^ 1 swap
+      // halves so that each holds 4 consecutive tokens of one matrix.
+      const int p2 = c.lane & 3;
+      const bool odd = p2 & 1;
+      for (int J = c.warp - 2; J < 32; J += kThreads / 32 - 2) {
+        const int kg = J & 15, tgb = (J >> 4) * 4;
+        uint32_t r[4];
+        ptx::ldmatrix_x4_trans(sK + (tgb + (c.lane >> 3)) * kSboKQ + kg * 128 + (c.lane & 7) * 16, r);
+        const int k = kg * 8 + (c.lane >> 2);
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const uint32_t mine = odd ? r[2 * pr + 1] : r[2 * pr];
+          const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? r[2 * pr] : r[2 * pr + 1], 1);
+          const uint32_t lo = odd ? got : mine, hi = odd ? mine : got;   // tokens t, t+1 | t+2, t+3
+          const int t = (tgb + 2 * pr + (odd ? 1 : 0)) * 8 + 2 * (p2 & 2);
+          const float4 sc = *reinterpret_cast<const float4*>(c.s_kh + t);
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
+          *reinterpret_cast<float4*>(at(rec + kRecKh, k, t, kSbo64)) =
+              make_float4(tc::to_tf32(f0.x * sc.x), tc::to_tf32(f0.y * sc.y), tc::to_tf32(f1.x * sc.z),
+                          tc::to_tf32(f1.y * sc.w));
+        }
+      }
     }
     __syncthreads();
-    for (int pass = 0; pass < 2 && ok; ++pass) {       // V: U0^T; then K: W^T (and K-hat^T to the record)
-      const bool is_k = pass == 1;
-      prep_columns(p, c, t0, nvalid, is_k, is_k ? c.s_kw : c.s_beta, c.sVt, is_k ? c.s_kh : nullptr,
-                   is_k ? rec + kRecKh : nullptr);
-      ptx::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      GDN_TICK(21);
-      ok = prep_mma_uw(c);
-      GDN_TICK(22);
-      if (ok) {
-        prep_epi_uw(c, rec, is_k);
-        tc::fence_before_sync();
-        __syncthreads();
-        GDN_TICK(23);
+    GDN_TICK(20);
+    solve_level(1, sA, sX, sY, c.tid);
+    GDN_TICK(11);
+    solve_level(2, sA, sX, sY, c.tid);
+    GDN_TICK(12);
+    solve_level(3, sA, sX, sY, c.tid);
+    GDN_TICK(13);
+
+    // right-hand operands, K-major (row j, token t), bf16 hi | lo:
+    // B_U[j][t] = beta_t X[j][t] over A, B_W[j][t] = beta_t g_t r_kt X[j][t] over X
+    uint4 uh[2], ul[2], wh[2], wl[2];
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int item = c.tid + it * kThreads;
+      const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
+      const float4 x0 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8);
+      const float4 x1 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8 + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8);
+      const float4 b1 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8 + 4);
+      const float4 w0 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8 + 4);
+      const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint32_t hu[4], lu[4], hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = tg * 8 + 2 * e;
+        const float xa = t <= j ? xs[2 * e] : 0.f, xb = t + 1 <= j ? xs[2 * e + 1] : 0.f;
+        split_bf16(xa * bs[2 * e], xb * bs[2 * e + 1], hu[e], lu[e]);
+        split_bf16(xa * ws[2 * e], xb * ws[2 * e + 1], hw[e], lw[e]);
       }
+      uh[it] = make_uint4(hu[0], hu[1], hu[2], hu[3]);
+      ul[it] = make_uint4(lu[0], lu[1], lu[2], lu[3]);
+      wh[it] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      wl[it] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    GDN_TICK(14);
+    __syncthreads();                  // every X value is read before the operands overwrite A and X
+    GDN_TICK(21);
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int item = c.tid + it * kThreads;
+      const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
+      const uint32_t off = tc::kmajor_offset(j, tg * 8, 2, kSboOp);
+      *reinterpret_cast<uint4*>(sm + kQA + off) = uh[it];
+      *reinterpret_cast<uint4*>(sm + kQA + kC * kC * 2 + off) = ul[it];
+      *reinterpret_cast<uint4*>(sm + kQX + off) = wh[it];
+      *reinterpret_cast<uint4*>(sm + kQX + kC * kC * 2 + off) = wl[it];
+    }
+  }
+  ptx::cp_async_wait<0>();            // this thread's V pieces
+  ptx::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  GDN_TICK(22);
+
+  if (ok) {
+    // U0^T = V^T B_U^T (columns [64, 128)), W^T = K^T B_W^T (columns [0, 64));
+    // A operands MN-major (LBO = one 8-token group of 128 rows, SBO 128),
+    // one MMA per 16 tokens, hi then lo
+    if (c.tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC, false, false, /*a_mn=*/true, false);
+      const uint32_t a_v = ptx::smem_u32(sQ), a_k = ptx::smem_u32(sK);
+      for (int part = 0; part < 2; ++part) {
+        const uint32_t boff = part * kC * kC * 2;
+        for (int j = 0; j < kC / 16; ++j) {
+          const uint64_t av = tc::smem_desc(a_v + j * 2 * kSboKQ, kSboKQ, 128);
+          const uint64_t ak = tc::smem_desc(a_k + j * 2 * kSboKQ, kSboKQ, 128);
+          tc::mma_ss<tc::kBF16>(c.tb + kPColU, av, desc(sm + kQA, boff + j * 256, kSboOp), id, part + j > 0);
+          tc::mma_ss<tc::kBF16>(c.tb + kPColW, ak, desc(sm + kQX, boff + j * 256, kSboOp), id, part + j > 0);
+        }
+      }
+      tc::mma_commit(c.bar);
+    }
+    ok = mma_wait(c);
+    GDN_TICK(23);
+    if (ok) {
+      float u[32], w[32];
+      tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(u));
+      tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
+      tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(w));
+      tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(w + 16));
+      tc::tmem_ld_wait();
+      float4* ud = reinterpret_cast<float4*>(rec + kRecU);      // U0^T by column quads
+#pragma unroll
+      for (int e = 0; e < 32; e += 4)
+        ud[(c.half * 8 + e / 4) * kD + c.row] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+      // -W: lane k holds W^T[k][j] for its 32 j; 4 x 4 transposes across lane
+      // quads give each lane 4 consecutive k of one j, one 16-byte store
+      const int u4 = c.lane & 3;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float v0 = w[e], v1 = w[e + 1], v2 = w[e + 2], v3 = w[e + 3];
+        quad_transpose(v0, v1, v2, v3, u4);
+        *reinterpret_cast<float4*>(at(rec + kRecW, c.half * 32 + e + u4, c.row - u4, kSbo128)) =
+            make_float4(-tc::to_tf32(v0), -tc::to_tf32(v1), -tc::to_tf32(v2), -tc::to_tf32(v3));
+      }
+      if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
     }
   }
   if (!ok) {
@@ -1102,6 +1286,7 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   }
   tc::fence_before_sync();
   __syncthreads();
+  GDN_TICK(31);
   if (c.warp == 0) tc::tmem_dealloc(c.tb, kPrepTmemCols);
 }
 
@@ -1640,10 +1825,8 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
       if (rc != GDN_OK) return rc;
     }
     if (p.n_slots > 0) {
-      const int ratio = p.Hv / p.Hk;
-      const int hpc = ratio <= kPrepHeads ? ratio : 1;
-      chunk_prep_kernel<<<dim3(static_cast<unsigned>(p.n_slots), static_cast<unsigned>(p.Hv / hpc)), kThreads,
-                          kPrepSmem, st>>>(p, hpc);
+      if (p.n_slots * p.Hv > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many (chunk, head) pairs for one launch");
+      chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * p.Hv), kThreads, kPrepSmem, st>>>(p);
       rc = cuda_status(cudaGetLastError(), "chunk prep launch");
       if (rc != GDN_OK) return rc;
     }

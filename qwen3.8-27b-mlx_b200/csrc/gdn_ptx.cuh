@@ -102,6 +102,18 @@ __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Four 8 x 8 matrices of 16-bit elements from shared memory, transposed:
+// lanes 8i .. 8i+7 give the addresses of the 16-byte rows of matrix i; lane
+// L receives in r[i] the elements (rows 2 (L % 4) and 2 (L % 4) + 1, column
+// L / 4) of matrix i -- row L / 4 of its transpose -- the lower row in the
+// low half.
+__device__ __forceinline__ void ldmatrix_x4_trans(const void* row_addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(row_addr))
+               : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (bulk copy / tensor core) reads of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

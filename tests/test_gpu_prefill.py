@@ -213,12 +213,13 @@ def test_chunked_varlen_packed(split):
 
 @pytest.mark.parametrize("lens", [[300], [130, 130, 130], [100, 0, 257, 64, 3, 1, 640]])
 def test_split_schedule_matches_fused(lens):
-    """The split schedule forms the same products as the fused kernel (W as
-    W^T = K^T diag(beta g r_k) T^-T; [K; Q] K^T from the raw bf16 rows with
-    bf16 operands where the fused kernel uses tf32 -- the same exact products,
-    summed in another order inside the tensor core), so the two agree far
-    inside the oracle bound of 2e-3 (1e-4 relative L2 here); a second call on
-    the same reused, unzeroed workspace gives the same bits as the first."""
+    """The two schedules compute the same recurrence with different operand
+    precision in one place: the fused kernel rounds T^-1 to tf32 (2^-11) for
+    U0 and W, the split prep carries diag(beta) T^-T and diag(beta g r_k) T^-T
+    as bf16 hi + lo pairs (2^-16).  So they agree to a few 1e-4 relative L2,
+    and the split result is no farther from the oracle than the fused one
+    (each sequence checked); a second call on the same reused, unzeroed
+    workspace gives the same bits as the first."""
     rng = np.random.default_rng(60 + len(lens))
     total = sum(lens)
     inp = chunk_inputs(rng, 1, total, 2, 6, slow_decay=False)
@@ -232,10 +233,25 @@ def test_split_schedule_matches_fused(lens):
     ws = torch.full((need,), 0xAB, dtype=torch.uint8, device="cuda")
     o_1, S_1 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
     o_2, S_2 = G.chunked_fwd(*args, state_in=S0, cu_seqlens=cu, split=True, workspace=ws)
-    assert O.rel_l2(host(o_1), host(o_f)) < 1e-4, O.rel_l2(host(o_1), host(o_f))
-    assert O.rel_l2(host(S_1), host(S_f)) < 1e-4, O.rel_l2(host(S_1), host(S_f))
+    assert O.rel_l2(host(o_1), host(o_f)) < 6e-4, O.rel_l2(host(o_1), host(o_f))
+    assert O.rel_l2(host(S_1), host(S_f)) < 6e-4, O.rel_l2(host(S_1), host(S_f))
     assert torch.equal(o_1, o_2) and torch.equal(S_1, S_2)
     assert G.take_device_error() == 0
+    cuh = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    for s, L in enumerate(lens):
+        if L == 0:
+            continue
+        sub = dict(inp)
+        for n in ("q", "k", "v", "a", "b"):
+            sub[n] = inp[n][:, cuh[s]:cuh[s + 1]]
+        sub["S0"] = host(S0)[s:s + 1]
+        ro, rS = oracle_chunked(sub)
+        rows = slice(cuh[s], cuh[s + 1])
+        pick = (lambda x: host(x)[rows]) if cu is not None else (lambda x: host(x)[0])  # noqa: E731
+        e_split, e_fused = O.rel_l2(pick(o_1), ro[0]), O.rel_l2(pick(o_f), ro[0])
+        assert e_split < PREFILL_TOL and e_split <= 1.1 * e_fused + 1e-5, (s, e_split, e_fused)
+        es_split, es_fused = O.rel_l2(host(S_1)[s:s + 1], rS), O.rel_l2(host(S_f)[s:s + 1], rS)
+        assert es_split < PREFILL_TOL and es_split <= 1.1 * es_fused + 1e-5, (s, es_split, es_fused)
 
 
 def test_split_schedule_rejects_a_short_or_misaligned_workspace():
