@@ -941,10 +941,11 @@ LAYER_FLOP_PER_TOKEN = 2 * HIDDEN * (2 * HK * D + 2 * HV * D + 2 * HV) + 2 * HV 
 
 
 def run_layer(args, device, world):
-    """A whole GDN layer (gdn_layer.GDNLayer) on configs 3 and 4: in_proj
-    GEMMs (cuBLAS) -> conv -> chunked recurrence with the norm (and, for N > 1,
-    the head all-gather fused into it) -> out_proj on this rank's token slice
-    (cuBLAS).  tokens/s counts every token once per max-over-ranks second;
+    """A whole GDN layer (gdn_layer.GDNLayer) on configs 3 and 4: in_proj_qkv
+    with the conv in its epilogue and in_proj_z|a|b (this library's tcgen05
+    GEMMs) -> chunked recurrence with the norm (and, for N > 1, the head
+    all-gather fused into it) -> out_proj on this rank's token slice (tcgen05
+    GEMM).  tokens/s counts every token once per max-over-ranks second;
     per-part ms and the GEMMs' TFLOP/s come from CUDA events on each rank."""
     import gdn_layer
     rank = torch.distributed.get_rank() if world > 1 else 0
@@ -979,31 +980,37 @@ def run_layer(args, device, world):
         ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
         if max_over_ranks(float(layer.gather_errors()), world, device):
             raise RuntimeError("layer gather wait timed out")
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
         ev[0].record(st)
-        qkv, z, a, b = layer.projections(x)
+        yc = layer.conv_projection(x, cu_seqlens=cu, B=B)
         ev[1].record(st)
-        out = layer.core(qkv, z, a, b, cu_seqlens=cu, B=B)
+        z, a, b = layer.projections_zab(x)
         ev[2].record(st)
-        y = out[lo:hi].reshape(hi - lo, HV * D) @ layer.W_out.t()
+        out = layer.core(yc, z, a, b, cu_seqlens=cu, B=B)
         ev[3].record(st)
+        y = layer.out_projection(out[lo:hi].reshape(hi - lo, HV * D))
+        ev[4].record(st)
         torch.cuda.synchronize(device)
-        parts = {"in_proj": ev[0].elapsed_time(ev[1]), "gdn_core": ev[1].elapsed_time(ev[2]),
-                 "out_proj": ev[2].elapsed_time(ev[3])}
-        in_flop = 2 * tokens * HIDDEN * (layer.C + layer.hv * D + 2 * layer.hv)
+        parts = {"in_proj_qkv_conv": ev[0].elapsed_time(ev[1]), "in_proj_zab": ev[1].elapsed_time(ev[2]),
+                 "gdn_core": ev[2].elapsed_time(ev[3]), "out_proj": ev[3].elapsed_time(ev[4])}
+        # the fused kernel computes 128 rows per 125 tokens (the conv halo); counted here as useful work only
+        qkv_flop = 2 * tokens * HIDDEN * layer.C
+        zab_flop = 2 * tokens * HIDDEN * (layer.hv * D + 2 * layer.hv)
         out_flop = 2 * (hi - lo) * HV * D * HIDDEN
         res[name] = {
-            "workload": (f"{name}: {B} seq, {tokens} tokens, hidden {HIDDEN}: in_proj_qkv/z/a/b (cuBLAS bf16) -> "
-                         f"conv -> chunked + gated norm" + (" + NVLink head gather" if world > 1 else "")
-                         + " -> out_proj on the rank's token slice (cuBLAS bf16)"),
+            "workload": (f"{name}: {B} seq, {tokens} tokens, hidden {HIDDEN}: in_proj_qkv with the conv + SiLU in "
+                         f"its epilogue (gdn_in_proj_conv) and in_proj_z|a|b (gdn_gemm_bf16), both tcgen05 -> "
+                         f"chunked + gated norm" + (" + NVLink head gather" if world > 1 else "")
+                         + " -> out_proj on the rank's token slice (gdn_gemm_bf16)"),
             "tokens_per_s": round(tokens / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
             "part_ms": {k: round(v, 4) for k, v in parts.items()},
-            "gemm_tflops": {"in_proj": round(in_flop / (parts["in_proj"] * 1e-3) / 1e12, 1),
+            "gemm_tflops": {"in_proj_qkv_conv": round(qkv_flop / (parts["in_proj_qkv_conv"] * 1e-3) / 1e12, 1),
+                            "in_proj_zab": round(zab_flop / (parts["in_proj_zab"] * 1e-3) / 1e12, 1),
                             "out_proj": round(out_flop / (parts["out_proj"] * 1e-3) / 1e12, 1)},
             "flop_per_token_projections": LAYER_FLOP_PER_TOKEN, "clocks": clk.summary(),
             "note": "the GEMMs hold the GPU at its power cap, so the latency-bound recurrence kernels run at the "
                     "capped SM clock here (compare prefill.kernel_ms)"}
-        del x, qkv, z, a, b, out, y
+        del x, yc, z, a, b, out, y
         torch.cuda.empty_cache()
     layer.close()
     del layer, w
@@ -1057,7 +1064,7 @@ def run_layer_decode(args, device, world, Lp=8):
     if int(err.item()):
         raise RuntimeError("decode layer recorded a slot error")
     per_layer = ms / Lp
-    out = {"workload": f"{Lp} whole layers x B={B} decode (hidden {HIDDEN}; in_proj / out_proj cuBLAS bf16, conv ring, "
+    out = {"workload": f"{Lp} whole layers x B={B} decode (hidden {HIDDEN}; in_proj / out_proj tcgen05 GEMMs, conv ring, "
                        f"state pool in random slots of {n_slots}, gated norm"
                        + (", NCCL head all-gather, token-sliced out_proj" if world > 1 else "") + ")",
            "ms_per_layer": round(per_layer, 4), "tokens_per_s_48_layers": round(B / (48 * per_layer * 1e-3), 1),

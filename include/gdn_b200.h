@@ -449,6 +449,45 @@ int gdn_gated_rmsnorm_fwd(const void* o, const void* z, const float* gamma, void
                           int D, float eps, unsigned flags, void* stream);
 
 /*
+ * gdn_gemm_bf16 -- C = A B^T on the tensor cores (tcgen05, fp32 accumulation,
+ * bf16 rounding of C): the block's plain projections, in_proj_z / in_proj_a /
+ * in_proj_b (weights cpp/src/model.cpp:174-176, applied at :608-609 and :625;
+ * python/qwen35.py:561-563, 597-598, 628) and out_proj (cpp/src/model.cpp:177,
+ * 641; python/qwen35.py:564, 640), which MLX runs as bf16 matmuls.  A (M, K) with row stride
+ * lda, B (N, K) with row stride ldb (a Linear's weight as stored), both bf16;
+ * N, K, lda, ldb multiples of 8, A and B 16-byte aligned.  C (M, ldc) bf16,
+ * 16-byte aligned, ldc a multiple of 8.  With C32 non-null, columns n_f32 ..
+ * N-1 (n_f32 a multiple of 8) are written to C32 as fp32 holding the
+ * bf16-rounded values -- the .astype(float32) of the a / b projections
+ * (cpp/src/model.cpp:608-609) -- as a stack of (M, ld32) matrices (column
+ * n_f32 + j goes to matrix j / ld32, column j % ld32; ld32 = N - n_f32 gives
+ * one (M, N - n_f32) matrix, ld32 = Hv gives a then b as two contiguous (M,
+ * Hv) arrays), and C receives columns 0 .. n_f32-1 only.
+ * Allocates nothing (the tensor maps are kernel parameters).
+ */
+int gdn_gemm_bf16(const void* A, const void* B, void* C, float* C32, int M, int N, int K, long long lda,
+                  long long ldb, long long ldc, long long ld32, int n_f32, void* stream);
+
+/*
+ * gdn_in_proj_conv -- in_proj_qkv followed by the causal depthwise conv1d
+ * (kernel 4) and SiLU in one tensor-core kernel (weights cpp/src/model.cpp:
+ * 173, applied at :586-588, DepthwiseConv cpp/src/model.cpp:385-395;
+ * python/qwen35.py:560, 577-578, 642-660):
+ *     p = bf16(x W^T)                       (the projection's own rounding)
+ *     y[t, c] = silu(sum_j w[c, j] * [window; p_seq][t + j, c]),  j = 0..3
+ * with fp32 tap arithmetic exactly as gdn_conv1d_fwd's default mode, so y is
+ * bit-identical to gdn_conv1d_fwd applied to gdn_gemm_bf16's output; the
+ * projection never reaches HBM.  x (tokens, K) bf16 with row stride ldx,
+ * packed with cu_seqlens (B+1) int32, or B sequences of T tokens when
+ * cu_seqlens is NULL; W (N, K) with row stride ldw; conv_w (N, 4) bf16;
+ * state_in / state_out (B, 3, N) bf16 carried windows (state_in NULL: zeros;
+ * state_out NULL: not written); y (tokens, ldy) bf16.  N, ldy multiples of 8.
+ */
+int gdn_in_proj_conv(const void* x, const void* W, const void* conv_w, const void* state_in, void* state_out,
+                     void* y, const int32_t* cu_seqlens, int B, int T, int N, int K, long long ldx,
+                     long long ldw, long long ldy, void* stream);
+
+/*
  * gdn_tc05_selftest -- diagnostic of the tensor-core path (no counterpart in
  * the reference): one CTA computes D (128 x N) = op(A) (128 x K) * B^T with
  * B (N x K), all row-major fp32, through tcgen05.mma into tensor memory.

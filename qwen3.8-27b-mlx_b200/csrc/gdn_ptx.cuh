@@ -114,6 +114,22 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* row_addr, uint32_t
                : "memory");
 }
 
+// 2-D tiled tensor copy global -> shared through a tensor map (no multicast:
+// this CTA only), completion counted in bytes on `bar`.  c0 is the innermost
+// coordinate (elements, 16-byte aligned), c1 the row; rows outside the
+// tensor read as zeros.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (bulk copy / tensor core) reads of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -161,6 +177,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
   return d;                             // base offset 0, layout type 0 = SWIZZLE_NONE
+}
+
+// Descriptor of a K-major operand in the 128-byte swizzled layout a tensor
+// map with CU_TENSOR_MAP_SWIZZLE_128B writes: rows of 128 bytes (64 bf16),
+// 8-row groups 1024 bytes apart, the pattern anchored at a 1024-byte aligned
+// tile base.  A K step inside the 128-byte row advances saddr by its bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused when swizzled)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2) << 61;                  // layout: 128-byte swizzle
+  return d;
 }
 
 enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };

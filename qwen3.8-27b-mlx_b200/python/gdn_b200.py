@@ -77,6 +77,8 @@ SIGNATURES = {
     "gdn_conv1d_fwd_pool": [_vp] * 5 + [_i] + [_vp] * 2 + [_i] * 4 + [_u, _vp, _vp],
     "gdn_conv_ring_append": [_vp] * 4 + [_i] + [_vp] * 2 + [_i] * 4 + [_vp, _vp],
     "gdn_gated_rmsnorm_fwd": [_vp] * 4 + [ctypes.c_longlong, _i, ctypes.c_float, _u, _vp],
+    "gdn_gemm_bf16": [_vp] * 4 + [_i] * 3 + [ctypes.c_longlong] * 4 + [_i, _vp],
+    "gdn_in_proj_conv": [_vp] * 7 + [_i] * 4 + [ctypes.c_longlong] * 3 + [_vp],
 }
 
 # return types other than int
@@ -354,6 +356,52 @@ def conv1d_fwd(x, w, state_in=None, state_out=None, y=None, cu_seqlens=None, *, 
     flags = (F_CONV_BF16_OPS if bf16_ops else 0) | (0 if silu else F_CONV_NO_SILU)
     check(lib().gdn_conv1d_fwd(ptr(x), ptr(w), ptr(state_in), ptr(state_out), ptr(y), ptr(cu_seqlens),
                                B, T, C, w.shape[1], flags, stream_ptr(dev)))
+    return y, state_out
+
+
+def gemm_bf16(A, B, C=None, n_f32=None, C32=None, f32_width=None):
+    """C = A B^T on the tensor cores (gdn_gemm_bf16): A (M, K), B (N, K) bf16,
+    fp32 accumulation, C (M, N) bf16.  With n_f32 set, columns n_f32 .. N-1
+    go to C32 as fp32 (the bf16-rounded values), as a stack of (M, f32_width)
+    matrices (default one (M, N - n_f32) matrix), and C has n_f32 columns.
+    Returns C, or (C, C32) with n_f32."""
+    M, K = A.shape
+    N = B.shape[0]
+    if B.shape[1] != K:
+        raise ValueError("A and B must share K")
+    dev = _dev(A, B, C, C32)
+    nc = N if n_f32 is None else n_f32
+    if C is None:
+        C = torch.empty((M, nc), dtype=torch.bfloat16, device=dev)
+    ld32 = 0
+    if n_f32 is not None:
+        ld32 = f32_width or (N - n_f32)
+        nblk = -(-(N - n_f32) // ld32)
+        if C32 is None:
+            C32 = torch.empty((nblk, M, ld32) if f32_width else (M, ld32), dtype=torch.float32, device=dev)
+    check(lib().gdn_gemm_bf16(ptr(A), ptr(B), ptr(C), ptr(C32), M, N, K, K, K, C.shape[1], ld32,
+                              0 if n_f32 is None else n_f32, stream_ptr(dev)))
+    return C if n_f32 is None else (C, C32)
+
+
+def in_proj_conv(x, W, conv_w, state_in=None, state_out=None, y=None, cu_seqlens=None, B=None):
+    """y = silu(conv1d(x W^T)) with the projection and the causal conv in one
+    tensor-core kernel (gdn_in_proj_conv).  x (tokens, K) bf16 packed with
+    cu_seqlens (B+1) int32, or (B, T, K); W (C, K) bf16; conv_w (C, 4) bf16;
+    state_in / state_out (B, 3, C) bf16 or None.  Returns (y, state_out)."""
+    if cu_seqlens is not None:
+        T, K = x.shape
+        Bq = cu_seqlens.numel() - 1
+        if cu_seqlens.dtype != torch.int32:
+            raise ValueError("cu_seqlens must be int32")
+    else:
+        Bq, T, K = x.shape
+    C = W.shape[0]
+    dev = _dev(x, W, conv_w, state_in, state_out, y, cu_seqlens)
+    if y is None:
+        y = torch.empty(tuple(x.shape[:-1]) + (C,), dtype=torch.bfloat16, device=dev)
+    check(lib().gdn_in_proj_conv(ptr(x), ptr(W), ptr(conv_w), ptr(state_in), ptr(state_out), ptr(y),
+                                 ptr(cu_seqlens), Bq, T, C, K, K, K, C, stream_ptr(dev)))
     return y, state_out
 
 

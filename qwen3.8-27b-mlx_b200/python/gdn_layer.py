@@ -1,23 +1,25 @@
 """One Gated DeltaNet layer around the GDN kernels: the host-side mirror of
 GatedDeltaNet::operator() (cpp/src/model.cpp:582-641; python/qwen35.py:
 575-640) for prefill and for a decode step over a serving batch's state pool,
-on this GPU's K-head shard.  Prefill:
+on this GPU's K-head shard.  Prefill, every step this library's own kernel:
 
-    qkv = in_proj_qkv(x)            bf16 GEMM (cuBLAS through torch.matmul)
-    z   = in_proj_z(x)              bf16 GEMM
-    a, b = in_proj_a(x), in_proj_b(x) -> fp32
-    y   = silu(conv1d(qkv))         gdn_conv1d_fwd
+    y   = silu(conv1d(in_proj_qkv(x)))   gdn_in_proj_conv: the tcgen05 GEMM
+                                         with the causal conv + SiLU in its
+                                         epilogue (the projection stays on chip)
+    z | a | b = in_proj_z/a/b(x)         gdn_gemm_bf16, one GEMM over the
+                                         stacked weights; a, b as fp32
     out = norm(chunked(q, k, v, a, b), z)
-                                    gdn_chunked_norm_fwd_ws, or on several ranks
-                                    gdn_chunked_norm_gather_ws + gdn_gather_wait
-                                    (every rank ends with all heads)
-    y   = out_proj(out)             bf16 GEMM on this rank's token slice
+                                         gdn_chunked_norm_fwd_ws, or on several
+                                         ranks gdn_chunked_norm_gather_ws +
+                                         gdn_gather_wait (every rank ends with
+                                         all heads)
+    y   = out_proj(out)                  gdn_gemm_bf16 on this rank's token slice
 
-The projections are plain library GEMMs.  With the heads sharded, in_proj
-needs no exchange (x is replicated and each rank produces its own channels);
-after the fused gather every rank holds all heads of every token, so each
-computes out_proj for 1/N of the tokens -- the result of a row-parallel
-out_proj followed by a reduce-scatter, with no further communication.
+With the heads sharded, in_proj needs no exchange (x is replicated and each
+rank produces its own channels); after the fused gather every rank holds all
+heads of every token, so each computes out_proj for 1/N of the tokens -- the
+result of a row-parallel out_proj followed by a reduce-scatter, with no
+further communication.
 """
 from __future__ import annotations
 
@@ -53,6 +55,8 @@ class GDNLayer:
         self._ws: Optional[torch.Tensor] = None
         self._gathers = None
         self._g_i = 0
+        # in_proj_z / in_proj_a / in_proj_b stacked: one GEMM, a and b as fp32
+        self.W_zab = torch.cat([W_z, W_a, W_b], 0).contiguous()
 
     def token_slice(self, tokens: int):
         """The rows of the layer output this rank computes."""
@@ -66,22 +70,35 @@ class GDNLayer:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
         return self._ws
 
+    def projections_zab(self, x):
+        """in_proj_z, in_proj_a, in_proj_b of x (tokens, hidden) bf16: z
+        (tokens, hv*128) bf16, a and b (tokens, hv) fp32 (one GEMM)."""
+        z, ab = G.gemm_bf16(x, self.W_zab, n_f32=self.hv * D, f32_width=self.hv)
+        return z, ab[0], ab[1]
+
     def projections(self, x):
-        """in_proj_qkv, in_proj_z, in_proj_a, in_proj_b of x (tokens, hidden) bf16."""
-        qkv = x @ self.W_qkv.t()
-        z = x @ self.W_z.t()
-        a = (x @ self.W_a.t()).float()
-        b = (x @ self.W_b.t()).float()
+        """in_proj_qkv (without the conv), in_proj_z, in_proj_a, in_proj_b of
+        x (tokens, hidden) bf16."""
+        qkv = G.gemm_bf16(x, self.W_qkv)
+        z, a, b = self.projections_zab(x)
         return qkv, z, a, b
 
-    def core(self, qkv, z, a, b, cu_seqlens=None, B: int = 1, state_out=None):
-        """conv -> chunked recurrence with the gated norm (and, on several
-        ranks, the head all-gather fused into it).  Returns (tokens, Hv, 128) bf16."""
-        tokens = qkv.shape[0]
-        dev = qkv.device
+    def conv_projection(self, x, cu_seqlens=None, B: int = 1):
+        """silu(conv1d(in_proj_qkv(x))) in one kernel: (tokens, C) bf16."""
+        if cu_seqlens is not None:
+            y, _ = G.in_proj_conv(x, self.W_qkv, self.conv_w, cu_seqlens=cu_seqlens)
+            return y
+        y, _ = G.in_proj_conv(x.view(B, x.shape[0] // B, x.shape[1]), self.W_qkv, self.conv_w)
+        return y.view(x.shape[0], self.C)
+
+    def core(self, y, z, a, b, cu_seqlens=None, B: int = 1, state_out=None):
+        """The chunked recurrence with the gated norm (and, on several ranks,
+        the head all-gather fused into it) on the conv output y (tokens, C).
+        Returns (tokens, Hv, 128) bf16."""
+        tokens = y.shape[0]
+        dev = y.device
         packed = cu_seqlens is not None
         T = tokens if packed else tokens // B
-        y, _ = G.conv1d_fwd(qkv if packed else qkv.view(B, T, qkv.shape[1]), self.conv_w, cu_seqlens=cu_seqlens)
         hk, hv, C = self.hk, self.hv, self.C
         P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         base = y.data_ptr()
@@ -113,11 +130,17 @@ class GDNLayer:
     def forward_prefill(self, x, cu_seqlens=None, B: int = 1, state_out=None):
         """The layer on x (tokens, hidden) bf16: returns (y rows of this
         rank's token slice (rows, hidden) bf16, (lo, hi))."""
-        qkv, z, a, b = self.projections(x)
-        out = self.core(qkv, z, a, b, cu_seqlens, B, state_out)
+        y = self.conv_projection(x, cu_seqlens, B)
+        z, a, b = self.projections_zab(x)
+        out = self.core(y, z, a, b, cu_seqlens, B, state_out)
         lo, hi = self.token_slice(x.shape[0])
-        y = out[lo:hi].reshape(hi - lo, self.Hv * D) @ self.W_out.t()
-        return y, (lo, hi)
+        return self.out_projection(out[lo:hi].reshape(hi - lo, self.Hv * D)), (lo, hi)
+
+    def out_projection(self, o):
+        """out_proj of (rows, Hv*128) bf16 normed head outputs."""
+        if o.shape[0] == 0:
+            return torch.empty((0, self.W_out.shape[0]), dtype=torch.bfloat16, device=o.device)
+        return G.gemm_bf16(o, self.W_out)
 
     def forward_decode(self, x, pool, slots, ring, ring_pos, err_flag=None):
         """One decode step of B sequences (x (B, hidden) bf16, one token each)
@@ -147,7 +170,7 @@ class GDNLayer:
             dist.all_gather_into_tensor(parts, normed)
             normed = parts.permute(1, 0, 2).reshape(B, self.Hv * D)
         lo, hi = self.token_slice(B)
-        return normed[lo:hi] @ self.W_out.t(), (lo, hi)
+        return self.out_projection(normed[lo:hi].contiguous()), (lo, hi)
 
     def gather_errors(self) -> int:
         return sum(int(pg.err.item()) for pg in self._gathers) if self._gathers else 0

@@ -47,8 +47,8 @@ def main():
         x = torch.randn((tokens, hidden), generator=g, device=dev).bfloat16()
         cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=dev) if packed else None
         full = gdn_layer.layer_from(w, Hk, Hv)
-        qkv, z, a, b = full.projections(x)
-        normed_full = full.core(qkv, z, a, b, cu_seqlens=cu, B=len(lens))
+        normed_full = full.core(full.conv_projection(x, cu, len(lens)), *full.projections_zab(x), cu_seqlens=cu,
+                                B=len(lens))
         y_full, _ = full.forward_prefill(x, cu_seqlens=cu, B=len(lens))
         part = gdn_layer.layer_from(w, Hk, Hv, rank, world)
         y, (lo, hi) = part.forward_prefill(x, cu_seqlens=cu, B=len(lens))

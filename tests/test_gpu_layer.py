@@ -55,8 +55,8 @@ def test_layer_prefill_matches_oracle_block(lens, packed):
     x = torch.randn((tokens, hidden), generator=g, device=dev).bfloat16()
     layer = gdn_layer.layer_from(w, Hk, Hv)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=dev) if packed else None
-    qkv, z, a, b = layer.projections(x)
-    normed = layer.core(qkv, z, a, b, cu_seqlens=cu, B=len(lens))
+    normed = layer.core(layer.conv_projection(x, cu, len(lens)), *layer.projections_zab(x), cu_seqlens=cu,
+                        B=len(lens))
     y, (lo, hi) = layer.forward_prefill(x, cu_seqlens=cu, B=len(lens))
     torch.cuda.synchronize()
     assert (lo, hi) == (0, tokens)
