@@ -38,18 +38,25 @@
 namespace gdn {
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
+constexpr int kBM = 128, kBN = 256, kBK = 64;          // accumulator rows per CTA, columns, K block
 constexpr int kGemmThreads = 192;                      // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTileA = kBM * kBK * 2;             // 16 KiB
-constexpr uint32_t kTileB = kBN * kBK * 2;             // 32 KiB
-constexpr uint32_t kOffB = kStages * kTileA;
-constexpr uint32_t kOffStage = kOffB + kStages * kTileB;   // conv row buffers (2 x 128 rows x 80 B)
 constexpr uint32_t kConvRow = 80;                      // 32 bf16 + 16 B pad: conflict-free 16-byte rows
-constexpr uint32_t kOffBars = kOffStage + 2 * kBM * kConvRow;
-constexpr uint32_t kGemmSmem = kOffBars + 128 + 1024;  // barriers; 1 KiB to align the base
 constexpr int kHalo = 3;                               // conv kernel 4 -> 3 rows before each token
-constexpr int kConvTileRows = kBM - kHalo;             // tokens written per conv tile
+constexpr int kConvTileRows = kBM - kHalo;             // tokens written per CTA tile in the conv epilogue
+
+// Shared-memory map of one CTA.  Single CTA: 4 stages of A (128 x 64) and B
+// (256 x 64).  CTA pair: 6 stages of A (128 x 64) and half of B (128 x 64).
+template <bool PAIR>
+struct Layout {
+  static constexpr int kStages = PAIR ? 6 : 4;
+  static constexpr uint32_t kTileB = (PAIR ? kBN / 2 : kBN) * kBK * 2;
+  static constexpr uint32_t kOffB = kStages * kTileA;
+  static constexpr uint32_t kOffStage = kOffB + kStages * kTileB;   // conv row buffers (2 x 128 rows x 80 B)
+  static constexpr uint32_t kOffBars = kOffStage + 2 * kBM * kConvRow;
+  static constexpr uint32_t kSmem = kOffBars + 256 + 1024;          // barriers; 1 KiB to align the base
+};
+static_assert(Layout<false>::kSmem <= 232448 && Layout<true>::kSmem <= 232448, "gemm: shared memory per CTA");
 
 struct GemmParams {
   int M, N, K;
@@ -104,19 +111,39 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, long long t, in
   mt = g * p.group + static_cast<int>(j - static_cast<long long>(nt) * bands);
 }
 
-template <bool CONV>
+// CTA pairs (PAIR): a cluster of 2 CTAs computes a 256 x 256 tile with
+// tcgen05 cta_group::2 -- each CTA loads its own 128 A rows and 128 of the
+// 256 B rows into its shared memory (no multicast), the pair's leader issues
+// the M = 256 MMAs, and each CTA's tensor memory holds its 128 accumulator
+// rows.  Both CTAs' loads complete on the leader's stage barrier; the
+// leader's commits arrive on both CTAs' stage-free and accumulator-ready
+// barriers; both CTAs' epilogue warps report a drained accumulator to the
+// leader.  Per SM this halves the B operand traffic of the single-CTA tile.
+template <bool CONV, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using L = Layout<PAIR>;
+  constexpr int kStages = L::kStages;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBars);      // [kStages] TMA -> MMA
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kOffBars);   // [kStages] TMA -> MMA (the leader's counts both CTAs)
   uint64_t* empty = full + kStages;                                 // [kStages] MMA -> TMA
   uint64_t* tfull = empty + kStages;                                // [2] MMA -> epilogue
-  uint64_t* tempty = tfull + 2;                                     // [2] epilogue -> MMA
+  uint64_t* tempty = tfull + 2;                                     // [2] epilogue -> MMA (the leader's counts both CTAs)
   volatile int* s_fail = reinterpret_cast<volatile int*>(tempty + 2);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(tempty + 3);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.K + kBK - 1) / kBK;
+  const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const long long unit = PAIR ? (blockIdx.x >> 1) : blockIdx.x;       // this CTA's (pair's) first tile
+  const long long units = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  // accumulator row 0 of this CTA: output row (plain) or token (conv, 3 halo rows first)
+  auto row_base = [&](int mt) -> long long {
+    if constexpr (CONV) return static_cast<long long>(mt) * (PAIR ? 2 * kConvTileRows : kConvTileRows) - kHalo +
+                               static_cast<long long>(rank) * kConvTileRows;
+    else return static_cast<long long>(mt) * (PAIR ? 2 * kBM : kBM) + static_cast<long long>(rank) * kBM;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -125,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(tfull + i, 1);
-      ptx::mbar_init(tempty + i, 4);
+      ptx::mbar_init(tempty + i, PAIR ? 8 : 4);
     }
     *s_fail = 0;
     ptx::fence_mbar_init();
@@ -133,15 +160,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ptx::prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tc::tmem_alloc(s_tmem, 512);
-    tc::tmem_relinquish();
+    if constexpr (PAIR) {
+      tc::tmem_alloc_pair(s_tmem, 512);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(s_tmem, 512);
+      tc::tmem_relinquish();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
+  if constexpr (PAIR) ptx::cluster_sync();     // both CTAs' barriers and tensor memory are ready
   tc::fence_after_sync();
   const uint32_t tbase = *s_tmem;
 
-  // a bounded wait that also gives up once another role has failed
+  // a bounded wait that also gives up once another role of this CTA has failed
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
     for (uint32_t i = 0; i < ptx::kSpinLimit; ++i) {
       if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -155,7 +188,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   };
 
   if (warp == 0) {
-    // ---- TMA producer ----
+    // ---- TMA producer (each CTA loads its own A rows and B rows) ----
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
@@ -163,36 +196,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int last[kStages];                         // parity of the last load into each stage, -1 for none
 #pragma unroll
       for (int i = 0; i < kStages; ++i) last[i] = -1;
-      for (long long t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (long long t = unit; t < p.tiles && ok; t += units) {
         int mt, nt;
         tile_coords(p, t, mt, nt);
-        const int row0 = CONV ? mt * kConvTileRows - kHalo : mt * kBM;
-        const int col0 = nt * kBN;
+        const int row0 = static_cast<int>(row_base(mt));
+        const int brow0 = nt * kBN + (PAIR ? static_cast<int>(rank) * (kBN / 2) : 0);
         for (int kb = 0; kb < nk; ++kb) {
           if (!wait(empty + s, ph ^ 1u)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(full + s, kTileA + kTileB);
-          ptx::tma_load_2d(sm + s * kTileA, &tmA, kb * kBK, row0, full + s);
-          ptx::tma_load_2d(sm + kOffB + s * kTileB, &tmB, kb * kBK, col0, full + s);
+          if constexpr (PAIR) {
+            const uint32_t cl_full = ptx::mapa(ptx::smem_u32(full + s), 0);
+            if (leader) ptx::mbar_arrive_expect_tx(full + s, 2 * (kTileA + L::kTileB));
+            ptx::tma_load_2d_pair(sm + s * kTileA, &tmA, kb * kBK, row0, cl_full);
+            ptx::tma_load_2d_pair(sm + L::kOffB + s * L::kTileB, &tmB, kb * kBK, brow0, cl_full);
+          } else {
+            ptx::mbar_arrive_expect_tx(full + s, kTileA + L::kTileB);
+            ptx::tma_load_2d(sm + s * kTileA, &tmA, kb * kBK, row0, full + s);
+            ptx::tma_load_2d(sm + L::kOffB + s * L::kTileB, &tmB, kb * kBK, brow0, full + s);
+          }
           last[s] = static_cast<int>(ph);
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
       }
       if (!ok) give_up();
-      // no copy may land after the CTA has exited (complete already unless a role gave up)
+      // no copy may land after the CTA has exited: the leader's stage barriers
+      // count both CTAs' copies (the peer's exit waits for the leader at the
+      // closing cluster barrier)
+      if (leader) {
 #pragma unroll
-      for (int i = 0; i < kStages; ++i)
-        if (last[i] >= 0) ptx::mbar_wait(full + i, static_cast<uint32_t>(last[i]));
+        for (int i = 0; i < kStages; ++i)
+          if (last[i] >= 0) ptx::mbar_wait(full + i, static_cast<uint32_t>(last[i]));
+      }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
-    if (lane == 0) {
+    // ---- MMA issuer (the leader's lane 0) ----
+    if (lane == 0 && leader) {
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
-      const uint32_t idesc = tc::instr_desc(tc::kBF16, kBM, kBN);
-      const uint32_t a0 = ptx::smem_u32(sm), b0 = ptx::smem_u32(sm + kOffB);
-      for (long long t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++it) {
+      const uint32_t idesc = tc::instr_desc(tc::kBF16, PAIR ? 2 * kBM : kBM, kBN);
+      const uint32_t a0 = ptx::smem_u32(sm), b0 = ptx::smem_u32(sm + L::kOffB);
+      for (long long t = unit; t < p.tiles && ok; t += units, ++it) {
         const int acc = it & 1;
         if (!wait(tempty + acc, ((it >> 1) & 1) ^ 1u)) { ok = false; break; }
         tc::fence_after_sync();
@@ -203,26 +247,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = tc::smem_desc_sw128(a0 + s * kTileA + k * 32);
-            const uint64_t bd = tc::smem_desc_sw128(b0 + s * kTileB + k * 32);
-            tc::mma_ss<tc::kBF16>(d, ad, bd, idesc, (kb | k) != 0);
+            const uint64_t bd = tc::smem_desc_sw128(b0 + s * L::kTileB + k * 32);
+            if constexpr (PAIR) tc::mma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0);
+            else tc::mma_ss<tc::kBF16>(d, ad, bd, idesc, (kb | k) != 0);
           }
-          tc::mma_commit(empty + s);           // the stage is free once these MMAs have read it
+          // the stage is free (in both CTAs) once these MMAs have read it
+          if constexpr (PAIR) tc::mma_commit_pair(empty + s, 3);
+          else tc::mma_commit(empty + s);
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
-        if (ok) tc::mma_commit(tfull + acc);   // the accumulator is complete
+        if (ok) {                               // the accumulator is complete
+          if constexpr (PAIR) tc::mma_commit_pair(tfull + acc, 3);
+          else tc::mma_commit(tfull + acc);
+        }
       }
       if (!ok) give_up();
-      // drain: every MMA issued has completed before the TMEM is released
+      // drain: every MMA issued has completed before the tensor memory is released
       if (it > 0) ptx::mbar_wait(tfull + ((it - 1) & 1), ((it - 1) >> 1) & 1);
     }
   } else {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 ----
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of this CTA ----
     const int q = warp & 3;
     const int r = q * 32 + lane;                 // accumulator row of this thread
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t cl_tempty0 = PAIR ? ptx::mapa(ptx::smem_u32(tempty), 0) : 0;
     int it = 0;
     bool ok = true;
-    for (long long t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++it) {
+    for (long long t = unit; t < p.tiles && ok; t += units, ++it) {
       const int acc = it & 1;
       int mt, nt;
       tile_coords(p, t, mt, nt);
@@ -231,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc::fence_after_sync();
       const int col0 = nt * kBN;
       if constexpr (!CONV) {
-        const long long row = static_cast<long long>(mt) * kBM + r;
+        const long long row = row_base(mt) + r;
         const bool live = row < p.M;
 #pragma unroll 1
         for (int cc = 0; cc < kBN; cc += 32) {
@@ -267,8 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        const long long t0 = static_cast<long long>(mt) * kConvTileRows - kHalo;   // token of row 0
-        const long long tok = t0 + r;
+        const long long tok = row_base(mt) + r;
         const bool out = r >= kHalo && tok < p.M;
         int seq = 0;
         long long st = 0, en = 0;
@@ -285,7 +335,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
 #pragma unroll 1
         for (int cc = 0; cc < kBN; cc += 32) {
-          unsigned char* buf = sm + kOffStage + ((cc >> 5) & 1) * (kBM * kConvRow);
+          unsigned char* buf = sm + L::kOffStage + ((cc >> 5) & 1) * (kBM * kConvRow);
           {
             float v[32];
             tc::tmem_ld16(lane_base + acc * kBN + cc, *reinterpret_cast<float(*)[16]>(v));
@@ -387,16 +437,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      // this warp is done with the accumulator
+      // this warp is done with the accumulator (the leader counts both CTAs' warps)
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(tempty + acc);
+      if (lane == 0) {
+        if constexpr (PAIR) ptx::mbar_arrive_cluster(cl_tempty0 + acc * 8);
+        else ptx::mbar_arrive(tempty + acc);
+      }
     }
     if (!ok && lane == 0) give_up();
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tbase, 512);
+  if constexpr (PAIR) ptx::cluster_sync();     // the leader's MMAs into this CTA's tensor memory are done
+  if (warp == 1) {
+    if constexpr (PAIR) tc::tmem_dealloc_pair(tbase, 512);
+    else tc::tmem_dealloc(tbase, 512);
+  }
 }
 
 // The carried conv window of empty packed sequences: state_in (or zeros)
@@ -472,39 +529,74 @@ int gemm_args(const void* A, const void* B, int M, int N, int K, long long lda, 
   return GDN_OK;
 }
 
+// Launch on a CTA pair per 256 x 256 tile when there are enough of them to
+// fill the GPU, else on single CTAs with 128 x 256 tiles.
 template <bool CONV>
 int launch_gemm(const void* A, const void* B, long long lda, long long ldb, GemmParams& p, long long a_rows,
                 cudaStream_t st) {
   static std::mutex mu;
-  static bool attr[2][64] = {{false}};
+  static bool attr[2][2][64] = {{{false}}};
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc != GDN_OK) return rc;
+  const int sms = sm_count();
+  const long long rows_per_tile = CONV ? kConvTileRows : kBM;
+  const long long pair_tiles = (p.M + 2 * rows_per_tile - 1) / (2 * rows_per_tile) * p.n_tiles;
+  const bool pair = pair_tiles >= sms / 2;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!attr[CONV][dev & 63]) {
-      rc = cuda_status(cudaFuncSetAttribute(gemm_kernel<CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(kGemmSmem)),
-                       "gemm smem attribute");
+    if (!attr[CONV][pair][dev & 63]) {
+      rc = pair ? cuda_status(cudaFuncSetAttribute(gemm_kernel<CONV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(Layout<true>::kSmem)),
+                              "gemm smem attribute")
+                : cuda_status(cudaFuncSetAttribute(gemm_kernel<CONV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(Layout<false>::kSmem)),
+                              "gemm smem attribute");
       if (rc != GDN_OK) return rc;
-      attr[CONV][dev & 63] = true;
+      attr[CONV][pair][dev & 63] = true;
     }
   }
   rc = device_error_ptr(&p.err);
   if (rc != GDN_OK) return rc;
+  p.m_tiles = static_cast<int>((p.M + (pair ? 2 : 1) * rows_per_tile - 1) / ((pair ? 2 : 1) * rows_per_tile));
+  p.tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   // B larger than ~80 MB does not stay in L2 next to the A bands in flight:
-  // group 32 bands (about 40 MB of A at K = 5120) and read B once per group
+  // group about 40 MB of A tile rows and read B once per group
   const double b_bytes = static_cast<double>(p.N) * p.K * 2;
-  p.group = b_bytes > 80e6 ? (p.m_tiles < 32 ? p.m_tiles : 32) : 1;
+  const double band_bytes = static_cast<double>((pair ? 2 : 1) * kBM) * p.K * 2;
+#ifdef GDN_GEMM_GROUP
+  p.group = GDN_GEMM_GROUP;                    // tuning builds only
+  (void)b_bytes;
+  (void)band_bytes;
+#else
+  p.group = b_bytes > 80e6 ? static_cast<int>(40e6 / band_bytes + 0.5) : 1;
+#endif
+  if (p.group > p.m_tiles) p.group = p.m_tiles;
   if (p.group < 1) p.group = 1;
   CUtensorMap ta, tb;
   rc = make_tmap(&ta, A, a_rows, p.K, lda, kBM);
   if (rc != GDN_OK) return rc;
-  rc = make_tmap(&tb, B, p.N, p.K, ldb, kBN);
+  rc = make_tmap(&tb, B, p.N, p.K, ldb, pair ? kBN / 2 : kBN);
   if (rc != GDN_OK) return rc;
-  const long long grid = p.tiles < sm_count() ? p.tiles : sm_count();
-  gemm_kernel<CONV><<<static_cast<unsigned>(grid), kGemmThreads, kGemmSmem, st>>>(ta, tb, p);
-  return cuda_status(cudaGetLastError(), "gemm launch");
+  if (!pair) {
+    const long long grid = p.tiles < sms ? p.tiles : sms;
+    gemm_kernel<CONV, false><<<static_cast<unsigned>(grid), kGemmThreads, Layout<false>::kSmem, st>>>(ta, tb, p);
+    return cuda_status(cudaGetLastError(), "gemm launch");
+  }
+  const long long pairs = p.tiles < sms / 2 ? p.tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Layout<true>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, gemm_kernel<CONV, true>, ta, tb, p), "gemm pair launch");
 }
 
 }  // namespace
@@ -530,9 +622,7 @@ extern "C" int gdn_gemm_bf16(const void* A, const void* B, void* C, float* C32, 
   p.M = M;
   p.N = N;
   p.K = K;
-  p.m_tiles = (M + kBM - 1) / kBM;
   p.n_tiles = (N + kBN - 1) / kBN;
-  p.tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   p.C = static_cast<__nv_bfloat16*>(C);
   p.ldc = ldc;
   p.C32 = C32;
@@ -563,9 +653,7 @@ extern "C" int gdn_in_proj_conv(const void* x, const void* W, const void* conv_w
   p.M = static_cast<int>(M);
   p.N = N;
   p.K = K;
-  p.m_tiles = static_cast<int>((M + kConvTileRows - 1) / kConvTileRows);
   p.n_tiles = (N + kBN - 1) / kBN;
-  p.tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   p.C = static_cast<__nv_bfloat16*>(y);
   p.ldc = ldy;
   p.conv_w = static_cast<const __nv_bfloat16*>(conv_w);

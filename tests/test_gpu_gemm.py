@@ -43,8 +43,10 @@ def _no_tf32():
     torch.backends.cuda.matmul.allow_tf32 = old
 
 
+# shapes with fewer than 74 tiles of 256 x 256 run on single CTAs (128 x 256
+# tiles), larger ones on CTA pairs (256 x 256, tcgen05 cta_group::2)
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (300, 520, 256), (129, 16, 128), (4096, 512, 6144),
-                                   (777, 1024, 5120)])
+                                   (777, 1024, 5120), (2048, 6144, 512), (3001, 2304, 1024)])
 def test_gemm_matches_fp32_matmul(M, N, K):
     g = torch.Generator(device="cuda")
     g.manual_seed(M + N + K)
@@ -106,13 +108,15 @@ def test_in_proj_conv_uniform_matches_unfused(with_state):
     assert G.take_device_error() == 0
 
 
-def test_in_proj_conv_packed_varlen_matches_unfused():
+@pytest.mark.parametrize("N", [768, 10240])
+def test_in_proj_conv_packed_varlen_matches_unfused(N):
     """Sequences shorter than the 3-row window, empty ones, and ones that cross
-    tile boundaries (125 tokens per tile)."""
+    tile boundaries (125 tokens per CTA tile, 250 per CTA pair); N = 768 runs
+    on single CTAs, N = 10240 on CTA pairs."""
     g = torch.Generator(device="cuda")
     g.manual_seed(12)
-    lens = [100, 0, 257, 1, 2, 640, 125, 126]
-    K, N = 256, 768
+    lens = [100, 0, 257, 1, 2, 640, 125, 126, 250, 251, 249]
+    K = 256
     tot = sum(lens)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device="cuda")
     x = rand_bf16((tot, K), 1.0, g)
