@@ -682,7 +682,8 @@ class PrefillLayer:
         self.o = torch.empty((self.N, hv, D), dtype=torch.float32, device=device)
         self.S = torch.empty((self.B, hv, D, D), dtype=torch.float32, device=device)
         self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
-        self.schedule = "fused"
+        self.schedule = self.base = "fused"
+        self.scan_flag = 0
         self.ws = None
         self.ws_cap = 0
         self.head0, self.hv_total = head0, hv_total if hv_total is not None else hv
@@ -701,6 +702,10 @@ class PrefillLayer:
         PeerGather buffers alternate across layers."""
         import gdn_b200 as G
         self.schedule = schedule
+        # a "_pair" suffix runs the same schedule with the scan on CTA pairs
+        self.base = schedule[:-5] if schedule.endswith("_pair") else schedule
+        self.scan_flag = G.F_SCAN_PAIR if schedule.endswith("_pair") else G.F_SCAN_SINGLE
+        schedule = self.base
         if schedule == "split_gather" and self.pgs is None:
             import gdn_shard
             self.pgs = [gdn_shard.PeerGather(self.N, self.hv_total, self.x.device) for _ in range(2)]
@@ -732,24 +737,24 @@ class PrefillLayer:
         q = ctypes.c_void_p(base)
         k = ctypes.c_void_p(base + hk * D * 2)
         v = ctypes.c_void_p(base + 2 * hk * D * 2)
-        if self.schedule == "split_gather":
+        if self.base == "split_gather":
             pg = self.pgs[self.pg_i]
             self.pg_i ^= 1
             pg.run(lib, q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias), None, P(self.S),
                    P(self.z), self.hv * D, P(self.gamma), 1e-6, self.head0, self._cu(), self.B, self.T, hk,
-                   self.hv, G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
+                   self.hv, G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
             self.pg_last = pg
             return
-        if self.schedule == "split_norm":
+        if self.base == "split_norm":
             rc = lib.gdn_chunked_norm_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log),
                                              P(self.dt_bias), None, P(self.S), P(self.z), self.hv * D,
                                              P(self.gamma), ctypes.c_float(1e-6), P(self.out), self.hv * D, 0,
-                                             self._cu(), self.B, self.T, hk, self.hv, D, D, G.F_QK_L2NORM,
-                                             P(self.ws), self.ws.numel(), h)
-        elif self.schedule == "split":
+                                             self._cu(), self.B, self.T, hk, self.hv, D, D,
+                                             G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
+        elif self.base == "split":
             rc = lib.gdn_chunked_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
                                         None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
-                                        G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
+                                        G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
         else:
             rc = lib.gdn_chunked_fwd(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
                                      None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
@@ -758,10 +763,10 @@ class PrefillLayer:
             raise RuntimeError(lib.gdn_last_error().decode())
 
     def norm(self, lib, h):
-        if self.schedule == "split_gather":
+        if self.base == "split_gather":
             self.pg_last.wait(lib, h)      # norm and gather fused into the scan; wait for every rank
             return
-        if self.schedule == "split_norm":
+        if self.base == "split_norm":
             return                         # fused into the scan
         P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         rc = lib.gdn_gated_rmsnorm_fwd(P(self.o), P(self.z), P(self.gamma), P(self.out),
@@ -801,7 +806,7 @@ def time_prefill_layer(X, lib, device, world, steps, warmup, gathered=None):
     st = torch.cuda.current_stream(device)
     h = ctypes.c_void_p(st.cuda_stream)
 
-    fused_gather = X.schedule == "split_gather"
+    fused_gather = X.base == "split_gather"
 
     def layer():
         X.step(lib, h)
@@ -854,7 +859,7 @@ def time_stack(X, lib, device, world, n_layers, gathered=None):
     (the same shapes in every layer, so one set of buffers serves them all)."""
     st = torch.cuda.current_stream(device)
     h = ctypes.c_void_p(st.cuda_stream)
-    fused_gather = X.schedule == "split_gather"
+    fused_gather = X.base == "split_gather"
     torch.cuda.synchronize(device)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -885,9 +890,10 @@ def run_prefill(args, lib, device, world):
     cases = [("config3", [args.prefill_T])]
     if not args.no_config4:
         cases.append(("config4", config4_lengths()))
-    schedules = ["fused", "split", "split_norm"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
+    schedules = (["fused", "split", "split_norm", "split_pair", "split_norm_pair"] if args.prefill_schedule == "auto"
+                 else [args.prefill_schedule])
     if world > 1 and args.prefill_schedule == "auto" and not args.no_peer_gather:
-        schedules.append("split_gather")
+        schedules += ["split_gather", "split_gather_pair"]
     for name, lens in cases:
         X = PrefillLayer(lens, device, seed=99 + rank, hk=hk, hv=hv, head0=shard.v0, hv_total=HV)
         X.ws_cap = int(args.prefill_ws_gb * 1e9)
@@ -912,14 +918,19 @@ def run_prefill(args, lib, device, world):
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
         kernel = {"fused": "chunked_kernel", "split": "chunk_prep_kernel + chunk_scan_kernel",
                   "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>",
-                  "split_gather": "chunk_prep_kernel + chunk_scan_kernel<norm, peer stores>"}[best]
+                  "split_gather": "chunk_prep_kernel + chunk_scan_kernel<norm, peer stores>",
+                  "split_pair": "chunk_prep_kernel + chunk_scan_pair_kernel (CTA pairs)",
+                  "split_norm_pair": "chunk_prep_kernel + chunk_scan_pair_kernel<norm> (CTA pairs)",
+                  "split_gather_pair": "chunk_prep_kernel + chunk_scan_pair_kernel<norm, peer stores> (CTA pairs)"
+                  }[best]
         res[name] = {
             "schedule": best,
             "ms_per_layer_by_schedule": {k: round(v[0], 4) for k, v in timed.items()},
             "workspace_bytes": int(X.ws.numel()) if X.ws is not None else 0,
             "workload": (f"{name}: {X.B} seq, {X.N} tokens, conv(C={X.C}, K=4)+SiLU -> chunked C=64 "
                          f"(Hk={hk} Hv={hv} per GPU, S0=0, in-kernel l2norm) -> gated RMSNorm"
-                         + ((" -> all-gather fused into the scan (NVLink peer stores)" if best == "split_gather"
+                         + ((" -> all-gather fused into the scan (NVLink peer stores)"
+                             if best.startswith("split_gather")
                              else " -> NCCL all-gather") if world > 1 else "")),
             ("tokens_per_s" if name == "config3" else "tokens_per_s_per_layer"): round(X.N / (ms * 1e-3), 1),
             "ms_per_layer": round(ms, 4),
@@ -1200,7 +1211,8 @@ def main():
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer prefill (projections included)")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
-    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather"],
+    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather",
+                                                   "split_pair", "split_norm_pair", "split_gather_pair"],
                     default="auto", help="chunked schedule for configs 3/4; auto times each and reports the fastest "
                     "(split_gather: N > 1 only)")
     ap.add_argument("--no-peer-gather", action="store_true",

@@ -72,6 +72,10 @@ extern "C" {
 #define GDN_F_CONV_NO_SILU  0x200u  /* conv: skip the SiLU after the convolution */
 #define GDN_F_NORM_IN_BF16  0x400u  /* gated norm: o is bf16 (default fp32) */
 #define GDN_F_NORM_OUT_F32  0x800u  /* gated norm: out is fp32 (default bf16) */
+#define GDN_F_SCAN_PAIR     0x1000u /* chunked (split schedule): run each (sequence, head) state
+                                       chain on a cluster of two CTAs, 64 value rows each */
+#define GDN_F_SCAN_SINGLE   0x2000u /* chunked (split schedule): one CTA per chain.  Neither bit:
+                                       the library chooses */
 
 /* Human-readable text of the last error on the calling thread ("" if none). */
 const char* gdn_last_error(void);
@@ -503,6 +507,19 @@ int gdn_in_proj_conv(const void* x, const void* W, const void* conv_w, const voi
  */
 int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                       int* status, void* stream);
+
+/*
+ * gdn_tc05_pair_selftest -- diagnostic of the CTA-pair tensor-core form (no
+ * counterpart in the reference): a cluster of two CTAs computes
+ * A (128 x K) * B^T, B (N x K), row-major fp32 holding tf32 values, with
+ * tcgen05.mma.cta_group::2 (M = 128): CTA r supplies A rows 64r..64r+63 and
+ * B rows (N/2)r..(N/2)r+N/2-1.  raw (2 x 128 x N/2 floats) receives each
+ * CTA's tensor memory as it lies, lane by lane, so that a test checks the
+ * accumulator layout the pair scan relies on.  N a multiple of 32 in
+ * [32, 256], K a multiple of 8 in [8, 128].  *status is set to 1 (and the
+ * device error word) if the bounded wait for the MMA timed out.
+ */
+int gdn_tc05_pair_selftest(const float* A, const float* B, float* raw, int N, int K, int* status, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

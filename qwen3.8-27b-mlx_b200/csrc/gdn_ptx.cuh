@@ -49,11 +49,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: for phases completed by arrivals of the
+// other CTA of a cluster (mbar_arrive_cluster) or by its multicast commits.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete; false once `limit`
 // polls have failed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = kSpinLimit) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
   }
   return false;
 }
@@ -144,6 +165,13 @@ __device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
 
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 32-bit load from the shared memory of a CTA of the cluster (cl_addr from mapa)
+__device__ __forceinline__ float ld_cluster_f32(uint32_t cl_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cl_addr) : "memory");
+  return v;
 }
 
 // arrive on the mbarrier at shared::cluster address cl_bar (this CTA's or a peer's)
@@ -311,6 +339,19 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, 
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::tf32 on a CTA pair.  With M = 128 each CTA supplies 64 A rows and N/2
+// B rows; each CTA's 64 x N accumulator occupies all 128 lanes over N/2
+// columns: element (m, n) at lane m, column n for n < N/2 and at lane 64 + m,
+// column n - N/2 otherwise.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -123,10 +123,101 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   if (warp == 0) tc::tmem_dealloc(base, kSelfTestCols);
 }
 
+// CTA-pair self-test: a cluster of two CTAs computes D (128 x N) = A B^T with
+// tcgen05.mma.cta_group::2 (M = 128, tf32), the form the pair scan of the
+// chunked prefill uses.  CTA r holds A rows 64r .. 64r+63 and B rows
+// (N/2) r .. (N/2) r + N/2 - 1 in its own shared memory (K-major, same
+// offsets in both CTAs); the leader issues the MMAs and commits to both
+// CTAs' barriers.  Each CTA writes its tensor memory as it lies -- 128 lanes
+// x N/2 columns -- to raw[r], so the host checks the accumulator layout.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128)
+    tc05_pair_selftest_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ raw,
+                              int N, int K, int* __restrict__ status, int* __restrict__ dev_err) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const uint32_t rank = ptx::cluster_ctarank();
+  const uint32_t kbytes = static_cast<uint32_t>(K * 4);
+  const uint32_t sbo = (kbytes / 16) * 128;
+  const int nh = N / 2;
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + 64 * kbytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sB + static_cast<size_t>(nh) * kbytes);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  for (int idx = tid; idx < 64 * K; idx += 128) {
+    const int r = idx / K, k = idx - r * K;
+    *reinterpret_cast<float*>(sA + tc::kmajor_offset(r, k, 4, sbo)) = A[(64 * rank + r) * K + k];
+  }
+  for (int idx = tid; idx < nh * K; idx += 128) {
+    const int r = idx / K, k = idx - r * K;
+    *reinterpret_cast<float*>(sB + tc::kmajor_offset(r, k, 4, sbo)) = B[(nh * rank + r) * K + k];
+  }
+  ptx::fence_proxy_async_smem();
+  if (warp == 0) {
+    tc::tmem_alloc_pair(slot, 128);
+    tc::tmem_relinquish_pair();
+  }
+  if (tid == 0) {
+    ptx::mbar_init(bar, 1);
+    ptx::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  ptx::cluster_sync();                 // both CTAs' operands, barrier and tensor memory are ready
+  tc::fence_after_sync();
+  const uint32_t tD = *slot;
+  if (rank == 0 && tid == 0) {
+    const uint32_t idesc = tc::instr_desc(tc::kTF32, 128, N);
+    for (int j = 0; j < K / 8; ++j)
+      tc::mma_tf32_pair(tD, tc::smem_desc(ptx::smem_u32(sA) + j * 256, 128, sbo),
+                        tc::smem_desc(ptx::smem_u32(sB) + j * 256, 128, sbo), idesc, j > 0);
+    tc::mma_commit_pair(bar, 3);
+  }
+  const bool ok = ptx::mbar_wait_cluster(bar, 0);
+  tc::fence_after_sync();
+  if (__syncthreads_and(ok)) {
+    for (int c = 0; c < nh; c += 16) {
+      float v[16];
+      tc::tmem_ld16(tc::tmem_addr(tD, warp, c), v);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) raw[(static_cast<size_t>(rank) * 128 + tid) * nh + c + i] = v[i];
+    }
+  } else if (tid == 0) {
+    *status = 1;
+    atomicExch(dev_err, 1);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  ptx::cluster_sync();                 // no CTA frees its tensor memory or exits while the pair is busy
+  if (warp == 0) tc::tmem_dealloc_pair(tD, 128);
+}
+
 }  // namespace
 }  // namespace gdn
 
 using namespace gdn;
+
+extern "C" int gdn_tc05_pair_selftest(const float* A, const float* B, float* raw, int N, int K, int* status,
+                                      void* stream) {
+  clear_error();
+  if (N < 32 || N > 256 || N % 32 || K < 8 || K > 128 || K % 8)
+    return fail(GDN_ERR_SHAPE, "N=%d K=%d: need N a multiple of 32 in [32, 256], K a multiple of 8 in [8, 128]", N,
+                K);
+  if (!A || !B || !raw || !status) return fail(GDN_ERR_NULL, "A, B, raw and status are required");
+  if (!aligned(A, 4) || !aligned(B, 4) || !aligned(raw, 4) || !aligned(status, 4))
+    return fail(GDN_ERR_ALIGN, "buffers must be 4-byte aligned");
+  const size_t smem = static_cast<size_t>(64 + N / 2) * K * 4 + 16;
+  int* dev_err = nullptr;
+  int rc = device_error_ptr(&dev_err);
+  if (rc != GDN_OK) return rc;
+  rc = cuda_status(cudaFuncSetAttribute(tc05_pair_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "tc05 pair self-test smem attribute");
+  if (rc != GDN_OK) return rc;
+  tc05_pair_selftest_kernel<<<2, 128, smem, static_cast<cudaStream_t>(stream)>>>(A, B, raw, N, K, status, dev_err);
+  return cuda_status(cudaGetLastError(), "tc05 pair self-test launch");
+}
 
 extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                                  int* status, void* stream) {

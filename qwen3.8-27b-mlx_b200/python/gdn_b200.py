@@ -37,6 +37,9 @@ F_CONV_BF16_OPS = 0x100
 F_CONV_NO_SILU = 0x200
 F_NORM_IN_BF16 = 0x400
 F_NORM_OUT_F32 = 0x800
+F_SCAN_PAIR = 0x1000
+F_SCAN_SINGLE = 0x2000
+_SCAN_FLAGS = {None: 0, "pair": F_SCAN_PAIR, "single": F_SCAN_SINGLE}
 
 D = 128
 
@@ -54,6 +57,7 @@ SIGNATURES = {
     "gdn_recurrent_fwd_pool": [_vp] * 9 + [_i] + [_vp] * 2 + [_i, _i] + [_vp] * 3 + [_i] * 6 + [_u, _vp],
     "gdn_delta_run": [_vp] * 9 + [_i] * 5 + [_vp],
     "gdn_tc05_selftest": [_vp] * 3 + [_i] * 3 + [_vp, _vp],
+    "gdn_tc05_pair_selftest": [_vp] * 3 + [_i] * 2 + [_vp, _vp],
     "gdn_conv1d_fwd": [_vp] * 6 + [_i] * 4 + [_u, _vp],
     "gdn_chunked_fwd": [_vp] * 3 + [ctypes.c_longlong] * 3 + [_vp] * 8 + [_i] * 6 + [_u, _vp],
     "gdn_chunked_workspace_bytes": [_i] * 4,
@@ -283,12 +287,26 @@ def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=Fal
     return D, status
 
 
+def tc05_pair_selftest(A, B):
+    """A @ B.T on a CTA pair through tcgen05 cta_group::2, M = 128 (diagnostic).
+    A (128,K), B (N,K) fp32 CUDA tensors holding tf32 values.  Returns
+    (raw, status): raw (2, 128, N/2) is each CTA's tensor memory, lane by
+    lane."""
+    dev = _dev(A, B)
+    N, K = B.shape
+    raw = torch.full((2, 128, N // 2), float("nan"), dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib().gdn_tc05_pair_selftest(ptr(A), ptr(B), ptr(raw), N, K, ptr(status), stream_ptr(dev)))
+    return raw, status
+
+
 def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, state_out=None, out=None,
-                     cu_seqlens=None, *, eps=1e-6, l2norm=True, out_head0=0, workspace=None):
+                     cu_seqlens=None, *, eps=1e-6, l2norm=True, out_head0=0, workspace=None, scan=None):
     """Chunked prefill with the gated RMSNorm fused in (gdn_chunked_norm_fwd_ws).
     q, k, v as chunked_fwd; z (..., Hv, 128) bf16 with contiguous heads;
     gamma (128,) fp32.  out: bf16 (..., H_out, 128) with H_out >= out_head0 +
-    Hv (allocated as (..., Hv, 128) when None).  Returns (out, state_out)."""
+    Hv (allocated as (..., Hv, 128) when None).  scan as chunked_fwd.
+    Returns (out, state_out)."""
     Hk, Hv = q.shape[-2], v.shape[-2]
     for t in (q, k, v, z):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
@@ -315,7 +333,8 @@ def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, sta
     check(lib().gdn_chunked_norm_fwd_ws(ptr(q), ptr(k), ptr(v), q.stride(-3), k.stride(-3), v.stride(-3), ptr(a),
                                         ptr(b), ptr(A_log), ptr(dt_bias), ptr(state_in), ptr(state_out), ptr(z),
                                         z.stride(-3), ptr(gamma), eps, ptr(out), out.stride(-3), out_head0,
-                                        ptr(cu_seqlens), B, T, Hk, Hv, D, D, F_QK_L2NORM if l2norm else 0,
+                                        ptr(cu_seqlens), B, T, Hk, Hv, D, D,
+                                        (F_QK_L2NORM if l2norm else 0) | _SCAN_FLAGS[scan],
                                         ptr(workspace), workspace.numel(), stream_ptr(dev)))
     return out, state_out
 
@@ -440,13 +459,14 @@ def chunked_workspace_min_bytes(B, Hv, has_state_out=True) -> int:
 
 
 def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=None, cu_seqlens=None, *,
-                l2norm=True, o_dtype=torch.float32, B=None, T=None, split=False, workspace=None):
+                l2norm=True, o_dtype=torch.float32, B=None, T=None, split=False, workspace=None, scan=None):
     """Chunked prefill.  q, k: (..., Hk, 128) bf16 views of token-major rows
     (any token stride); v: (..., Hv, 128).  Leading dims are (B, T) or, with
     cu_seqlens, (total,).  split=False runs gdn_chunked_fwd (one launch, no
     scratch); split=True runs gdn_chunked_fwd_ws on `workspace` (a uint8 CUDA
     tensor of at least chunked_workspace_bytes(...) bytes, allocated here
-    when None).  Returns (o, state_out)."""
+    when None); its state scan runs on CTA pairs (scan="pair"), one CTA per
+    chain ("single") or as the library chooses (None).  Returns (o, state_out)."""
     Hk, Hv = q.shape[-2], v.shape[-2]
     for t in (q, k, v):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
@@ -466,7 +486,7 @@ def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=
         o = torch.empty(lead + (Hv, D), dtype=o_dtype, device=dev)
     if state_out is None:
         state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
-    flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0)
+    flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0) | _SCAN_FLAGS[scan]
     if not split:
         check(lib().gdn_chunked_fwd(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
                                     ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,

@@ -59,3 +59,24 @@ def test_tc05_wide_n_and_column_offsets(N, K, mode, d_col):
     ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
     assert int(st.item()) == 0
     assert O.rel_err(D.cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.parametrize("N,K", [(64, 128), (128, 64), (256, 32), (64, 8)])
+def test_tc05_pair_accumulator_layout(N, K):
+    """The CTA-pair MMA (cta_group::2, M = 128) of the pair scan: CTA r's
+    64 x N accumulator (rows 64r..64r+63 of D) lies at lane m, column n for
+    n < N/2 and at lane 64 + m, column n - N/2 for the rest."""
+    g = torch.Generator(device="cuda").manual_seed(N * 31 + K)
+    A = tf32(torch.randn((128, K), generator=g, device="cuda"))
+    B = tf32(torch.randn((N, K), generator=g, device="cuda"))
+    raw, st = G.tc05_pair_selftest(A, B)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    raw = raw.cpu().numpy()
+    ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
+    nh = N // 2
+    D = np.empty((128, N))
+    for r in range(2):
+        D[64 * r:64 * r + 64, :nh] = raw[r, :64]
+        D[64 * r:64 * r + 64, nh:] = raw[r, 64:]
+    assert O.rel_err(D, ref) < 1e-5
