@@ -2280,8 +2280,6 @@ bool plan_split(int B, int T, int Hv, bool packed, bool has_state_out, size_t ws
   return true;
 }
 
-// Launch the split schedule, window by window, on a workspace of ws_size bytes
-// (at least workspace_min_bytes()).
 // The scan on CTA pairs (chunk_scan_pair_kernel) or one CTA per chain
 // (chunk_scan_kernel): the caller's flag, else the library's choice.
 bool scan_on_pairs(const ChunkParams& p) {
@@ -2290,6 +2288,37 @@ bool scan_on_pairs(const ChunkParams& p) {
   return false;
 }
 
+// One window's launches: the chunk prefix (packed), the prep, the scan.
+int launch_window(ChunkParams p, int T, int w, int win_len, bool pair, cudaStream_t st) {
+  const bool packed = p.cu != nullptr;
+  const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
+  p.win_c0 = w * win_len;
+  const long long left = nch - p.win_c0;
+  p.nch_uniform = packed ? 0 : static_cast<int>(left < win_len ? left : win_len);
+  p.n_slots = packed ? window_slots(p.B, T, true, win_len) : static_cast<long long>(p.B) * p.nch_uniform;
+  if (p.n_slots > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
+  int rc;
+  if (packed) {
+    chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.win_c0, win_len, p.chunk_prefix);
+    rc = cuda_status(cudaGetLastError(), "chunk prefix launch");
+    if (rc != GDN_OK) return rc;
+  }
+  if (p.n_slots > 0) {
+    if (p.n_slots * p.Hv > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many (chunk, head) pairs for one launch");
+    chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * p.Hv), kThreads, kPrepSmem, st>>>(p);
+    rc = cuda_status(cudaGetLastError(), "chunk prep launch");
+    if (rc != GDN_OK) return rc;
+  }
+  const unsigned chains = static_cast<unsigned>(p.B * p.Hv);
+  if (pair && p.z) chunk_scan_pair_kernel<true><<<2 * chains, kScanThreadsNorm, kPSmemNorm, st>>>(p);
+  else if (pair) chunk_scan_pair_kernel<false><<<2 * chains, kScanThreads, kPSmem, st>>>(p);
+  else if (p.z) chunk_scan_kernel<true><<<chains, kScanThreadsNorm, kScanSmemNorm, st>>>(p);
+  else chunk_scan_kernel<false><<<chains, kScanThreads, kScanSmem, st>>>(p);
+  return cuda_status(cudaGetLastError(), "chunk scan launch");
+}
+
+// Launch the split schedule on a workspace of ws_size bytes (at least
+// workspace_min_bytes()): one pass, or windows in order on `st`.
 int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStream_t st) {
   const bool packed = p.cu != nullptr;
   SplitPlan pl;
@@ -2297,10 +2326,6 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
     return fail(GDN_ERR_SHAPE, "workspace of %zu bytes, at least %zu needed (%zu for one window)", ws_size,
                 workspace_min_bytes(p.B, p.Hv, p.state_out == nullptr), workspace_bytes(p.B, T, p.Hv, packed));
   p.ws = ws;
-  p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
-  p.rec_off = pl.rec_off;
-  p.carry = p.state_out ? p.state_out : (pl.n_windows > 1 ? reinterpret_cast<float*>(ws + pl.carry_off) : nullptr);
-  p.win_len = pl.win_len;
   static bool attr_prep[64] = {false}, attr_scan[64] = {false};
   int rc = set_smem_attr(reinterpret_cast<const void*>(chunk_prep_kernel), kPrepSmem, attr_prep);
   if (rc != GDN_OK) return rc;
@@ -2316,30 +2341,12 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
              : set_smem_attr(reinterpret_cast<const void*>(chunk_scan_pair_kernel<false>), kPSmem, attr_pair);
     if (rc != GDN_OK) return rc;
   }
-  const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
+  p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
+  p.rec_off = pl.rec_off;
+  p.carry = p.state_out ? p.state_out : (pl.n_windows > 1 ? reinterpret_cast<float*>(ws + pl.carry_off) : nullptr);
+  p.win_len = pl.win_len;
   for (int w = 0; w < pl.n_windows; ++w) {
-    p.win_c0 = w * pl.win_len;
-    const long long left = nch - p.win_c0;
-    p.nch_uniform = packed ? 0 : static_cast<int>(left < pl.win_len ? left : pl.win_len);
-    p.n_slots = packed ? window_slots(p.B, T, true, pl.win_len) : static_cast<long long>(p.B) * p.nch_uniform;
-    if (p.n_slots > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many chunks for one launch");
-    if (packed) {
-      chunk_prefix_kernel<<<1, 1024, 0, st>>>(p.cu, p.B, p.win_c0, pl.win_len, p.chunk_prefix);
-      rc = cuda_status(cudaGetLastError(), "chunk prefix launch");
-      if (rc != GDN_OK) return rc;
-    }
-    if (p.n_slots > 0) {
-      if (p.n_slots * p.Hv > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many (chunk, head) pairs for one launch");
-      chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * p.Hv), kThreads, kPrepSmem, st>>>(p);
-      rc = cuda_status(cudaGetLastError(), "chunk prep launch");
-      if (rc != GDN_OK) return rc;
-    }
-    const unsigned chains = static_cast<unsigned>(p.B * p.Hv);
-    if (pair && p.z) chunk_scan_pair_kernel<true><<<2 * chains, kScanThreadsNorm, kPSmemNorm, st>>>(p);
-    else if (pair) chunk_scan_pair_kernel<false><<<2 * chains, kScanThreads, kPSmem, st>>>(p);
-    else if (p.z) chunk_scan_kernel<true><<<chains, kScanThreadsNorm, kScanSmemNorm, st>>>(p);
-    else chunk_scan_kernel<false><<<chains, kScanThreads, kScanSmem, st>>>(p);
-    rc = cuda_status(cudaGetLastError(), "chunk scan launch");
+    rc = launch_window(p, T, w, pl.win_len, pair, st);
     if (rc != GDN_OK) return rc;
   }
   return GDN_OK;

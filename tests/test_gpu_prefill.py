@@ -584,3 +584,4 @@ def test_pair_scan_matches_single_scan(lens, slow):
     ro, rS = oracle_chunked(sub)
     assert O.rel_l2(host(o_p)[cuh[s]:cuh[s + 1]], ro[0]) < PREFILL_TOL
     assert O.rel_l2(host(S_p)[s:s + 1], rS) < PREFILL_TOL
+
