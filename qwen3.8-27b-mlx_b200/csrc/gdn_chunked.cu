@@ -96,8 +96,8 @@ constexpr uint32_t kQK = 0;                         // K rows, bf16 (16 KiB)
 constexpr uint32_t kQQ = kQK + kC * kD * 2;         // Q rows (16 KiB); V rows once G | P and Q-tilde are done
 constexpr uint32_t kQA = kQQ + kC * kD * 2;         // A, row-major, row stride kPadA; then the U0 operand hi | lo
 constexpr uint32_t kQX = kQA + kC * kPadA * 4;      // X = T^-1, row-major, row stride kPadA; then the W operand hi | lo
-constexpr uint32_t kQY = kQX + kC * kPadA * 4;      // level products of the blocked solve, 3 x 16 x 16
-constexpr uint32_t kQSc = kQY + 3 * 256 * 4;        // per-token scalars, 10 x 64
+constexpr uint32_t kQY = kQX + kC * kPadA * 4;      // products of the blocked solve, 1024 floats
+constexpr uint32_t kQSc = kQY + 1024 * 4;           // per-token scalars, 10 x 64
 constexpr uint32_t kQBar = kQSc + 10 * kC * 4;      // mbarrier, TMEM base, (sequence, chunk) broadcast
 constexpr uint32_t kPrepSmem = kQBar + 64;
 constexpr uint32_t kSboOp = (kC * 2 / 16) * 128;    // 8-row group stride of the 64-token bf16 operands (1024)
@@ -388,13 +388,14 @@ __device__ __forceinline__ bool mma_wait(Ctx& c, bool ok_in = true) {
 
 // Gates and the in-chunk decay prefix.  s_g, s_ratio, s_misc[0] are written by
 // threads 0-63 without a trailing barrier (the next phase ends with one).
-__device__ __forceinline__ void phase_gates(const ChunkParams& p, Ctx& c, long long t0, int nvalid) {
+// The same from gate inputs already loaded: thread i < 64 holds token i's a
+// and b (valid: i < nvalid).
+__device__ __forceinline__ void phase_gates_from(Ctx& c, float a_in, float b_in, bool valid) {
   if (c.tid < kC) {
     float lg = 0.f, beta = 0.f;
-    if (c.tid < nvalid) {
-      const size_t gi = static_cast<size_t>(t0 + c.tid) * p.Hv + c.h;
-      lg = fmaxf(-(c.A_h * softplus_f(__ldg(p.a + gi) + c.dtb)), c.log_clip);
-      beta = 1.f / (1.f + expf(-__ldg(p.b + gi)));
+    if (valid) {
+      lg = fmaxf(-(c.A_h * softplus_f(a_in + c.dtb)), c.log_clip);
+      beta = 1.f / (1.f + expf(-b_in));
     }
     float x = lg;
 #pragma unroll
@@ -414,6 +415,17 @@ __device__ __forceinline__ void phase_gates(const ChunkParams& p, Ctx& c, long l
     c.s_ratio[c.tid] = expf(gl - c.s_gam[c.tid]);
     if (c.tid == 0) c.s_misc[0] = expf(gl);
   }
+}
+
+__device__ __forceinline__ void phase_gates(const ChunkParams& p, Ctx& c, long long t0, int nvalid) {
+  float a_in = 0.f, b_in = 0.f;
+  const bool valid = c.tid < kC && c.tid < nvalid;
+  if (valid) {
+    const size_t gi = static_cast<size_t>(t0 + c.tid) * p.Hv + c.h;
+    a_in = __ldg(p.a + gi);
+    b_in = __ldg(p.b + gi);
+  }
+  phase_gates_from(c, a_in, b_in, valid);
 }
 
 // Rows of K and Q (thread -> token i, 32-dim quarter) into [K; Q], and their norms.
@@ -939,75 +951,89 @@ __device__ __forceinline__ void quad_transpose(float& v0, float& v1, float& v2, 
   if (o2) { v0 = s0; v1 = s1; } else { v2 = s0; v3 = s1; }
 }
 
-// One level of the blocked inverse X = (I + A)^-1 over 16 x 16 blocks: for
-// the 4 - lv output blocks (b + lv, b),
-//   Y = sum_{m < lv} A[b+lv][b+m] X[b+m][b],   X[b+lv][b] = -D[b+lv] Y
-// with D the (already stored) inverse diagonal blocks -- block forward
-// substitution, the same products as row-by-row substitution in another
-// order.  Thread (block b, 4 x 4 tile (ti, tj)) keeps its tile in registers
-// and reads 4 x 4 operand tiles as float4 rows; ends with a barrier.
-__device__ __forceinline__ void solve_level(int lv, const float* sA, float* sX, float* sY, int tid) {
-  const int nb = 4 - lv;
-  const bool act = tid < nb * 16;
-  const int b = tid >> 4, ti = (tid >> 2) & 3, tj = tid & 3;
-  const int rb = b + lv;
-  if (act) {
-    float y[4][4] = {};
-    for (int m = 0; m < lv; ++m) {
-      const int cb = b + m;
-      const float* arow = sA + (16 * rb + 4 * ti) * kPadA + 16 * cb;
-      const float* xrow = sX + (16 * cb) * kPadA + 16 * b + 4 * tj;
+// The rest of X = (I + A)^-1 for the unit lower-triangular 64 x 64 chunk
+// matrix, once its inverted 16 x 16 diagonal blocks D_b are in X: by doubling
+// over the 32 x 32 halves,
+//   X[2p+1][2p] = -D[2p+1] (A[2p+1][2p] D[2p])         (p = 0, 1 at once)
+//   X21         = -X22 (A21 X11)                       (32 x 32 products)
+// -- the same inverse as block forward substitution, in four rounds of
+// products in which every thread takes part (2 outputs per thread in the
+// 16 x 16 rounds, a 2 x 2 tile in the 32 x 32 ones).  Entries above the
+// diagonal of X are not stored: the products mask them.  sY holds 1024
+// floats.  Ends with a barrier.
+__device__ __forceinline__ void solve_doubling(const float* sA, float* sX, float* sY, int tid) {
+  {
+    // Y_p = A[2p+1][2p] D[2p]: block p = tid / 128, row i, columns c, c + 1
+    const int p = tid >> 7, i = (tid >> 3) & 15, cc = (tid & 7) * 2;
+    const float* arow = sA + (32 * p + 16 + i) * kPadA + 32 * p;
+    const float* dcol = sX + (32 * p) * kPadA + 32 * p + cc;
+    float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < 16; kk += 4) {
-        float4 a[4], x[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(arow + r * kPadA + kk);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const float4*>(xrow + (kk + u) * kPadA);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const float av[4] = {a[r].x, a[r].y, a[r].z, a[r].w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            y[r][0] += av[u] * x[u].x;
-            y[r][1] += av[u] * x[u].y;
-            y[r][2] += av[u] * x[u].z;
-            y[r][3] += av[u] * x[u].w;
-          }
-        }
-      }
+    for (int k = 0; k < 16; ++k) {
+      const float a = arow[k];
+      const float2 d = *reinterpret_cast<const float2*>(dcol + k * kPadA);
+      y0 += a * d.x;
+      y1 += a * d.y;
     }
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-      *reinterpret_cast<float4*>(sY + b * 256 + (4 * ti + r) * 16 + 4 * tj) = make_float4(y[r][0], y[r][1], y[r][2], y[r][3]);
+    *reinterpret_cast<float2*>(sY + p * 256 + i * 16 + cc) = make_float2(y0, y1);
   }
   __syncthreads();
-  if (act) {
-    float x[4][4] = {};
-    const float* drow = sX + (16 * rb + 4 * ti) * kPadA + 16 * rb;
+  {
+    // X[2p+1][2p] = -D[2p+1] Y_p
+    const int p = tid >> 7, i = (tid >> 3) & 15, cc = (tid & 7) * 2;
+    const float* drow = sX + (32 * p + 16 + i) * kPadA + 32 * p + 16;
+    float x0 = 0.f, x1 = 0.f;
 #pragma unroll
-    for (int mm = 0; mm < 16; mm += 4) {
-      float4 d[4], yv[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) d[r] = *reinterpret_cast<const float4*>(drow + r * kPadA + mm);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) yv[u] = *reinterpret_cast<const float4*>(sY + b * 256 + (mm + u) * 16 + 4 * tj);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float dv[4] = {d[r].x, d[r].y, d[r].z, d[r].w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          x[r][0] -= dv[u] * yv[u].x;
-          x[r][1] -= dv[u] * yv[u].y;
-          x[r][2] -= dv[u] * yv[u].z;
-          x[r][3] -= dv[u] * yv[u].w;
-        }
-      }
+    for (int k = 0; k < 16; ++k) {
+      const float d = drow[k];
+      const float2 y = *reinterpret_cast<const float2*>(sY + p * 256 + k * 16 + cc);
+      x0 -= d * y.x;
+      x1 -= d * y.y;
     }
+    *reinterpret_cast<float2*>(sX + (32 * p + 16 + i) * kPadA + 32 * p + cc) = make_float2(x0, x1);
+  }
+  __syncthreads();
+  const int r2 = (tid >> 4) * 2, c2 = (tid & 15) * 2;   // a 2 x 2 tile of a 32 x 32 product
+  {
+    // Z = A21 X11 (A21 = A[32..63][0..31]; X11[k][j] = 0 for k < j)
+    // unrolled over all 32 k with the zeros selected (the unstored entries
+    // may hold anything), two partial sums per output
+    const float* a0 = sA + (32 + r2) * kPadA;
+    const float* a1 = a0 + kPadA;
+    float z[2][2][2] = {};
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      *reinterpret_cast<float4*>(sX + (16 * rb + 4 * ti + r) * kPadA + 16 * b + 4 * tj) =
-          make_float4(x[r][0], x[r][1], x[r][2], x[r][3]);
+    for (int k = 0; k < 32; ++k) {
+      const float2 x = *reinterpret_cast<const float2*>(sX + k * kPadA + c2);
+      const float xa = k >= c2 ? x.x : 0.f, xb = k > c2 ? x.y : 0.f;
+      const float u0 = a0[k], u1 = a1[k];
+      z[k & 1][0][0] += u0 * xa;
+      z[k & 1][0][1] += u0 * xb;
+      z[k & 1][1][0] += u1 * xa;
+      z[k & 1][1][1] += u1 * xb;
+    }
+    *reinterpret_cast<float2*>(sY + r2 * 32 + c2) = make_float2(z[0][0][0] + z[1][0][0], z[0][0][1] + z[1][0][1]);
+    *reinterpret_cast<float2*>(sY + (r2 + 1) * 32 + c2) =
+        make_float2(z[0][1][0] + z[1][1][0], z[0][1][1] + z[1][1][1]);
+  }
+  __syncthreads();
+  {
+    // X21 = -X22 Z (X22 = X[32..63][32..63]; X22[i][k] = 0 for k > i)
+    const float* x0 = sX + (32 + r2) * kPadA + 32;
+    const float* x1 = x0 + kPadA;
+    float v[2][2][2] = {};
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const float2 z = *reinterpret_cast<const float2*>(sY + k * 32 + c2);
+      const float u0 = k <= r2 ? x0[k] : 0.f, u1 = k <= r2 + 1 ? x1[k] : 0.f;
+      v[k & 1][0][0] += u0 * z.x;
+      v[k & 1][0][1] += u0 * z.y;
+      v[k & 1][1][0] += u1 * z.x;
+      v[k & 1][1][1] += u1 * z.y;
+    }
+    *reinterpret_cast<float2*>(sX + (32 + r2) * kPadA + c2) =
+        make_float2(-(v[0][0][0] + v[1][0][0]), -(v[0][0][1] + v[1][0][1]));
+    *reinterpret_cast<float2*>(sX + (33 + r2) * kPadA + c2) =
+        make_float2(-(v[0][1][0] + v[1][1][0]), -(v[0][1][1] + v[1][1][1]));
   }
   __syncthreads();
 }
@@ -1018,7 +1044,7 @@ __device__ __forceinline__ void solve_level(int lv, const float* sA, float* sX, 
 //   G | P = [K; Q] K^T (kind::f16, exact bf16 operands) -> A (shared memory),
 //   M to the record; V rows (cp.async) -> T^-1 = (I + A)^-1 blocked: the 16 x 16
 //   diagonal blocks by substitution while the other warps write K-hat^T to the
-//   record, then three levels of block products -> the U0 / W right-hand
+//   record, then the off-diagonal blocks by doubling (solve_doubling) -> the U0 / W right-hand
 //   operands diag(beta) T^-T and diag(beta g r_k) T^-T as bf16 hi + lo pairs
 //   (x = hi + lo to 2^-16 relative) -> U0^T = V^T B_U, W^T = K^T B_W
 //   (kind::f16, V^T and K^T MN-major straight from the rows) -> the record.
@@ -1026,19 +1052,42 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   extern __shared__ __align__(1024) unsigned char sm[];
   const long long unit = blockIdx.x;
   const long long slot = unit / p.Hv;
+  Ctx c;
+  ctx_init(c, p, static_cast<int>(unit - slot * p.Hv));   // per-head constants in flight during the lookup
+  // (sequence, chunk) of this slot and the sequence's token range: for a
+  // packed batch thread t < B tests sequence t (one round of loads, exactly
+  // one writer), thread B marks a slot past the last chunk
   int* s_bc = reinterpret_cast<int*>(sm + kQBar + 16);
-  if (threadIdx.x == 0) {
-    int b = 0, ch = 0;
-    const bool used = slot_to_chunk(p, slot, b, ch);
-    s_bc[0] = used ? b : -1;
-    s_bc[1] = ch;
+  long long* s_rng = reinterpret_cast<long long*>(sm + kQBar + 32);
+  if (!p.cu) {
+    if (c.tid == 0) {
+      int b = 0, ch = 0;
+      const bool used = slot_to_chunk(p, slot, b, ch);
+      s_bc[0] = used ? b : -1;
+      s_bc[1] = ch;
+      seq_range(p, b, s_rng[0], s_rng[1]);
+    }
+  } else {
+    for (int t = c.tid; t <= p.B; t += kThreads) {
+      const long long lo = p.chunk_prefix[t];
+      if (t < p.B) {
+        const long long hi = p.chunk_prefix[t + 1];
+        const long long q0 = p.cu[t], q1 = p.cu[t + 1];
+        if (lo <= slot && slot < hi) {
+          s_bc[0] = t;
+          s_bc[1] = p.win_c0 + static_cast<int>(slot - lo);
+          s_rng[0] = q0;
+          s_rng[1] = q1 < q0 ? q0 : q1;
+        }
+      } else if (slot >= lo) {
+        s_bc[0] = -1;
+      }
+    }
   }
   __syncthreads();
   const int b = s_bc[0];
   if (b < 0) return;
   const int ch = s_bc[1];
-  Ctx c;
-  ctx_init(c, p, static_cast<int>(unit - slot * p.Hv));
   ctx_scalars(c, reinterpret_cast<float*>(sm + kQSc));
   c.bar = reinterpret_cast<uint64_t*>(sm + kQBar);
   unsigned char* sK = sm + kQK;
@@ -1046,17 +1095,24 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   float* sA = reinterpret_cast<float*>(sm + kQA);
   float* sX = reinterpret_cast<float*>(sm + kQX);
   float* sY = reinterpret_cast<float*>(sm + kQY);
-  long long s0, s1;
-  seq_range(p, b, s0, s1);
+  const long long s0 = s_rng[0], s1 = s_rng[1];
   const long long t0 = s0 + static_cast<long long>(ch) * kC;
   const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
   unsigned char* rec = record(p, slot, c.h);
+  // gate inputs first: their latency overlaps the row copies and the TMEM set-up
+  float a_in = 0.f, b_in = 0.f;
+  const bool gvalid = c.tid < kC && c.tid < nvalid;
+  if (gvalid) {
+    const size_t gi = static_cast<size_t>(t0 + c.tid) * p.Hv + c.h;
+    a_in = __ldg(p.a + gi);
+    b_in = __ldg(p.b + gi);
+  }
 
   prep_copy_rows(sK, p.k + t0 * p.k_stride + c.kh * kD, p.k_stride, nvalid, c.warp, c.lane);
   prep_copy_rows(sQ, p.q + t0 * p.q_stride + c.kh * kD, p.q_stride, nvalid, c.warp, c.lane);
   ptx::cp_async_commit();
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kQBar + 8), c.bar, 1, kPrepTmemCols);
-  phase_gates(p, c, t0, nvalid);
+  phase_gates_from(c, a_in, b_in, gvalid);
   ptx::cp_async_wait<0>();
   ptx::fence_proxy_async_smem();
   __syncthreads();
@@ -1225,11 +1281,7 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
     }
     __syncthreads();
     GDN_TICK(20);
-    solve_level(1, sA, sX, sY, c.tid);
-    GDN_TICK(11);
-    solve_level(2, sA, sX, sY, c.tid);
-    GDN_TICK(12);
-    solve_level(3, sA, sX, sY, c.tid);
+    solve_doubling(sA, sX, sY, c.tid);
     GDN_TICK(13);
 
     // right-hand operands, K-major (row j, token t), bf16 hi | lo:
