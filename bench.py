@@ -683,7 +683,6 @@ class PrefillLayer:
         self.S = torch.empty((self.B, hv, D, D), dtype=torch.float32, device=device)
         self.out = torch.empty((self.N, hv, D), dtype=torch.bfloat16, device=device)
         self.schedule = self.base = "fused"
-        self.scan_flag = 0
         self.ws = None
         self.ws_cap = 0
         self.head0, self.hv_total = head0, hv_total if hv_total is not None else hv
@@ -701,11 +700,7 @@ class PrefillLayer:
         NVLink, then gdn_gather_wait -- no separate all-gather.  Two
         PeerGather buffers alternate across layers."""
         import gdn_b200 as G
-        self.schedule = schedule
-        # a "_pair" suffix runs the same schedule with the scan on CTA pairs
-        self.base = schedule[:-5] if schedule.endswith("_pair") else schedule
-        self.scan_flag = G.F_SCAN_PAIR if schedule.endswith("_pair") else G.F_SCAN_SINGLE
-        schedule = self.base
+        self.schedule = self.base = schedule
         if schedule == "split_gather" and self.pgs is None:
             import gdn_shard
             self.pgs = [gdn_shard.PeerGather(self.N, self.hv_total, self.x.device) for _ in range(2)]
@@ -742,7 +737,7 @@ class PrefillLayer:
             self.pg_i ^= 1
             pg.run(lib, q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias), None, P(self.S),
                    P(self.z), self.hv * D, P(self.gamma), 1e-6, self.head0, self._cu(), self.B, self.T, hk,
-                   self.hv, G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
+                   self.hv, G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
             self.pg_last = pg
             return
         if self.base == "split_norm":
@@ -750,11 +745,11 @@ class PrefillLayer:
                                              P(self.dt_bias), None, P(self.S), P(self.z), self.hv * D,
                                              P(self.gamma), ctypes.c_float(1e-6), P(self.out), self.hv * D, 0,
                                              self._cu(), self.B, self.T, hk, self.hv, D, D,
-                                             G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
+                                             G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
         elif self.base == "split":
             rc = lib.gdn_chunked_fwd_ws(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
                                         None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
-                                        G.F_QK_L2NORM | self.scan_flag, P(self.ws), self.ws.numel(), h)
+                                        G.F_QK_L2NORM, P(self.ws), self.ws.numel(), h)
         else:
             rc = lib.gdn_chunked_fwd(q, k, v, C, C, C, P(self.a), P(self.b), P(self.A_log), P(self.dt_bias),
                                      None, P(self.S), P(self.o), self._cu(), self.B, self.T, hk, self.hv, D, D,
@@ -890,8 +885,6 @@ def run_prefill(args, lib, device, world):
     cases = [("config3", [args.prefill_T])]
     if not args.no_config4:
         cases.append(("config4", config4_lengths()))
-    # the pair-scan schedules ("_pair") are measured slower (per-instruction cost of the
-    # small cta_group::2 MMAs) and are timed only when asked for
     schedules = ["fused", "split", "split_norm"] if args.prefill_schedule == "auto" else [args.prefill_schedule]
     if world > 1 and args.prefill_schedule == "auto" and not args.no_peer_gather:
         schedules.append("split_gather")
@@ -919,11 +912,7 @@ def run_prefill(args, lib, device, world):
         achieved = X.flops() / (kms["chunked"] * 1e-3) / 1e12
         kernel = {"fused": "chunked_kernel", "split": "chunk_prep_kernel + chunk_scan_kernel",
                   "split_norm": "chunk_prep_kernel + chunk_scan_kernel<norm>",
-                  "split_gather": "chunk_prep_kernel + chunk_scan_kernel<norm, peer stores>",
-                  "split_pair": "chunk_prep_kernel + chunk_scan_pair_kernel (CTA pairs)",
-                  "split_norm_pair": "chunk_prep_kernel + chunk_scan_pair_kernel<norm> (CTA pairs)",
-                  "split_gather_pair": "chunk_prep_kernel + chunk_scan_pair_kernel<norm, peer stores> (CTA pairs)"
-                  }[best]
+                  "split_gather": "chunk_prep_kernel + chunk_scan_kernel<norm, peer stores>"}[best]
         res[name] = {
             "schedule": best,
             "ms_per_layer_by_schedule": {k: round(v[0], 4) for k, v in timed.items()},
@@ -1212,8 +1201,7 @@ def main():
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer prefill (projections included)")
     ap.add_argument("--prefill-T", type=int, default=4096)
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 layer (B=8 varlen 16K-64K)")
-    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather",
-                                                   "split_pair", "split_norm_pair", "split_gather_pair"],
+    ap.add_argument("--prefill-schedule", choices=["auto", "fused", "split", "split_norm", "split_gather"],
                     default="auto", help="chunked schedule for configs 3/4; auto times each and reports the fastest "
                     "(split_gather: N > 1 only)")
     ap.add_argument("--no-peer-gather", action="store_true",

@@ -72,10 +72,6 @@ extern "C" {
 #define GDN_F_CONV_NO_SILU  0x200u  /* conv: skip the SiLU after the convolution */
 #define GDN_F_NORM_IN_BF16  0x400u  /* gated norm: o is bf16 (default fp32) */
 #define GDN_F_NORM_OUT_F32  0x800u  /* gated norm: out is fp32 (default bf16) */
-#define GDN_F_SCAN_PAIR     0x1000u /* chunked (split schedule): run each (sequence, head) state
-                                       chain on a cluster of two CTAs, 64 value rows each */
-#define GDN_F_SCAN_SINGLE   0x2000u /* chunked (split schedule): one CTA per chain.  Neither bit:
-                                       the library chooses */
 
 /* Human-readable text of the last error on the calling thread ("" if none). */
 const char* gdn_last_error(void);

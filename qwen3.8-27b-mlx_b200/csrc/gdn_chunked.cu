@@ -125,8 +125,7 @@ constexpr uint32_t kRecU = kRecKh + kD * kC * 4;    // U0^T by column quads, see
 constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // [0] = g_last                         group 3
 constexpr uint32_t kRecBytes = kRecSc + 1024;       // multiple of 256
 // float4 index of U0^T[row][4 quad .. 4 quad + 3] in the record: value rows
-// 0-63 and 64-127 are two contiguous blocks of 16 quads x 64 rows, so that
-// each CTA of a pair scan takes its half in one copy.
+// 0-63 and 64-127 are two contiguous blocks of 16 quads x 64 rows.
 __host__ __device__ constexpr int u0_index(int quad, int row) {
   return (row >> 6) * (16 * 64) + quad * 64 + (row & 63);
 }
@@ -155,45 +154,6 @@ constexpr uint32_t kZBuf = kC * kD * 2;
 constexpr uint32_t kScanSmemNorm = kScanZ + 3 * kZBuf;
 static_assert(kScanSmemNorm <= 232448, "scan with the fused norm: shared memory per CTA");
 
-// ---- the pair scan: one chain on a cluster of two CTAs ----------------------
-// CTA r of the pair holds value rows 64r .. 64r+63 of the state and issues
-// nothing but copies; the pair's leader (r = 0) issues the tcgen05 cta_group::2
-// MMAs (M = 128: 64 rows from each CTA, each CTA's B operand half from its own
-// shared memory).  Each CTA copies only its half of every B operand from the
-// record (tokens 32r .. 32r+31 of -W, Q-tilde and M; key columns 64r .. 64r+63
-// of K-hat^T) and of U0^T, 72 KiB per chunk instead of 145.
-// Shared memory of a CTA (offsets in bytes):
-constexpr uint32_t kPW = 0;                          // -W, 32 tokens x 128, SBO 4096           group 1
-constexpr uint32_t kPQ = kPW + 32 * kD * 4;          // Q-tilde, 32 tokens x 128                group 1
-constexpr uint32_t kPM = kPQ + 32 * kD * 4;          // M, 32 tokens x 64, SBO 2048             group 2
-constexpr uint32_t kPKh = kPM + 32 * kC * 4;         // K-hat^T, 64 key columns x 64 tokens     group 2
-constexpr uint32_t kPU0 = kPKh + 64 * kC * 4;        // U0^T half, u0_index order (16 KiB)      group 3
-constexpr uint32_t kPSc = kPU0 + 64 * kC * 4;        // g_last                                  group 3
-constexpr uint32_t kPA1 = kPSc + 256;                // tf32(R): 64 rows x 128 keys, SBO 4096 (A of batch 1)
-constexpr uint32_t kPA2 = kPA1 + 64 * kD * 4;        // U^T: 64 rows x 64 tokens, SBO 2048 (A of batch 2)
-constexpr uint32_t kPBar = kPA2 + 64 * kC * 4;       // [0] MMA, [1..3] record groups, [4] pair ready; TMEM base at +64
-constexpr uint32_t kPNorm = kPBar + 128;             // fused norm: see below (2 KiB)
-constexpr uint32_t kPSmem = kPNorm + 2048;
-// fused norm area: [0, 512) per-quarter partial sums of y^2 (2 groups x 4
-// quarters x 16 tokens), [512, 1024) this CTA's 64-value sums that the peer
-// reads (2 parities x 2 groups x 32 tokens), then the mbarriers -- y ready
-// (2, the leader's commit), y read (2, one arrival per norm warp), the peer's
-// sums written (4, by parity and group) -- and the failure flag
-constexpr uint32_t kPNormLoc = kPNorm + 512;
-constexpr uint32_t kPNormBar = kPNorm + 1024;
-constexpr uint32_t kPNormFail = kPNormBar + 64;
-// fused norm: z rows (this CTA's 64 values of each token) of three chunks
-constexpr uint32_t kPZBuf = kC * 64 * 2;
-constexpr uint32_t kPZ = kPSmem;
-constexpr uint32_t kPSmemNorm = kPZ + 3 * kPZBuf;
-static_assert(kPSmemNorm <= 232448, "pair scan with the fused norm: shared memory per CTA");
-// tensor memory of a CTA (256 columns): R fp32 (N = 128 -> 64 columns), U
-// (N = 64 -> 32), y of even and odd chunks (32 each).  A 64-row accumulator
-// of N columns lies at lane m, column n for n < N/2 and at lane 64 + m,
-// column n - N/2 otherwise: lanes 0-63 hold keys 0-63 of R (tokens 0-31 of
-// U and y), lanes 64-127 keys 64-127 (tokens 32-63).
-constexpr uint32_t kPairColR = 0, kPairColU = 64, kPairColY = 96;
-constexpr uint32_t kPTmemCols = 256;
 
 __host__ __device__ constexpr size_t records_offset(int B) {
   return kWsHeader + (static_cast<size_t>(B + 1) * 4 + 255) / 256 * 256;
@@ -1779,446 +1739,6 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
   if (c.warp == 0) tc::tmem_dealloc(c.tb, kTmemCols);
 }
 
-// ---- the split schedule on CTA pairs ------------------------------------------
-
-// One (sequence, value head) chain per cluster of two CTAs (see kPW).  17
-// warps per CTA: warps 0-15 are the epilogue workers -- warp w reaches TMEM
-// lanes 32 (w % 4) .. +31 and takes column group w / 4 of each accumulator;
-// warp 16's lane 0 issues this CTA's copies and, in the leader, the MMAs.
-// Per chunk, as in chunk_scan_kernel: batch 1 [U | y] = R [-W; Q-tilde]^T
-// (two N = 64 products from tf32(R) in shared memory) under which the
-// workers scale R by g_last; U^T = U + U0^T to shared memory; batch 2
-// y += U^T M^T (N = 64) and R += U^T K-hat'^T^T (N = 128); tf32(R) to
-// shared memory.  Before each batch both CTAs' issuers arrive on the
-// leader's "pair ready" barrier (each after its own copies have landed and
-// its workers' operands are written); the leader's commit arrives on both
-// CTAs' MMA barriers.
-template <bool NORM>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1)
-    chunk_scan_pair_kernel(const ChunkParams p) {
-  extern __shared__ __align__(1024) unsigned char sm[];
-  const uint32_t rank = ptx::cluster_ctarank();
-  const bool leader = rank == 0;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kPBar);   // [0] MMA, [1..3] groups, [4] pair ready
-  const int bh = blockIdx.x >> 1;
-  const int b = bh / p.Hv;
-  Ctx c;
-  ctx_init(c, p, bh - b * p.Hv);
-  c.bar = bars;
-  const bool mw = c.warp == kScanWorkers / 32;
-  const bool worker = c.warp < kScanWorkers / 32;
-  const bool issuer = mw && c.lane == 0;
-  const bool nw = NORM && c.warp > kScanWorkers / 32;   // a norm warp
-  uint64_t* ybar = reinterpret_cast<uint64_t*>(sm + kPNormBar);   // [0..1] y ready, [2..3] y read, [4..7] peer sums
-  volatile int* s_fail = reinterpret_cast<volatile int*>(sm + kPNormFail);
-  auto chain_sync = [&]() { asm volatile("bar.sync 7, %0;" ::"n"(kScanThreads) : "memory"); };
-  auto chain_or = [&](bool pred) -> bool {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.or.pred p, 7, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(r)
-        : "r"(static_cast<uint32_t>(pred)), "n"(kScanThreads)
-        : "memory");
-    return r != 0;
-  };
-  const int cg = (c.warp >> 2) & 3;                  // column group of a worker
-  const int hi = c.quarter >> 1;                     // lanes 64-127: keys 64-127 of R, tokens 32-63 of U and y
-  const int lrow = (c.quarter & 1) * 32 + c.lane;    // value row of this CTA's 64 (lanes m and 64 + m)
-  const int vrow = static_cast<int>(rank) * 64 + lrow;
-  long long s0, s1;
-  seq_range(p, b, s0, s1);
-  int n_chunks = static_cast<int>((s1 - s0 + kC - 1) / kC) - p.win_c0;
-  n_chunks = n_chunks < 0 ? 0 : (n_chunks > p.win_len ? p.win_len : n_chunks);
-  if (p.win_c0 > 0 && n_chunks == 0) return;         // both CTAs of the pair: finished in an earlier window
-  const long long slot0 = seq_first_slot(p, b);
-  if (c.tid == 0) {
-    for (int i = 0; i < 4; ++i) ptx::mbar_init(bars + i, 1);
-    ptx::mbar_init(bars + 4, 2);
-    if (NORM) {
-      ptx::mbar_init(ybar + 0, 1);
-      ptx::mbar_init(ybar + 1, 1);
-      ptx::mbar_init(ybar + 2, 8);
-      ptx::mbar_init(ybar + 3, 8);
-      for (int i = 4; i < 8; ++i) ptx::mbar_init(ybar + i, 1);
-      *s_fail = 0;
-    }
-    ptx::fence_mbar_init();
-  }
-  if (c.warp == 0) {
-    tc::tmem_alloc_pair(reinterpret_cast<uint32_t*>(sm + kPBar + 64), kPTmemCols);
-    tc::tmem_relinquish_pair();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  ptx::cluster_sync();                               // both CTAs' barriers and tensor memory exist
-  tc::fence_after_sync();
-  c.tb = *reinterpret_cast<uint32_t*>(sm + kPBar + 64);
-  const uint32_t rdy_leader = ptx::mapa(ptx::smem_u32(bars + 4), 0);
-  // this worker's 16 columns of R (keys 64 hi + 16 cg ..) at its lanes
-  const uint32_t r_cols = c.tb + c.my + kPairColR + cg * 16;
-  {
-    const float* st = p.win_c0 == 0 ? p.state_in : p.carry;
-    const float* src = st ? st + (static_cast<size_t>(bh) * kD + vrow) * kD + hi * 64 + cg * 16 : nullptr;
-    if (worker) {
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        const float4 f = src ? *reinterpret_cast<const float4*>(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
-      }
-      tc::tmem_st16(r_cols, v);
-      tc::tmem_st_wait();
-    }
-  }
-
-  // record groups issued and waited for, counted by the copy warp only
-  int issued[4] = {0, 0, 0, 0}, done[4] = {0, 0, 0, 0};
-  // this CTA's half of group g of chunk ch
-  auto load = [&](int g, int ch) {
-    if (issuer) {
-      const unsigned char* rec = record(p, slot0 + ch, c.h);
-      if (g == 1) {
-        ptx::mbar_arrive_expect_tx(&bars[1], 2 * 32 * kD * 4);
-        ptx::bulk_g2s(sm + kPW, rec + kRecW + rank * (32 * kD * 4), 32 * kD * 4, &bars[1]);
-        ptx::bulk_g2s(sm + kPQ, rec + kRecQ + rank * (32 * kD * 4), 32 * kD * 4, &bars[1]);
-      } else if (g == 2) {
-        ptx::mbar_arrive_expect_tx(&bars[2], 32 * kC * 4 + 64 * kC * 4);
-        ptx::bulk_g2s(sm + kPM, rec + kRecM + rank * (32 * kC * 4), 32 * kC * 4, &bars[2]);
-        ptx::bulk_g2s(sm + kPKh, rec + kRecKh + rank * (64 * kC * 4), 64 * kC * 4, &bars[2]);
-      } else {
-        ptx::fence_proxy_async_smem();               // the workers' reads of U0^T and g_last come first
-        ptx::mbar_arrive_expect_tx(&bars[3], 64 * kC * 4 + 16);
-        ptx::bulk_g2s(sm + kPU0, rec + kRecU + rank * (64 * kC * 4), 64 * kC * 4, &bars[3]);
-        ptx::bulk_g2s(sm + kPSc, rec + kRecSc, 16, &bars[3]);
-      }
-    }
-    if (mw) ++issued[g];
-  };
-  auto wait_group = [&](int g, int ch) -> bool {
-    if (!mw) return true;
-    const bool ok = ptx::mbar_wait(&bars[g], ch & 1);
-    done[g] += ok;
-    return ok;
-  };
-  // the leader's commit: the copy warp polls, the CTA agrees
-  auto mma_done = [&](bool ok_in) -> bool {
-    bool ok = ok_in;
-    if (mw) ok = ok && ptx::mbar_wait_cluster(c.bar, c.phase);
-    c.phase ^= 1u;
-    const bool all = !chain_or(!ok);
-    tc::fence_after_sync();
-    return all;
-  };
-  // the issuer says this CTA is ready for the next batch; the leader's waits
-  // for both CTAs (false if it gave up)
-  uint32_t pu = 0;
-  auto pair_ready = [&]() -> bool {
-    ptx::mbar_arrive_cluster(rdy_leader);
-    bool ok = true;
-    if (leader) ok = ptx::mbar_wait_cluster(&bars[4], pu & 1u);
-    ++pu;
-    return ok;
-  };
-  // R *= g_last in place (a worker's 16 columns)
-  auto r_scale = [&](float gl) {
-    float v[16];
-    tc::tmem_ld16(r_cols, v);
-    tc::tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] *= gl;
-    tc::tmem_st16(r_cols, v);
-  };
-  // tf32(R) -> the A operand of batch 1 (row lrow, keys 64 hi + 16 cg ..)
-  auto r_pass = [&]() {
-    float v[16];
-    tc::tmem_ld16(r_cols, v);
-    tc::tmem_ld_wait();
-#pragma unroll
-    for (int e = 0; e < 16; e += 4)
-      *reinterpret_cast<float4*>(at(sm + kPA1, lrow, hi * 64 + cg * 16 + e, kSbo128)) =
-          make_float4(tc::to_tf32(v[e]), tc::to_tf32(v[e + 1]), tc::to_tf32(v[e + 2]), tc::to_tf32(v[e + 3]));
-    ptx::fence_proxy_async_smem();
-  };
-  // U^T = U + U0^T -> the A operand of batch 2 (row lrow, tokens 32 hi + 8 cg ..)
-  auto epi_u = [&]() {
-    float u[8];
-    tc::tmem_ld8(c.tb + c.my + kPairColU + cg * 8, u);
-    tc::tmem_ld_wait();
-    const int tok = hi * 32 + cg * 8;
-    const float4* u0 = reinterpret_cast<const float4*>(sm + kPU0);
-#pragma unroll
-    for (int e = 0; e < 8; e += 4) {
-      const float4 f = u0[u0_index((tok + e) >> 2, lrow)];
-      *reinterpret_cast<float4*>(at(sm + kPA2, lrow, tok + e, kSbo64)) =
-          make_float4(tc::to_tf32(u[e] + f.x), tc::to_tf32(u[e + 1] + f.y), tc::to_tf32(u[e + 2] + f.z),
-                      tc::to_tf32(u[e + 3] + f.w));
-    }
-    ptx::fence_proxy_async_smem();
-  };
-  // o rows of chunk ch (plain scan): value vrow, tokens 32 hi + 8 cg .. +7
-  auto epi_o = [&](int ch) {
-    const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
-    const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-    const int tok = hi * 32 + cg * 8;
-    const int nv = nvalid - tok;
-    float y[8];
-    tc::tmem_ld8(c.tb + c.my + kPairColY + (ch & 1) * 32 + cg * 8, y);
-    tc::tmem_ld_wait();
-    const size_t orow = static_cast<size_t>(p.Hv) * kD;
-    const size_t base = (static_cast<size_t>(t0 + tok) * p.Hv + c.h) * kD + vrow;
-    if (p.flags & GDN_F_O_BF16) {
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.o) + base;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i < nv) o[i * orow] = __float2bfloat16_rn(y[i]);
-    } else {
-      float* o = static_cast<float*>(p.o) + base;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i < nv) o[i * orow] = y[i];
-    }
-  };
-  // ---- fused norm on the pair: the 8 norm warps (warp % 4 = TMEM lane
-  // quarter; group grp of 4 warps takes columns 16 grp .. +15 of y, i.e.
-  // tokens 32 h + 16 grp + i for the lanes of half h) normalise chunk ch
-  // while the chain runs chunk ch + 1.  A token's sum of squares spans both
-  // CTAs: each group adds its two quarters of a half, publishes the 32 sums
-  // in its shared memory, arrives on the peer's barrier and reads the peer's
-  // 32 through distributed shared memory.  The y columns are released ("y
-  // read") only after that read, so a CTA overwrites its published sums two
-  // chunks later only after the peer has read them.  z (this CTA's 64 values
-  // of each token) comes by cp.async three chunks ahead.
-  auto norm_chunks = [&]() {
-    const int grp = (c.tid - kScanThreads) >> 7;
-    const int nt = (c.tid - kScanThreads) & 127;
-    const int bar_id = 5 + grp;
-    const float gam = __ldg(p.gamma + vrow);
-    float* s_part = reinterpret_cast<float*>(sm + kPNorm) + grp * 64;   // [quarter][16 tokens]
-    float* s_loc = reinterpret_cast<float*>(sm + kPNormLoc);            // [parity][group][32]
-    auto nbar = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory"); };
-    auto group_or = [&](bool pred) -> bool {
-      uint32_t r;
-      asm volatile(
-          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
-          "bar.red.or.pred p, %2, 128, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-          : "=r"(r)
-          : "r"(static_cast<uint32_t>(pred)), "r"(bar_id)
-          : "memory");
-      return r != 0;
-    };
-    auto tok_of = [&](int tk) { return (tk >> 4) * 32 + grp * 16 + (tk & 15); };   // tk: 0..31 of the group
-    auto load_z = [&](int ch) {
-      const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
-      const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-      unsigned char* zb = sm + kPZ + (ch % 3) * kPZBuf;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int piece = nt + k * 128;
-        const int tok = tok_of(piece >> 3);
-        const int seg = (piece & 7) * 8;
-        if (tok < nvalid)
-          ptx::cp_async16(zb + (tok * 64 + seg) * 2,
-                          p.z + (t0 + tok) * p.z_stride + c.h * kD + static_cast<int>(rank) * 64 + seg);
-      }
-      ptx::cp_async_commit();
-    };
-    auto wait_or_fail = [&](uint64_t* bar, uint32_t parity) -> bool {
-      for (uint32_t i = 0; i < ptx::kSpinLimit; ++i) {
-        if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
-        if (*s_fail) return false;
-      }
-      return false;
-    };
-    const int h = c.quarter >> 1;
-    for (int ch = 0; ch < 3 && ch < n_chunks; ++ch) load_z(ch);
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int par = ch & 1;
-      if (group_or(!wait_or_fail(&ybar[par], (ch >> 1) & 1))) {
-        if (nt == 0) atomicExch(p.err, 1);
-        break;
-      }
-      tc::fence_after_sync();
-      const int newer = n_chunks - 1 - ch;           // z groups committed after this chunk's
-      if (newer >= 2) ptx::cp_async_wait<2>();
-      else if (newer == 1) ptx::cp_async_wait<1>();
-      else ptx::cp_async_wait<0>();
-      const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
-      const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-      __nv_bfloat16* zt = reinterpret_cast<__nv_bfloat16*>(sm + kPZ + (ch % 3) * kPZBuf);
-      float y[16];
-      tc::tmem_ld16(c.tb + c.my + kPairColY + par * 32 + grp * 16, y);
-      tc::tmem_ld_wait();
-      // sums of y^2 over this warp's 32 values for its 16 tokens: halve the
-      // token set per exchange; lanes 2t, 2t + 1 end with token t
-      float s8[8], s4[4], s2[2], s1v;
-      const bool b16 = c.lane & 16, b8 = c.lane & 8, b4 = c.lane & 4, b2 = c.lane & 2;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float lo = y[i] * y[i], hi2 = y[i + 8] * y[i + 8];
-        s8[i] = (b16 ? hi2 : lo) + __shfl_xor_sync(0xffffffffu, b16 ? lo : hi2, 16);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s4[i] = (b8 ? s8[i + 4] : s8[i]) + __shfl_xor_sync(0xffffffffu, b8 ? s8[i] : s8[i + 4], 8);
-#pragma unroll
-      for (int i = 0; i < 2; ++i) s2[i] = (b4 ? s4[i + 2] : s4[i]) + __shfl_xor_sync(0xffffffffu, b4 ? s4[i] : s4[i + 2], 4);
-      s1v = (b2 ? s2[1] : s2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s2[0] : s2[1], 2);
-      s1v += __shfl_xor_sync(0xffffffffu, s1v, 1);
-      if ((c.lane & 1) == 0) s_part[c.quarter * 16 + (c.lane >> 1)] = s1v;
-      nbar();                                        // every z piece of the chunk and every partial sum is in
-      float* loc = s_loc + (par * 2 + grp) * 32;
-      if (nt < 32) loc[nt] = s_part[(nt >> 4) * 32 + (nt & 15)] + s_part[(nt >> 4) * 32 + 16 + (nt & 15)];
-      nbar();
-      uint64_t* sums_bar = &ybar[4 + par * 2 + grp];
-      if (nt == 0) ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(sums_bar), rank ^ 1u));
-      if (group_or(!wait_or_fail(sums_bar, (ch >> 1) & 1))) {
-        if (nt == 0) atomicExch(p.err, 1);
-        break;
-      }
-      const int ti = h * 16 + (c.lane & 15);
-      const float tot = loc[ti] + ptx::ld_cluster_f32(ptx::mapa(ptx::smem_u32(loc + ti), rank ^ 1u));
-      const float rr = rsqrtf(tot / static_cast<float>(kD) + p.eps);
-      tc::fence_before_sync();
-      __syncwarp();
-      if (c.lane == 0) ptx::mbar_arrive(&ybar[2 + par]);   // this warp is done with y and the peer's sums
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {                 // normed rows over the z they gate (same element)
-        const float ri = __shfl_sync(0xffffffffu, rr, i);
-        __nv_bfloat16* e = zt + (h * 32 + grp * 16 + i) * 64 + lrow;
-        const float zz = __bfloat162float(*e);
-        const float sg = __fdividef(1.f, 1.f + __expf(-zz));
-        *e = __float2bfloat16_rn((y[i] * ri * gam) * (zz * sg));
-      }
-      nbar();
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {                  // 32 rows x 8 pieces of 16 bytes
-        const int piece = nt + k * 128;
-        const int tok = tok_of(piece >> 3);
-        const int seg = (piece & 7) * 8;
-        if (tok < nvalid) {
-          const uint4 v = *reinterpret_cast<const uint4*>(zt + tok * 64 + seg);
-          const long long off = (t0 + tok) * p.out_stride + static_cast<long long>(p.out_head0 + c.h) * kD +
-                                static_cast<int>(rank) * 64 + seg;
-          if (off + 8 <= p.out_elems) {
-#pragma unroll
-            for (int d = 0; d < 8; ++d)
-              if (d < p.n_dst) *reinterpret_cast<uint4*>(p.dst[d] + off) = v;
-          } else {
-            atomicExch(p.err, 1);
-          }
-        }
-      }
-      nbar();                                        // buffer ch % 3 fully stored: refill it
-      if (ch + 3 < n_chunks) load_z(ch + 3);
-    }
-    ptx::cp_async_wait<0>();                         // no z copy may land after the CTA exits
-  };
-
-  bool failed = false;
-  if (nw) {
-    if (n_chunks > 0) norm_chunks();
-  } else {
-    if (n_chunks > 0) {
-      load(1, 0);
-      load(2, 0);
-      load(3, 0);
-      if (worker) r_pass();                            // tf32(R_0)
-      tc::fence_before_sync();
-      chain_sync();
-    }
-    for (int ch = 0; ch < n_chunks && !failed; ++ch) {
-      const uint32_t col_y = kPairColY + (ch & 1) * 32;
-      bool ok = wait_group(1, ch);
-      ok = wait_group(3, ch) && ok;
-      if (chain_or(!ok)) { failed = true; break; }
-      tc::fence_after_sync();
-      GDN_TICK(1);
-      bool mok = true;
-      if (issuer) {              // first batch: U = R (-W)^T, y = R Q-tilde^T (U0^T is added in the epilogue)
-        // both CTAs' norm warps have read y of chunk ch - 2, whose columns this batch overwrites
-        if (NORM && ch >= 2) mok = ptx::mbar_wait(&ybar[2 + (ch & 1)], ((ch >> 1) - 1) & 1);
-        mok = mok && pair_ready();
-        if (leader && mok) {
-          tc::fence_after_sync();
-          const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC);
-          for (int j = 0; j < kD / 8; ++j) {
-            const uint64_t a = desc(sm + kPA1, j * 256, kSbo128);
-            tc::mma_tf32_pair(c.tb + kPairColU, a, desc(sm + kPW, j * 256, kSbo128), id, j > 0);
-            tc::mma_tf32_pair(c.tb + col_y, a, desc(sm + kPQ, j * 256, kSbo128), id, j > 0);
-          }
-          tc::mma_commit_pair(c.bar, 3);
-        }
-      } else if (worker) {       // under it: R *= g_last(ch) for the update, the previous o
-        r_scale(reinterpret_cast<const float*>(sm + kPSc)[0]);
-        if (!NORM && ch > 0) epi_o(ch - 1);
-        tc::tmem_st_wait();
-      }
-      tc::fence_before_sync();
-      if (!mma_done(mok)) { failed = true; break; }
-      GDN_TICK(2);
-      if (ch + 1 < n_chunks) load(1, ch + 1);
-      if (worker) epi_u();
-      ok = wait_group(2, ch);
-      tc::fence_before_sync();
-      if (chain_or(!ok)) { failed = true; break; }
-      tc::fence_after_sync();
-      GDN_TICK(3);
-      mok = true;
-      if (issuer) {              // second batch: y += U^T M^T, R += U^T K-hat'^T^T
-        mok = pair_ready();
-        if (leader && mok) {
-          tc::fence_after_sync();
-          const uint32_t idy = tc::instr_desc(tc::kTF32, 128, kC);
-          const uint32_t idr = tc::instr_desc(tc::kTF32, 128, kD);
-          for (int j = 0; j < kC / 8; ++j) {
-            const uint64_t a = desc(sm + kPA2, j * 256, kSbo64);
-            tc::mma_tf32_pair(c.tb + col_y, a, desc(sm + kPM, j * 256, kSbo64), idy, 1);
-            tc::mma_tf32_pair(c.tb + kPairColR, a, desc(sm + kPKh, j * 256, kSbo64), idr, 1);
-          }
-          tc::mma_commit_pair(c.bar, 3);
-          if (NORM) tc::mma_commit_pair(&ybar[ch & 1], 3);   // y of chunk ch complete: the norm warps take it
-        }
-      }
-      if (ch + 1 < n_chunks) load(3, ch + 1);          // U0^T and g_last of this chunk are consumed
-      tc::fence_before_sync();
-      if (!mma_done(mok)) { failed = true; break; }
-      GDN_TICK(4);
-      if (ch + 1 < n_chunks) {
-        load(2, ch + 1);
-        if (worker) r_pass();                          // tf32(R_{ch+1}) for the next first batch
-      }
-      tc::fence_before_sync();
-      chain_sync();
-      GDN_TICK(5);
-    }
-    if (!NORM && !failed && n_chunks > 0 && worker) epi_o(n_chunks - 1);
-    if (failed) {
-      // bounded waits for the MMA and the bulk copies still in flight
-      if (c.tid == 0) {
-        atomicExch(p.err, 1);
-        if (NORM) *s_fail = 1;
-      }
-      if (mw) {
-        ptx::mbar_wait_cluster(c.bar, c.phase ^ 1u);
-        for (int g = 1; g <= 3; ++g)
-          if (issued[g] > done[g]) ptx::mbar_wait(&bars[g], done[g] & 1);
-      }
-    } else if (worker && p.carry) {
-      float v[16];
-      tc::tmem_ld16(r_cols, v);
-      tc::tmem_ld_wait();
-      float* dst = p.carry + (static_cast<size_t>(bh) * kD + vrow) * kD + hi * 64 + cg * 16;
-  #pragma unroll
-      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    }
-  }
-  if (NORM && p.n_dst > 1) __threadfence_system();  // peer stores performed before the call's signal
-  tc::fence_before_sync();
-  __syncthreads();
-  ptx::cluster_sync();                               // the leader's MMAs into this CTA are done, its barriers unused
-  if (c.warp == 0) tc::tmem_dealloc_pair(c.tb, kPTmemCols);
-}
-
 // ---- host side ----------------------------------------------------------------
 
 int set_smem_attr(const void* fn, uint32_t bytes, bool (&done)[64]) {
@@ -2242,10 +1762,7 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
                  long long v_stride, const float* a, const float* b, const float* A_log, const float* dt_bias,
                  const float* state_in, float* state_out, void* o, const int32_t* cu_seqlens, int B, int T, int Hk,
                  int Hv, int Dk, int Dv, unsigned flags) {
-  if (flags & ~(GDN_F_O_BF16 | GDN_F_QK_L2NORM | GDN_F_SCAN_PAIR | GDN_F_SCAN_SINGLE))
-    return fail(GDN_ERR_FLAGS, "unknown flag bits 0x%x", flags);
-  if ((flags & GDN_F_SCAN_PAIR) && (flags & GDN_F_SCAN_SINGLE))
-    return fail(GDN_ERR_FLAGS, "GDN_F_SCAN_PAIR and GDN_F_SCAN_SINGLE exclude each other");
+  if (flags & ~(GDN_F_O_BF16 | GDN_F_QK_L2NORM)) return fail(GDN_ERR_FLAGS, "unknown flag bits 0x%x", flags);
   if (B < 0 || T < 0 || Hk <= 0 || Hv <= 0) return fail(GDN_ERR_SHAPE, "bad sizes B=%d T=%d Hk=%d Hv=%d", B, T, Hk, Hv);
   if (Dk != kD || Dv != kD) return fail(GDN_ERR_SHAPE, "Dk=%d Dv=%d: only 128x128 heads are built", Dk, Dv);
   if (Hv % Hk) return fail(GDN_ERR_SHAPE, "Hv=%d is not a multiple of Hk=%d", Hv, Hk);
@@ -2332,16 +1849,8 @@ bool plan_split(int B, int T, int Hv, bool packed, bool has_state_out, size_t ws
   return true;
 }
 
-// The scan on CTA pairs (chunk_scan_pair_kernel) or one CTA per chain
-// (chunk_scan_kernel): the caller's flag, else the library's choice.
-bool scan_on_pairs(const ChunkParams& p) {
-  if (p.flags & GDN_F_SCAN_PAIR) return true;
-  if (p.flags & GDN_F_SCAN_SINGLE) return false;
-  return false;
-}
-
 // One window's launches: the chunk prefix (packed), the prep, the scan.
-int launch_window(ChunkParams p, int T, int w, int win_len, bool pair, cudaStream_t st) {
+int launch_window(ChunkParams p, int T, int w, int win_len, cudaStream_t st) {
   const bool packed = p.cu != nullptr;
   const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
   p.win_c0 = w * win_len;
@@ -2362,9 +1871,7 @@ int launch_window(ChunkParams p, int T, int w, int win_len, bool pair, cudaStrea
     if (rc != GDN_OK) return rc;
   }
   const unsigned chains = static_cast<unsigned>(p.B * p.Hv);
-  if (pair && p.z) chunk_scan_pair_kernel<true><<<2 * chains, kScanThreadsNorm, kPSmemNorm, st>>>(p);
-  else if (pair) chunk_scan_pair_kernel<false><<<2 * chains, kScanThreads, kPSmem, st>>>(p);
-  else if (p.z) chunk_scan_kernel<true><<<chains, kScanThreadsNorm, kScanSmemNorm, st>>>(p);
+  if (p.z) chunk_scan_kernel<true><<<chains, kScanThreadsNorm, kScanSmemNorm, st>>>(p);
   else chunk_scan_kernel<false><<<chains, kScanThreads, kScanSmem, st>>>(p);
   return cuda_status(cudaGetLastError(), "chunk scan launch");
 }
@@ -2386,19 +1893,12 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
                          : reinterpret_cast<const void*>(chunk_scan_kernel<false>);
   rc = set_smem_attr(scan, p.z ? kScanSmemNorm : kScanSmem, p.z ? attr_scan_norm : attr_scan);
   if (rc != GDN_OK) return rc;
-  const bool pair = scan_on_pairs(p);
-  static bool attr_pair[64] = {false}, attr_pair_norm[64] = {false};
-  if (pair) {
-    rc = p.z ? set_smem_attr(reinterpret_cast<const void*>(chunk_scan_pair_kernel<true>), kPSmemNorm, attr_pair_norm)
-             : set_smem_attr(reinterpret_cast<const void*>(chunk_scan_pair_kernel<false>), kPSmem, attr_pair);
-    if (rc != GDN_OK) return rc;
-  }
   p.chunk_prefix = reinterpret_cast<int32_t*>(ws + kWsHeader);
   p.rec_off = pl.rec_off;
   p.carry = p.state_out ? p.state_out : (pl.n_windows > 1 ? reinterpret_cast<float*>(ws + pl.carry_off) : nullptr);
   p.win_len = pl.win_len;
   for (int w = 0; w < pl.n_windows; ++w) {
-    rc = launch_window(p, T, w, pl.win_len, pair, st);
+    rc = launch_window(p, T, w, pl.win_len, st);
     if (rc != GDN_OK) return rc;
   }
   return GDN_OK;
@@ -2471,10 +1971,7 @@ int run_norm(const void* q, const void* k, const void* v, long long q_stride, lo
              float eps, void* const* dst, int n_dst, long long out_elems, long long out_stride, int out_head0,
              const int32_t* cu_seqlens, int B, int T, int Hk, int Hv, int Dk, int Dv, unsigned flags,
              void* workspace, size_t workspace_size, cudaStream_t stream) {
-  if (flags & ~(GDN_F_QK_L2NORM | GDN_F_SCAN_PAIR | GDN_F_SCAN_SINGLE))
-    return fail(GDN_ERR_FLAGS, "only GDN_F_QK_L2NORM and the scan choice apply (out is bf16)");
-  if ((flags & GDN_F_SCAN_PAIR) && (flags & GDN_F_SCAN_SINGLE))
-    return fail(GDN_ERR_FLAGS, "GDN_F_SCAN_PAIR and GDN_F_SCAN_SINGLE exclude each other");
+  if (flags & ~GDN_F_QK_L2NORM) return fail(GDN_ERR_FLAGS, "only GDN_F_QK_L2NORM applies (out is bf16)");
   if (n_dst < 1 || n_dst > 8 || !dst) return fail(GDN_ERR_SHAPE, "1 to 8 output destinations");
   ChunkParams p;
   int rc = chunked_args(p, q, k, v, q_stride, k_stride, v_stride, a, b, A_log, dt_bias, state_in, state_out, dst[0],

@@ -167,13 +167,6 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// 32-bit load from the shared memory of a CTA of the cluster (cl_addr from mapa)
-__device__ __forceinline__ float ld_cluster_f32(uint32_t cl_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cl_addr) : "memory");
-  return v;
-}
-
 // arrive on the mbarrier at shared::cluster address cl_bar (this CTA's or a peer's)
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_bar) : "memory");

@@ -37,9 +37,6 @@ F_CONV_BF16_OPS = 0x100
 F_CONV_NO_SILU = 0x200
 F_NORM_IN_BF16 = 0x400
 F_NORM_OUT_F32 = 0x800
-F_SCAN_PAIR = 0x1000
-F_SCAN_SINGLE = 0x2000
-_SCAN_FLAGS = {None: 0, "pair": F_SCAN_PAIR, "single": F_SCAN_SINGLE}
 
 D = 128
 
@@ -301,12 +298,11 @@ def tc05_pair_selftest(A, B):
 
 
 def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, state_out=None, out=None,
-                     cu_seqlens=None, *, eps=1e-6, l2norm=True, out_head0=0, workspace=None, scan=None):
+                     cu_seqlens=None, *, eps=1e-6, l2norm=True, out_head0=0, workspace=None):
     """Chunked prefill with the gated RMSNorm fused in (gdn_chunked_norm_fwd_ws).
     q, k, v as chunked_fwd; z (..., Hv, 128) bf16 with contiguous heads;
     gamma (128,) fp32.  out: bf16 (..., H_out, 128) with H_out >= out_head0 +
-    Hv (allocated as (..., Hv, 128) when None).  scan as chunked_fwd.
-    Returns (out, state_out)."""
+    Hv (allocated as (..., Hv, 128) when None).  Returns (out, state_out)."""
     Hk, Hv = q.shape[-2], v.shape[-2]
     for t in (q, k, v, z):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
@@ -334,7 +330,7 @@ def chunked_norm_fwd(q, k, v, a, b, A_log, dt_bias, z, gamma, state_in=None, sta
                                         ptr(b), ptr(A_log), ptr(dt_bias), ptr(state_in), ptr(state_out), ptr(z),
                                         z.stride(-3), ptr(gamma), eps, ptr(out), out.stride(-3), out_head0,
                                         ptr(cu_seqlens), B, T, Hk, Hv, D, D,
-                                        (F_QK_L2NORM if l2norm else 0) | _SCAN_FLAGS[scan],
+                                        F_QK_L2NORM if l2norm else 0,
                                         ptr(workspace), workspace.numel(), stream_ptr(dev)))
     return out, state_out
 
@@ -459,14 +455,13 @@ def chunked_workspace_min_bytes(B, Hv, has_state_out=True) -> int:
 
 
 def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=None, cu_seqlens=None, *,
-                l2norm=True, o_dtype=torch.float32, B=None, T=None, split=False, workspace=None, scan=None):
+                l2norm=True, o_dtype=torch.float32, B=None, T=None, split=False, workspace=None):
     """Chunked prefill.  q, k: (..., Hk, 128) bf16 views of token-major rows
     (any token stride); v: (..., Hv, 128).  Leading dims are (B, T) or, with
     cu_seqlens, (total,).  split=False runs gdn_chunked_fwd (one launch, no
     scratch); split=True runs gdn_chunked_fwd_ws on `workspace` (a uint8 CUDA
     tensor of at least chunked_workspace_bytes(...) bytes, allocated here
-    when None); its state scan runs on CTA pairs (scan="pair"), one CTA per
-    chain ("single") or as the library chooses (None).  Returns (o, state_out)."""
+    when None).  Returns (o, state_out)."""
     Hk, Hv = q.shape[-2], v.shape[-2]
     for t in (q, k, v):
         if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.stride(-2) != 128:
@@ -486,7 +481,7 @@ def chunked_fwd(q, k, v, a, b, A_log, dt_bias, state_in=None, state_out=None, o=
         o = torch.empty(lead + (Hv, D), dtype=o_dtype, device=dev)
     if state_out is None:
         state_out = torch.empty((B, Hv, D, D), dtype=torch.float32, device=dev)
-    flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0) | _SCAN_FLAGS[scan]
+    flags = (F_QK_L2NORM if l2norm else 0) | (F_O_BF16 if o_dtype == torch.bfloat16 else 0)
     if not split:
         check(lib().gdn_chunked_fwd(ptr(q), ptr(k), ptr(v), qs, ks, vs, ptr(a), ptr(b), ptr(A_log), ptr(dt_bias),
                                     ptr(state_in), ptr(state_out), ptr(o), ptr(cu_seqlens), B, T, Hk, Hv, D, D,

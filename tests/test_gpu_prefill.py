@@ -151,22 +151,14 @@ def oracle_chunked(inp, sl=slice(None)):
     return O.chunked_delta(O.expand_heads(q, Hv), O.expand_heads(k, Hv), inp["v"][sl], al, bt, S0)
 
 
-def sched(split):
-    """chunked_fwd keywords of a schedule: False (one kernel), True (split,
-    one CTA per scan chain) or "pair" (split, scan chains on CTA pairs)."""
-    if split == "pair":
-        return dict(split=True, scan="pair")
-    return dict(split=split, scan="single" if split else None)
-
-
 def run_chunked(inp, cu=None, o_dtype=torch.float32, split=False):
     t = lambda n: dev(inp[n], torch.bfloat16)  # noqa: E731
     S0 = None if inp["S0"] is None else dev(inp["S0"])
     return G.chunked_fwd(t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]),
-                         dev(inp["dt_bias"]), state_in=S0, cu_seqlens=cu, o_dtype=o_dtype, **sched(split))
+                         dev(inp["dt_bias"]), state_in=S0, cu_seqlens=cu, o_dtype=o_dtype, split=split)
 
 
-SCHEDULES = [pytest.param(False, id="fused"), pytest.param(True, id="split"), pytest.param("pair", id="pair")]
+SCHEDULES = [pytest.param(False, id="fused"), pytest.param(True, id="split")]
 
 
 @pytest.mark.parametrize("split", SCHEDULES)
@@ -204,7 +196,7 @@ def test_chunked_varlen_packed(split):
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
     o, S = G.chunked_fwd(t("q"), t("k"), t("v"), dev(inp["a"][0]), dev(inp["b"][0]), dev(inp["A_log"]),
-                         dev(inp["dt_bias"]), state_in=dev(S0), cu_seqlens=dev(cu, torch.int32), **sched(split))
+                         dev(inp["dt_bias"]), state_in=dev(S0), cu_seqlens=dev(cu, torch.int32), split=split)
     oh, Sh = host(o), host(S)
     for s, L in enumerate(lens):
         sub = dict(inp)
@@ -312,7 +304,7 @@ def test_config3_pipeline_conv_chunked_norm(split):
     q = y[..., :2048].view(1, T, 16, 128)
     k = y[..., 2048:4096].view(1, T, 16, 128)
     v = y[..., 4096:].view(1, T, 48, 128)
-    o, S = G.chunked_fwd(q, k, v, dev(a), dev(b), dev(A_log), dev(dt), **sched(split))
+    o, S = G.chunked_fwd(q, k, v, dev(a), dev(b), dev(A_log), dev(dt), split=split)
     out = G.gated_rmsnorm_fwd(o, dev(z, torch.bfloat16), dev(gamma), out_dtype=torch.float32)
 
     yo, _ = O.depthwise_conv(x, w)
@@ -342,8 +334,7 @@ def norm_inputs(rng, shape):
 
 
 @pytest.mark.parametrize("lens", [[200, 200], [100, 0, 257, 64, 3]])
-@pytest.mark.parametrize("scan", ["single", "pair"])
-def test_chunked_norm_matches_chunked_then_norm(lens, scan):
+def test_chunked_norm_matches_chunked_then_norm(lens):
     """gdn_chunked_norm_fwd_ws against gdn_chunked_fwd_ws followed by
     gdn_gated_rmsnorm_fwd (bf16 out): the same arithmetic but for the order of
     the sum of squares, so within one bf16 rounding; and against the oracle."""
@@ -366,9 +357,9 @@ def test_chunked_norm_matches_chunked_then_norm(lens, scan):
         g = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]))  # noqa: E731
         zz = dev(z.reshape(B, T, Hv, 128), torch.bfloat16)
     args = (t("q"), t("k"), t("v"), g("a"), g("b"), dev(inp["A_log"]), dev(inp["dt_bias"]))
-    o, S = G.chunked_fwd(*args, state_in=dev(S0), cu_seqlens=cu, split=True, scan=scan)
+    o, S = G.chunked_fwd(*args, state_in=dev(S0), cu_seqlens=cu, split=True)
     ref = G.gated_rmsnorm_fwd(o, zz, dev(gamma))
-    out, S2 = G.chunked_norm_fwd(*args, zz, dev(gamma), state_in=dev(S0), cu_seqlens=cu, scan=scan)
+    out, S2 = G.chunked_norm_fwd(*args, zz, dev(gamma), state_in=dev(S0), cu_seqlens=cu)
     torch.cuda.synchronize()
     a, r = host(out), host(ref)
     assert np.max(np.abs(a - r)) <= 2 ** -8 * np.max(np.abs(r)) + 1e-6
@@ -387,8 +378,7 @@ def test_chunked_norm_matches_chunked_then_norm(lens, scan):
     assert G.take_device_error() == 0
 
 
-@pytest.mark.parametrize("scan", ["single", "pair"])
-def test_chunked_norm_writes_its_heads_inside_wider_rows(scan):
+def test_chunked_norm_writes_its_heads_inside_wider_rows():
     """out_head0 / out_stride place the call's heads inside a wider output row
     (the head-sharded layout); the other heads of the row are left alone."""
     rng = np.random.default_rng(90)
@@ -397,10 +387,9 @@ def test_chunked_norm_writes_its_heads_inside_wider_rows(scan):
     z, gamma = norm_inputs(rng, (1, T, Hv, 128))
     t = lambda n: dev(inp[n], torch.bfloat16)  # noqa: E731
     args = (t("q"), t("k"), t("v"), dev(inp["a"]), dev(inp["b"]), dev(inp["A_log"]), dev(inp["dt_bias"]))
-    own, _ = G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]), scan=scan)
+    own, _ = G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]))
     wide = torch.full((1, T, 12, 128), 3.0, dtype=torch.bfloat16, device="cuda")
-    G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]), out=wide, out_head0=6,
-                       scan=scan)
+    G.chunked_norm_fwd(*args, dev(z, torch.bfloat16), dev(gamma), state_in=dev(inp["S0"]), out=wide, out_head0=6)
     torch.cuda.synchronize()
     assert torch.equal(wide[:, :, 6:9], own)
     assert bool((wide[:, :, :6] == 3.0).all()) and bool((wide[:, :, 9:] == 3.0).all())
@@ -408,8 +397,7 @@ def test_chunked_norm_writes_its_heads_inside_wider_rows(scan):
 
 @pytest.mark.parametrize("lens", [[300, 300], [100, 0, 257, 64, 3, 1, 640]])
 @pytest.mark.parametrize("with_state_out", [True, False])
-@pytest.mark.parametrize("scan", ["single", "pair"])
-def test_split_schedule_in_windows_matches_one_pass(lens, with_state_out, scan):
+def test_split_schedule_in_windows_matches_one_pass(lens, with_state_out):
     """A workspace smaller than one pass runs the call in windows of w chunks
     per sequence (state carried in state_out, or in the workspace when the
     call keeps none): o and the final state are bit-identical to one pass,
@@ -433,8 +421,8 @@ def test_split_schedule_in_windows_matches_one_pass(lens, with_state_out, scan):
         g = lambda n: dev(inp[n][0].reshape((B, T) + inp[n].shape[2:]))  # noqa: E731
     q, k, v, a, b = t("q"), t("k"), t("v"), g("a"), g("b")
     A_log, dtb = dev(inp["A_log"]), dev(inp["dt_bias"])      # kept alive across the asynchronous calls
-    o_ref, S_ref = G.chunked_fwd(q, k, v, a, b, A_log, dtb, state_in=S0, cu_seqlens=cu, split=True, scan=scan)
-    flags = G.F_QK_L2NORM | G._SCAN_FLAGS[scan]
+    o_ref, S_ref = G.chunked_fwd(q, k, v, a, b, A_log, dtb, state_in=S0, cu_seqlens=cu, split=True)
+    flags = G.F_QK_L2NORM
     L = G.lib()
     rec = L.gdn_chunked_workspace_bytes(1, 64, 1, 0) - L.gdn_chunked_workspace_bytes(1, 0, 1, 0)
     base = G.chunked_workspace_min_bytes(B, Hv, with_state_out)
@@ -473,10 +461,10 @@ def test_chunked_empty_batch_copies_the_state(split):
     v = torch.empty((2, 0, Hv, 128), dtype=torch.bfloat16, device="cuda")
     g = torch.empty((2, 0, Hv), device="cuda")
     A_log, dtb = dev(np.zeros(Hv, np.float32)), dev(np.zeros(Hv, np.float32))
-    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, state_in=dev(S0), **sched(split))
+    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, state_in=dev(S0), split=split)
     torch.cuda.synchronize()
     assert o.numel() == 0 and np.array_equal(host(S), S0)
-    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, **sched(split))
+    o, S = G.chunked_fwd(q, q, v, g, g, A_log, dtb, split=split)
     torch.cuda.synchronize()
     assert not host(S).any()
     cu = dev(np.zeros(4, np.int32), torch.int32)             # three empty packed sequences
@@ -484,7 +472,7 @@ def test_chunked_empty_batch_copies_the_state(split):
     vp = torch.empty((0, Hv, 128), dtype=torch.bfloat16, device="cuda")
     gp = torch.empty((0, Hv), device="cuda")
     S3 = rng.standard_normal((3, Hv, 128, 128), dtype=np.float32)
-    o, S = G.chunked_fwd(qp, qp, vp, gp, gp, A_log, dtb, state_in=dev(S3), cu_seqlens=cu, **sched(split))
+    o, S = G.chunked_fwd(qp, qp, vp, gp, gp, A_log, dtb, state_in=dev(S3), cu_seqlens=cu, split=split)
     torch.cuda.synchronize()
     assert np.array_equal(host(S), S3)
     assert G.take_device_error() == 0
@@ -503,8 +491,7 @@ def test_chunked_head_ratios(Hk, Hv, split):
 
 
 @pytest.mark.parametrize("lens", [[300, 300], [100, 0, 257, 64, 3, 1, 640]])
-@pytest.mark.parametrize("scan", ["single", "pair"])
-def test_chunked_norm_in_windows_matches_one_pass(lens, scan):
+def test_chunked_norm_in_windows_matches_one_pass(lens):
     """gdn_chunked_norm_fwd_ws with a workspace of w = 1, 2, 3 chunks per
     sequence (the norm warps take the window's chunk offsets for z and the
     output rows): the normed output and the final state bit-identical to one
@@ -531,7 +518,7 @@ def test_chunked_norm_in_windows_matches_one_pass(lens, scan):
         zz = dev(z.reshape(B, T, Hv, 128), torch.bfloat16)
     q, k, v, a, b = t("q"), t("k"), t("v"), g("a"), g("b")
     A_log, dtb, gam = dev(inp["A_log"]), dev(inp["dt_bias"]), dev(gamma)
-    out_ref, S_ref = G.chunked_norm_fwd(q, k, v, a, b, A_log, dtb, zz, gam, state_in=S0, cu_seqlens=cu, scan=scan)
+    out_ref, S_ref = G.chunked_norm_fwd(q, k, v, a, b, A_log, dtb, zz, gam, state_in=S0, cu_seqlens=cu)
     L = G.lib()
     rec = L.gdn_chunked_workspace_bytes(1, 64, 1, 0) - L.gdn_chunked_workspace_bytes(1, 0, 1, 0)
     base = G.chunked_workspace_min_bytes(B, Hv, True)
@@ -543,45 +530,11 @@ def test_chunked_norm_in_windows_matches_one_pass(lens, scan):
         S = torch.empty_like(S_ref)
         rc = L.gdn_chunked_norm_fwd_ws(P(q), P(k), P(v), q.stride(-3), k.stride(-3), v.stride(-3), P(a), P(b),
                                        P(A_log), P(dtb), P(S0), P(S), P(zz), Hv * 128, P(gam), ctypes.c_float(1e-6),
-                                       P(out), Hv * 128, 0, P(cu), B, T, Hk, Hv, 128, 128,
-                                       G.F_QK_L2NORM | G._SCAN_FLAGS[scan], P(ws),
+                                       P(out), Hv * 128, 0, P(cu), B, T, Hk, Hv, 128, 128, G.F_QK_L2NORM, P(ws),
                                        ctypes.c_size_t(size), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         assert rc == G.GDN_OK, L.gdn_last_error().decode()
         torch.cuda.synchronize()
         assert torch.equal(out, out_ref), w
         assert torch.equal(S, S_ref), w
     assert G.take_device_error() == 0
-
-
-@pytest.mark.parametrize("lens,slow", [([300], True), ([100, 0, 257, 64, 3, 1, 640], False),
-                                       ([2000, 513], True)])
-def test_pair_scan_matches_single_scan(lens, slow):
-    """The scan on CTA pairs (GDN_F_SCAN_PAIR: each chain's value rows split
-    64 + 64 over two CTAs, cta_group::2 MMAs) computes the same products as
-    the one-CTA scan in the same order per element: outputs and final states
-    agree to 1e-6 relative L2, and both stay within the prefill bound of the
-    oracle."""
-    rng = np.random.default_rng(90 + len(lens))
-    Hk, Hv = 2, 6
-    total = sum(lens)
-    inp = chunk_inputs(rng, 1, total, Hk, Hv, slow_decay=slow)
-    S0 = rng.standard_normal((len(lens), Hv, 128, 128), dtype=np.float32) * np.float32(0.05)
-    cu = dev(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), torch.int32)
-    t = lambda n: dev(inp[n][0], torch.bfloat16)  # noqa: E731
-    g = lambda n: dev(inp[n][0])  # noqa: E731
-    args = (t("q"), t("k"), t("v"), g("a"), g("b"), dev(inp["A_log"]), dev(inp["dt_bias"]))
-    o_s, S_s = G.chunked_fwd(*args, state_in=dev(S0), cu_seqlens=cu, split=True, scan="single")
-    o_p, S_p = G.chunked_fwd(*args, state_in=dev(S0), cu_seqlens=cu, split=True, scan="pair")
-    assert G.take_device_error() == 0
-    assert O.rel_l2(host(o_p), host(o_s)) < 1e-6, O.rel_l2(host(o_p), host(o_s))
-    assert O.rel_l2(host(S_p), host(S_s)) < 1e-6, O.rel_l2(host(S_p), host(S_s))
-    cuh = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
-    s = int(np.argmax(lens))
-    sub = dict(inp)
-    for n in ("q", "k", "v", "a", "b"):
-        sub[n] = inp[n][:, cuh[s]:cuh[s + 1]]
-    sub["S0"] = S0[s:s + 1]
-    ro, rS = oracle_chunked(sub)
-    assert O.rel_l2(host(o_p)[cuh[s]:cuh[s + 1]], ro[0]) < PREFILL_TOL
-    assert O.rel_l2(host(S_p)[s:s + 1], rS) < PREFILL_TOL
 
