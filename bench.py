@@ -1019,6 +1019,48 @@ def run_layer(args, device, world):
     return res
 
 
+def run_gemm(args, device):
+    """The layer's projection GEMMs on their own (rows = tokens, the three
+    weight shapes of the 27B GDN layer): this library's tcgen05 kernels
+    (gdn_gemm_bf16, gdn_in_proj_conv with the conv + SiLU in its epilogue)
+    against cuBLAS through torch.matmul, CUDA events over `steps` calls each
+    after `warmup` calls.  For --gemm-only and ncu captures of the GEMM."""
+    import gdn_b200 as G
+    M, steps, warmup = args.gemm_m, max(args.steps, 1), max(args.warmup, 1)
+    g = torch.Generator(device=device).manual_seed(7)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    res = {"workload": f"M={M} token rows, bf16 in / fp32 accumulate / bf16 out", "shapes": {}}
+    for name, N, K in (("in_proj_qkv", 10240, 5120), ("in_proj_zab", 6240, 5120), ("out_proj", 5120, 6144)):
+        A = torch.randn((M, K), generator=g, device=device).bfloat16()
+        B = (torch.randn((N, K), generator=g, device=device) * K ** -0.5).bfloat16()
+        C = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+        fl = 2.0 * M * N * K
+        ms = timed(lambda: G.gemm_bf16(A, B, C))
+        ms_cublas = timed(lambda: torch.matmul(A, B.t(), out=C))
+        r = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "cublas_ms": round(ms_cublas, 4),
+             "cublas_tflops": round(fl / ms_cublas / 1e9, 1), "vs_cublas": round(ms_cublas / ms, 3)}
+        if name == "in_proj_qkv":
+            w = (torch.randn((N, 4), generator=g, device=device) * 0.5).bfloat16()
+            y = torch.empty_like(C)
+            r["with_conv_ms"] = round(timed(lambda: G.in_proj_conv(A.view(1, M, K), B, w, y=y.view(1, M, N))), 4)
+        res["shapes"][name] = r
+        del A, B, C
+    res["device_error"] = G.take_device_error()
+    return res
+
+
 def run_layer_decode(args, device, world, Lp=8):
     """Decode steps through whole layers (gdn_layer.GDNLayer.forward_decode):
     B = args.batch x N sequences per step in seeded random slots of per-layer
@@ -1209,6 +1251,8 @@ def main():
     ap.add_argument("--prefill-only", action="store_true", help="only the config-3 prefill (for profiling)")
     ap.add_argument("--stack-layers", type=int, default=48,
                     help="config 4: also time this many layer steps back to back (BASELINE's 48-layer stack; 0 = skip)")
+    ap.add_argument("--gemm-only", action="store_true", help="only the projection GEMMs against cuBLAS (--gemm-m rows)")
+    ap.add_argument("--gemm-m", type=int, default=65536)
     ap.add_argument("--prefill-ws-gb", type=float, default=0.0,
                     help="cap the split schedule's workspace (GB); smaller than one pass runs in windows")
     args = ap.parse_args()
@@ -1228,6 +1272,13 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=torch.device("cuda", local))
     try:
+        if args.gemm_only:
+            device = torch.device("cuda", local)
+            torch.cuda.set_device(device)
+            line = {"gemm": run_gemm(args, device)}
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return 0
         if args.prefill_only:
             import gdn_b200 as G
             device = torch.device("cuda", local)
