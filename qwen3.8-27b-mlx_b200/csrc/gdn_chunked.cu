@@ -34,6 +34,7 @@
 //     only the state chain, so the serial work per chunk shrinks to the
 //     state-dependent MMAs and their epilogues.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -116,14 +117,31 @@ constexpr uint32_t kPColGP = 0, kPColW = 0, kPColU = 64;
 // One workspace record per (chunk, value head): the prep kernel's outputs as
 // tensor-core operands (K-major, no swizzle) in three groups that the scan
 // kernel bulk-copies into shared memory a chunk ahead of their use.  -W and
-// Qs form one 128-row B operand, M and K-hat^T one 192-row B operand.
-constexpr uint32_t kRecW = 0;                       // -W, 64 x 128, SBO 4096               group 1
-constexpr uint32_t kRecQ = kRecW + kC * kD * 4;     // diag(g r_q) Q, 64 x 128, SBO 4096    group 1
-constexpr uint32_t kRecM = kRecQ + kC * kD * 4;     // M, 64 x 64, SBO 2048                 group 2
-constexpr uint32_t kRecKh = kRecM + kC * kC * 4;    // K-hat^T, 128 x 64, SBO 2048          group 2
-constexpr uint32_t kRecU = kRecKh + kD * kC * 4;    // U0^T by column quads, see u0_index      group 3
-constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // [0] = g_last                         group 3
+// Qs form one 128-row B operand, M and K-hat^T one 192-row B operand, all
+// fp16 for kind::f16 products (the same 10-bit mantissa as tf32, at half the
+// bytes and half the MMA instructions of the state chain); U0^T stays fp32
+// (it is added in the scan's epilogue).
+constexpr uint32_t kSboH128 = (kD * 2 / 16) * 128;  // 8-row group stride of 128-wide 16-bit rows (2048)
+constexpr uint32_t kSboH64 = (kC * 2 / 16) * 128;   // ... of 64-wide 16-bit rows (1024)
+constexpr uint32_t kRecW = 0;                       // -W, 64 x 128 fp16, SBO 2048           group 1
+constexpr uint32_t kRecQ = kRecW + kC * kD * 2;     // diag(g r_q) Q, 64 x 128 fp16         group 1
+constexpr uint32_t kRecM = kRecQ + kC * kD * 2;     // M, 64 x 64 fp16, SBO 1024             group 2
+constexpr uint32_t kRecKh = kRecM + kC * kC * 2;    // K-hat^T, 128 x 64 fp16, SBO 1024      group 2
+constexpr uint32_t kRecU = kRecKh + kD * kC * 2;    // U0^T fp32 by column quads, see u0_index  group 3
+constexpr uint32_t kRecSc = kRecU + kD * kC * 4;    // [0] = g_last                          group 3
 constexpr uint32_t kRecBytes = kRecSc + 1024;       // multiple of 256
+// fp16 pairs and quads for the record's operands (round to nearest)
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint2 pack_h4(float a, float b, float c, float d) {
+  return make_uint2(pack_h2(a, b), pack_h2(c, d));
+}
+// address of element (r, k) of a K-major 16-bit operand with 8-row stride sbo
+__device__ __forceinline__ unsigned char* at_h(unsigned char* base, int r, int k, uint32_t sbo) {
+  return base + tc::kmajor_offset(r, k, 2, sbo);
+}
 // float4 index of U0^T[row][4 quad .. 4 quad + 3] in the record: value rows
 // 0-63 and 64-127 are two contiguous blocks of 16 quads x 64 rows.
 __host__ __device__ constexpr int u0_index(int quad, int row) {
@@ -137,8 +155,9 @@ constexpr size_t kWsHeader = 256;                   // then the chunk prefix (B+
 // kernel); group 3 at the record's own offsets; then U^T and the barriers
 constexpr uint32_t kScanG1 = 0;
 constexpr uint32_t kScanG2 = kRecM;
-constexpr uint32_t kScanU = kRecBytes;              // U^T 128 x 64 (32 KiB), operand of (e2), (f)
-constexpr uint32_t kScanBar = kScanU + kD * kC * 4; // 4 mbarriers, TMEM base at +32
+constexpr uint32_t kScanR = kRecBytes;              // fp16(R) 128 x 128 (32 KiB), A of the first batch
+constexpr uint32_t kScanU = kScanR + kD * kD * 2;   // fp16(U^T) 128 x 64 (16 KiB), A of the second batch
+constexpr uint32_t kScanBar = kScanU + kD * kC * 2; // 4 mbarriers, TMEM base at +32
 constexpr uint32_t kScanNorm = kScanBar + 64;       // fused norm: partial sums of squares, 4 x 64 floats
 constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
 // fused norm: mbarriers "y of a chunk parity is in TMEM" (arrived by the MMA
@@ -1119,16 +1138,13 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&qr[m]);
-      float x[8];
+      uint32_t x[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(hq[e]);
-        x[2 * e] = tc::to_tf32(f.x * s);
-        x[2 * e + 1] = tc::to_tf32(f.y * s);
+        x[e] = pack_h2(f.x * s, f.y * s);
       }
-      *reinterpret_cast<float4*>(at(rec + kRecQ, i, qd * 32 + m * 8, kSbo128)) = make_float4(x[0], x[1], x[2], x[3]);
-      *reinterpret_cast<float4*>(at(rec + kRecQ, i, qd * 32 + m * 8 + 4, kSbo128)) =
-          make_float4(x[4], x[5], x[6], x[7]);
+      *reinterpret_cast<uint4*>(at_h(rec + kRecQ, i, qd * 32 + m * 8, kSboH128)) = make_uint4(x[0], x[1], x[2], x[3]);
     }
   }
   __syncthreads();
@@ -1184,9 +1200,9 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = c.half * 32 + e + u;
-          m[u] = (j <= i) ? tc::to_tf32(fi * rk[u] * __expf(gi - gm[u]) * gp[e + u]) : 0.f;
+          m[u] = (j <= i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
         }
-        *reinterpret_cast<float4*>(at(rec + kRecM, i, c.half * 32 + e, kSbo64)) = make_float4(m[0], m[1], m[2], m[3]);
+        *reinterpret_cast<uint2*>(at_h(rec + kRecM, i, c.half * 32 + e, kSboH64)) = pack_h4(m[0], m[1], m[2], m[3]);
       }
     }
   }
@@ -1233,9 +1249,8 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
           const float4 sc = *reinterpret_cast<const float4*>(c.s_kh + t);
           const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
           const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
-          *reinterpret_cast<float4*>(at(rec + kRecKh, k, t, kSbo64)) =
-              make_float4(tc::to_tf32(f0.x * sc.x), tc::to_tf32(f0.y * sc.y), tc::to_tf32(f1.x * sc.z),
-                          tc::to_tf32(f1.y * sc.w));
+          *reinterpret_cast<uint2*>(at_h(rec + kRecKh, k, t, kSboH64)) =
+              pack_h4(f0.x * sc.x, f0.y * sc.y, f1.x * sc.z, f1.y * sc.w);
         }
       }
     }
@@ -1326,14 +1341,14 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
       for (int e = 0; e < 32; e += 4)
         ud[u0_index(c.half * 8 + e / 4, c.row)] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
       // -W: lane k holds W^T[k][j] for its 32 j; 4 x 4 transposes across lane
-      // quads give each lane 4 consecutive k of one j, one 16-byte store
+      // quads give each lane 4 consecutive k of one j, one 8-byte fp16 store
       const int u4 = c.lane & 3;
 #pragma unroll
       for (int e = 0; e < 32; e += 4) {
         float v0 = w[e], v1 = w[e + 1], v2 = w[e + 2], v3 = w[e + 3];
         quad_transpose(v0, v1, v2, v3, u4);
-        *reinterpret_cast<float4*>(at(rec + kRecW, c.half * 32 + e + u4, c.row - u4, kSbo128)) =
-            make_float4(-tc::to_tf32(v0), -tc::to_tf32(v1), -tc::to_tf32(v2), -tc::to_tf32(v3));
+        *reinterpret_cast<uint2*>(at_h(rec + kRecW, c.half * 32 + e + u4, c.row - u4, kSboH128)) =
+            pack_h4(-v0, -v1, -v2, -v3);
       }
       if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
     }
@@ -1397,11 +1412,12 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
   n_chunks = n_chunks < 0 ? 0 : (n_chunks > p.win_len ? p.win_len : n_chunks);
   if (p.win_c0 > 0 && n_chunks == 0) return;       // finished in an earlier window: its state is in place
   const long long slot0 = seq_first_slot(p, b);
-  // TMEM columns: R tf32 [0,128) | U (even) | y (even) | R fp32 [256,384) | y (odd) | U (odd).
+  // TMEM columns: [0,128) unused | U (even) | y (even) | R fp32 [256,384) | y (odd) | U (odd).
   // The first MMA batch writes [U | y] (even) or [y | U] (odd) in one N = 128
   // product, the second [y | R] or [R | y] in one N = 192 product; odd chunks
   // mirror the order of the stacked B operands in shared memory to match.
-  constexpr uint32_t cR = 0, cDR = 256;
+  // Both batches are kind::f16: fp16(R) and fp16(U^T) from shared memory.
+  constexpr uint32_t cDR = 256;
   if (NORM && c.tid == 0) {
     ptx::mbar_init(ybar + 0, 1);
     ptx::mbar_init(ybar + 1, 1);
@@ -1421,20 +1437,13 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       const unsigned char* rec = record(p, slot0 + ch, c.h);
       const bool odd = ch & 1;
       if (g == 1) {
-        ptx::mbar_arrive_expect_tx(&bars[1], 2 * kC * kD * 4);
-        unsigned char* dw = sm + kScanG1 + (odd ? kC * kD * 4 : 0);
-        unsigned char* dq = sm + kScanG1 + (odd ? 0 : kC * kD * 4);
-        for (uint32_t off = 0; off < kC * kD * 4; off += 16384) {
-          ptx::bulk_g2s(dw + off, rec + kRecW + off, 16384, &bars[1]);
-          ptx::bulk_g2s(dq + off, rec + kRecQ + off, 16384, &bars[1]);
-        }
+        ptx::mbar_arrive_expect_tx(&bars[1], 2 * kC * kD * 2);
+        ptx::bulk_g2s(sm + kScanG1 + (odd ? kC * kD * 2 : 0), rec + kRecW, kC * kD * 2, &bars[1]);
+        ptx::bulk_g2s(sm + kScanG1 + (odd ? 0 : kC * kD * 2), rec + kRecQ, kC * kD * 2, &bars[1]);
       } else if (g == 2) {
-        ptx::mbar_arrive_expect_tx(&bars[2], kC * kC * 4 + kD * kC * 4);
-        unsigned char* dm = sm + kScanG2 + (odd ? kD * kC * 4 : 0);
-        unsigned char* dk = sm + kScanG2 + (odd ? 0 : kC * kC * 4);
-        ptx::bulk_g2s(dm, rec + kRecM, kC * kC * 4, &bars[2]);
-        for (uint32_t off = 0; off < kD * kC * 4; off += 16384)
-          ptx::bulk_g2s(dk + off, rec + kRecKh + off, 16384, &bars[2]);
+        ptx::mbar_arrive_expect_tx(&bars[2], kC * kC * 2 + kD * kC * 2);
+        ptx::bulk_g2s(sm + kScanG2 + (odd ? kD * kC * 2 : 0), rec + kRecM, kC * kC * 2, &bars[2]);
+        ptx::bulk_g2s(sm + kScanG2 + (odd ? 0 : kC * kC * 2), rec + kRecKh, kD * kC * 2, &bars[2]);
       } else {
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive_expect_tx(&bars[3], kRecBytes - kRecU);
@@ -1461,20 +1470,33 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
     return all;
   };
   // R (fp32 master) -> tf32 operand copy, or R *= gl in place (a worker's 32 columns)
-  auto r_pass = [&](bool to_tf32, float gl) {
+  auto r_pass = [&](bool to_f16, float gl) {
     float v[16], w[16];
     tc::tmem_ld16(lane_cols + cDR, v);
     tc::tmem_ld16(lane_cols + cDR + 16, w);
     tc::tmem_ld_wait();
+    if (to_f16) {              // fp16(R) rows -> the first batch's A operand (row c.row, keys 32 cg ..)
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = to_tf32 ? tc::to_tf32(v[i]) : v[i] * gl;
-      w[i] = to_tf32 ? tc::to_tf32(w[i]) : w[i] * gl;
+      for (int i = 0; i < 16; i += 8) {
+        *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + i, kSboH128)) =
+            make_uint4(pack_h2(v[i], v[i + 1]), pack_h2(v[i + 2], v[i + 3]), pack_h2(v[i + 4], v[i + 5]),
+                       pack_h2(v[i + 6], v[i + 7]));
+        *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + 16 + i, kSboH128)) =
+            make_uint4(pack_h2(w[i], w[i + 1]), pack_h2(w[i + 2], w[i + 3]), pack_h2(w[i + 4], w[i + 5]),
+                       pack_h2(w[i + 6], w[i + 7]));
+      }
+      ptx::fence_proxy_async_smem();
+    } else {                   // R *= g_last in place
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] *= gl;
+        w[i] *= gl;
+      }
+      tc::tmem_st16(lane_cols + cDR, v);
+      tc::tmem_st16(lane_cols + cDR + 16, w);
     }
-    tc::tmem_st16(lane_cols + (to_tf32 ? cR : cDR), v);
-    tc::tmem_st16(lane_cols + (to_tf32 ? cR : cDR) + 16, w);
   };
-  // U^T = (R (-W)^T from TMEM) + U0^T (shared memory) -> tf32 rows of the U^T operand
+  // U^T = (R (-W)^T from TMEM) + U0^T (shared memory) -> fp16 rows of the U^T operand
   auto epi_u = [&](uint32_t col_u) {
     float u[16];
     tc::tmem_ld16(c.tb + col_u + c.my + cg * 16, u);
@@ -1482,10 +1504,16 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
 #pragma unroll
     for (int e = 0; e < 16; e += 4) {
       const float4 f = sU0[u0_index(cg * 4 + e / 4, c.row)];
-      *reinterpret_cast<float4*>(at(sU, c.row, cg * 16 + e, kSbo64)) =
-          make_float4(tc::to_tf32(u[e] + f.x), tc::to_tf32(u[e + 1] + f.y), tc::to_tf32(u[e + 2] + f.z),
-                      tc::to_tf32(u[e + 3] + f.w));
+      u[e] += f.x;
+      u[e + 1] += f.y;
+      u[e + 2] += f.z;
+      u[e + 3] += f.w;
     }
+#pragma unroll
+    for (int e = 0; e < 16; e += 8)
+      *reinterpret_cast<uint4*>(at_h(sU, c.row, cg * 16 + e, kSboH64)) =
+          make_uint4(pack_h2(u[e], u[e + 1]), pack_h2(u[e + 2], u[e + 3]), pack_h2(u[e + 4], u[e + 5]),
+                     pack_h2(u[e + 6], u[e + 7]));
     ptx::fence_proxy_async_smem();
   };
   // ---- fused norm: the 8 norm warps (warp % 4 = TMEM lane quarter q, dv =
@@ -1647,7 +1675,7 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       load(2, 0);
       load(3, 0);
       if (worker) {
-        r_pass(true, 1.f);                  // tf32(R_0)
+        r_pass(true, 1.f);                  // fp16(R_0)
         tc::tmem_st_wait();
       }
       tc::fence_before_sync();
@@ -1670,9 +1698,10 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
         if (NORM && ch >= 2) yok = ptx::mbar_wait(&ybar[2 + (ch & 1)], ((ch >> 1) - 1) & 1);
         if (yok) {
           tc::fence_after_sync();
-          const uint32_t id = tc::instr_desc(tc::kTF32, 128, 2 * kC);
-          for (int j = 0; j < kD / 8; ++j)
-            tc::mma_ts_tf32(c.tb + col_b1, c.tb + cR + j * 8, desc(sm + kScanG1, j * 256, kSbo128), id, j > 0);
+          const uint32_t id = tc::instr_desc(tc::kF16, 128, 2 * kC);
+          for (int j = 0; j < kD / 16; ++j)
+            tc::mma_ss<tc::kF16>(c.tb + col_b1, desc(sm + kScanR, j * 256, kSboH128),
+                                 desc(sm + kScanG1, j * 256, kSboH128), id, j > 0);
           tc::mma_commit(c.bar);
         }
       } else if (worker) {       // under it: R *= g_last(ch) for the update, half of the previous o
@@ -1691,9 +1720,9 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       tc::fence_after_sync();
       GDN_TICK(25);
       if (issuer) {              // second batch: [y | R] += U^T [M; K-hat^T]^T
-        const uint32_t id = tc::instr_desc(tc::kTF32, 128, kC + kD);
-        for (int j = 0; j < kC / 8; ++j)
-          tc::mma_ss<tc::kTF32>(c.tb + col_b2, desc(sU, j * 256, kSbo64), desc(sm + kScanG2, j * 256, kSbo64), id, 1);
+        const uint32_t id = tc::instr_desc(tc::kF16, 128, kC + kD);
+        for (int j = 0; j < kC / 16; ++j)
+          tc::mma_ss<tc::kF16>(c.tb + col_b2, desc(sU, j * 256, kSboH64), desc(sm + kScanG2, j * 256, kSboH64), id, 1);
         tc::mma_commit(c.bar);
         if (NORM) tc::mma_commit(&ybar[ch & 1]);   // y of chunk ch complete: the norm warps take it
       } else if (worker && !NORM && ch > 0) {
@@ -1706,7 +1735,7 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       if (ch + 1 < n_chunks) {
         load(2, ch + 1);
         if (worker) {
-          r_pass(true, 1.f);                // tf32(R_{ch+1}) for the next first batch
+          r_pass(true, 1.f);                // fp16(R_{ch+1}) for the next first batch
           tc::tmem_st_wait();
         }
       }

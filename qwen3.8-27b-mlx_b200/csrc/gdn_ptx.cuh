@@ -250,7 +250,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
-enum Kind : uint32_t { kBF16 = 1, kTF32 = 2 };
+enum Kind : uint32_t { kF16 = 0, kBF16 = 1, kTF32 = 2 };
 
 // Instruction descriptor of kind::f16 / kind::tf32 with an fp32 accumulator;
 // a_mn / b_mn select the MN-major layout for A / B (default K-major).

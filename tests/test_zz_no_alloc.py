@@ -126,7 +126,7 @@ def test_static_scratch_matches_workspace_entry_on_two_calls_in_a_row():
 
 
 def test_static_scratch_runs_a_longer_call_in_windows():
-    """1,024 tokens x 48 value heads need 109 MiB of records in one pass; the
+    """1,024 tokens x 48 value heads need 67 MiB of records in one pass; the
     static entry runs them in windows of its 64 MiB, bit-identical to one pass
     on a caller workspace (with and without state_out)."""
     L = G.lib()
@@ -146,13 +146,13 @@ def test_static_scratch_runs_a_longer_call_in_windows():
 
 
 def test_static_scratch_rejects_a_batch_whose_smallest_window_does_not_fit():
-    """10 sequences x 48 value heads: one record each (480 records of 145 KiB)
+    """16 sequences x 48 value heads: one record each (768 records of 89 KiB)
     already exceed the 64 MiB scratch: GDN_ERR_SHAPE, outputs untouched.  The
     buffers have the call's full size, so nothing could be out of bounds
     either way."""
     L = G.lib()
-    X = make_inputs(72, [64] * 10, Hk=16, Hv=48, packed=False, state=False)
-    assert G.chunked_workspace_min_bytes(10, 48, True) > 64 << 20
+    X = make_inputs(72, [64] * 16, Hk=16, Hv=48, packed=False, state=False)
+    assert G.chunked_workspace_min_bytes(16, 48, True) > 64 << 20
     o, S = outputs(X, torch.float32)
     rc = call(L.gdn_chunked_fwd_static, X, o, S, G.F_QK_L2NORM)
     assert rc == G.GDN_ERR_SHAPE
