@@ -55,8 +55,12 @@ class GDNLayer:
         self._ws: Optional[torch.Tensor] = None
         self._gathers = None
         self._g_i = 0
-        # in_proj_z / in_proj_a / in_proj_b stacked: one GEMM, a and b as fp32
-        self.W_zab = torch.cat([W_z, W_a, W_b], 0).contiguous()
+        # in_proj_z / in_proj_a / in_proj_b stacked: one GEMM, a and b as fp32;
+        # zero rows pad the stack to a multiple of 8 columns (the GEMM's
+        # output granule), e.g. 6 value heads per rank: 768 + 6 + 6 -> 784
+        pad = (-(self.hv * D + 2 * self.hv)) % 8
+        parts = [W_z, W_a, W_b] + ([W_z.new_zeros((pad, W_z.shape[1]))] if pad else [])
+        self.W_zab = torch.cat(parts, 0).contiguous()
 
     def token_slice(self, tokens: int):
         """The rows of the layer output this rank computes."""

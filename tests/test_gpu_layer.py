@@ -45,8 +45,10 @@ def reference(x, w, Hk, Hv, lens):
 
 
 @pytest.mark.parametrize("lens,packed", [([80, 80], False), ([50, 0, 130, 7], True)])
-def test_layer_prefill_matches_oracle_block(lens, packed):
-    Hk, Hv, hidden = 4, 12, 512
+@pytest.mark.parametrize("Hk,Hv", [(4, 12), (2, 6)])
+def test_layer_prefill_matches_oracle_block(lens, packed, Hk, Hv):
+    """(2, 6) is an 8-GPU rank's shard: z | a | b is 780 columns, padded to 784."""
+    hidden = 512
     dev = torch.device("cuda")
     w = gdn_layer.random_weights(hidden, Hk, Hv, dev, seed=7)
     tokens = sum(lens)
