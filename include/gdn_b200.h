@@ -208,7 +208,7 @@ int gdn_chunked_fwd(const void* q, const void* k, const void* v,
  * gdn_chunked_workspace_bytes -- device workspace with which
  * gdn_chunked_fwd_ws runs B sequences of T tokens (packed = 0), or B packed
  * sequences of T tokens in all (packed != 0, an upper bound that holds for
- * any cu_seqlens), in one pass: 145 KiB per (64-token chunk, value head).
+ * any cu_seqlens), in one pass: 89 KiB per (64-token chunk, value head).
  * 0 for bad sizes.
  */
 size_t gdn_chunked_workspace_bytes(int B, int T, int Hv, int packed);
@@ -358,7 +358,7 @@ int gdn_ipc_close(void* base);
  *   one in windows of chunks (bit-identical results); only a call with
  *   gdn_chunked_workspace_min_bytes(B, Hv, state_out != NULL) above
  *   GDN_CHUNKED_STATIC_SCRATCH_BYTES (one record per sequence and value head
- *   no longer fits, e.g. B x Hv above about 450) returns GDN_ERR_SHAPE and
+ *   no longer fits, e.g. B x Hv above about 730 with state_out, 430 without) returns GDN_ERR_SHAPE and
  *   touches nothing.
  *   The first call on each device looks up the scratch's address
  *   (cudaGetSymbolAddress, with that device current) and sets the kernels'
