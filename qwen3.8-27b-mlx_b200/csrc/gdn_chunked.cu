@@ -165,6 +165,7 @@ constexpr uint32_t kScanSmem = kScanNorm + 4 * kC * 4;
 // failure flag the norm warps poll; the first 256 bytes of kScanNorm hold
 // the norm warps' per-token partial sums
 constexpr uint32_t kScanYBar = kScanNorm + 768;
+constexpr uint32_t kScanGl1 = kScanNorm + 640;      // g_last, copied with group 1 (for the first batch's R scaling)
 constexpr uint32_t kScanFail = kScanNorm + 800;
 // fused norm: z rows of three chunks (chunk ch in buffer ch % 3), 64 x 128
 // bf16 each; a chunk's normed output rows overwrite its z rows in place
@@ -1377,7 +1378,6 @@ template <bool NORM>
 __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chunk_scan_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const float4* sU0 = reinterpret_cast<const float4*>(sm + kRecU);
-  const float* sSc = reinterpret_cast<const float*>(sm + kRecSc);
   unsigned char* sU = sm + kScanU;
   // [0] MMA; record groups [1] -W | Qs, [2] M | K-hat^T, [3] U0^T | g_last
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kScanBar);
@@ -1437,9 +1437,10 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       const unsigned char* rec = record(p, slot0 + ch, c.h);
       const bool odd = ch & 1;
       if (g == 1) {
-        ptx::mbar_arrive_expect_tx(&bars[1], 2 * kC * kD * 2);
+        ptx::mbar_arrive_expect_tx(&bars[1], 2 * kC * kD * 2 + 16);   // one arrival: the barrier counts 1
         ptx::bulk_g2s(sm + kScanG1 + (odd ? kC * kD * 2 : 0), rec + kRecW, kC * kD * 2, &bars[1]);
         ptx::bulk_g2s(sm + kScanG1 + (odd ? 0 : kC * kD * 2), rec + kRecQ, kC * kD * 2, &bars[1]);
+        ptx::bulk_g2s(sm + kScanGl1, rec + kRecSc, 16, &bars[1]);
       } else if (g == 2) {
         ptx::mbar_arrive_expect_tx(&bars[2], kC * kC * 2 + kD * kC * 2);
         ptx::bulk_g2s(sm + kScanG2 + (odd ? kD * kC * 2 : 0), rec + kRecM, kC * kC * 2, &bars[2]);
@@ -1461,9 +1462,11 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
     return ok;
   };
   // MMA completion: the copy warp polls, the CTA agrees (false if it gave up)
-  auto mma_done = [&](bool ok_in) -> bool {
+  // (g3_ch >= 0: also group 3 of that chunk)
+  auto mma_done = [&](bool ok_in, int g3_ch = -1) -> bool {
     bool ok = ok_in;
     if (mw) ok = ok && ptx::mbar_wait(c.bar, c.phase);
+    if (g3_ch >= 0) ok = wait_group(3, g3_ch) && ok;
     c.phase ^= 1u;
     const bool all = !chain_or(!ok);
     tc::fence_after_sync();
@@ -1686,9 +1689,9 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
       const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
       const uint32_t col_u = odd ? 448 : 128;
-      // -W | Qs and U0^T | g_last of this chunk in shared memory
+      // -W | Qs and g_last of this chunk in shared memory (U0^T is waited for
+      // under the first batch, before the epilogue that adds it)
       bool ok = wait_group(1, ch);
-      ok = wait_group(3, ch) && ok;
       if (chain_or(!ok)) { failed = true; break; }
       tc::fence_after_sync();
       GDN_TICK(29);
@@ -1705,12 +1708,12 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
           tc::mma_commit(c.bar);
         }
       } else if (worker) {       // under it: R *= g_last(ch) for the update, half of the previous o
-        r_pass(false, sSc[0]);
+        r_pass(false, reinterpret_cast<const float*>(sm + kScanGl1)[0]);
         if (!NORM && ch > 0) epi_o(ch - 1, 0);
         tc::tmem_st_wait();
       }
       tc::fence_before_sync();
-      if (!mma_done(yok)) { failed = true; break; }
+      if (!mma_done(yok, ch)) { failed = true; break; }
       GDN_TICK(24);
       if (ch + 1 < n_chunks) load(1, ch + 1);
       if (worker) epi_u(col_u);
