@@ -494,7 +494,8 @@ int gdn_in_proj_conv(const void* x, const void* W, const void* conv_w, const voi
  * mode bit 0: operands rounded to bf16 (kind::f16) instead of tf32;
  * bit 1: A negated by the instruction descriptor; bit 2: A read from tensor
  * memory (tf32 only); bit 3: A laid out MN-major in shared memory; bit 4: B
- * laid out MN-major; bit 7 (alone): issue no MMA and wait on the barrier
+ * laid out MN-major; bit 8 (with bit 0): fp16 instead of bf16; bit 7
+ * (alone): issue no MMA and wait on the barrier
  * with a poll budget of 4096, so that the bounded wait runs out (a test of
  * the timeout path: *status and the device error word are set, D is not
  * written, the kernel returns).  N, K multiples of 16 in [16, 128].

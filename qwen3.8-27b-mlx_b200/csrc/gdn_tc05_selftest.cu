@@ -2,13 +2,14 @@
 // is built on: one CTA computes D (128 x N) = op(A) (128 x K) * B^T (B is
 // N x K) through tcgen05.mma with the accumulator in tensor memory, using the
 // same shared-memory layout, descriptors and TMEM load/store helpers as the
-// prefill kernel.  Modes: tf32 or bf16 operands, A negated by the instruction
+// prefill kernel.  Modes: tf32, bf16 or fp16 operands, A negated by the instruction
 // descriptor, A read from tensor memory instead of shared memory, MN-major
 // operands, D at a column offset of 64 and/or 128 (N up to 256).  A last mode
 // issues no MMA at all and waits on the barrier with a small poll budget, so
 // that the bounded wait runs out: the kernel must then report the timeout
 // (status word and the library's device error word) and return cleanly.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "gdn_internal.h"
@@ -23,7 +24,8 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
                                                             float* __restrict__ D, int N, int K, int mode,
                                                             int* __restrict__ status, int* __restrict__ dev_err) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const bool bf = (mode & 1) != 0;
+  const bool bf = (mode & 1) != 0;                 // 16-bit operands: bf16, or fp16 with bit 8
+  const bool h16 = (mode & 256) != 0;
   const int E = bf ? 2 : 4;
   const uint32_t kbytes = static_cast<uint32_t>(K * E);
   const uint32_t sbo = (kbytes / 16) * 128;
@@ -42,13 +44,15 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   for (int idx = tid; idx < 128 * K; idx += 128) {
     const int r = idx / K, k = idx - r * K;
     const uint32_t off = a_mn ? tc::mnmajor_offset(r, k, E, 128, lboA_mn) : tc::kmajor_offset(r, k, E, sbo);
-    if (bf) *reinterpret_cast<__nv_bfloat16*>(sA + off) = __float2bfloat16_rn(A[idx]);
+    if (bf && h16) *reinterpret_cast<__half*>(sA + off) = __float2half_rn(A[idx]);
+    else if (bf) *reinterpret_cast<__nv_bfloat16*>(sA + off) = __float2bfloat16_rn(A[idx]);
     else *reinterpret_cast<float*>(sA + off) = A[idx];
   }
   for (int idx = tid; idx < N * K; idx += 128) {
     const int r = idx / K, k = idx - r * K;
     const uint32_t off = b_mn ? tc::mnmajor_offset(r, k, E, 128, lboB_mn) : tc::kmajor_offset(r, k, E, sbo);
-    if (bf) *reinterpret_cast<__nv_bfloat16*>(sB + off) = __float2bfloat16_rn(B[idx]);
+    if (bf && h16) *reinterpret_cast<__half*>(sB + off) = __float2half_rn(B[idx]);
+    else if (bf) *reinterpret_cast<__nv_bfloat16*>(sB + off) = __float2bfloat16_rn(B[idx]);
     else *reinterpret_cast<float*>(sB + off) = B[idx];
   }
   ptx::fence_proxy_async_smem();
@@ -84,7 +88,8 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
   const bool no_mma = (mode & 128) != 0;
   const uint32_t limit = no_mma ? (1u << 12) : ptx::kSpinLimit;
   if (tid == 0 && !no_mma) {
-    const uint32_t idesc = tc::instr_desc(bf ? tc::kBF16 : tc::kTF32, 128, N, (mode & 2) != 0, false, a_mn, b_mn);
+    const uint32_t idesc = tc::instr_desc(bf ? (h16 ? tc::kF16 : tc::kBF16) : tc::kTF32, 128, N, (mode & 2) != 0,
+                                          false, a_mn, b_mn);
     const int steps = static_cast<int>(kbytes / 32);
     const int kgroups = bf ? 2 : 1;                 // K groups of 8 per MMA
     for (int j = 0; j < steps; ++j) {
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(128) tc05_selftest_kernel(const float* __restr
       } else {
         const uint64_t ad = a_mn ? tc::smem_desc(ptx::smem_u32(sA) + j * kgroups * lboA_mn, lboA_mn, 128)
                                  : tc::smem_desc(ptx::smem_u32(sA) + j * 256, 128, sbo);
-        if (bf) tc::mma_ss<tc::kBF16>(tD, ad, bd, idesc, j > 0);
+        if (bf) tc::mma_ss<tc::kBF16>(tD, ad, bd, idesc, j > 0);   // kind::f16: bf16 or fp16 by idesc
         else tc::mma_ss<tc::kTF32>(tD, ad, bd, idesc, j > 0);
       }
     }
@@ -222,7 +227,8 @@ extern "C" int gdn_tc05_pair_selftest(const float* A, const float* B, float* raw
 extern "C" int gdn_tc05_selftest(const float* A, const float* B, float* D, int N, int K, int mode,
                                  int* status, void* stream) {
   clear_error();
-  if (mode & ~255) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~255);
+  if (mode & ~511) return fail(GDN_ERR_FLAGS, "unknown mode bits 0x%x", mode & ~511);
+  if ((mode & 256) && !(mode & 1)) return fail(GDN_ERR_FLAGS, "fp16 operands (bit 8) go with bit 0");
   if ((mode & 128) && (mode & 127)) return fail(GDN_ERR_FLAGS, "the timeout mode (bit 7) takes no other bit");
   if ((mode & 4) && (mode & 1)) return fail(GDN_ERR_FLAGS, "A from tensor memory is tested with tf32 only");
   if ((mode & 4) && (mode & 8)) return fail(GDN_ERR_FLAGS, "A from tensor memory has no MN-major form");

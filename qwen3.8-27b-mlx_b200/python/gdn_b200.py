@@ -268,17 +268,20 @@ def conv_ring_append(x, ring, ring_pos, slots, counts=None, cu_seqlens=None, err
                                      ptr(cu_seqlens), B, T, C, 4, ptr(err_flag), stream_ptr(dev)))
 
 
-def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=False, b_mn=False, d_col=0):
+def tc05_selftest(A, B, *, bf16=False, negate_a=False, a_in_tmem=False, a_mn=False, b_mn=False, d_col=0,
+                  fp16=False):
     """D = op(A) @ B.T on one CTA through tcgen05 (diagnostic).  A (128,K),
-    B (N,K) fp32 CUDA tensors, N <= 256; the accumulator starts at TMEM
-    column d_col (0, 64, 128 or 192).  Returns (D, status)."""
+    B (N,K) fp32 CUDA tensors, N <= 256; operands rounded to bf16, fp16 or
+    (neither) tf32; the accumulator starts at TMEM column d_col (0, 64, 128
+    or 192).  Returns (D, status)."""
     dev = _dev(A, B)
     N, K = B.shape
     if d_col not in (0, 64, 128, 192):
         raise ValueError("d_col must be 0, 64, 128 or 192")
     D = torch.empty((128, N), dtype=torch.float32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    mode = (1 if bf16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0) | (8 if a_mn else 0) | \
+    mode = (1 if bf16 or fp16 else 0) | (256 if fp16 else 0) | (2 if negate_a else 0) | (4 if a_in_tmem else 0) | \
+        (8 if a_mn else 0) | \
         (16 if b_mn else 0) | (32 if d_col & 64 else 0) | (64 if d_col & 128 else 0)
     check(lib().gdn_tc05_selftest(ptr(A), ptr(B), ptr(D), N, K, mode, ptr(status), stream_ptr(dev)))
     return D, status

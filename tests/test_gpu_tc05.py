@@ -80,3 +80,21 @@ def test_tc05_pair_accumulator_layout(N, K):
         D[64 * r:64 * r + 64, :nh] = raw[r, :64]
         D[64 * r:64 * r + 64, nh:] = raw[r, 64:]
     assert O.rel_err(D, ref) < 1e-5
+
+
+def f16r(x):
+    return x.half().float()
+
+
+@pytest.mark.parametrize("N,K,b_mn", [(64, 128, True), (128, 128, False), (192, 64, False), (64, 64, True)])
+def test_tc05_fp16(N, K, b_mn):
+    """kind::f16 with fp16 operands, the scan's form: K-major A and B, and B
+    MN-major (a K-major [dk][token] tile read as [token][dk]) for N = 64."""
+    g = torch.Generator(device="cuda").manual_seed(N * 3 + K + (1 if b_mn else 0))
+    A = f16r(torch.randn((128, K), generator=g, device="cuda"))
+    B = f16r(torch.randn((N, K), generator=g, device="cuda"))
+    D, st = G.tc05_selftest(A, B, fp16=True, b_mn=b_mn)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    ref = A.double().cpu().numpy() @ B.double().cpu().numpy().T
+    assert O.rel_err(D.cpu().numpy(), ref) < 1e-5
