@@ -99,7 +99,9 @@ constexpr uint32_t kQA = kQQ + kC * kD * 2;         // A, row-major, row stride 
 constexpr uint32_t kQX = kQA + kC * kPadA * 4;      // X = T^-1, row-major, row stride kPadA; then the W operand hi | lo
 constexpr uint32_t kQY = kQX + kC * kPadA * 4;      // products of the blocked solve, 1024 floats
 constexpr uint32_t kQSc = kQY + 1024 * 4;           // per-token scalars, 10 x 64
-constexpr uint32_t kQBar = kQSc + 10 * kC * 4;      // mbarrier, TMEM base, (sequence, chunk) broadcast
+constexpr uint32_t kQGa = kQSc + 10 * kC * 4;       // log-decay prefixes, then betas, of up to kPrepGroup value heads
+constexpr int kPrepGroup = 3;                       // value heads per prep CTA (at most)
+constexpr uint32_t kQBar = kQGa + 2 * kPrepGroup * kC * 4;   // mbarrier, TMEM base, (sequence, chunk) broadcast
 constexpr uint32_t kPrepSmem = kQBar + 64;
 constexpr uint32_t kSboOp = (kC * 2 / 16) * 128;    // 8-row group stride of the 64-token bf16 operands (1024)
 static_assert(2 * kC * kC * 2 <= kC * kPadA * 4, "prep: an operand pair fits the A / X region it replaces");
@@ -202,6 +204,7 @@ struct ChunkParams {
   int nch_uniform;                // chunks per sequence in this window when cu == null
   size_t rec_off;                 // byte offset of the records in the workspace
   int win_c0, win_len;            // window: chunks [win_c0, win_c0 + win_len) of every sequence
+  int prep_group;                 // value heads per prep CTA (they share one key head)
   float* carry;                   // state between windows (state_out, a workspace region, or null)
   // gated RMSNorm fused into the scan's epilogue (o is then the bf16 output):
   // out[t * out_stride + (out_head0 + h) * 128 + d] = rms_norm(o)[d] gamma[d] silu(z[t, h, d])
@@ -1018,22 +1021,119 @@ __device__ __forceinline__ void solve_doubling(const float* sA, float* sX, float
   __syncthreads();
 }
 
-// One CTA per (chunk, value head), value head fastest in the grid so that the
-// CTAs sharing a key head read its K / Q rows from L2.  Phases:
-//   rows of K, Q (cp.async) | gates -> norms, Q-tilde to the record ->
-//   G | P = [K; Q] K^T (kind::f16, exact bf16 operands) -> A (shared memory),
-//   M to the record; V rows (cp.async) -> T^-1 = (I + A)^-1 blocked: the 16 x 16
-//   diagonal blocks by substitution while the other warps write K-hat^T to the
-//   record, then the off-diagonal blocks by doubling (solve_doubling) -> the U0 / W right-hand
-//   operands diag(beta) T^-T and diag(beta g r_k) T^-T as bf16 hi + lo pairs
-//   (x = hi + lo to 2^-16 relative) -> U0^T = V^T B_U, W^T = K^T B_W
-//   (kind::f16, V^T and K^T MN-major straight from the rows) -> the record.
+// One right-hand product of the prep into TMEM column col (thread 0 issues):
+// D^T = A^T B^T with A the 64 x 128 bf16 rows at shared address a_rows read
+// MN-major (LBO = one 8-token group of 128 rows, SBO 128) and B the bf16
+// hi | lo operand pair at b (K-major, 64 x 64 each), one MMA per 16 tokens.
+__device__ __forceinline__ void prep_rhs_mma(const Ctx& c, uint32_t a_rows, const unsigned char* b, uint32_t col) {
+  const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC, false, false, /*a_mn=*/true, false);
+  for (int part = 0; part < 2; ++part) {
+    const uint32_t boff = part * kC * kC * 2;
+    for (int j = 0; j < kC / 16; ++j) {
+      const uint64_t a = tc::smem_desc(a_rows + j * 2 * kSboKQ, kSboKQ, 128);
+      tc::mma_ss<tc::kBF16>(c.tb + col, a, desc(b, boff + j * 256, kSboOp), id, part + j > 0);
+    }
+  }
+}
+
+// U0^T (lane = value row, this warp's 32 token columns in u) to the record, by
+// column quads.
+__device__ __forceinline__ void prep_store_u0(const Ctx& c, unsigned char* rec, const float (&u)[32]) {
+  float4* ud = reinterpret_cast<float4*>(rec + kRecU);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4)
+    ud[u0_index(c.half * 8 + e / 4, c.row)] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+}
+
+// -W to the record from W^T (lane k holds W^T[k][j] for its 32 j in w): 4 x 4
+// transposes across lane quads give each lane 4 consecutive k of one j, one
+// 8-byte fp16 store; thread 0 adds e^{Gam_last}.
+__device__ __forceinline__ void prep_store_negw(const Ctx& c, unsigned char* rec, const float (&w)[32]) {
+  const int u4 = c.lane & 3;
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    float v0 = w[e], v1 = w[e + 1], v2 = w[e + 2], v3 = w[e + 3];
+    quad_transpose(v0, v1, v2, v3, u4);
+    *reinterpret_cast<uint2*>(at_h(rec + kRecW, c.half * 32 + e + u4, c.row - u4, kSboH128)) =
+        pack_h4(-v0, -v1, -v2, -v3);
+  }
+  if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
+}
+
+// Gates of the group's value heads h0 .. h0 + gsz - 1: thread t < 64 gsz holds
+// the gate inputs of head t / 64 at token t % 64 (valid: a token of the chunk)
+// and leaves the head's in-chunk log-decay prefix Gam in gam[t] and beta in
+// beta[t].  Ends after the first barrier: the caller's next barrier publishes
+// gam for tokens 32-63.
+__device__ __forceinline__ void phase_gates_group(const Ctx& c, float* gam, float* beta_out, int gsz, float A_h,
+                                                  float dtb, float a_in, float b_in, bool valid) {
+  const bool mine = c.tid < kC * gsz;           // whole warps: kC is a multiple of 32
+  if (mine) {
+    float lg = 0.f, beta = 0.f;
+    if (valid) {
+      lg = fmaxf(-(A_h * softplus_f(a_in + dtb)), c.log_clip);
+      beta = 1.f / (1.f + expf(-b_in));
+    }
+    float x = lg;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, off);
+      if (c.lane >= off) x += y;
+    }
+    gam[c.tid] = x;
+    beta_out[c.tid] = beta;
+  }
+  __syncthreads();
+  if (mine && (c.tid & (kC - 1)) >= 32) gam[c.tid] += gam[(c.tid & ~(kC - 1)) + 31];
+}
+
+// Per-token scalars of the group's head hh that the later phases read through
+// the context (threads 0-63; rk = r_k of the token): g, e^{Gam_last-Gam}, the
+// K columns of W's right-hand side (beta g r_k) and of K-hat (e^{Gam_last-Gam}
+// r_k), and e^{Gam_last}.
+__device__ __forceinline__ void head_scalars(Ctx& c, const float* gam, const float* beta, int t, float rk) {
+  const float gl = gam[kC - 1];
+  const float g = expf(gam[t]);
+  const float ratio = expf(gl - gam[t]);
+  c.s_g[t] = g;
+  c.s_ratio[t] = ratio;
+  c.s_kw[t] = beta[t] * g * rk;
+  c.s_kh[t] = ratio * rk;
+  if (t == 0) c.s_misc[0] = expf(gl);
+}
+
+// One CTA per (chunk, group of value heads sharing a key head), group fastest
+// in the grid.  Phases:
+//   rows of K, Q (cp.async) | gates of the group's heads -> norms, Q-tilde of
+//   every head to its record -> G | P = [K; Q] K^T (kind::bf16, exact
+//   operands; tensor-memory columns [0, 64), kept for all heads) -> per head:
+//   A (shared memory) and M to the record from G | P; V rows (cp.async) ->
+//   T^-1 = (I + A)^-1 blocked: the 16 x 16 diagonal blocks by substitution
+//   while the other warps write K-hat^T to the record, then the off-diagonal
+//   blocks by doubling (solve_doubling) -> the U0 / W right-hand operands
+//   diag(beta) T^-T and diag(beta g r_k) T^-T as bf16 hi + lo pairs (x = hi +
+//   lo to 2^-16 relative) -> U0^T = V^T B_U, W^T = K^T B_W (kind::bf16, V^T
+//   and K^T MN-major straight from the rows) -> the record.  The last head
+//   puts W^T over G | P and runs both products at once; the others run them
+//   one after the other in columns [64, 128), the next head's V rows loading
+//   as soon as U0^T is done.
 __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
+  const int gsz = p.prep_group;
+  const int ngroups = p.Hv / gsz;
   const long long unit = blockIdx.x;
-  const long long slot = unit / p.Hv;
+  const long long slot = unit / ngroups;
+  const int h0 = static_cast<int>(unit - slot * ngroups) * gsz;
   Ctx c;
-  ctx_init(c, p, static_cast<int>(unit - slot * p.Hv));   // per-head constants in flight during the lookup
+  ctx_init(c, p, h0);   // key head and per-CTA constants in flight during the lookup
+  // gate constants of this thread's head (thread t < 64 gsz: head t / 64)
+  const int ghh = c.tid / kC;
+  const bool gin = ghh < gsz;
+  float A_h = 0.f, dtb = 0.f;
+  if (gin) {
+    A_h = expf(__ldg(p.A_log + h0 + ghh));
+    dtb = __ldg(p.dt_bias + h0 + ghh);
+  }
   // (sequence, chunk) of this slot and the sequence's token range: for a
   // packed batch thread t < B tests sequence t (one round of loads, exactly
   // one writer), thread B marks a slot past the last chunk
@@ -1070,6 +1170,8 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   const int ch = s_bc[1];
   ctx_scalars(c, reinterpret_cast<float*>(sm + kQSc));
   c.bar = reinterpret_cast<uint64_t*>(sm + kQBar);
+  float* gamA = reinterpret_cast<float*>(sm + kQGa);   // [gsz][64]
+  float* betaA = gamA + kPrepGroup * kC;                // [gsz][64]
   unsigned char* sK = sm + kQK;
   unsigned char* sQ = sm + kQQ;   // then V
   float* sA = reinterpret_cast<float*>(sm + kQA);
@@ -1078,12 +1180,11 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   const long long s0 = s_rng[0], s1 = s_rng[1];
   const long long t0 = s0 + static_cast<long long>(ch) * kC;
   const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
-  unsigned char* rec = record(p, slot, c.h);
   // gate inputs first: their latency overlaps the row copies and the TMEM set-up
   float a_in = 0.f, b_in = 0.f;
-  const bool gvalid = c.tid < kC && c.tid < nvalid;
+  const bool gvalid = gin && (c.tid & (kC - 1)) < nvalid;
   if (gvalid) {
-    const size_t gi = static_cast<size_t>(t0 + c.tid) * p.Hv + c.h;
+    const size_t gi = static_cast<size_t>(t0 + (c.tid & (kC - 1))) * p.Hv + h0 + ghh;
     a_in = __ldg(p.a + gi);
     b_in = __ldg(p.b + gi);
   }
@@ -1092,7 +1193,7 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   prep_copy_rows(sQ, p.q + t0 * p.q_stride + c.kh * kD, p.q_stride, nvalid, c.warp, c.lane);
   ptx::cp_async_commit();
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kQBar + 8), c.bar, 1, kPrepTmemCols);
-  phase_gates_from(c, a_in, b_in, gvalid);
+  phase_gates_group(c, gamA, betaA, gsz, A_h, dtb, a_in, b_in, gvalid);
   ptx::cp_async_wait<0>();
   ptx::fence_proxy_async_smem();
   __syncthreads();
@@ -1100,8 +1201,8 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
 
   // norms (thread: token i = 8 warp + lane % 8, 32-dim quarter qd = lane / 8,
   // so that the 8 lanes of each 16-byte shared-memory wavefront read 8
-  // distinct rows), the per-token scales of the record's K-hat^T and of W's
-  // right-hand side, Q-tilde to the record
+  // distinct rows), the first head's per-token scalars, Q-tilde of every head
+  // to its record
   {
     const int i = c.warp * 8 + (c.lane & 7), qd = c.lane >> 3;
     uint4 kr[4], qr[4];
@@ -1132,26 +1233,28 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
     if (qd == 0) {
       c.s_rk[i] = rk;
       c.s_rq[i] = rq;
-      c.s_kw[i] = c.s_beta[i] * c.s_g[i] * rk;
-      c.s_kh[i] = c.s_ratio[i] * rk;
+      head_scalars(c, gamA, betaA, i, rk);
     }
-    const float s = c.s_g[i] * rq;
+    for (int hh = 0; hh < gsz; ++hh) {
+      unsigned char* rq_dst = record(p, slot, h0 + hh) + kRecQ;
+      const float s = expf(gamA[hh * kC + i]) * rq;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&qr[m]);
-      uint32_t x[4];
+      for (int m = 0; m < 4; ++m) {
+        const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&qr[m]);
+        uint32_t x[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(hq[e]);
-        x[e] = pack_h2(f.x * s, f.y * s);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hq[e]);
+          x[e] = pack_h2(f.x * s, f.y * s);
+        }
+        *reinterpret_cast<uint4*>(at_h(rq_dst, i, qd * 32 + m * 8, kSboH128)) = make_uint4(x[0], x[1], x[2], x[3]);
       }
-      *reinterpret_cast<uint4*>(at_h(rec + kRecQ, i, qd * 32 + m * 8, kSboH128)) = make_uint4(x[0], x[1], x[2], x[3]);
     }
   }
   __syncthreads();
   GDN_TICK(17);
 
-  // (a) G | P = [K; Q] K^T at TMEM columns [0, 64)
+  // (a) G | P = [K; Q] K^T at TMEM columns [0, 64), read by every head
   if (c.tid == 0) {
     tc::fence_after_sync();
     const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC);
@@ -1161,57 +1264,64 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   }
   bool ok = mma_wait(c);
   GDN_TICK(18);
-  // the Q rows are no longer read: V rows into their place, landing during the solve
-  prep_copy_rows(sQ, p.v + t0 * p.v_stride + c.h * kD, p.v_stride, nvalid, c.warp, c.lane);
+  // the Q rows are no longer read: the first head's V rows into their place,
+  // landing during its solve
+  prep_copy_rows(sQ, p.v + t0 * p.v_stride + h0 * kD, p.v_stride, nvalid, c.warp, c.lane);
   ptx::cp_async_commit();
   GDN_TICK(8);
-  if (ok) {
-    // A (lanes 0-63, row-major) and M (lanes 64-127, to the record)
-    float gp[32];
-    tmem_ld<32>(c.tb + kPColGP + c.my + c.half * 32, gp);
-    GDN_TICK(9);
-    if (c.quarter < 2) {
-      const int i = c.row;
-      const float fi = c.s_beta[i] * c.s_rk[i];
-      const float gi = c.s_gam[i];
-      float* arow = sA + i * kPadA + c.half * 32;
+
+  for (int hh = 0; hh < gsz && ok; ++hh) {     // ok is the same in every thread
+    const bool last = hh == gsz - 1;
+    c.h = h0 + hh;
+    c.s_gam = gamA + hh * kC;
+    c.s_beta = betaA + hh * kC;
+    unsigned char* rec = record(p, slot, c.h);
+    {
+      // A (lanes 0-63, row-major) and M (lanes 64-127, to the record)
+      float gp[32];
+      tmem_ld<32>(c.tb + kPColGP + c.my + c.half * 32, gp);
+      GDN_TICK(9);
+      if (c.quarter < 2) {
+        const int i = c.row;
+        const float fi = c.s_beta[i] * c.s_rk[i];
+        const float gi = c.s_gam[i];
+        float* arow = sA + i * kPadA + c.half * 32;
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
-        const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
-        const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
-        float a[4];
+        for (int e = 0; e < 32; e += 4) {
+          const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
+          const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
+          const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
+          float a[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = c.half * 32 + e + u;
-          a[u] = (j < i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+          for (int u = 0; u < 4; ++u) {
+            const int j = c.half * 32 + e + u;
+            a[u] = (j < i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+          }
+          *reinterpret_cast<float4*>(arow + e) = make_float4(a[0], a[1], a[2], a[3]);
         }
-        *reinterpret_cast<float4*>(arow + e) = make_float4(a[0], a[1], a[2], a[3]);
-      }
-    } else {
-      const int i = c.row - kC;
-      const float fi = c.s_rq[i];
-      const float gi = c.s_gam[i];
+      } else {
+        const int i = c.row - kC;
+        const float fi = c.s_rq[i];
+        const float gi = c.s_gam[i];
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
-        const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
-        const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
-        float m[4];
+        for (int e = 0; e < 32; e += 4) {
+          const float4 rk4 = *reinterpret_cast<const float4*>(c.s_rk + c.half * 32 + e);
+          const float4 gm4 = *reinterpret_cast<const float4*>(c.s_gam + c.half * 32 + e);
+          const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
+          float m[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = c.half * 32 + e + u;
-          m[u] = (j <= i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+          for (int u = 0; u < 4; ++u) {
+            const int j = c.half * 32 + e + u;
+            m[u] = (j <= i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+          }
+          *reinterpret_cast<uint2*>(at_h(rec + kRecM, i, c.half * 32 + e, kSboH64)) = pack_h4(m[0], m[1], m[2], m[3]);
         }
-        *reinterpret_cast<uint2*>(at_h(rec + kRecM, i, c.half * 32 + e, kSboH64)) = pack_h4(m[0], m[1], m[2], m[3]);
       }
     }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  GDN_TICK(19);
+    tc::fence_before_sync();
+    __syncthreads();
+    GDN_TICK(19);
 
-  if (ok) {
     // diagonal blocks D_bb = (I + A_bb)^-1 (warps 0-1: block bb, column cc) ...
     if (c.tid < 64) {
       const int bb = c.tid >> 4, cc = c.tid & 15;
@@ -1262,105 +1372,125 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
 
     // right-hand operands, K-major (row j, token t), bf16 hi | lo:
     // B_U[j][t] = beta_t X[j][t] over A, B_W[j][t] = beta_t g_t r_kt X[j][t] over X
-    uint4 uh[2], ul[2], wh[2], wl[2];
+    {
+      uint4 uh[2], ul[2], wh[2], wl[2];
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int item = c.tid + it * kThreads;
-      const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
-      const float4 x0 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8);
-      const float4 x1 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8 + 4);
-      const float4 b0 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8);
-      const float4 b1 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8 + 4);
-      const float4 w0 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8);
-      const float4 w1 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8 + 4);
-      const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint32_t hu[4], lu[4], hw[4], lw[4];
+      for (int it = 0; it < 2; ++it) {
+        const int item = c.tid + it * kThreads;
+        const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
+        const float4 x0 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(sX + j * kPadA + tg * 8 + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8);
+        const float4 b1 = *reinterpret_cast<const float4*>(c.s_beta + tg * 8 + 4);
+        const float4 w0 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8);
+        const float4 w1 = *reinterpret_cast<const float4*>(c.s_kw + tg * 8 + 4);
+        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t hu[4], lu[4], hw[4], lw[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = tg * 8 + 2 * e;
-        const float xa = t <= j ? xs[2 * e] : 0.f, xb = t + 1 <= j ? xs[2 * e + 1] : 0.f;
-        split_bf16(xa * bs[2 * e], xb * bs[2 * e + 1], hu[e], lu[e]);
-        split_bf16(xa * ws[2 * e], xb * ws[2 * e + 1], hw[e], lw[e]);
-      }
-      uh[it] = make_uint4(hu[0], hu[1], hu[2], hu[3]);
-      ul[it] = make_uint4(lu[0], lu[1], lu[2], lu[3]);
-      wh[it] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      wl[it] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
-    GDN_TICK(14);
-    __syncthreads();                  // every X value is read before the operands overwrite A and X
-    GDN_TICK(21);
-#pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int item = c.tid + it * kThreads;
-      const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
-      const uint32_t off = tc::kmajor_offset(j, tg * 8, 2, kSboOp);
-      *reinterpret_cast<uint4*>(sm + kQA + off) = uh[it];
-      *reinterpret_cast<uint4*>(sm + kQA + kC * kC * 2 + off) = ul[it];
-      *reinterpret_cast<uint4*>(sm + kQX + off) = wh[it];
-      *reinterpret_cast<uint4*>(sm + kQX + kC * kC * 2 + off) = wl[it];
-    }
-  }
-  ptx::cp_async_wait<0>();            // this thread's V pieces
-  ptx::fence_proxy_async_smem();
-  tc::fence_before_sync();
-  __syncthreads();
-  GDN_TICK(22);
-
-  if (ok) {
-    // U0^T = V^T B_U^T (columns [64, 128)), W^T = K^T B_W^T (columns [0, 64));
-    // A operands MN-major (LBO = one 8-token group of 128 rows, SBO 128),
-    // one MMA per 16 tokens, hi then lo
-    if (c.tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id = tc::instr_desc(tc::kBF16, 128, kC, false, false, /*a_mn=*/true, false);
-      const uint32_t a_v = ptx::smem_u32(sQ), a_k = ptx::smem_u32(sK);
-      for (int part = 0; part < 2; ++part) {
-        const uint32_t boff = part * kC * kC * 2;
-        for (int j = 0; j < kC / 16; ++j) {
-          const uint64_t av = tc::smem_desc(a_v + j * 2 * kSboKQ, kSboKQ, 128);
-          const uint64_t ak = tc::smem_desc(a_k + j * 2 * kSboKQ, kSboKQ, 128);
-          tc::mma_ss<tc::kBF16>(c.tb + kPColU, av, desc(sm + kQA, boff + j * 256, kSboOp), id, part + j > 0);
-          tc::mma_ss<tc::kBF16>(c.tb + kPColW, ak, desc(sm + kQX, boff + j * 256, kSboOp), id, part + j > 0);
+        for (int e = 0; e < 4; ++e) {
+          const int t = tg * 8 + 2 * e;
+          const float xa = t <= j ? xs[2 * e] : 0.f, xb = t + 1 <= j ? xs[2 * e + 1] : 0.f;
+          split_bf16(xa * bs[2 * e], xb * bs[2 * e + 1], hu[e], lu[e]);
+          split_bf16(xa * ws[2 * e], xb * ws[2 * e + 1], hw[e], lw[e]);
         }
+        uh[it] = make_uint4(hu[0], hu[1], hu[2], hu[3]);
+        ul[it] = make_uint4(lu[0], lu[1], lu[2], lu[3]);
+        wh[it] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        wl[it] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      tc::mma_commit(c.bar);
-    }
-    ok = mma_wait(c);
-    GDN_TICK(23);
-    if (ok) {
-      float u[32], w[32];
-      tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(u));
-      tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
-      tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(w));
-      tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(w + 16));
-      tc::tmem_ld_wait();
-      float4* ud = reinterpret_cast<float4*>(rec + kRecU);      // U0^T by column quads
+      GDN_TICK(14);
+      __syncthreads();                  // every X value is read before the operands overwrite A and X
+      GDN_TICK(21);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        ud[u0_index(c.half * 8 + e / 4, c.row)] = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
-      // -W: lane k holds W^T[k][j] for its 32 j; 4 x 4 transposes across lane
-      // quads give each lane 4 consecutive k of one j, one 8-byte fp16 store
-      const int u4 = c.lane & 3;
-#pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        float v0 = w[e], v1 = w[e + 1], v2 = w[e + 2], v3 = w[e + 3];
-        quad_transpose(v0, v1, v2, v3, u4);
-        *reinterpret_cast<uint2*>(at_h(rec + kRecW, c.half * 32 + e + u4, c.row - u4, kSboH128)) =
-            pack_h4(-v0, -v1, -v2, -v3);
+      for (int it = 0; it < 2; ++it) {
+        const int item = c.tid + it * kThreads;
+        const int j = (item >> 6) * 8 + (item & 7), tg = (item >> 3) & 7;
+        const uint32_t off = tc::kmajor_offset(j, tg * 8, 2, kSboOp);
+        *reinterpret_cast<uint4*>(sm + kQA + off) = uh[it];
+        *reinterpret_cast<uint4*>(sm + kQA + kC * kC * 2 + off) = ul[it];
+        *reinterpret_cast<uint4*>(sm + kQX + off) = wh[it];
+        *reinterpret_cast<uint4*>(sm + kQX + kC * kC * 2 + off) = wl[it];
       }
-      if (c.tid == 0) reinterpret_cast<float*>(rec + kRecSc)[0] = c.s_misc[0];
     }
+    ptx::cp_async_wait<0>();            // this thread's V pieces
+    ptx::fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    GDN_TICK(22);
+
+    // U0^T = V^T B_U^T, W^T = K^T B_W^T; A operands MN-major (LBO = one
+    // 8-token group of 128 rows, SBO 128), one MMA per 16 tokens, hi then lo
+    const uint32_t a_v = ptx::smem_u32(sQ), a_k = ptx::smem_u32(sK);
+    if (last) {
+      if (c.tid == 0) {
+        tc::fence_after_sync();
+        prep_rhs_mma(c, a_v, sm + kQA, kPColU);
+        prep_rhs_mma(c, a_k, sm + kQX, kPColW);   // over G | P, read for the last time above
+        tc::mma_commit(c.bar);
+      }
+      ok = mma_wait(c);
+      GDN_TICK(23);
+      if (ok) {
+        float u[32], w[32];
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(u));
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
+        tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(w));
+        tc::tmem_ld16(c.tb + kPColW + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(w + 16));
+        tc::tmem_ld_wait();
+        prep_store_u0(c, rec, u);
+        prep_store_negw(c, rec, w);
+      }
+    } else {
+      // U0^T, then W^T in the same columns: G | P stays for the next head
+      if (c.tid == 0) {
+        tc::fence_after_sync();
+        prep_rhs_mma(c, a_v, sm + kQA, kPColU);
+        tc::mma_commit(c.bar);
+      }
+      ok = mma_wait(c);
+      if (ok) {
+        // the V rows are read: the next head's into their place
+        prep_copy_rows(sQ, p.v + t0 * p.v_stride + (c.h + 1) * kD, p.v_stride, nvalid, c.warp, c.lane);
+        ptx::cp_async_commit();
+        float u[32];
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(u));
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
+        tc::tmem_ld_wait();
+        prep_store_u0(c, rec, u);
+      }
+      tc::fence_before_sync();
+      __syncthreads();                  // U0^T is out of its columns before W^T overwrites them
+      if (ok) {
+        if (c.tid == 0) {
+          tc::fence_after_sync();
+          prep_rhs_mma(c, a_k, sm + kQX, kPColU);
+          tc::mma_commit(c.bar);
+        }
+        ok = mma_wait(c);
+      }
+      GDN_TICK(23);
+      if (ok) {
+        float w[32];
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(w));
+        tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(w + 16));
+        tc::tmem_ld_wait();
+        prep_store_negw(c, rec, w);
+        if (c.tid < kC) head_scalars(c, gamA + (hh + 1) * kC, betaA + (hh + 1) * kC, c.tid, c.s_rk[c.tid]);
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    GDN_TICK(31);
   }
+  ptx::cp_async_wait<0>();              // no row copy outlives the CTA
   if (!ok) {
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);
   }
   tc::fence_before_sync();
   __syncthreads();
-  GDN_TICK(31);
   if (c.warp == 0) tc::tmem_dealloc(c.tb, kPrepTmemCols);
 }
 
@@ -1790,6 +1920,14 @@ int set_smem_attr(const void* fn, uint32_t bytes, bool (&done)[64]) {
 
 // Argument checks shared by the chunked entry points; fills p without the
 // workspace fields.
+// Value heads per prep CTA for `r` value heads per key head: the largest
+// divisor of r that is at most kPrepGroup.
+int prep_group_size(int r) {
+  for (int g = kPrepGroup; g > 1; --g)
+    if (r % g == 0) return g;
+  return 1;
+}
+
 int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, long long q_stride, long long k_stride,
                  long long v_stride, const float* a, const float* b, const float* A_log, const float* dt_bias,
                  const float* state_in, float* state_out, void* o, const int32_t* cu_seqlens, int B, int T, int Hk,
@@ -1823,7 +1961,7 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
   p = ChunkParams{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                   static_cast<const __nv_bfloat16*>(v), q_stride, k_stride, v_stride, a, b, A_log, dt_bias,
                   state_in, state_out, o, cu_seqlens, B, cu_seqlens ? 0 : T, Hk, Hv, flags, err,
-                  nullptr, nullptr, 0, 0, 0, 0, 0, nullptr, nullptr, 0, nullptr, 0.f, 0, 0,
+                  nullptr, nullptr, 0, 0, 0, 0, 0, prep_group_size(Hv / Hk), nullptr, nullptr, 0, nullptr, 0.f, 0, 0,
                   {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr}, 0, 0};
   return GDN_OK;
 }
@@ -1898,7 +2036,7 @@ int launch_window(ChunkParams p, int T, int w, int win_len, cudaStream_t st) {
   }
   if (p.n_slots > 0) {
     if (p.n_slots * p.Hv > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many (chunk, head) pairs for one launch");
-    chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * p.Hv), kThreads, kPrepSmem, st>>>(p);
+    chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * (p.Hv / p.prep_group)), kThreads, kPrepSmem, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "chunk prep launch");
     if (rc != GDN_OK) return rc;
   }
