@@ -25,6 +25,7 @@ constexpr int kConvThreads = 128;
 constexpr int kConvRun = 64;         // tokens per thread
 constexpr int kConvBatch = 4;        // rows per cp.async group
 constexpr int kConvStages = 4;       // groups per thread in the shared-memory ring (stages x batch = 16 rows, 256 bytes)
+constexpr int kConvSmBlocks = 148;   // SMs of a B200, for sizing the prefill grid
 constexpr int kConvShortT = 16;      // uniform batches of at most this many tokens per sequence: one thread per token
 
 struct alignas(16) Bf16x8 {
@@ -78,27 +79,42 @@ struct ConvParams {
   const int32_t* ring_pos;
   int n_slots;
   int32_t* err;
+  int run;                         // tokens per block of the prefill kernel (set by run_conv)
 };
 
-// One output vector of 8 channels: the K taps over [window; x] and the SiLU.
+// One output vector of 8 channels: the K taps over the window rows r0 (oldest)
+// .. r2 and the current row x, then the SiLU.
 template <bool BF16_OPS>
-__device__ __forceinline__ Bf16x8 conv_taps(const float (&win)[kConvK - 1][kConvVec], const float (&xv)[kConvVec],
+__device__ __forceinline__ Bf16x8 conv_taps(const float (&r0)[kConvVec], const float (&r1)[kConvVec],
+                                           const float (&r2)[kConvVec], const float (&xv)[kConvVec],
                                            const float (&w)[kConvK][kConvVec], bool silu) {
   float out[kConvVec];
+  if constexpr (BF16_OPS) {   // MLX per-op bf16: each product and each partial sum rounded
 #pragma unroll
-  for (int e = 0; e < kConvVec; ++e) {
-    float acc;
-    if constexpr (BF16_OPS) {   // MLX per-op bf16: each product and each partial sum rounded
-      acc = bf16r(win[0][e] * w[0][e]);
-      acc = bf16r(acc + bf16r(win[1][e] * w[1][e]));
-      acc = bf16r(acc + bf16r(win[2][e] * w[2][e]));
+    for (int e = 0; e < kConvVec; ++e) {
+      float acc = bf16r(r0[e] * w[0][e]);
+      acc = bf16r(acc + bf16r(r1[e] * w[1][e]));
+      acc = bf16r(acc + bf16r(r2[e] * w[2][e]));
       acc = bf16r(acc + bf16r(xv[e] * w[3][e]));
       if (silu) acc = bf16r(acc * bf16r(sigmoid_f(acc)));
-    } else {          // fp32 accumulation; the bf16 output rounding dwarfs the fast-exp error
-      acc = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
-      if (silu) acc = __fdividef(acc, 1.f + __expf(-acc));
+      out[e] = acc;
     }
-    out[e] = acc;
+  } else {
+    // fp32 accumulation, two channels per packed f32x2 instruction, taps in
+    // order (oldest first); the bf16 output rounding dwarfs the fast-exp error
+#pragma unroll
+    for (int e = 0; e < kConvVec; e += 2) {
+      float2 acc = __fmul2_rn(make_float2(r0[e], r0[e + 1]), make_float2(w[0][e], w[0][e + 1]));
+      acc = __ffma2_rn(make_float2(r1[e], r1[e + 1]), make_float2(w[1][e], w[1][e + 1]), acc);
+      acc = __ffma2_rn(make_float2(r2[e], r2[e + 1]), make_float2(w[2][e], w[2][e + 1]), acc);
+      acc = __ffma2_rn(make_float2(xv[e], xv[e + 1]), make_float2(w[3][e], w[3][e + 1]), acc);
+      if (silu) {
+        const float2 den = __fadd2_rn(make_float2(1.f, 1.f), make_float2(__expf(-acc.x), __expf(-acc.y)));
+        acc = make_float2(__fdividef(acc.x, den.x), __fdividef(acc.y, den.y));
+      }
+      out[e] = acc.x;
+      out[e + 1] = acc.y;
+    }
   }
   return pack8(out);
 }
@@ -170,7 +186,7 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_tok_kernel(const ConvPara
     }
   }
   unpack8(xr, xv);
-  *reinterpret_cast<Bf16x8*>(p.y + tok * p.C + c0) = conv_taps<BF16_OPS>(win, xv, w, silu);
+  *reinterpret_cast<Bf16x8*>(p.y + tok * p.C + c0) = conv_taps<BF16_OPS>(win[0], win[1], win[2], xv, w, silu);
   if (p.state_out && t == p.T - 1) {
     // the carried window: rows T .. T+K-2 of [state (K-1 rows); x_seq (T rows)]
 #pragma unroll
@@ -190,15 +206,19 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_tok_kernel(const ConvPara
   }
 }
 
-// One thread: 8 channels x a run of up to 64 consecutive packed tokens, with
-// the 3-row causal window in registers, so every x element is read once
-// (plus a 3-row halo at the start of the run); rows stream in through a
-// per-thread ring of cp.async groups in shared memory (4 groups of 4 rows,
-// 32 KiB per block, 80 registers, six blocks per SM), so 12 rows are in
-// flight while 4 are computed.
+// One thread: 8 channels x a run of up to p.run (<= 64) consecutive packed
+// tokens, with the 3-row causal window in registers, so every x element is
+// read once (plus a 3-row halo at the start of the run).  Rows stream in
+// through a per-thread ring of cp.async groups in shared memory (4 groups of
+// 4 rows, 32 KiB per block, six blocks per SM), so 12 rows are in flight while
+// 4 are computed.  The window lives in a ring of 4 row slots: before row u of
+// a 4-row batch, slots (u+1)%4, (u+2)%4, (u+3)%4 hold rows t-3, t-2, t-1 and
+// row t lands in slot u, so the window moves without copies.  Batches that
+// cross no sequence boundary and hold no sequence's last row (nearly all)
+// take a branch-free path.
 template <bool BF16_OPS>
 __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParams p) {
-  const long long t_begin = static_cast<long long>(blockIdx.y) * kConvRun;
+  const long long t_begin = static_cast<long long>(blockIdx.y) * p.run;
   if (t_begin >= p.total) return;
   // one binary search of cu_seqlens per block, shared through shared memory
   __shared__ int s_seq;
@@ -206,7 +226,7 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
   __syncthreads();
   const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * kConvVec;
   if (c0 >= p.C) return;
-  const long long t_end = t_begin + kConvRun < p.total ? t_begin + kConvRun : p.total;
+  const long long t_end = t_begin + p.run < p.total ? t_begin + p.run : p.total;
   const bool silu = !(p.flags & GDN_F_CONV_NO_SILU);
   constexpr bool bf16_ops = BF16_OPS;
 
@@ -220,30 +240,32 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
   long long s_begin = seq_begin(seq);
   long long s_end = seq_end(seq);
 
-  float win[kConvK - 1][kConvVec];
-  auto load_window = [&](long long t) {
-    // rows t-3 .. t-1 of [state; x] for the sequence that holds t
+  float win[4][kConvVec];
+  // rows t-3 .. t-1 of [state; x] for the sequence that holds t, into the
+  // slots (u+1)%4 .. (u+3)%4 (u: t's place in its batch)
+  auto load_window = [&](long long t, int u) {
 #pragma unroll
     for (int j = 0; j < kConvK - 1; ++j) {
+      float(&dst)[kConvVec] = win[(u + 1 + j) & 3];
       const long long pos = t - s_begin - (kConvK - 1) + j;     // position in the sequence
       const long long row = s_begin + pos;                       // packed row (guards a bad cu_seqlens)
       if (pos >= 0 && row >= 0 && row < p.total) {
-        unpack8(*reinterpret_cast<const Bf16x8*>(p.x + row * p.C + c0), win[j]);
+        unpack8(*reinterpret_cast<const Bf16x8*>(p.x + row * p.C + c0), dst);
       } else if (p.state_in && pos < 0 && pos >= -(kConvK - 1)) {
         const __nv_bfloat16* sp = window_row(p, seq, static_cast<int>((kConvK - 1) + pos), c0);   // oldest first
         if (sp) {
-          unpack8(*reinterpret_cast<const Bf16x8*>(sp), win[j]);
+          unpack8(*reinterpret_cast<const Bf16x8*>(sp), dst);
         } else {
 #pragma unroll
-          for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
+          for (int e = 0; e < kConvVec; ++e) dst[e] = 0.f;
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < kConvVec; ++e) win[j][e] = 0.f;
+        for (int e = 0; e < kConvVec; ++e) dst[e] = 0.f;
       }
     }
   };
-  load_window(t_begin);
+  load_window(t_begin, 0);
 
   // x rows go through a per-thread ring of kConvStages groups in shared
   // memory by cp.async: batches k + 1 .. k + kConvStages - 1 stream in while
@@ -251,9 +273,10 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
   // Each thread reads only its own slots, so no barrier is needed.
   __shared__ Bf16x8 stage[kConvStages][kConvBatch][kConvThreads];
   auto issue = [&](long long tb, int sbuf) {
+    const __nv_bfloat16* src = p.x + tb * p.C + c0;
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u)
-      if (tb + u < t_end) ptx::cp_async16(&stage[sbuf][u][threadIdx.x], p.x + (tb + u) * p.C + c0);
+      if (tb + u < t_end) ptx::cp_async16(&stage[sbuf][u][threadIdx.x], src + static_cast<long long>(u) * p.C);
     ptx::cp_async_commit();
   };
 #pragma unroll
@@ -267,6 +290,16 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
     if (nxt < t_end) issue(nxt, (sbuf + kConvStages - 1) % kConvStages);
     else ptx::cp_async_commit();
     ptx::cp_async_wait<kConvStages - 1>();                // this batch's group has landed
+    __nv_bfloat16* yb = p.y + tb * p.C + c0;
+    if (tb + kConvBatch <= t_end && tb + kConvBatch < s_end) {
+#pragma unroll
+      for (int u = 0; u < kConvBatch; ++u) {
+        unpack8(stage[sbuf][u][threadIdx.x], win[u]);
+        *reinterpret_cast<Bf16x8*>(yb + static_cast<long long>(u) * p.C) =
+            conv_taps<bf16_ops>(win[(u + 1) & 3], win[(u + 2) & 3], win[(u + 3) & 3], win[u], w, silu);
+      }
+      continue;
+    }
 #pragma unroll
     for (int u = 0; u < kConvBatch; ++u) {
       const long long t = tb + u;
@@ -280,23 +313,17 @@ __global__ void __launch_bounds__(kConvThreads, 6) conv1d_kernel(const ConvParam
           s_begin = seq_begin(seq);
           s_end = seq_end(seq);
         }
-        load_window(t);
+        load_window(t, u);
       }
-      float xv[kConvVec];
-      unpack8(stage[sbuf][u][threadIdx.x], xv);
-      *reinterpret_cast<Bf16x8*>(p.y + t * p.C + c0) = conv_taps<bf16_ops>(win, xv, w, silu);
-#pragma unroll
-      for (int e = 0; e < kConvVec; ++e) {
-        win[0][e] = win[1][e];
-        win[1][e] = win[2][e];
-        win[2][e] = xv[e];
-      }
+      unpack8(stage[sbuf][u][threadIdx.x], win[u]);
+      *reinterpret_cast<Bf16x8*>(yb + static_cast<long long>(u) * p.C) =
+          conv_taps<bf16_ops>(win[(u + 1) & 3], win[(u + 2) & 3], win[(u + 3) & 3], win[u], w, silu);
       if (p.state_out && t == s_end - 1) {
-        // the carried window: the last K-1 rows of [state; x]
+        // the carried window: the last K-1 rows of [state; x], oldest first
 #pragma unroll
         for (int j = 0; j < kConvK - 1; ++j)
           *reinterpret_cast<Bf16x8*>(p.state_out + (static_cast<long long>(seq) * (kConvK - 1) + j) * p.C + c0) =
-              pack8(win[j]);
+              pack8(win[(u + 2 + j) & 3]);
       }
     }
   }
@@ -465,7 +492,8 @@ extern "C" int gdn_conv1d_fwd(const void* x, const void* w, const void* state_in
 namespace gdn {
 namespace {
 
-int run_conv(const ConvParams& p, void* stream) {
+int run_conv(const ConvParams& p_in, void* stream) {
+  ConvParams p = p_in;
   const int C = p.C, B = p.B;
   const long long total = p.total;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -479,9 +507,13 @@ int run_conv(const ConvParams& p, void* stream) {
     int rc = cuda_status(cudaGetLastError(), "conv1d launch");
     if (rc != GDN_OK) return rc;
   } else if (total > 0) {
-    const long long gy = (total + kConvRun - 1) / kConvRun;
-    if (gy > 65535LL * 1024) return fail(GDN_ERR_SHAPE, "too many tokens (%lld)", total);
-    // grid.y is limited to 65535: fold extra runs into grid.z is not needed below 2M tokens
+    // runs of 64 tokens, or 32 / 16 when that leaves the GPU less than two
+    // waves of blocks (short prefills: the 3-row halo per run costs less
+    // than idle SMs)
+    const long long min_blocks = 2LL * kConvSmBlocks * 6;
+    p.run = kConvRun;
+    while (p.run > 4 * kConvBatch && ((total + p.run - 1) / p.run) * gx < min_blocks) p.run /= 2;
+    const long long gy = (total + p.run - 1) / p.run;
     if (gy > 65535) return fail(GDN_ERR_SHAPE, "at most %d tokens per call", 65535 * kConvRun);
     if (p.flags & GDN_F_CONV_BF16_OPS) conv1d_kernel<true><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
     else conv1d_kernel<false><<<dim3(gx, static_cast<unsigned>(gy)), kConvThreads, 0, st>>>(p);
