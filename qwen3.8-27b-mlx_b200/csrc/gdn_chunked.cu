@@ -1592,42 +1592,43 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
     return ok;
   };
   // MMA completion: the copy warp polls, the CTA agrees (false if it gave up)
-  // (g3_ch >= 0: also group 3 of that chunk)
-  auto mma_done = [&](bool ok_in, int g3_ch = -1) -> bool {
+  // (g3_ch >= 0: also group 3 of that chunk; g1_ch >= 0: also group 1)
+  auto mma_done = [&](bool ok_in, int g3_ch = -1, int g1_ch = -1) -> bool {
     bool ok = ok_in;
     if (mw) ok = ok && ptx::mbar_wait(c.bar, c.phase);
     if (g3_ch >= 0) ok = wait_group(3, g3_ch) && ok;
+    if (g1_ch >= 0) ok = wait_group(1, g1_ch) && ok;
     c.phase ^= 1u;
     const bool all = !chain_or(!ok);
     tc::fence_after_sync();
     return all;
   };
-  // R (fp32 master) -> tf32 operand copy, or R *= gl in place (a worker's 32 columns)
-  auto r_pass = [&](bool to_f16, float gl) {
+  // R (fp32 master, a worker's 32 columns) -> fp16(R), the next first batch's
+  // A operand; then R *= gl in place for the next second batch, which adds
+  // U^T K-hat^T to g_last R (one pass over R per chunk)
+  auto r_pass = [&](float gl) {
     float v[16], w[16];
     tc::tmem_ld16(lane_cols + cDR, v);
     tc::tmem_ld16(lane_cols + cDR + 16, w);
     tc::tmem_ld_wait();
-    if (to_f16) {              // fp16(R) rows -> the first batch's A operand (row c.row, keys 32 cg ..)
 #pragma unroll
-      for (int i = 0; i < 16; i += 8) {
-        *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + i, kSboH128)) =
-            make_uint4(pack_h2(v[i], v[i + 1]), pack_h2(v[i + 2], v[i + 3]), pack_h2(v[i + 4], v[i + 5]),
-                       pack_h2(v[i + 6], v[i + 7]));
-        *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + 16 + i, kSboH128)) =
-            make_uint4(pack_h2(w[i], w[i + 1]), pack_h2(w[i + 2], w[i + 3]), pack_h2(w[i + 4], w[i + 5]),
-                       pack_h2(w[i + 6], w[i + 7]));
-      }
-      ptx::fence_proxy_async_smem();
-    } else {                   // R *= g_last in place
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] *= gl;
-        w[i] *= gl;
-      }
-      tc::tmem_st16(lane_cols + cDR, v);
-      tc::tmem_st16(lane_cols + cDR + 16, w);
+    for (int i = 0; i < 16; i += 8) {          // row c.row, keys 32 cg ..
+      *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + i, kSboH128)) =
+          make_uint4(pack_h2(v[i], v[i + 1]), pack_h2(v[i + 2], v[i + 3]), pack_h2(v[i + 4], v[i + 5]),
+                     pack_h2(v[i + 6], v[i + 7]));
+      *reinterpret_cast<uint4*>(at_h(sm + kScanR, c.row, cg * 32 + 16 + i, kSboH128)) =
+          make_uint4(pack_h2(w[i], w[i + 1]), pack_h2(w[i + 2], w[i + 3]), pack_h2(w[i + 4], w[i + 5]),
+                     pack_h2(w[i + 6], w[i + 7]));
     }
+    ptx::fence_proxy_async_smem();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] *= gl;
+      w[i] *= gl;
+    }
+    tc::tmem_st16(lane_cols + cDR, v);
+    tc::tmem_st16(lane_cols + cDR + 16, w);
+    tc::tmem_st_wait();
   };
   // U^T = (R (-W)^T from TMEM) + U0^T (shared memory) -> fp16 rows of the U^T operand
   auto epi_u = [&](uint32_t col_u) {
@@ -1807,9 +1808,12 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       load(1, 0);
       load(2, 0);
       load(3, 0);
-      if (worker) {
-        r_pass(true, 1.f);                  // fp16(R_0)
-        tc::tmem_st_wait();
+      const bool ok = wait_group(1, 0);      // g_last of chunk 0
+      if (chain_or(!ok)) {
+        failed = true;
+      } else {
+        tc::fence_after_sync();
+        if (worker) r_pass(reinterpret_cast<const float*>(sm + kScanGl1)[0]);   // fp16(R_0), g_last R_0
       }
       tc::fence_before_sync();
       chain_sync();
@@ -1819,10 +1823,9 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       const uint32_t col_b1 = odd ? 384 : 128;       // [y | U] or [U | y]
       const uint32_t col_b2 = odd ? 256 : 192;       // [R | y] or [y | R]
       const uint32_t col_u = odd ? 448 : 128;
-      // -W | Qs and g_last of this chunk in shared memory (U0^T is waited for
-      // under the first batch, before the epilogue that adds it)
-      bool ok = wait_group(1, ch);
-      if (chain_or(!ok)) { failed = true; break; }
+      // -W | Qs of this chunk are in shared memory (waited for with the previous
+      // second batch; U0^T is waited for under the first batch, before the
+      // epilogue that adds it)
       tc::fence_after_sync();
       GDN_TICK(29);
       bool yok = true;
@@ -1837,17 +1840,15 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
                                  desc(sm + kScanG1, j * 256, kSboH128), id, j > 0);
           tc::mma_commit(c.bar);
         }
-      } else if (worker) {       // under it: R *= g_last(ch) for the update, half of the previous o
-        r_pass(false, reinterpret_cast<const float*>(sm + kScanGl1)[0]);
-        if (!NORM && ch > 0) epi_o(ch - 1, 0);
-        tc::tmem_st_wait();
+      } else if (worker && !NORM && ch > 0) {   // under it: half of the previous o
+        epi_o(ch - 1, 0);
       }
       tc::fence_before_sync();
       if (!mma_done(yok, ch)) { failed = true; break; }
       GDN_TICK(24);
       if (ch + 1 < n_chunks) load(1, ch + 1);
       if (worker) epi_u(col_u);
-      ok = wait_group(2, ch);
+      bool ok = wait_group(2, ch);
       tc::fence_before_sync();
       if (chain_or(!ok)) { failed = true; break; }
       tc::fence_after_sync();
@@ -1863,14 +1864,11 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       }
       if (ch + 1 < n_chunks) load(3, ch + 1);
       tc::fence_before_sync();
-      if (!mma_done(true)) { failed = true; break; }
+      if (!mma_done(true, -1, ch + 1 < n_chunks ? ch + 1 : -1)) { failed = true; break; }   // + group 1 of ch + 1
       GDN_TICK(26);
       if (ch + 1 < n_chunks) {
         load(2, ch + 1);
-        if (worker) {
-          r_pass(true, 1.f);                // fp16(R_{ch+1}) for the next first batch
-          tc::tmem_st_wait();
-        }
+        if (worker) r_pass(reinterpret_cast<const float*>(sm + kScanGl1)[0]);   // fp16(R), g_last(ch + 1) R
       }
       tc::fence_before_sync();
       chain_sync();
