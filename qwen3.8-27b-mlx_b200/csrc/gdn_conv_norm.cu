@@ -52,6 +52,27 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
+// The hardware's approximate 2^x and 1/x (PTX ex2.approx.ftz / rcp.approx.ftz).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// silu on two channels: a / (1 + e^-a) with e^-a = 2^(-a log2 e); a very
+// negative a gives 2^+inf = inf, 1/inf = 0 and a signed zero.
+__device__ __forceinline__ float2 silu2(float2 a) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float2 t = __fmul2_rn(a, make_float2(-kLog2e, -kLog2e));
+  const float2 den = __fadd2_rn(make_float2(1.f, 1.f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+  return __fmul2_rn(a, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
+}
+
 // Sequence of packed token `tok` (binary search over cu_seqlens[0..B]).
 __device__ __forceinline__ int seq_of(const int32_t* cu, int B, long long tok) {
   int lo = 0, hi = B - 1;
@@ -101,17 +122,15 @@ __device__ __forceinline__ Bf16x8 conv_taps(const float (&r0)[kConvVec], const f
     }
   } else {
     // fp32 accumulation, two channels per packed f32x2 instruction, taps in
-    // order (oldest first); the bf16 output rounding dwarfs the fast-exp error
+    // order (oldest first); the bf16 output rounding dwarfs the error of the
+    // approximate exponential and reciprocal (a few ulp of fp32)
 #pragma unroll
     for (int e = 0; e < kConvVec; e += 2) {
       float2 acc = __fmul2_rn(make_float2(r0[e], r0[e + 1]), make_float2(w[0][e], w[0][e + 1]));
       acc = __ffma2_rn(make_float2(r1[e], r1[e + 1]), make_float2(w[1][e], w[1][e + 1]), acc);
       acc = __ffma2_rn(make_float2(r2[e], r2[e + 1]), make_float2(w[2][e], w[2][e + 1]), acc);
       acc = __ffma2_rn(make_float2(xv[e], xv[e + 1]), make_float2(w[3][e], w[3][e + 1]), acc);
-      if (silu) {
-        const float2 den = __fadd2_rn(make_float2(1.f, 1.f), make_float2(__expf(-acc.x), __expf(-acc.y)));
-        acc = make_float2(__fdividef(acc.x, den.x), __fdividef(acc.y, den.y));
-      }
+      if (silu) acc = silu2(acc);
       out[e] = acc.x;
       out[e + 1] = acc.y;
     }
