@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "gdn_conv_math.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
 
@@ -51,27 +52,6 @@ __device__ __forceinline__ Bf16x8 pack8(const float (&f)[8]) {
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
-
-// The hardware's approximate 2^x and 1/x (PTX ex2.approx.ftz / rcp.approx.ftz).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// silu on two channels: a / (1 + e^-a) with e^-a = 2^(-a log2 e); a very
-// negative a gives 2^+inf = inf, 1/inf = 0 and a signed zero.
-__device__ __forceinline__ float2 silu2(float2 a) {
-  constexpr float kLog2e = 1.4426950408889634f;
-  const float2 t = __fmul2_rn(a, make_float2(-kLog2e, -kLog2e));
-  const float2 den = __fadd2_rn(make_float2(1.f, 1.f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
-  return __fmul2_rn(a, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
-}
 
 // Sequence of packed token `tok` (binary search over cu_seqlens[0..B]).
 __device__ __forceinline__ int seq_of(const int32_t* cu, int B, long long tok) {
@@ -126,10 +106,10 @@ __device__ __forceinline__ Bf16x8 conv_taps(const float (&r0)[kConvVec], const f
     // approximate exponential and reciprocal (a few ulp of fp32)
 #pragma unroll
     for (int e = 0; e < kConvVec; e += 2) {
-      float2 acc = __fmul2_rn(make_float2(r0[e], r0[e + 1]), make_float2(w[0][e], w[0][e + 1]));
-      acc = __ffma2_rn(make_float2(r1[e], r1[e + 1]), make_float2(w[1][e], w[1][e + 1]), acc);
-      acc = __ffma2_rn(make_float2(r2[e], r2[e + 1]), make_float2(w[2][e], w[2][e + 1]), acc);
-      acc = __ffma2_rn(make_float2(xv[e], xv[e + 1]), make_float2(w[3][e], w[3][e + 1]), acc);
+      float2 acc = conv_pair(make_float2(r0[e], r0[e + 1]), make_float2(r1[e], r1[e + 1]),
+                             make_float2(r2[e], r2[e + 1]), make_float2(xv[e], xv[e + 1]),
+                             make_float2(w[0][e], w[0][e + 1]), make_float2(w[1][e], w[1][e + 1]),
+                             make_float2(w[2][e], w[2][e + 1]), make_float2(w[3][e], w[3][e + 1]));
       if (silu) acc = silu2(acc);
       out[e] = acc.x;
       out[e + 1] = acc.y;

@@ -32,6 +32,7 @@
 
 #include <mutex>
 
+#include "gdn_conv_math.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
 
@@ -408,16 +409,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
               for (int e2 = 0; e2 < 4; ++e2) {
-                float y2[2];
-#pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                  const int e = 2 * e2 + h2;
-                  // the same expression as gdn_conv1d_fwd's fp32 mode, so the results match it bit for bit
-                  float a = win[0][e] * w[0][e] + win[1][e] * w[1][e] + win[2][e] * w[2][e] + xv[e] * w[3][e];
-                  a = __fdividef(a, 1.f + __expf(-a));
-                  y2[h2] = a;
-                }
-                const __nv_bfloat162 hh = __floats2bfloat162_rn(y2[0], y2[1]);
+                // the arithmetic of gdn_conv1d_fwd's fp32 mode, so the results match it bit for bit
+                const int e = 2 * e2;
+                const float2 a = silu2(conv_pair(
+                    make_float2(win[0][e], win[0][e + 1]), make_float2(win[1][e], win[1][e + 1]),
+                    make_float2(win[2][e], win[2][e + 1]), make_float2(xv[e], xv[e + 1]),
+                    make_float2(w[0][e], w[0][e + 1]), make_float2(w[1][e], w[1][e + 1]),
+                    make_float2(w[2][e], w[2][e + 1]), make_float2(w[3][e], w[3][e + 1])));
+                const __nv_bfloat162 hh = __floats2bfloat162_rn(a.x, a.y);
                 ow[e2] = *reinterpret_cast<const uint32_t*>(&hh);
               }
               *reinterpret_cast<uint4*>(p.C + tok * p.ldc + c) = o;
