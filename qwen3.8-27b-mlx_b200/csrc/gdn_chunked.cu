@@ -39,6 +39,7 @@
 
 #include <mutex>
 
+#include "gdn_conv_math.cuh"
 #include "gdn_internal.h"
 #include "gdn_ptx.cuh"
 
@@ -1713,16 +1714,20 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
       const long long t0 = s0 + static_cast<long long>(p.win_c0 + ch) * kC;
       const int nvalid = static_cast<int>((s1 - t0) < kC ? (s1 - t0) : kC);
       __nv_bfloat16* zt = reinterpret_cast<__nv_bfloat16*>(sm + kScanZ + (ch % 3) * kZBuf);
+      // this warp's y of the chunk (both rounds) out of TMEM first, and its
+      // columns released at once: the chain's first batch two chunks on
+      // waits only for these loads, not for the norm arithmetic
+      float ya[16], yb[16];
+      tc::tmem_ld16(c.tb + col_y + c.my + grp * 32, ya);
+      tc::tmem_ld16(c.tb + col_y + c.my + grp * 32 + 16, yb);
+      tc::tmem_ld_wait();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (c.lane == 0) ptx::mbar_arrive(&ybar[2 + (ch & 1)]);
+#pragma unroll
       for (int r = 0; r < 2; ++r) {                  // 16 tokens per round
         const int tb = grp * 32 + r * 16;            // first token of the round
-        float y[16];
-        tc::tmem_ld16(c.tb + col_y + c.my + tb, y);
-        tc::tmem_ld_wait();
-        if (r == 1) {                                // this warp's y of the chunk is read: release its columns
-          tc::fence_before_sync();
-          __syncwarp();
-          if (c.lane == 0) ptx::mbar_arrive(&ybar[2 + (ch & 1)]);
-        }
+        const float(&y)[16] = r ? yb : ya;
         // sums of y^2 over this warp's 32 dv for the 16 tokens: halve the
         // token set per exchange (8 + 4 + 2 + 1 shuffles), then one more; the
         // pair of lanes 2t, 2t + 1 ends with token t
@@ -1748,7 +1753,7 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
           const float ri = __shfl_sync(0xffffffffu, rr, i);
           __nv_bfloat16* e = zt + (tb + i) * kD + c.row;
           const float zz = __bfloat162float(*e);
-          const float sg = __fdividef(1.f, 1.f + __expf(-zz));
+          const float sg = rcp_approx(1.f + ex2_approx(zz * -1.4426950408889634f));   // sigmoid(z), 2^(-z log2 e)
           *e = __float2bfloat16_rn((y[i] * ri * gam) * (zz * sg));
         }
         nbar();
