@@ -91,6 +91,37 @@ def test_conv1d_varlen_packed_with_empty_and_short_sequences():
         assert np.array_equal(sh[s], xp[0, -3:]), s
 
 
+@pytest.mark.parametrize("lens,uniform", [([5000, 3, 0, 4100, 2998], False), ([3500, 3500], True)])
+def test_conv1d_full_width_long_runs(lens, uniform):
+    """C = 10,240 (the model's q|k|v width) at sizes where the kernel takes
+    64-token runs (packed, 12,101 tokens: sequence ends inside batches, an
+    empty sequence) and 32-token runs (2 x 3,500 uniform): the branch-free
+    batches and the per-row path around sequence ends against the oracle."""
+    rng = np.random.default_rng(35 + len(lens))
+    C = 10240
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    total = int(cu[-1])
+    x = O.bf16_round(rng.standard_normal((total, C), dtype=np.float32))
+    w = O.bf16_round(rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5))
+    st = O.bf16_round(rng.standard_normal((len(lens), 3, C), dtype=np.float32))
+    st_out = torch.empty((len(lens), 3, C), dtype=torch.bfloat16, device="cuda")
+    if uniform:
+        y, so = G.conv1d_fwd(dev(x.reshape(len(lens), lens[0], C), torch.bfloat16), dev(w, torch.bfloat16),
+                             dev(st, torch.bfloat16), st_out)
+        yh = host(y).reshape(total, C)
+    else:
+        y, so = G.conv1d_fwd(dev(x, torch.bfloat16), dev(w, torch.bfloat16), dev(st, torch.bfloat16), st_out,
+                             cu_seqlens=dev(cu, torch.int32))
+        yh = host(y)
+    sh = host(so)
+    for s, L in enumerate(lens):
+        ry, xp = O.depthwise_conv(x[None, cu[s]:cu[s + 1]], w, st[s:s + 1])
+        ry = O.silu(ry)[0]
+        if L:
+            assert np.max(np.abs(yh[cu[s]:cu[s + 1]] - ry)) <= 2 ** -8 * np.max(np.abs(ry)) + 1e-6, s
+        assert np.array_equal(sh[s], xp[0, -3:]), s
+
+
 def test_conv_commit_after_verify_block():
     rng = np.random.default_rng(34)
     B, T, C = 4, 4, 128
