@@ -33,6 +33,7 @@
 //     scan kernel per (sequence, value head) bulk-copies them in and runs
 //     only the state chain, so the serial work per chunk shrinks to the
 //     state-dependent MMAs and their epilogues.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -895,23 +896,6 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
   if (threadIdx.x == 0) prefix[B] = carry;
 }
 
-// 16-byte row pieces of one 64 x 128 bf16 matrix (rows at src + t * stride,
-// t < nvalid; zero rows after) into the prep layout at dst, by cp.async.  Warp
-// item it covers tokens 8 (it / 4) .. +7 and the 16-byte pieces 4 (it % 4) ..
-// +3 of each: a warp reads 8 rows x 64 bytes and writes 32 distinct bank
-// groups.
-__device__ __forceinline__ void prep_copy_rows(unsigned char* dst, const __nv_bfloat16* src, long long stride,
-                                               int nvalid, int warp, int lane) {
-#pragma unroll
-  for (int it = warp; it < 32; it += 8) {
-    const int t = (it >> 2) * 8 + (lane & 7);
-    const int kg = (it & 3) * 4 + (lane >> 3);
-    unsigned char* d = dst + tc::kmajor_offset(t, kg * 8, 2, kSboKQ);
-    if (t < nvalid) ptx::cp_async16(d, src + t * stride + kg * 8);
-    else *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
-  }
-}
-
 // (x0, x1) as bf16 pairs hi = bf16(x), lo = bf16(x - hi): hi + lo equals x to
 // about 2^-16 relative, so two kind::f16 products (hi, then lo) carry an fp32
 // operand more precisely than one tf32 product.
@@ -1022,6 +1006,25 @@ __device__ __forceinline__ void solve_doubling(const float* sA, float* sX, float
   __syncthreads();
 }
 
+// Rows [nvalid, 64) of a 64 x 128 bf16 row tile in the prep layout set to
+// zero (a sequence's last chunk: the tensor copy brought the next sequence's
+// rows, or zeros past the tensor's end).
+__device__ __forceinline__ void prep_zero_rows(unsigned char* dst, int nvalid, int tid) {
+  for (int q = tid; q < (kC - nvalid) * 16; q += kThreads)
+    *reinterpret_cast<uint4*>(dst + tc::kmajor_offset(nvalid + (q >> 4), (q & 15) * 8, 2, kSboKQ)) =
+        make_uint4(0, 0, 0, 0);
+}
+
+// The rows of 64 tokens t0 .. t0 + 63 of one head (channel group cg0 = 16 x
+// head) by eight tensor copies, one 8-row group of the prep layout each
+// (thread 0 issues; completion counted on bar).
+__device__ __forceinline__ void prep_rows_tma(unsigned char* dst, const CUtensorMap* tm, long long t0, int cg0,
+                                              uint64_t* bar) {
+#pragma unroll
+  for (int g = 0; g < kC / 8; ++g)
+    ptx::tma_load_3d(dst + g * kSboKQ, tm, 0, static_cast<int>(t0) + 8 * g, cg0, bar);
+}
+
 // One right-hand product of the prep into TMEM column col (thread 0 issues):
 // D^T = A^T B^T with A the 64 x 128 bf16 rows at shared address a_rows read
 // MN-major (LBO = one 8-token group of 128 rows, SBO 128) and B the bf16
@@ -1105,10 +1108,10 @@ __device__ __forceinline__ void head_scalars(Ctx& c, const float* gam, const flo
 
 // One CTA per (chunk, group of value heads sharing a key head), group fastest
 // in the grid.  Phases:
-//   rows of K, Q (cp.async) | gates of the group's heads -> norms, Q-tilde of
+//   rows of K, Q (tensor copies) | gates of the group's heads -> norms, Q-tilde of
 //   every head to its record -> G | P = [K; Q] K^T (kind::bf16, exact
 //   operands; tensor-memory columns [0, 64), kept for all heads) -> per head:
-//   A (shared memory) and M to the record from G | P; V rows (cp.async) ->
+//   A (shared memory) and M to the record from G | P; V rows (tensor copies) ->
 //   T^-1 = (I + A)^-1 blocked: the 16 x 16 diagonal blocks by substitution
 //   while the other warps write K-hat^T to the record, then the off-diagonal
 //   blocks by doubling (solve_doubling) -> the U0 / W right-hand operands
@@ -1118,7 +1121,9 @@ __device__ __forceinline__ void head_scalars(Ctx& c, const float* gam, const flo
 //   puts W^T over G | P and runs both products at once; the others run them
 //   one after the other in columns [64, 128), the next head's V rows loading
 //   as soon as U0^T is done.
-__global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkParams p) {
+__global__ void __launch_bounds__(kThreads, 3)
+    chunk_prep_kernel(const ChunkParams p, const __grid_constant__ CUtensorMap tmq,
+                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const int gsz = p.prep_group;
   const int ngroups = p.Hv / gsz;
@@ -1190,14 +1195,47 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
     b_in = __ldg(p.b + gi);
   }
 
-  prep_copy_rows(sK, p.k + t0 * p.k_stride + c.kh * kD, p.k_stride, nvalid, c.warp, c.lane);
-  prep_copy_rows(sQ, p.q + t0 * p.q_stride + c.kh * kD, p.q_stride, nvalid, c.warp, c.lane);
-  ptx::cp_async_commit();
+  // K and Q rows by tensor copies on their own barrier (one arrival per
+  // phase: K | Q, then each head's V rows); rows_wait is the CTA's bounded
+  // wait for the current phase
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(sm + kQBar + 48);
+  uint32_t rphase = 0;
+  bool rows_pending = false;               // a phase issued and not yet waited for (same in every thread)
+  auto rows_wait = [&]() -> bool {
+    bool okw = true;
+    if (c.warp == 0) okw = ptx::mbar_wait(rbar, rphase);
+    const bool all = !__syncthreads_or(!okw);
+    if (all) {                             // else the phase stays pending for the exit's last wait
+      rphase ^= 1u;
+      rows_pending = false;
+    }
+    return all;
+  };
+  if (c.tid == 0) {
+    ptx::mbar_init(rbar, 1);
+    ptx::fence_mbar_init();
+    ptx::mbar_arrive_expect_tx(rbar, 2 * kC * kD * 2);
+    prep_rows_tma(sK, &tmk, t0, c.kh * (kD / 8), rbar);
+    prep_rows_tma(sQ, &tmq, t0, c.kh * (kD / 8), rbar);
+  }
+  rows_pending = true;
   tmem_setup(c, reinterpret_cast<uint32_t*>(sm + kQBar + 8), c.bar, 1, kPrepTmemCols);
   phase_gates_group(c, gamA, betaA, gsz, A_h, dtb, a_in, b_in, gvalid);
-  ptx::cp_async_wait<0>();
-  ptx::fence_proxy_async_smem();
-  __syncthreads();
+  if (!rows_wait()) {
+    // the rows never arrived: record it, give the copies one more bounded wait, leave
+    if (c.tid == 0) atomicExch(p.err, 1);
+    if (c.warp == 0) ptx::mbar_wait(rbar, rphase);
+    tc::fence_before_sync();
+    __syncthreads();
+    if (c.warp == 0) tc::tmem_dealloc(c.tb, kPrepTmemCols);
+    return;
+  }
+  if (nvalid < kC) {                       // a sequence's last chunk: rows past its end are zero
+    prep_zero_rows(sK, nvalid, c.tid);
+    prep_zero_rows(sQ, nvalid, c.tid);
+    ptx::fence_proxy_async_smem();
+    __syncthreads();
+  }
   GDN_TICK(16);
 
   // norms (thread: token i = 8 warp + lane % 8, 32-dim quarter qd = lane / 8,
@@ -1267,8 +1305,11 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
   GDN_TICK(18);
   // the Q rows are no longer read: the first head's V rows into their place,
   // landing during its solve
-  prep_copy_rows(sQ, p.v + t0 * p.v_stride + h0 * kD, p.v_stride, nvalid, c.warp, c.lane);
-  ptx::cp_async_commit();
+  if (ok && c.tid == 0) {
+    ptx::mbar_arrive_expect_tx(rbar, kC * kD * 2);
+    prep_rows_tma(sQ, &tmv, t0, h0 * (kD / 8), rbar);
+  }
+  rows_pending = ok;
   GDN_TICK(8);
 
   for (int hh = 0; hh < gsz && ok; ++hh) {     // ok is the same in every thread
@@ -1415,10 +1456,15 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
         *reinterpret_cast<uint4*>(sm + kQX + kC * kC * 2 + off) = wl[it];
       }
     }
-    ptx::cp_async_wait<0>();            // this thread's V pieces
-    ptx::fence_proxy_async_smem();
+    ptx::fence_proxy_async_smem();      // the operands above, for the MMAs
     tc::fence_before_sync();
-    __syncthreads();
+    ok = rows_wait();                   // this head's V rows (and the barrier for the operands)
+    if (!ok) break;
+    if (nvalid < kC) {
+      prep_zero_rows(sQ, nvalid, c.tid);
+      ptx::fence_proxy_async_smem();
+      __syncthreads();
+    }
     GDN_TICK(22);
 
     // U0^T = V^T B_U^T, W^T = K^T B_W^T; A operands MN-major (LBO = one
@@ -1453,8 +1499,11 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
       ok = mma_wait(c);
       if (ok) {
         // the V rows are read: the next head's into their place
-        prep_copy_rows(sQ, p.v + t0 * p.v_stride + (c.h + 1) * kD, p.v_stride, nvalid, c.warp, c.lane);
-        ptx::cp_async_commit();
+        if (c.tid == 0) {
+          ptx::mbar_arrive_expect_tx(rbar, kC * kD * 2);
+          prep_rows_tma(sQ, &tmv, t0, (c.h + 1) * (kD / 8), rbar);
+        }
+        rows_pending = true;
         float u[32];
         tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32, *reinterpret_cast<float(*)[16]>(u));
         tc::tmem_ld16(c.tb + kPColU + c.my + c.half * 32 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
@@ -1485,11 +1534,11 @@ __global__ void __launch_bounds__(kThreads, 3) chunk_prep_kernel(const ChunkPara
     __syncthreads();
     GDN_TICK(31);
   }
-  ptx::cp_async_wait<0>();              // no row copy outlives the CTA
   if (!ok) {
     if (c.tid == 0) atomicExch(p.err, 1);
     ptx::mbar_wait(c.bar, c.phase ^ 1u);
   }
+  if (rows_pending && c.warp == 0) ptx::mbar_wait(rbar, rphase);   // no row copy outlives the CTA
   tc::fence_before_sync();
   __syncthreads();
   if (c.warp == 0) tc::tmem_dealloc(c.tb, kPrepTmemCols);
@@ -2022,8 +2071,36 @@ bool plan_split(int B, int T, int Hv, bool packed, bool has_state_out, size_t ws
   return true;
 }
 
+// Tensor maps of the prep's row copies: q, k (Hk heads) and v (Hv heads) as
+// 3-D tensors (8 elements, tokens, 16-byte channel groups) so that one box of
+// 8 x 8 x 16 lands as one 8-row group of the K-major no-swizzle layout (16
+// core matrices of 8 rows x 16 bytes); tokens past the tensor read as zeros.
+struct RowMaps {
+  CUtensorMap q, k, v;
+};
+
+int make_rows_tmap(CUtensorMap* tm, const void* base, long long tokens, int heads, long long stride) {
+  void* fn = nullptr;
+  const int rc = tensor_map_encoder(&fn);
+  if (rc != GDN_OK) return rc;
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  const cuuint64_t dims[3] = {8, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads) * (kD / 8)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride) * 2, 16};
+  const cuuint32_t box[3] = {8, 8, kD / 8};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = reinterpret_cast<Encode>(fn)(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+                                                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(GDN_ERR_CUDA, "cuTensorMapEncodeTiled (prefill rows) failed (CUresult %d)", static_cast<int>(r));
+  return GDN_OK;
+}
+
 // One window's launches: the chunk prefix (packed), the prep, the scan.
-int launch_window(ChunkParams p, int T, int w, int win_len, cudaStream_t st) {
+int launch_window(ChunkParams p, int T, int w, int win_len, const RowMaps& rm, cudaStream_t st) {
   const bool packed = p.cu != nullptr;
   const long long nch = (static_cast<long long>(T) + kC - 1) / kC;
   p.win_c0 = w * win_len;
@@ -2039,7 +2116,8 @@ int launch_window(ChunkParams p, int T, int w, int win_len, cudaStream_t st) {
   }
   if (p.n_slots > 0) {
     if (p.n_slots * p.Hv > 0x7fffffffLL) return fail(GDN_ERR_SHAPE, "too many (chunk, head) pairs for one launch");
-    chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * (p.Hv / p.prep_group)), kThreads, kPrepSmem, st>>>(p);
+    chunk_prep_kernel<<<static_cast<unsigned>(p.n_slots * (p.Hv / p.prep_group)), kThreads, kPrepSmem, st>>>(
+        p, rm.q, rm.k, rm.v);
     rc = cuda_status(cudaGetLastError(), "chunk prep launch");
     if (rc != GDN_OK) return rc;
   }
@@ -2070,8 +2148,17 @@ int run_split(ChunkParams p, int T, unsigned char* ws, size_t ws_size, cudaStrea
   p.rec_off = pl.rec_off;
   p.carry = p.state_out ? p.state_out : (pl.n_windows > 1 ? reinterpret_cast<float*>(ws + pl.carry_off) : nullptr);
   p.win_len = pl.win_len;
+  RowMaps rm;
+  const long long tokens = packed ? static_cast<long long>(T) : static_cast<long long>(p.B) * T;
+  if (tokens > 0) {
+    if (tokens > 0x7fffff00LL) return fail(GDN_ERR_SHAPE, "too many tokens for one call");
+    rc = make_rows_tmap(&rm.q, p.q, tokens, p.Hk, p.q_stride);
+    if (rc == GDN_OK) rc = make_rows_tmap(&rm.k, p.k, tokens, p.Hk, p.k_stride);
+    if (rc == GDN_OK) rc = make_rows_tmap(&rm.v, p.v, tokens, p.Hv, p.v_stride);
+    if (rc != GDN_OK) return rc;
+  }
   for (int w = 0; w < pl.n_windows; ++w) {
-    rc = launch_window(p, T, w, pl.win_len, st);
+    rc = launch_window(p, T, w, pl.win_len, rm, st);
     if (rc != GDN_OK) return rc;
   }
   return GDN_OK;

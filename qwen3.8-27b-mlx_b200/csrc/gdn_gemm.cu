@@ -487,19 +487,10 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 int encode_fn(EncodeTiledFn* out) {
-  static std::once_flag once;
-  static EncodeTiledFn fn = nullptr;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  if (!fn) return err != cudaSuccess ? cuda_status(err, "cuTensorMapEncodeTiled lookup")
-                                     : fail(GDN_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  *out = fn;
-  return GDN_OK;
+  void* fn = nullptr;
+  const int rc = tensor_map_encoder(&fn);
+  if (rc == GDN_OK) *out = reinterpret_cast<EncodeTiledFn>(fn);
+  return rc;
 }
 
 // Tensor map of a row-major (rows, K) bf16 matrix with row stride ld
@@ -599,6 +590,23 @@ int launch_gemm(const void* A, const void* B, long long lda, long long ldb, Gemm
 }
 
 }  // namespace
+
+int tensor_map_encoder(void** out) {
+  static std::once_flag once;
+  static void* fn = nullptr;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = p;
+  });
+  if (!fn) return err != cudaSuccess ? cuda_status(err, "cuTensorMapEncodeTiled lookup")
+                                     : fail(GDN_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  *out = fn;
+  return GDN_OK;
+}
+
 }  // namespace gdn
 
 using namespace gdn;

@@ -33,6 +33,11 @@ inline bool overlap(const void* p, size_t n, const void* q, size_t m) {
 // give up), cached per device; GDN_OK or GDN_ERR_CUDA.
 int device_error_ptr(int** out);
 
+// cuTensorMapEncodeTiled, looked up once through the runtime's driver entry
+// point (so that the library loads on a machine without a driver): *fn is
+// the function, to be cast to its CUDA signature; GDN_OK or GDN_ERR_CUDA.
+int tensor_map_encoder(void** fn);
+
 constexpr int kD = 128;  // Dk = Dv, fixed by the model (TextConfig, python/qwen35.py:88-91)
 
 }  // namespace gdn

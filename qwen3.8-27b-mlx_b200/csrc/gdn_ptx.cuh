@@ -147,6 +147,17 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, in
       : "memory");
 }
 
+// 3-D tiled tensor copy global -> shared (no multicast: this CTA only),
+// completion counted in bytes on `bar`; c0 innermost (elements, 16-byte
+// aligned), coordinates outside the tensor read as zeros.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---- CTA pairs (a cluster of 2 running one tcgen05 cta_group::2 MMA) ----
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
