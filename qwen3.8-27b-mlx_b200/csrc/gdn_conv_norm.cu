@@ -418,6 +418,9 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const void* o, const
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
   const size_t base = static_cast<size_t>(row) * kD + lane * 4;
+  // z and gamma do not depend on the row's norm: their loads go out with o's
+  const uint2 zr = *reinterpret_cast<const uint2*>(z + base);
+  const float4 g = *reinterpret_cast<const float4*>(gamma + lane * 4);
   float x[4];
   if (flags & GDN_F_NORM_IN_BF16) {
     const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(o) + base);
@@ -432,15 +435,14 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const void* o, const
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float r = rsqrtf(ss / static_cast<float>(kD) + eps);
-  const uint2 zr = *reinterpret_cast<const uint2*>(z + base);
   const float2 zlo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zr.x));
   const float2 zhi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zr.y));
   const float zz[4] = {zlo.x, zlo.y, zhi.x, zhi.y};
-  const float4 g = *reinterpret_cast<const float4*>(gamma + lane * 4);
   const float gg[4] = {g.x, g.y, g.z, g.w};
   float y[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) y[i] = (x[i] * r * gg[i]) * (zz[i] * sigmoid_f(zz[i]));
+  for (int i = 0; i < 4; ++i)    // sigmoid(z) = 1 / (1 + 2^(-z log2 e)), hardware exp2 and reciprocal
+    y[i] = (x[i] * r * gg[i]) * (zz[i] * rcp_approx(1.f + ex2_approx(zz[i] * -1.4426950408889634f)));
   if (flags & GDN_F_NORM_OUT_F32) {
     *reinterpret_cast<float4*>(static_cast<float*>(out) + base) = make_float4(y[0], y[1], y[2], y[3]);
   } else {
