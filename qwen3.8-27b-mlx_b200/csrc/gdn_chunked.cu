@@ -1335,9 +1335,13 @@ __global__ void __launch_bounds__(kThreads, 3)
           const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
           float a[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 4; u += 2) {     // ((fi r_k) e^{gi - gm}) g on channel pairs
             const int j = c.half * 32 + e + u;
-            a[u] = (j < i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+            float2 t = __fmul2_rn(make_float2(fi, fi), make_float2(rk[u], rk[u + 1]));
+            t = __fmul2_rn(t, make_float2(__expf(gi - gm[u]), __expf(gi - gm[u + 1])));
+            t = __fmul2_rn(t, make_float2(gp[e + u], gp[e + u + 1]));
+            a[u] = (j < i) ? t.x : 0.f;
+            a[u + 1] = (j + 1 < i) ? t.y : 0.f;
           }
           *reinterpret_cast<float4*>(arow + e) = make_float4(a[0], a[1], a[2], a[3]);
         }
@@ -1352,9 +1356,13 @@ __global__ void __launch_bounds__(kThreads, 3)
           const float rk[4] = {rk4.x, rk4.y, rk4.z, rk4.w}, gm[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
           float m[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 4; u += 2) {
             const int j = c.half * 32 + e + u;
-            m[u] = (j <= i) ? fi * rk[u] * __expf(gi - gm[u]) * gp[e + u] : 0.f;
+            float2 t = __fmul2_rn(make_float2(fi, fi), make_float2(rk[u], rk[u + 1]));
+            t = __fmul2_rn(t, make_float2(__expf(gi - gm[u]), __expf(gi - gm[u + 1])));
+            t = __fmul2_rn(t, make_float2(gp[e + u], gp[e + u + 1]));
+            m[u] = (j <= i) ? t.x : 0.f;
+            m[u + 1] = (j + 1 <= i) ? t.y : 0.f;
           }
           *reinterpret_cast<uint2*>(at_h(rec + kRecM, i, c.half * 32 + e, kSboH64)) = pack_h4(m[0], m[1], m[2], m[3]);
         }
