@@ -899,10 +899,11 @@ __global__ void __launch_bounds__(1024) chunk_prefix_kernel(const int32_t* cu, i
 // (x0, x1) as bf16 pairs hi = bf16(x), lo = bf16(x - hi): hi + lo equals x to
 // about 2^-16 relative, so two kind::f16 products (hi, then lo) carry an fp32
 // operand more precisely than one tf32 product.
-__device__ __forceinline__ void split_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+__device__ __forceinline__ void split_bf16(float2 x, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x.x, x.y);
   const float2 hf = __bfloat1622float2(h);
-  const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+  const float2 r = __ffma2_rn(hf, make_float2(-1.f, -1.f), x);   // x - hi, exact
+  const __nv_bfloat162 l = __floats2bfloat162_rn(r.x, r.y);
   hi = *reinterpret_cast<const uint32_t*>(&h);
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
@@ -935,30 +936,26 @@ __device__ __forceinline__ void solve_doubling(const float* sA, float* sX, float
     const int p = tid >> 7, i = (tid >> 3) & 15, cc = (tid & 7) * 2;
     const float* arow = sA + (32 * p + 16 + i) * kPadA + 32 * p;
     const float* dcol = sX + (32 * p) * kPadA + 32 * p + cc;
-    float y0 = 0.f, y1 = 0.f;
+    float2 y = make_float2(0.f, 0.f);     // packed f32x2: the two columns' fused multiply-adds
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
       const float a = arow[k];
-      const float2 d = *reinterpret_cast<const float2*>(dcol + k * kPadA);
-      y0 += a * d.x;
-      y1 += a * d.y;
+      y = __ffma2_rn(make_float2(a, a), *reinterpret_cast<const float2*>(dcol + k * kPadA), y);
     }
-    *reinterpret_cast<float2*>(sY + p * 256 + i * 16 + cc) = make_float2(y0, y1);
+    *reinterpret_cast<float2*>(sY + p * 256 + i * 16 + cc) = y;
   }
   __syncthreads();
   {
     // X[2p+1][2p] = -D[2p+1] Y_p
     const int p = tid >> 7, i = (tid >> 3) & 15, cc = (tid & 7) * 2;
     const float* drow = sX + (32 * p + 16 + i) * kPadA + 32 * p + 16;
-    float x0 = 0.f, x1 = 0.f;
+    float2 x = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
       const float d = drow[k];
-      const float2 y = *reinterpret_cast<const float2*>(sY + p * 256 + k * 16 + cc);
-      x0 -= d * y.x;
-      x1 -= d * y.y;
+      x = __ffma2_rn(make_float2(-d, -d), *reinterpret_cast<const float2*>(sY + p * 256 + k * 16 + cc), x);
     }
-    *reinterpret_cast<float2*>(sX + (32 * p + 16 + i) * kPadA + 32 * p + cc) = make_float2(x0, x1);
+    *reinterpret_cast<float2*>(sX + (32 * p + 16 + i) * kPadA + 32 * p + cc) = x;
   }
   __syncthreads();
   const int r2 = (tid >> 4) * 2, c2 = (tid & 15) * 2;   // a 2 x 2 tile of a 32 x 32 product
@@ -968,40 +965,34 @@ __device__ __forceinline__ void solve_doubling(const float* sA, float* sX, float
     // may hold anything), two partial sums per output
     const float* a0 = sA + (32 + r2) * kPadA;
     const float* a1 = a0 + kPadA;
-    float z[2][2][2] = {};
+    float2 z[2][2] = {};                  // [k parity][row], the two columns packed
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       const float2 x = *reinterpret_cast<const float2*>(sX + k * kPadA + c2);
-      const float xa = k >= c2 ? x.x : 0.f, xb = k > c2 ? x.y : 0.f;
+      const float2 xab = make_float2(k >= c2 ? x.x : 0.f, k > c2 ? x.y : 0.f);
       const float u0 = a0[k], u1 = a1[k];
-      z[k & 1][0][0] += u0 * xa;
-      z[k & 1][0][1] += u0 * xb;
-      z[k & 1][1][0] += u1 * xa;
-      z[k & 1][1][1] += u1 * xb;
+      z[k & 1][0] = __ffma2_rn(make_float2(u0, u0), xab, z[k & 1][0]);
+      z[k & 1][1] = __ffma2_rn(make_float2(u1, u1), xab, z[k & 1][1]);
     }
-    *reinterpret_cast<float2*>(sY + r2 * 32 + c2) = make_float2(z[0][0][0] + z[1][0][0], z[0][0][1] + z[1][0][1]);
-    *reinterpret_cast<float2*>(sY + (r2 + 1) * 32 + c2) =
-        make_float2(z[0][1][0] + z[1][1][0], z[0][1][1] + z[1][1][1]);
+    *reinterpret_cast<float2*>(sY + r2 * 32 + c2) = __fadd2_rn(z[0][0], z[1][0]);
+    *reinterpret_cast<float2*>(sY + (r2 + 1) * 32 + c2) = __fadd2_rn(z[0][1], z[1][1]);
   }
   __syncthreads();
   {
     // X21 = -X22 Z (X22 = X[32..63][32..63]; X22[i][k] = 0 for k > i)
     const float* x0 = sX + (32 + r2) * kPadA + 32;
     const float* x1 = x0 + kPadA;
-    float v[2][2][2] = {};
+    float2 v[2][2] = {};
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       const float2 z = *reinterpret_cast<const float2*>(sY + k * 32 + c2);
       const float u0 = k <= r2 ? x0[k] : 0.f, u1 = k <= r2 + 1 ? x1[k] : 0.f;
-      v[k & 1][0][0] += u0 * z.x;
-      v[k & 1][0][1] += u0 * z.y;
-      v[k & 1][1][0] += u1 * z.x;
-      v[k & 1][1][1] += u1 * z.y;
+      v[k & 1][0] = __ffma2_rn(make_float2(u0, u0), z, v[k & 1][0]);
+      v[k & 1][1] = __ffma2_rn(make_float2(u1, u1), z, v[k & 1][1]);
     }
-    *reinterpret_cast<float2*>(sX + (32 + r2) * kPadA + c2) =
-        make_float2(-(v[0][0][0] + v[1][0][0]), -(v[0][0][1] + v[1][0][1]));
-    *reinterpret_cast<float2*>(sX + (33 + r2) * kPadA + c2) =
-        make_float2(-(v[0][1][0] + v[1][1][0]), -(v[0][1][1] + v[1][1][1]));
+    const float2 s0 = __fadd2_rn(v[0][0], v[1][0]), s1 = __fadd2_rn(v[0][1], v[1][1]);
+    *reinterpret_cast<float2*>(sX + (32 + r2) * kPadA + c2) = make_float2(-s0.x, -s0.y);
+    *reinterpret_cast<float2*>(sX + (33 + r2) * kPadA + c2) = make_float2(-s1.x, -s1.y);
   }
   __syncthreads();
 }
@@ -1284,7 +1275,8 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(hq[e]);
-          x[e] = pack_h2(f.x * s, f.y * s);
+          const float2 fs = __fmul2_rn(f, make_float2(s, s));
+          x[e] = pack_h2(fs.x, fs.y);
         }
         *reinterpret_cast<uint4*>(at_h(rq_dst, i, qd * 32 + m * 8, kSboH128)) = make_uint4(x[0], x[1], x[2], x[3]);
       }
@@ -1411,7 +1403,11 @@ __global__ void __launch_bounds__(kThreads, 3)
           const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
           const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
           *reinterpret_cast<uint2*>(at_h(rec + kRecKh, k, t, kSboH64)) =
-              pack_h4(f0.x * sc.x, f0.y * sc.y, f1.x * sc.z, f1.y * sc.w);
+              [&] {
+                const float2 p0 = __fmul2_rn(f0, make_float2(sc.x, sc.y));
+                const float2 p1 = __fmul2_rn(f1, make_float2(sc.z, sc.w));
+                return pack_h4(p0.x, p0.y, p1.x, p1.y);
+              }();
         }
       }
     }
@@ -1442,8 +1438,9 @@ __global__ void __launch_bounds__(kThreads, 3)
         for (int e = 0; e < 4; ++e) {
           const int t = tg * 8 + 2 * e;
           const float xa = t <= j ? xs[2 * e] : 0.f, xb = t + 1 <= j ? xs[2 * e + 1] : 0.f;
-          split_bf16(xa * bs[2 * e], xb * bs[2 * e + 1], hu[e], lu[e]);
-          split_bf16(xa * ws[2 * e], xb * ws[2 * e + 1], hw[e], lw[e]);
+          const float2 x2 = make_float2(xa, xb);
+          split_bf16(__fmul2_rn(x2, make_float2(bs[2 * e], bs[2 * e + 1])), hu[e], lu[e]);
+          split_bf16(__fmul2_rn(x2, make_float2(ws[2 * e], ws[2 * e + 1])), hw[e], lw[e]);
         }
         uh[it] = make_uint4(hu[0], hu[1], hu[2], hu[3]);
         ul[it] = make_uint4(lu[0], lu[1], lu[2], lu[3]);
