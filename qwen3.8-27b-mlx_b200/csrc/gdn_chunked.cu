@@ -1677,9 +1677,13 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
     }
     ptx::fence_proxy_async_smem();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] *= gl;
-      w[i] *= gl;
+    for (int i = 0; i < 16; i += 2) {          // packed f32x2
+      const float2 a = __fmul2_rn(make_float2(v[i], v[i + 1]), make_float2(gl, gl));
+      const float2 b = __fmul2_rn(make_float2(w[i], w[i + 1]), make_float2(gl, gl));
+      v[i] = a.x;
+      v[i + 1] = a.y;
+      w[i] = b.x;
+      w[i + 1] = b.y;
     }
     tc::tmem_st16(lane_cols + cDR, v);
     tc::tmem_st16(lane_cols + cDR + 16, w);
@@ -1693,10 +1697,12 @@ __global__ void __launch_bounds__(NORM ? kScanThreadsNorm : kScanThreads, 1) chu
 #pragma unroll
     for (int e = 0; e < 16; e += 4) {
       const float4 f = sU0[u0_index(cg * 4 + e / 4, c.row)];
-      u[e] += f.x;
-      u[e + 1] += f.y;
-      u[e + 2] += f.z;
-      u[e + 3] += f.w;
+      const float2 lo = __fadd2_rn(make_float2(u[e], u[e + 1]), make_float2(f.x, f.y));
+      const float2 hi = __fadd2_rn(make_float2(u[e + 2], u[e + 3]), make_float2(f.z, f.w));
+      u[e] = lo.x;
+      u[e + 1] = lo.y;
+      u[e + 2] = hi.x;
+      u[e + 3] = hi.y;
     }
 #pragma unroll
     for (int e = 0; e < 16; e += 8)
