@@ -2018,6 +2018,7 @@ int chunked_args(ChunkParams& p, const void* q, const void* k, const void* v, lo
     return fail(GDN_ERR_ALIAS, "state_out partially overlaps state_in");
   if (overlap(o, obytes, state_in, sbytes) || overlap(o, obytes, state_out, sbytes))
     return fail(GDN_ERR_ALIAS, "o overlaps a state buffer");
+  if (B == 0) return GDN_OK;               // nothing to launch: no CUDA call either
   int* err = nullptr;
   int rc = device_error_ptr(&err);
   if (rc != GDN_OK) return rc;

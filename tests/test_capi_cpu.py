@@ -167,3 +167,74 @@ def test_overlap_flag_is_refused_outside_the_dense_decode_entry():
                                     G.POOL_FINAL, v(FAKE + (3 << 32)), None, v(FAKE + (4 << 32)),
                                     1, 1, 16, 48, 128, 128, G.F_OVERLAP_PREV, None)
     assert rc == G.GDN_ERR_FLAGS
+
+
+# ---------------------------------------------------------------------------
+# the split chunked prefill (gdn_chunked_fwd_ws): argument checks and sizing
+# ---------------------------------------------------------------------------
+
+def chunked(**kw):
+    C = 2 * 16 * 128 + 48 * 128                  # q | k | v rows of the conv output
+    args = dict(q=FAKE, k=FAKE + 4096, v=FAKE + 8192, q_stride=C, k_stride=C, v_stride=C,
+                a=FAKE + (1 << 33), b=FAKE + (2 << 33), A_log=FAKE + (3 << 33), dt_bias=FAKE + (4 << 33),
+                state_in=None, state_out=FAKE + (5 << 33), o=FAKE + (6 << 33), cu=None,
+                B=1, T=256, Hk=16, Hv=48, Dk=128, Dv=128, flags=G.F_QK_L2NORM,
+                ws=FAKE + (8 << 33), ws_size=1 << 30)
+    args.update(kw)
+    p = lambda x: None if x is None else ctypes.c_void_p(x)  # noqa: E731
+    return G.lib().gdn_chunked_fwd_ws(p(args["q"]), p(args["k"]), p(args["v"]), args["q_stride"],
+                                      args["k_stride"], args["v_stride"], p(args["a"]), p(args["b"]),
+                                      p(args["A_log"]), p(args["dt_bias"]), p(args["state_in"]),
+                                      p(args["state_out"]), p(args["o"]), p(args["cu"]), args["B"], args["T"],
+                                      args["Hk"], args["Hv"], args["Dk"], args["Dv"], args["flags"],
+                                      p(args["ws"]), args["ws_size"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(flags=0x40000), G.GDN_ERR_FLAGS),
+    (dict(Dk=64), G.GDN_ERR_SHAPE),
+    (dict(Hk=5), G.GDN_ERR_SHAPE),             # 48 value heads are not a multiple of 5 key heads
+    (dict(T=-1), G.GDN_ERR_SHAPE),
+    (dict(q_stride=16 * 128 - 8), G.GDN_ERR_SHAPE),   # rows narrower than the heads
+    (dict(v_stride=48 * 128 - 8), G.GDN_ERR_SHAPE),
+    (dict(k_stride=2 * 16 * 128 + 48 * 128 + 4), G.GDN_ERR_ALIGN),   # not whole 16-byte pieces
+    (dict(q=FAKE + 8), G.GDN_ERR_ALIGN),
+    (dict(state_out=FAKE + (5 << 33) + 4), G.GDN_ERR_ALIGN),
+    (dict(q=None), G.GDN_ERR_NULL),
+    (dict(A_log=None), G.GDN_ERR_NULL),
+    (dict(o=None), G.GDN_ERR_NULL),
+    (dict(state_in=FAKE + (5 << 33) + 4096), G.GDN_ERR_ALIAS),     # partial overlap of the two states
+    (dict(o=FAKE + (5 << 33) + 65536), G.GDN_ERR_ALIAS),           # o inside state_out
+])
+def test_chunked_bad_arguments_are_rejected(kw, code):
+    assert chunked(**kw) == code
+    assert G.lib().gdn_last_error().decode() != ""
+
+
+def test_chunked_batch_zero_is_a_no_op():
+    assert chunked(B=0) == G.GDN_OK
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path only")
+def test_chunked_valid_call_without_gpu_reports_cuda_error_not_a_cpu_fallback():
+    assert chunked() == G.GDN_ERR_CUDA
+    assert chunked(cu=FAKE + (7 << 33), B=3, T=700) == G.GDN_ERR_CUDA
+
+
+def test_chunked_workspace_sizes():
+    """One pass needs a record per (chunk, value head) on top of a fixed
+    header; the smallest workspace (one chunk per sequence, windows) is far
+    below it and holds the carried state when the call keeps none; a packed
+    batch may need one partial chunk per sequence more than a uniform one."""
+    one = G.chunked_workspace_bytes(1, 4096, 48)
+    two = G.chunked_workspace_bytes(1, 8192, 48)
+    assert 0 < one < two
+    rec = (two - one) // (64 * 48)                       # bytes per (chunk, value head) record
+    assert rec % 256 == 0 and 64 * 1024 < rec < 160 * 1024
+    assert G.chunked_workspace_bytes(1, 4096, 24) < one
+    mn = G.chunked_workspace_min_bytes(1, 48, True)
+    assert 0 < mn < one
+    assert G.chunked_workspace_min_bytes(1, 48, False) >= mn + 48 * 128 * 128 * 4
+    assert G.chunked_workspace_bytes(8, 4096, 48, packed=True) >= G.chunked_workspace_bytes(8, 512, 48)
+    assert G.chunked_workspace_bytes(0, 0, 48) >= 0
+    assert G.lib().gdn_chunked_workspace_bytes(1, 64, 0, 0) == 0     # invalid sizes report 0
