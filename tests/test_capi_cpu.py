@@ -238,3 +238,93 @@ def test_chunked_workspace_sizes():
     assert G.chunked_workspace_bytes(8, 4096, 48, packed=True) >= G.chunked_workspace_bytes(8, 512, 48)
     assert G.chunked_workspace_bytes(0, 0, 48) >= 0
     assert G.lib().gdn_chunked_workspace_bytes(1, 64, 0, 0) == 0     # invalid sizes report 0
+
+
+# ---------------------------------------------------------------------------
+# conv1d, gated RMSNorm and the projection GEMM: argument checks
+# ---------------------------------------------------------------------------
+
+def conv(**kw):
+    args = dict(x=FAKE, w=FAKE + (1 << 33), state_in=None, state_out=None, y=FAKE + (2 << 33), cu=None,
+                B=2, T=100, C=640, K=4, flags=0)
+    args.update(kw)
+    p = lambda x: None if x is None else ctypes.c_void_p(x)  # noqa: E731
+    return G.lib().gdn_conv1d_fwd(p(args["x"]), p(args["w"]), p(args["state_in"]), p(args["state_out"]),
+                                  p(args["y"]), p(args["cu"]), args["B"], args["T"], args["C"], args["K"],
+                                  args["flags"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(K=3), G.GDN_ERR_SHAPE),
+    (dict(C=644), G.GDN_ERR_SHAPE),                # channels in whole 16-byte vectors
+    (dict(B=-1), G.GDN_ERR_SHAPE),
+    (dict(flags=0x1), G.GDN_ERR_FLAGS),
+    (dict(w=None), G.GDN_ERR_NULL),
+    (dict(y=None), G.GDN_ERR_NULL),
+    (dict(x=FAKE + 8), G.GDN_ERR_ALIGN),
+    (dict(y=FAKE + 4096), G.GDN_ERR_ALIAS),       # y over x (the halo rows are re-read)
+    (dict(state_out=FAKE + 64), G.GDN_ERR_ALIAS),  # the carried window over x
+])
+def test_conv_bad_arguments_are_rejected(kw, code):
+    assert conv(**kw) == code
+    assert G.lib().gdn_last_error().decode() != ""
+
+
+def test_conv_batch_zero_is_a_no_op():
+    assert conv(B=0) == G.GDN_OK
+
+
+def norm(**kw):
+    args = dict(o=FAKE, z=FAKE + (1 << 33), gamma=FAKE + (2 << 33), out=FAKE + (3 << 33), rows=4096, D=128,
+                flags=0)
+    args.update(kw)
+    p = lambda x: None if x is None else ctypes.c_void_p(x)  # noqa: E731
+    return G.lib().gdn_gated_rmsnorm_fwd(p(args["o"]), p(args["z"]), p(args["gamma"]), p(args["out"]),
+                                         args["rows"], args["D"], ctypes.c_float(1e-6), args["flags"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(D=64), G.GDN_ERR_SHAPE),
+    (dict(rows=-1), G.GDN_ERR_SHAPE),
+    (dict(flags=0x8000), G.GDN_ERR_FLAGS),
+    (dict(gamma=None), G.GDN_ERR_NULL),
+    (dict(z=FAKE + (1 << 33) + 4), G.GDN_ERR_ALIGN),
+    (dict(out=FAKE + 1024), G.GDN_ERR_ALIAS),     # out partly over o
+    (dict(out=FAKE + (1 << 33)), G.GDN_ERR_ALIAS),  # out over z
+])
+def test_norm_bad_arguments_are_rejected(kw, code):
+    assert norm(**kw) == code
+
+
+def test_norm_in_place_over_o_and_zero_rows_are_accepted():
+    assert norm(rows=0) == G.GDN_OK
+    if not torch.cuda.is_available():           # out == o passes the checks, then needs the GPU
+        assert norm(out=FAKE) == G.GDN_ERR_CUDA
+
+
+def gemm(**kw):
+    args = dict(A=FAKE, B=FAKE + (1 << 33), C=FAKE + (2 << 33), C32=None, M=256, N=512, K=5120, lda=5120,
+                ldb=5120, ldc=512, ld32=0, n_f32=0)
+    args.update(kw)
+    p = lambda x: None if x is None else ctypes.c_void_p(x)  # noqa: E731
+    return G.lib().gdn_gemm_bf16(p(args["A"]), p(args["B"]), p(args["C"]), p(args["C32"]), args["M"], args["N"],
+                                 args["K"], args["lda"], args["ldb"], args["ldc"], args["ld32"], args["n_f32"],
+                                 None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(K=5124, lda=5128, ldb=5128), G.GDN_ERR_SHAPE),   # K in whole 16-byte pieces
+    (dict(lda=5112), G.GDN_ERR_SHAPE),                      # stride below K
+    (dict(N=516, ldc=520), G.GDN_ERR_SHAPE),                # N a multiple of 8
+    (dict(ldc=500), G.GDN_ERR_SHAPE),
+    (dict(C32=FAKE + (3 << 33), n_f32=12, ld32=12), G.GDN_ERR_SHAPE),
+    (dict(A=None), G.GDN_ERR_NULL),
+    (dict(C=None), G.GDN_ERR_NULL),
+    (dict(B=FAKE + (1 << 33) + 8), G.GDN_ERR_ALIGN),
+])
+def test_gemm_bad_arguments_are_rejected(kw, code):
+    assert gemm(**kw) == code
+
+
+def test_gemm_no_rows_is_a_no_op():
+    assert gemm(M=0) == G.GDN_OK
